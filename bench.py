@@ -1,0 +1,308 @@
+#!/usr/bin/env python
+"""bench.py -- training tokens/s of forge-llm's ~125M Llama-style
+TrainableTransformer step (fwd + bwd + Adam) on 1..8 B200s.
+
+Workload: vocab 32000, d_model 768, 12 layers, 12 q / 4 kv
+heads x 64, SwiGLU hidden 2048, RMSNorm eps 1e-5, RoPE 10000, context 1024,
+global batch 64 sequences split over the ranks (strong scaling), weights
+initWeights(cfg, 5) ~N(0, 0.02), tokens uniform in [0, 32000) from RNG(5),
+Adam lr 3e-4.  A step is one lossBatch + backward + Adam.step through the
+forgellm API (the JS TrainableTransformer API), every kernel from
+libforgecu.so.
+
+One JSON line on rank 0.  `value` = whole-job tokens/s with the batch already
+in HBM; `e2e` = the same step through the public API with the batch copied
+from pinned host memory and the loss read back every step.  `roofline` is the
+matmulT contractions (the dominant kernels), timed live with CUDA events on
+the launching stream inside the timed region.  `cpu_baseline` is the CPU
+oracle (a restatement of the reference's JS loops) timed on a bounded sample
+on this host.  `--impl reference` times that CPU path alone (the reference is
+JavaScript and no JS runtime exists on this box).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "forge-llm_b200"))
+
+C5 = dict(vocabSize=32000, dim=768, nLayers=12, nHeads=12, nKvHeads=4, hidden=2048,
+          normEps=1e-5, ropeTheta=10000)
+GLOBAL_BATCH, SEQ, LR, SEED = 64, 1024, 3e-4, 5
+MATMUL_PARAMS = 100_073_472
+FLOP_PER_TOKEN = 6 * MATMUL_PARAMS + 12 * 3 * 2 * 768 * 1024   # 657.06 MFLOP (fwd + bwd)
+METRIC = "train tokens/s fwd+bwd+Adam (125M Llama-style, ctx 1024, global batch 64)"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(threads: int, tokens: int = 16):
+    """The CPU oracle on a bounded sample of the same workload: one sequence
+    of `tokens` tokens through the full config-5 model, forward + backward +
+    Adam over all 100M parameters.  Returns tokens/s."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as O
+    O.set_threads(threads)
+    cfg = O.Config(**C5)
+    P = O.init_weights(cfg, SEED)
+    ids = O.RNG(SEED).ints(tokens + 1, C5["vocabSize"])
+    G = np.zeros_like(P)
+    m, v = np.zeros_like(P), np.zeros_like(P)
+    t0 = time.perf_counter()
+    O.model_step(cfg, P, ids[:-1], ids[1:], 1, tokens, G)
+    O.adam_step(P, G, m, v, 1, lr=LR)
+    dt = time.perf_counter() - t0
+    return tokens / dt, dt
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    toks = 16
+    for _ in range(args.warmup):
+        cpu_baseline(threads, toks)
+    vals = [cpu_baseline(threads, toks) for _ in range(args.steps)]
+    tps = sum(v[0] for v in vals) / len(vals)
+    sec = sum(v[1] for v in vals) / len(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "c5-125m-train-step", "model": "llama-125m (forge-llm TrainableTransformer)",
+                   "global_batch": GLOBAL_BATCH, "seq_len": SEQ, "parallelism": "none (host CPU)"},
+        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"1 sequence x {toks} tokens of the config-5 model, fwd+bwd+Adam "
+                                   "over all 100M params; the reference is JavaScript and this box "
+                                   "has no JS runtime, so its C restatement (oracle/) runs"},
+        "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--precision", default=os.environ.get("FORGECU_PRECISION", "fp32"),
+                    choices=["fp32", "tf32x3", "bf16"])
+    ap.add_argument("--batch", type=int, default=GLOBAL_BATCH)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    import forgellm as F
+    from forgellm import autograd as AD
+    from forgellm import tensor as TS
+    from forgellm._lib import lib
+    from forgellm.dist import DataParallel, shard_rows
+    F.set_precision(args.precision)
+
+    cfg = F.Config(**C5)
+    model = F.TrainableTransformer(cfg, seed=SEED)
+    opt = F.Adam(model.paramList, lr=LR)
+    dp = DataParallel(model) if world > 1 else None
+    toks = F.RNG(SEED).ints(args.batch * (SEQ + 1), C5["vocabSize"]).reshape(args.batch, SEQ + 1)
+    local_rows = toks if world == 1 else shard_rows(torch.from_numpy(toks), rank, world).numpy()
+    batch_dev = torch.from_numpy(np.ascontiguousarray(local_rows)).cuda()
+    batch_host = torch.from_numpy(np.ascontiguousarray(local_rows)).pin_memory()
+
+    def step(batch):
+        F.resetTape()
+        model.zeroGrad()
+        loss = model.lossBatch(batch)
+        AD.backward(loss)
+        if dp is not None:
+            dp.finish()
+        opt.step()
+        return loss
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---------------- warm-up
+    for _ in range(args.warmup):
+        step(batch_dev)
+    barrier()
+
+    # ---------------- timed region 1: inputs resident in HBM
+    sampler = ClockSampler(local)
+    sampler.start()
+    TS.GEMM_TIMER = []
+    launches0 = lib().fcu_launch_count()
+    stream = torch.cuda.current_stream()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step(batch_dev)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = lib().fcu_launch_count() - launches0
+    ms = ev0.elapsed_time(ev1)
+    gemm = TS.GEMM_TIMER
+    TS.GEMM_TIMER = None
+    clocks = sampler.stop()
+    gemm_ms = sum(a.elapsed_time(b) for _, a, b in gemm)
+    gemm_flops = sum(f for f, _, _ in gemm)
+    t = torch.tensor([ms, gemm_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, gemm_ms_max = float(t[0]), float(t[1])
+    tokens_per_step = args.batch * SEQ
+    value = tokens_per_step * args.steps / (ms / 1e3)
+
+    # ---------------- timed region 2: end to end through the public API
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        b = batch_host.to("cuda", non_blocking=True)
+        F.resetTape()
+        model.zeroGrad()
+        loss = model.lossBatch(b)
+        AD.backward(loss)
+        if dp is not None:
+            dp.finish()
+        opt.step()
+        _ = float(loss.data[0].item())          # device -> host read of the loss
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = tokens_per_step * args.steps / (float(te[0]) / 1e3)
+
+    if rank == 0:
+        pk, pk_kind = peaks()
+        achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
+        peak = pk["bf16_tflops_sustained"]
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": {"fp32": "f32", "tf32x3": "f32 (3xtf32 tensor cores)",
+                      "bf16": "bf16 operands, f32 accumulate/master"}[args.precision],
+            "data": "synthetic (RNG(5) tokens, initWeights seed 5)",
+            "config": {"workload": "c5-125m-train-step",
+                       "model": "llama-125m (forge-llm TrainableTransformer: V32000 D768 L12 H12/4 F2048)",
+                       "global_batch": args.batch, "seq_len": SEQ, "parallelism": f"dp{world}",
+                       "precision": args.precision, "l2": "working set >> L2 (GBs of activations)"},
+            "e2e": {"value": e2e_value, "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(args.batch * (SEQ + 1) * 4),
+                    "d2h_bytes_per_step": 4 * world},
+            "gpu_launches": int(launches),
+            "roofline": {"kernel": "matmulT contractions (fcu_matmulT_fwd/bwd)", "bound": "tensor",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak if peak else None,
+                         "peak_kind": f"bf16 dense sustained ({pk_kind})", "traffic": None,
+                         "gemm_share_of_step": gemm_ms / ms if ms else None,
+                         "model_tflops": FLOP_PER_TOKEN * value / 1e12},
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            tps, sec = cpu_baseline(1)
+            line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": 1, "kind": "port",
+                                    "sample": "1 sequence x 16 tokens of the config-5 model, "
+                                              f"fwd+bwd+Adam over all 100M params ({sec:.1f} s)"}
+        print(json.dumps(line), flush=True)
+    if dp is not None:
+        dp.detach()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

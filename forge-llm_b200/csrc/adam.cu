@@ -1,0 +1,160 @@
+// Adam with global-norm clipping (src/L2/autograd.js:214-244).
+//
+// Two passes over the flat parameter vector: a deterministic double-precision
+// sum of squares of the gradients (fixed grid, fixed reduction order), then
+// one fused update pass that reads p, g, m, v once and writes p, m, v once
+// (28 bytes per parameter).  The per-element arithmetic is in double, like the
+// JS, with fp32 stores.
+#include <math.h>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+
+__global__ void sumsq_partial_kernel(const float *__restrict__ g, int64_t n,
+                                     double *__restrict__ part, int vec) {
+  __shared__ double sh[32];
+  double s = 0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t n4 = vec ? (n >> 2) : 0;
+  const float4 *g4 = reinterpret_cast<const float4 *>(g);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    float4 v = g4[i];
+    s += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+  }
+  for (int64_t i = (n4 << 2) + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride)
+    s += (double)g[i] * g[i];
+  s = block_sum(s, sh);
+  if (threadIdx.x == 0) part[blockIdx.x] = s;
+}
+
+__global__ void sumsq_final_kernel(const double *__restrict__ part, int nblk,
+                                   double *__restrict__ out, int acc) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    double s = 0;
+    for (int b = 0; b < nblk; b++) s += part[b];
+    out[0] = acc ? out[0] + s : s;
+  }
+}
+
+struct Hyper {
+  double lr, b1, b2, eps, wd, clip, bc1, bc2;
+};
+
+__device__ __forceinline__ void adam_elem(float &p, float g, float &m, float &v, double scale,
+                                          const Hyper &h) {
+  double gg = (double)g * scale + h.wd * (double)p;
+  m = (float)(h.b1 * (double)m + (1.0 - h.b1) * gg);
+  v = (float)(h.b2 * (double)v + (1.0 - h.b2) * gg * gg);
+  double mh = (double)m / h.bc1;
+  double vh = (double)v / h.bc2;
+  p = (float)((double)p - h.lr * mh / (sqrt(vh) + h.eps));
+}
+
+__global__ void adam_update_kernel(float *__restrict__ p, const float *__restrict__ g,
+                                   float *__restrict__ m, float *__restrict__ v, int64_t n, Hyper h,
+                                   const double *__restrict__ sumsq, double *__restrict__ info,
+                                   int vec) {
+  const double gnorm = sqrt(sumsq[0]);
+  const double scale = gnorm > h.clip ? h.clip / gnorm : 1.0;
+  if (info && blockIdx.x == 0 && threadIdx.x == 0) {
+    info[0] = gnorm;
+    info[1] = scale;
+  }
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t start = 0;
+  if (vec) {
+    const int64_t n4 = n >> 2;
+    float4 *p4 = reinterpret_cast<float4 *>(p);
+    float4 *m4 = reinterpret_cast<float4 *>(m);
+    float4 *v4 = reinterpret_cast<float4 *>(v);
+    const float4 *g4 = reinterpret_cast<const float4 *>(g);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+      float4 pp = p4[i], gg = g4[i], mm = m4[i], vv = v4[i];
+      adam_elem(pp.x, gg.x, mm.x, vv.x, scale, h);
+      adam_elem(pp.y, gg.y, mm.y, vv.y, scale, h);
+      adam_elem(pp.z, gg.z, mm.z, vv.z, scale, h);
+      adam_elem(pp.w, gg.w, mm.w, vv.w, scale, h);
+      p4[i] = pp;
+      m4[i] = mm;
+      v4[i] = vv;
+    }
+    start = n4 << 2;
+  }
+  for (int64_t i = start + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    float pp = p[i], mm = m[i], vv = v[i];
+    adam_elem(pp, g[i], mm, vv, scale, h);
+    p[i] = pp;
+    m[i] = mm;
+    v[i] = vv;
+  }
+}
+
+inline bool aligned16(const void *a) { return ((uintptr_t)a & 15) == 0; }
+
+int sumsq_impl(fcu_ctx *ctx, const float *g, int64_t n, double *out, int acc) {
+  const int nblk = 2 * ctx->num_sms;
+  void *scr = nullptr;
+  int rc = fcu::ctx_scratch(ctx, sizeof(double) * nblk, &scr);
+  if (rc) return rc;
+  sumsq_partial_kernel<<<nblk, kThreads, 0, ctx->stream>>>(g, n, (double *)scr, aligned16(g) ? 1 : 0);
+  FCU_CHECK_LAUNCH();
+  sumsq_final_kernel<<<1, 32, 0, ctx->stream>>>((const double *)scr, nblk, out, acc);
+  FCU_CHECK_LAUNCH();
+  return FCU_OK;
+}
+
+int update_impl(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int64_t n,
+                const fcu_adam_hyper *hh, const double *sumsq, double *info) {
+  Hyper h{hh->lr, hh->b1, hh->b2, hh->eps, hh->wd, hh->clip, hh->bc1, hh->bc2};
+  int vec = aligned16(p) && aligned16(g) && aligned16(m) && aligned16(v);
+  int64_t work = vec ? (n >> 2) : n;
+  int64_t blocks = (work + kThreads - 1) / kThreads;
+  int64_t cap = 16 * (int64_t)ctx->num_sms;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  adam_update_kernel<<<(int)blocks, kThreads, 0, ctx->stream>>>(p, g, m, v, n, h, sumsq, info, vec);
+  FCU_CHECK_LAUNCH();
+  return FCU_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fcu_sumsq(fcu_ctx *ctx, const float *g, int64_t n, double *sumsq_dev, int accumulate) {
+  FCU_CTX(ctx);
+  FCU_REQUIRE(n >= 0 && g && sumsq_dev, "fcu_sumsq: bad args");
+  return sumsq_impl(ctx, g, n, sumsq_dev, accumulate);
+}
+
+int fcu_adam_step_sumsq(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int64_t n,
+                        const fcu_adam_hyper *h, const double *sumsq_dev, double *info_dev) {
+  FCU_CTX(ctx);
+  FCU_REQUIRE(n >= 0 && p && g && m && v && h && sumsq_dev, "fcu_adam_step: bad args");
+  FCU_REQUIRE(h->bc1 > 0 && h->bc2 > 0, "fcu_adam_step: bias corrections must be > 0 (t >= 1)");
+  if (n == 0) return FCU_OK;
+  return update_impl(ctx, p, g, m, v, n, h, sumsq_dev, info_dev);
+}
+
+int fcu_adam_step(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int64_t n,
+                  const fcu_adam_hyper *h, double *info_dev) {
+  FCU_CTX(ctx);
+  FCU_REQUIRE(n >= 0 && p && g && m && v && h, "fcu_adam_step: bad args");
+  FCU_REQUIRE(h->bc1 > 0 && h->bc2 > 0, "fcu_adam_step: bias corrections must be > 0 (t >= 1)");
+  if (n == 0) return FCU_OK;
+  // The sum of squares lands in the tail of the context scratch, after the
+  // per-block partials that sumsq_impl keeps at its head.
+  const int nblk = 2 * ctx->num_sms;
+  void *scr = nullptr;
+  int rc = fcu::ctx_scratch(ctx, sizeof(double) * (nblk + 1), &scr);
+  if (rc) return rc;
+  double *ss = (double *)scr + nblk;
+  rc = sumsq_impl(ctx, g, n, ss, 0);
+  if (rc) return rc;
+  return update_impl(ctx, p, g, m, v, n, h, ss, info_dev);
+}
+
+}  // extern "C"

@@ -1,0 +1,96 @@
+// Shared definitions for the libforgecu.so kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include <string>
+
+#include "../../include/forgecu.h"
+
+struct fcu_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int precision = FCU_PREC_FP32;
+  int num_sms = 148;
+  // Scratch owned by the context (grown on demand, freed by fcu_ctx_destroy).
+  void *scratch = nullptr;
+  size_t scratch_bytes = 0;
+  // RoPE cos/sin table cache: (cos, sin) doubles for [rope_pos][rope_half].
+  double2 *rope_tab = nullptr;
+  int rope_pos = 0, rope_half = 0;
+  double rope_theta = 0;
+};
+
+namespace fcu {
+
+void set_error(const char *fmt, ...);
+int cuda_fail(cudaError_t e, const char *what, const char *file, int line);
+// Returns a device buffer of at least `bytes` owned by ctx (reused across
+// calls; contents undefined).
+int ctx_scratch(fcu_ctx *ctx, size_t bytes, void **out);
+
+inline int div_up(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
+
+// Number of kernels this library has launched (fcu_launch_count).
+void note_launch();
+
+}  // namespace fcu
+
+#define FCU_CHECK_CUDA(expr)                                                  \
+  do {                                                                        \
+    cudaError_t _e = (expr);                                                  \
+    if (_e != cudaSuccess) return fcu::cuda_fail(_e, #expr, __FILE__, __LINE__); \
+  } while (0)
+
+#define FCU_CHECK_LAUNCH()           \
+  do {                               \
+    fcu::note_launch();              \
+    FCU_CHECK_CUDA(cudaGetLastError()); \
+  } while (0)
+
+#define FCU_REQUIRE(cond, ...)            \
+  do {                                    \
+    if (!(cond)) {                        \
+      fcu::set_error(__VA_ARGS__);        \
+      return FCU_ERR_ARG;                 \
+    }                                     \
+  } while (0)
+
+#define FCU_CTX(ctx) FCU_REQUIRE((ctx) != nullptr, "null fcu_ctx")
+
+// ---------------------------------------------------------------- device helpers
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum over blockDim.x threads (multiple of 32, <= 1024).  `sh`
+// holds >= 32 entries.  Result valid in every thread.
+template <typename T>
+__device__ __forceinline__ T block_sum(T v, T *sh) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if (lane == 0) sh[wid] = v;
+  __syncthreads();
+  T r = lane < nw ? sh[lane] : T(0);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+  return r;
+}

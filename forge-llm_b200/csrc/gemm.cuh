@@ -1,0 +1,21 @@
+// Internal GEMM interface shared by gemm.cu (CUDA-core path and dispatch)
+// and gemm_tc.cu (tcgen05 tensor-core path).
+#pragma once
+#include "common.cuh"
+
+namespace fcu {
+
+// The three contractions of matmulT, all computing C[M,N] (+)= ...:
+//   kFwd: C = A[M,K] . B[N,K]^T   (Y = X . W^T)
+//   kDx : C = A[M,K] . B[K,N]     (dX = dY . W)
+//   kDw : C = A[K,M]^T . B[K,N]   (dW = dY^T . X)
+enum class GemmOp { kFwd = 0, kDx = 1, kDw = 2 };
+
+int gemm_simt(cudaStream_t st, GemmOp op, const float *A, const float *B, float *C, int64_t M,
+              int64_t N, int64_t K, int beta);
+int gemm_tc(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float *C, int64_t M,
+            int64_t N, int64_t K, int beta);
+int gemm_dispatch(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float *C, int64_t M,
+                  int64_t N, int64_t K, int beta);
+
+}  // namespace fcu

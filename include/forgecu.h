@@ -1,0 +1,232 @@
+/*
+ * forgecu.h -- the C-ABI of libforgecu.so, the B200 (sm_100a) implementation
+ * of forge-llm's training hot path.
+ *
+ * This is the drop-in boundary.  forge-llm's operators (src/L2/tensor.js,
+ * src/L2/autograd.js, src/L6/train.js) keep their JavaScript signatures; a
+ * host binding (N-API addon, ctypes, ...) marshals their typed arrays to
+ * device buffers and calls the entry points below.  Each entry point cites
+ * the JS function it replaces.
+ *
+ * Conventions
+ *   - Every tensor is a plain device pointer to row-major, token-major data
+ *     (fp32 unless the name says otherwise), exactly the Float32Array layout
+ *     the JS uses.  Sizes are int64_t element counts.
+ *   - Gradient outputs follow the JS `grad += ...` contract: an `accumulate`
+ *     flag of 1 adds into the buffer, 0 overwrites it (the JS `??=` of a fresh
+ *     zero array followed by `+=`).
+ *   - All work is enqueued on the context's stream (fcu_ctx_set_stream) and
+ *     returns without waiting; fcu_sync waits.  A context is not re-entrant.
+ *   - Every function returns an fcu_status; FCU_OK is 0.  On any other value
+ *     fcu_last_error() (thread-local) describes the failure.  Shapes are
+ *     validated before anything is launched.
+ */
+#ifndef FORGECU_H
+#define FORGECU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+typedef enum {
+  FCU_OK = 0,
+  FCU_ERR_ARG = -1,        /* bad shape, null pointer, unsupported size */
+  FCU_ERR_CUDA = -2,       /* a CUDA runtime/driver call failed */
+  FCU_ERR_NCCL = -3,       /* a collective failed */
+  FCU_ERR_TIMEOUT = -4,    /* a bounded wait ran out */
+  FCU_ERR_UNSUPPORTED = -5 /* not available on this device / build */
+} fcu_status;
+
+/* Arithmetic used by the contractions (matmulT, attention).
+ *   FP32   : fp32 operands and accumulation on the CUDA cores.  Parity mode:
+ *            relL2 <= 1e-5 against the JS operators.
+ *   TF32X3 : tensor cores (tcgen05 kind::tf32), each operand split into a
+ *            tf32 head and a tf32 tail, three products, fp32 accumulate.
+ *            Same relL2 <= 1e-5 bound as FP32.
+ *   BF16   : tensor cores (tcgen05 kind::f16) on bf16-rounded operands, fp32
+ *            accumulate.  Looser bound, relL2 <= 1e-2 (stated per test). */
+typedef enum { FCU_PREC_FP32 = 0, FCU_PREC_TF32X3 = 1, FCU_PREC_BF16 = 2 } fcu_precision;
+
+typedef struct fcu_ctx fcu_ctx;
+
+/* ---------------------------------------------------------------- context */
+const char *fcu_last_error(void);
+const char *fcu_version(void);
+int fcu_ctx_create(int device, fcu_ctx **out);
+int fcu_ctx_destroy(fcu_ctx *ctx);
+int fcu_ctx_set_stream(fcu_ctx *ctx, void *cuda_stream); /* NULL = legacy default stream */
+int fcu_ctx_set_precision(fcu_ctx *ctx, int precision);   /* fcu_precision */
+int fcu_ctx_get_precision(const fcu_ctx *ctx);
+int fcu_sync(fcu_ctx *ctx);
+/* Kernels launched by this library since it was loaded (all contexts). */
+unsigned long long fcu_launch_count(void);
+
+/* Device memory for hosts without an allocator of their own (the N-API
+ * addon).  The Python host allocates through PyTorch instead. */
+int fcu_malloc(fcu_ctx *ctx, size_t bytes, void **out);
+int fcu_free(fcu_ctx *ctx, void *ptr);
+int fcu_memcpy_h2d(fcu_ctx *ctx, void *dst, const void *src, size_t bytes);
+int fcu_memcpy_d2h(fcu_ctx *ctx, void *dst, const void *src, size_t bytes);
+int fcu_memset_zero(fcu_ctx *ctx, void *dst, size_t bytes);
+
+/* ---------------------------------------------------------------- matmulT */
+/* Y[M,N] = X[M,K] . W[N,K]^T.
+ * Replaces matmulT forward, src/L2/tensor.js:34-36 (-> gemm, src/L0/numeric.js:111-129). */
+int fcu_matmulT_fwd(fcu_ctx *ctx, const float *X, const float *W, float *Y, int64_t M, int64_t K,
+                    int64_t N);
+
+/* dX[M,K] (+)= dY[M,N] . W[N,K];  dW[N,K] (+)= dY^T . X.  Either output may be
+ * NULL to skip it.  Replaces the matmulT closure, src/L2/tensor.js:37-52. */
+int fcu_matmulT_bwd(fcu_ctx *ctx, const float *dY, const float *X, const float *W, float *dX,
+                    int accumulate_dx, float *dW, int accumulate_dw, int64_t M, int64_t K,
+                    int64_t N);
+
+/* ---------------------------------------------------------------- embedding */
+/* out[T,D] = W[ids[t], :].  Replaces embedLookup, src/L2/tensor.js:85-91. */
+int fcu_embed_fwd(fcu_ctx *ctx, const float *W, const int32_t *ids, int64_t T, int64_t V,
+                  int64_t D, float *out);
+/* dW[ids[t], :] += dX[t, :], deterministic: every row of dW receives its terms
+ * in ascending t, as the JS loop adds them (src/L2/tensor.js:92-98). */
+int fcu_embed_bwd(fcu_ctx *ctx, const float *dX, const int32_t *ids, int64_t T, int64_t V,
+                  int64_t D, float *dW);
+
+/* ---------------------------------------------------------------- rmsNorm */
+/* out = X * inv[t] * w, inv[t] = 1/sqrt(mean(X[t]^2) + eps) (stored).
+ * Replaces rmsNorm forward, src/L2/tensor.js:103-113. */
+int fcu_rmsnorm_fwd(fcu_ctx *ctx, const float *X, const float *w, int64_t T, int64_t D, double eps,
+                    float *out, float *inv);
+/* Replaces the rmsNorm closure, src/L2/tensor.js:114-127. */
+int fcu_rmsnorm_bwd(fcu_ctx *ctx, const float *dY, const float *X, const float *w,
+                    const float *inv, int64_t T, int64_t D, float *dX, int accumulate_dx,
+                    float *dw, int accumulate_dw);
+
+/* ---------------------------------------------------------------- ropeRows */
+/* Interleaved-pair rotation, position pos0 + (posStride > 0 ? t % posStride : t).
+ * Replaces ropeRows, src/L2/tensor.js:133-149; backward (R^T) :150-165. */
+int fcu_rope_fwd(fcu_ctx *ctx, const float *X, int64_t T, int nHead, int dHead, int pos0,
+                 double theta, int posStride, float *out);
+int fcu_rope_bwd(fcu_ctx *ctx, const float *dY, int64_t T, int nHead, int dHead, int pos0,
+                 double theta, int posStride, float *dX, int accumulate);
+
+/* ---------------------------------------------------------------- sliceCols */
+/* out[M,len] = X[:, off:off+len].  Replaces sliceCols, src/L2/tensor.js:170-183. */
+int fcu_slicecols_fwd(fcu_ctx *ctx, const float *X, int64_t M, int64_t K, int64_t off,
+                      int64_t len, float *out);
+int fcu_slicecols_bwd(fcu_ctx *ctx, const float *dY, int64_t M, int64_t K, int64_t off,
+                      int64_t len, float *dX, int accumulate);
+
+/* ---------------------------------------------------------------- attention */
+/* Causal attention with GQA (kv head = h / (nH/nKV)) over B sequences of T
+ * tokens under the block-diagonal causal mask; B == 1 is causalAttn.
+ * Q [B*T, nH*dH], K/V [B*T, nKV*dH], O like Q, lse [B, nH, T] = log-sum-exp
+ * of each score row (kept for the backward instead of the JS's T x T P).
+ * Replaces causalAttn (src/L2/tensor.js:191-229) and causalAttnBatch
+ * (src/L2/tensor.js:299-337).  Requires nH % nKV == 0 and 1 <= dH <= 128. */
+int fcu_attn_fwd(fcu_ctx *ctx, const float *Q, const float *K, const float *V, int B, int T,
+                 int nH, int nKV, int dH, float *O, float *lse);
+/* Replaces the attention closures, src/L2/tensor.js:231-267 / :339-375. */
+int fcu_attn_bwd(fcu_ctx *ctx, const float *dO, const float *Q, const float *K, const float *V,
+                 const float *O, const float *lse, int B, int T, int nH, int nKV, int dH,
+                 float *dQ, float *dK, float *dV, int accumulate);
+
+/* ---------------------------------------------------------------- swiglu */
+/* out = G * sigmoid(G) * U.  Replaces swigluRows, src/L2/tensor.js:272-280. */
+int fcu_swiglu_fwd(fcu_ctx *ctx, const float *G, const float *U, int64_t n, float *out);
+/* Replaces the swigluRows closure, src/L2/tensor.js:281-289. */
+int fcu_swiglu_bwd(fcu_ctx *ctx, const float *dO, const float *G, const float *U, int64_t n,
+                   float *dG, float *dU, int accumulate);
+
+/* ---------------------------------------------------------------- residual add */
+/* out = a + b; backward passes g to both (src/L6/train.js:230-238). */
+int fcu_add_fwd(fcu_ctx *ctx, const float *a, const float *b, int64_t n, float *out);
+int fcu_add_bwd(fcu_ctx *ctx, const float *g, int64_t n, float *da, int accumulate_a, float *db,
+                int accumulate_b);
+
+/* ---------------------------------------------------------------- cross entropy */
+/* Fused crossEntropyMean forward and unit-gradient pass (src/L2/tensor.js:393-417):
+ * loss_out[0] = -(1/T) sum_t log softmax(logits_t)[targets_t]  (device scalar)
+ * dunit[T,V]  = (softmax(logits_t) - onehot(targets_t)) / T
+ * One read of logits; dunit may alias logits (in-place).  The backward of the
+ * JS closure is then dLogits += g * dunit (fcu_axpy). */
+int fcu_ce_fwd(fcu_ctx *ctx, const float *logits, const int32_t *targets, int64_t T, int64_t V,
+               float *loss_out, float *dunit);
+
+/* y (+)= alpha_dev[0] * x, alpha read from device memory (a loss gradient). */
+int fcu_axpy_dev(fcu_ctx *ctx, const float *alpha_dev, const float *x, int64_t n, float *y,
+                 int accumulate);
+
+/* ---------------------------------------------------------------- weightedSum */
+/* out[0] = sum_i Y[i] t[i] (src/L2/tensor.js:380-389), device scalar. */
+int fcu_wsum_fwd(fcu_ctx *ctx, const float *Y, const float *t, int64_t n, float *out);
+
+/* ---------------------------------------------------------------- Adam */
+typedef struct {
+  double lr;    /* the cosine-scheduled lr of this step (autograd.js:229) */
+  double b1, b2, eps, wd, clip;
+  double bc1;   /* 1 - b1^t */
+  double bc2;   /* 1 - b2^t */
+} fcu_adam_hyper;
+
+/* One Adam step over flat p/g/m/v of n elements (all params concatenated in
+ * paramList order), with global-norm clipping: gnorm = ||g||_2 over all n,
+ * scale = gnorm > clip ? clip/gnorm : 1, then per element
+ * g' = g*scale + wd*p; m = b1 m + (1-b1) g'; v = b2 v + (1-b2) g'^2;
+ * p -= lr * (m/bc1) / (sqrt(v/bc2) + eps).
+ * info_dev (device, 2 doubles) receives {gnorm, scale}.
+ * Replaces Adam.step, src/L2/autograd.js:221-243. */
+int fcu_adam_step(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int64_t n,
+                  const fcu_adam_hyper *h, double *info_dev);
+
+/* Same update with the gradient sum of squares supplied by the caller
+ * (device double, e.g. after an all-reduce); info_dev as above. */
+int fcu_adam_step_sumsq(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int64_t n,
+                        const fcu_adam_hyper *h, const double *sumsq_dev, double *info_dev);
+
+/* sumsq_dev[0] (+)= sum g[i]^2 in double, deterministic. */
+int fcu_sumsq(fcu_ctx *ctx, const float *g, int64_t n, double *sumsq_dev, int accumulate);
+
+/* ---------------------------------------------------------------- RNG / init (host) */
+/* xorshift128+ with splitmix32 seeding, Box-Muller normals: the seeded
+ * generator every forge-llm config draws from (RNG, src/L0/numeric.js:27-49).
+ * Host functions; they touch no device. */
+typedef struct { uint32_t s0, s1; } fcu_rng;
+void fcu_rng_init(fcu_rng *r, uint32_t seed);
+double fcu_rng_next(fcu_rng *r);
+double fcu_rng_normal(fcu_rng *r);
+int fcu_rng_int(fcu_rng *r, int n);
+/* out[i] = (float)(normal() * scale), i in [0, n): the `Float32Array` fill of
+ * initWeights / randArr. */
+void fcu_rng_fill_normal(fcu_rng *r, float *host_out, int64_t n, double scale);
+void fcu_rng_fill_int(fcu_rng *r, int32_t *host_out, int64_t n, int range);
+
+/* Model shape (Config, src/L6/transformer.js:29-53). */
+typedef struct {
+  int vocab, dim, n_layers, n_heads, n_kv_heads, hidden;
+  double norm_eps, rope_theta;
+} fcu_model_cfg;
+
+/* Number of parameters in the flat layout below. */
+int64_t fcu_model_num_params(const fcu_model_cfg *cfg);
+/* initWeights (src/L6/train.js:33-57) into one flat host array in paramList
+ * order (toParams, src/L6/train.js:60-78): tok_emb[V*D], ln_f[D], then per
+ * layer ln1[D], ln2[D], wqkv[qkvOut*D], wo[D*qD], ffn_gate[H*D], ffn_up[H*D],
+ * ffn_down[D*H]. */
+int fcu_init_weights(const fcu_model_cfg *cfg, uint32_t seed, float *host_out);
+
+/* ---------------------------------------------------------------- misc */
+/* y[i] *= alpha (data-parallel gradient averaging). */
+int fcu_scale(fcu_ctx *ctx, float *y, int64_t n, float alpha);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif /* FORGECU_H */
