@@ -154,6 +154,11 @@ int gemm_dispatch(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float
 
 extern "C" {
 
+int fcu_check_device_error(fcu_ctx *ctx) {
+  FCU_CTX(ctx);
+  return fcu::gemm_tc_error(ctx);
+}
+
 int fcu_matmulT_fwd(fcu_ctx *ctx, const float *X, const float *W, float *Y, int64_t M, int64_t K,
                     int64_t N) {
   FCU_CTX(ctx);

@@ -19,3 +19,11 @@ int gemm_dispatch(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float
                   int64_t N, int64_t K, int beta);
 
 }  // namespace fcu
+
+namespace fcu {
+// True when the tensor-core path can take this shape (TMA row strides).
+bool gemm_tc_supported(GemmOp op, int64_t M, int64_t N, int64_t K);
+// FCU_ERR_TIMEOUT if a tensor-core kernel on this context recorded a bounded
+// wait that ran out (synchronises the stream).
+int gemm_tc_error(fcu_ctx *ctx);
+}  // namespace fcu

@@ -1,12 +1,571 @@
-// Tensor-core (tcgen05) GEMM path -- placeholder until the sm_100a kernel lands.
+// Tensor-core GEMM for sm_100a: tcgen05.mma with TMEM accumulators, operands
+// staged in shared memory by TMA, persistent warp-specialised CTAs.
+//
+//   C[M,N] (+)= sum_k A(m,k) B(n,k)      (bf16 operands, fp32 accumulate)
+//
+// A and B are each either K-major (k contiguous: the forward's X and W, the
+// dX contraction's dY) or MN-major (m/n contiguous: W in dX = dY.W, both
+// operands of dW = dY^T.X).  tcgen05 reads both majors straight from the
+// 128-byte-swizzled tiles TMA writes, so no operand is ever transposed.
+//
+// CTA = 6 warps, one CTA per SM, looping over output tiles:
+//   warp 0      TMA producer: STAGES-deep ring of (A,B) k-blocks
+//   warp 1      TMEM owner + MMA issuer (one thread): 4 x (128x256x16) per k-block
+//   warps 2..5  epilogue: TMEM -> registers -> global, double-buffered
+//               accumulators so the epilogue of tile i overlaps the
+//               mainloop of tile i+1 (2 x 256 TMEM columns = all 512).
+// Every wait is bounded: on timeout the CTA records an error, drains what it
+// issued, frees TMEM and returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
 #include "gemm.cuh"
 
 namespace fcu {
+namespace {
 
-int gemm_tc(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float *C, int64_t M,
-            int64_t N, int64_t K, int beta) {
-  set_error("tensor-core precision mode %d is not built yet", ctx->precision);
-  return FCU_ERR_UNSUPPORTED;
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int UMMA_K = 16;
+constexpr int A_BYTES = BM * BK * 2;            // 16 KB
+constexpr int B_BYTES = BN * BK * 2;            // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
+constexpr int NUM_THREADS = 192;
+constexpr uint32_t TMEM_COLS = 2 * BN;          // 512
+constexpr int GROUP_M = 16;                     // tile raster: GROUP_M m-blocks per n sweep
+constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + (size_t)STAGES * STAGE_BYTES + 256;
+constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 2 GHz
+
+struct TcParams {
+  int M, N, K;
+  float *C;
+  int64_t ldc;
+  int beta;
+  int a_mn, b_mn;
+  int tiles_m, tiles_n;
+  int *err;
+};
+
+// ------------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: false if the phase did not complete within kWaitCycles or
+// another role of this CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) return false;
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32"
+      " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15,"
+      " %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31},"
+      " [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor (sm_100 "version 1" format), 128B swizzle:
+// bits 0-13 start>>4, 16-29 LBO>>4, 32-45 SBO>>4, 46-47 version=1,
+// 61-63 layout (2 = SWIZZLE_128B).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Descriptor of the k-th 16-deep slice of a staged operand tile.
+//   K-major : rows of 64 elements (128 B), 8-row swizzle atoms 1024 B apart;
+//             the slice starts k*32 B into each row.
+//   MN-major: boxes of 64 (MN) x BK (K) elements, one 128-B row per k,
+//             box j at j*BK*128 B (LBO), 8-row K groups 1024 B apart (SBO);
+//             the slice starts 16 rows = 2048 B further.
+__device__ __forceinline__ uint64_t operand_desc(uint32_t tile, int k, int mn_major) {
+  if (!mn_major) return smem_desc(tile + (uint32_t)k * 32u, 16u, 1024u);
+  return smem_desc(tile + (uint32_t)k * 2048u, (uint32_t)BK * 128u, 1024u);
+}
+
+// Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A/B bf16 (bits
+// 7-9 / 10-12 = 1), majors (bits 15/16), N>>3 (bits 17-22), M>>4 (bits 24-28).
+__device__ __forceinline__ uint32_t instr_desc_bf16(int a_mn, int b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &tm, int &tn) {
+  const int per_group = GROUP_M * tiles_n;
+  const int g = t / per_group;
+  const int first = g * GROUP_M;
+  const int gm = min(GROUP_M, tiles_m - first);
+  const int r = t - g * per_group;
+  tm = first + r % gm;
+  tn = r / gm;
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t *sA = smem;
+  uint8_t *sB = smem + STAGES * A_BYTES;
+  uint64_t *full = (uint64_t *)(sB + STAGES * B_BYTES);
+  uint64_t *empty = full + STAGES;
+  uint64_t *tfull = empty + STAGES;   // [2]
+  uint64_t *tempty = tfull + 2;       // [2]
+  uint64_t *mma_done = tempty + 2;    // [1]
+  uint32_t *tmem_slot = (uint32_t *)(mma_done + 1);
+  volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = p.tiles_m * p.tiles_n;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+      const int m0 = tm * BM, n0 = tn * BN;
+      for (int kb = 0; kb < nk; kb++, it++) {
+        const int s = it % STAGES;
+        const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(&full[s], STAGE_BYTES);
+        uint8_t *a = sA + s * A_BYTES;
+        uint8_t *b = sB + s * B_BYTES;
+        const int k0 = kb * BK;
+        if (!p.a_mn) {
+          tma_load_2d(a, &tmA, k0, m0, &full[s]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BM / 64; j++) tma_load_2d(a + j * BK * 128, &tmA, m0 + 64 * j, k0, &full[s]);
+        }
+        if (!p.b_mn) {
+          tma_load_2d(b, &tmB, k0, n0, &full[s]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 64; j++) tma_load_2d(b + j * BK * 128, &tmB, n0 + 64 * j, k0, &full[s]);
+        }
+      }
+    }
+    if (!ok) {
+      *abort_flag = 1;
+      atomicExch(p.err, 1);
+    }
+    // Drain: every copy this thread issued has landed before the CTA exits.
+    for (int i = it - STAGES < 0 ? 0 : it - STAGES; i < it; i++)
+      mbar_wait(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u, abort_flag);
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer
+    const uint32_t idesc = instr_desc_bf16(p.a_mn, p.b_mn);
+    int it = 0, ti = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ti++) {
+      const int acc = ti & 1;
+      const uint32_t aph = (uint32_t)(ti >> 1) & 1u;
+      if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+      for (int kb = 0; kb < nk; kb++, it++) {
+        const int s = it % STAGES;
+        const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+        if (!mbar_wait(&full[s], ph, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a = smem_u32(sA + s * A_BYTES);
+        const uint32_t b = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+        for (int k = 0; k < BK / UMMA_K; k++)
+          umma_bf16(d_tmem, operand_desc(a, k, p.a_mn), operand_desc(b, k, p.b_mn), idesc,
+                    (kb | k) != 0 ? 1u : 0u);
+        umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+      }
+      if (!ok) break;
+      umma_commit(&tfull[acc]);  // accumulator complete
+    }
+    if (!ok) {
+      *abort_flag = 1;
+      atomicExch(p.err, 2);
+    }
+    umma_commit(mma_done);
+    mbar_wait(mma_done, 0, abort_flag);
+  } else if (warp >= 2) {
+    // ---------------- epilogue
+    const int q = warp & 3;             // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    int ti = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ti++) {
+      int tm, tn;
+      tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+      const int acc = ti & 1;
+      const uint32_t aph = (uint32_t)(ti >> 1) & 1u;
+      if (!mbar_wait(&tfull[acc], aph, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int64_t gm = (int64_t)tm * BM + row;
+      const int n0 = tn * BN;
+      float *crow = p.C + gm * p.ldc;
+      const bool vec = ((p.ldc & 3) == 0) && (((uintptr_t)p.C & 15) == 0);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; c++) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
+        if (gm < p.M) {
+          const int nb = n0 + c * 32;
+          if (vec && nb + 32 <= p.N) {
+            float4 *dst = reinterpret_cast<float4 *>(crow + nb);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+              float4 v = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                     __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+              if (p.beta) {
+                float4 o = dst[i];
+                v.x += o.x;
+                v.y += o.y;
+                v.z += o.z;
+                v.w += o.w;
+              }
+              dst[i] = v;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+              if (nb + i < p.N) {
+                float v = __uint_as_float(r[i]);
+                crow[nb + i] = p.beta ? crow[nb + i] + v : v;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+    if (!ok) {
+      *abort_flag = 1;
+      atomicExch(p.err, 3);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS));
+  }
+}
+
+// ------------------------------------------------------------------ fp32 -> bf16
+__global__ void to_bf16_kernel(const float *__restrict__ x, int64_t n, __nv_bfloat16 *__restrict__ y) {
+  const int64_t n4 = n >> 2;
+  const float4 *x4 = reinterpret_cast<const float4 *>(x);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float4 v = x4[i];
+    __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+    uint2 o;
+    o.x = *reinterpret_cast<uint32_t *>(&a);
+    o.y = *reinterpret_cast<uint32_t *>(&b);
+    reinterpret_cast<uint2 *>(y)[i] = o;
+  }
+  for (int64_t i = (n4 << 2) + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = __float2bfloat16_rn(x[i]);
+}
+
+// ------------------------------------------------------------------ host side
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int get_encode() {
+  if (g_encode) return FCU_OK;
+  cudaDriverEntryPointQueryResult q;
+  void *fn = nullptr;
+  FCU_CHECK_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+  if (q != cudaDriverEntryPointSuccess || !fn) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return FCU_ERR_UNSUPPORTED;
+  }
+  g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+  return FCU_OK;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with a
+// {box_cols, box_rows} box and 128-byte swizzle (box_cols * 2 == 128).
+int make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols, uint32_t box_cols,
+             uint32_t box_rows) {
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu box=%ux%u", (int)r,
+              (unsigned long long)rows, (unsigned long long)cols, box_cols, box_rows);
+    return FCU_ERR_CUDA;
+  }
+  return FCU_OK;
+}
+
+struct Workspace {
+  void *ptr = nullptr;
+  size_t bytes = 0;
+  int *err = nullptr;
+};
+
+// Per-context bf16 operand workspace (grown on demand, never shrunk).
+int workspace(fcu_ctx *ctx, size_t bytes, void **out, int **err) {
+  static thread_local Workspace *ws_by_dev[64] = {nullptr};
+  Workspace *&ws = ws_by_dev[ctx->device & 63];
+  if (!ws) ws = new Workspace();
+  if (!ws->err) {
+    FCU_CHECK_CUDA(cudaMalloc(&ws->err, sizeof(int)));
+    FCU_CHECK_CUDA(cudaMemsetAsync(ws->err, 0, sizeof(int), ctx->stream));
+  }
+  if (bytes > ws->bytes) {
+    if (ws->ptr) {
+      FCU_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
+      FCU_CHECK_CUDA(cudaFree(ws->ptr));
+      ws->ptr = nullptr;
+      ws->bytes = 0;
+    }
+    FCU_CHECK_CUDA(cudaMalloc(&ws->ptr, bytes));
+    ws->bytes = bytes;
+  }
+  *out = ws->ptr;
+  *err = ws->err;
+  return FCU_OK;
+}
+
+int convert(fcu_ctx *ctx, const float *x, int64_t n, __nv_bfloat16 *y) {
+  FCU_REQUIRE(((uintptr_t)x & 15) == 0, "tensor-core path: fp32 operand must be 16-byte aligned");
+  int64_t work = (n >> 2) > 0 ? (n >> 2) : 1;
+  int blocks = (int)((work + 255) / 256);
+  if (blocks > 16 * ctx->num_sms) blocks = 16 * ctx->num_sms;
+  to_bf16_kernel<<<blocks, 256, 0, ctx->stream>>>(x, n, y);
+  FCU_CHECK_LAUNCH();
+  return FCU_OK;
+}
+
+inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+bool gemm_tc_supported(GemmOp op, int64_t M, int64_t N, int64_t K) {
+  // TMA needs 16-byte row strides: every row length of a bf16 operand a
+  // multiple of 8 elements.
+  if (M <= 0 || N <= 0 || K <= 0) return false;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return false;
+  switch (op) {
+    case GemmOp::kFwd: return K % 8 == 0;                  // A[M,K], B[N,K]
+    case GemmOp::kDx: return K % 8 == 0 && N % 8 == 0;     // A[M,K], B[K,N]
+    case GemmOp::kDw: return M % 8 == 0 && N % 8 == 0;     // A[K,M], B[K,N]
+  }
+  return false;
+}
+
+// C[M,N] (+)= A . B in the layouts of `op`, operands already bf16.
+int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfloat16 *B, float *C,
+                 int64_t M, int64_t N, int64_t K, int beta, int *err) {
+  int rc = get_encode();
+  if (rc) return rc;
+  CUtensorMap ta, tb;
+  int a_mn = 0, b_mn = 0;
+  switch (op) {
+    case GemmOp::kFwd:
+      rc = make_map(&ta, A, M, K, 64, BM);
+      if (!rc) rc = make_map(&tb, B, N, K, 64, BN);
+      break;
+    case GemmOp::kDx:
+      b_mn = 1;
+      rc = make_map(&ta, A, M, K, 64, BM);
+      if (!rc) rc = make_map(&tb, B, K, N, 64, BK);
+      break;
+    case GemmOp::kDw:
+      a_mn = b_mn = 1;
+      rc = make_map(&ta, A, K, M, 64, BK);
+      if (!rc) rc = make_map(&tb, B, K, N, 64, BK);
+      break;
+  }
+  if (rc) return rc;
+  TcParams p;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.C = C;
+  p.ldc = N;
+  p.beta = beta;
+  p.a_mn = a_mn;
+  p.b_mn = b_mn;
+  p.tiles_m = (int)((M + BM - 1) / BM);
+  p.tiles_n = (int)((N + BN - 1) / BN);
+  p.err = err;
+  static bool attr_set = false;
+  if (!attr_set) {
+    FCU_CHECK_CUDA(cudaFuncSetAttribute(gemm_bf16_tc_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
+    attr_set = true;
+  }
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = tiles < ctx->num_sms ? tiles : ctx->num_sms;
+  gemm_bf16_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, ctx->stream>>>(ta, tb, p);
+  FCU_CHECK_LAUNCH();
+  return FCU_OK;
+}
+
+int gemm_tc(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float *C, int64_t M, int64_t N,
+            int64_t K, int beta) {
+  if (ctx->precision != FCU_PREC_BF16) {
+    set_error("precision mode %d has no tensor-core kernel in this build", ctx->precision);
+    return FCU_ERR_UNSUPPORTED;
+  }
+  if (!gemm_tc_supported(op, M, N, K) || ((uintptr_t)A & 15) || ((uintptr_t)B & 15))
+    return gemm_simt(ctx->stream, op, A, B, C, M, N, K, beta);
+  // Element counts of the two operands in this op's layout.
+  const int64_t na = (op == GemmOp::kDw) ? K * M : M * K;
+  const int64_t nb = (op == GemmOp::kFwd) ? N * K : K * N;
+  const size_t off_b = round_up((size_t)na * 2, 1024);
+  void *ws = nullptr;
+  int *err = nullptr;
+  int rc = workspace(ctx, off_b + round_up((size_t)nb * 2, 1024), &ws, &err);
+  if (rc) return rc;
+  __nv_bfloat16 *Ab = (__nv_bfloat16 *)ws;
+  __nv_bfloat16 *Bb = (__nv_bfloat16 *)((uint8_t *)ws + off_b);
+  rc = convert(ctx, A, na, Ab);
+  if (!rc) rc = convert(ctx, B, nb, Bb);
+  if (!rc) rc = gemm_bf16_tc(ctx, op, Ab, Bb, C, M, N, K, beta, err);
+  return rc;
+}
+
+int gemm_tc_error(fcu_ctx *ctx) {
+  void *ws = nullptr;
+  int *err = nullptr;
+  int rc = workspace(ctx, 0, &ws, &err);
+  if (rc) return rc;
+  int h = 0;
+  FCU_CHECK_CUDA(cudaMemcpyAsync(&h, err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+  FCU_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
+  if (h) {
+    set_error("tensor-core GEMM: a bounded wait ran out (role %d)", h);
+    return FCU_ERR_TIMEOUT;
+  }
+  return FCU_OK;
 }
 
 }  // namespace fcu

@@ -53,6 +53,7 @@ _SIGS = {
     "fcu_ctx_get_precision": (_INT, [_P]),
     "fcu_sync": (_INT, [_P]),
     "fcu_launch_count": (C.c_ulonglong, []),
+    "fcu_check_device_error": (_INT, [_P]),
     "fcu_malloc": (_INT, [_P, C.c_size_t, C.POINTER(_P)]),
     "fcu_free": (_INT, [_P, _P]),
     "fcu_memcpy_h2d": (_INT, [_P, _P, _P, C.c_size_t]),

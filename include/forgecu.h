@@ -64,6 +64,10 @@ int fcu_ctx_set_stream(fcu_ctx *ctx, void *cuda_stream); /* NULL = legacy defaul
 int fcu_ctx_set_precision(fcu_ctx *ctx, int precision);   /* fcu_precision */
 int fcu_ctx_get_precision(const fcu_ctx *ctx);
 int fcu_sync(fcu_ctx *ctx);
+/* FCU_ERR_TIMEOUT if a kernel on this context recorded a bounded wait that
+ * ran out (the kernel then returned early; its outputs are invalid).
+ * Synchronises the context's stream and clears nothing. */
+int fcu_check_device_error(fcu_ctx *ctx);
 /* Kernels launched by this library since it was loaded (all contexts). */
 unsigned long long fcu_launch_count(void);
 

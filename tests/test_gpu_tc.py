@@ -1,0 +1,109 @@
+"""Tensor-core (tcgen05) matmulT in FCU_PREC_BF16 mode.
+
+Two bars:
+  * exactness of the kernel: against a float64 product of the SAME
+    bf16-rounded operands, so only the fp32 accumulation order differs --
+    relL2 <= 1e-5;
+  * the stated bf16-mode bound against the fp32 oracle: relL2 <= 1e-2
+    (bf16 keeps 8 mantissa bits; random-sign inputs land near 3e-3).
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+EXACT = 1e-5
+BF16_BOUND = 1e-2
+
+
+@pytest.fixture(autouse=True)
+def bf16_mode():
+    import forgellm as F
+    F.set_precision("bf16")
+    yield
+    F.set_precision("fp32")
+
+
+def bf16_round(a):
+    """Round float32 to the nearest bf16 (ties to even), kept as float32."""
+    u = np.asarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+def host(t):
+    return t.detach().float().cpu().numpy().ravel()
+
+
+def relf(ref, got):
+    ref = np.asarray(ref, np.float64).ravel()
+    got = np.asarray(got, np.float64).ravel()
+    return float(np.linalg.norm(ref - got) / max(np.linalg.norm(ref), 1e-30))
+
+
+def device_ok():
+    from forgellm import _lib
+    from forgellm.autograd import ctx
+    assert _lib.lib().fcu_check_device_error(ctx().handle) == 0, _lib.lib().fcu_last_error()
+
+
+@pytest.mark.parametrize("M,K,N", [(128, 64, 256), (300, 200, 520), (1, 8, 8), (129, 1024, 257),
+                                   (1024, 768, 1280), (4096, 2048, 8192)])
+def test_tc_matmulT_fwd_bwd(M, K, N):
+    import forgellm as F
+    rng = np.random.default_rng(M * 7 + K * 3 + N)
+    X = rng.standard_normal(M * K).astype(np.float32)
+    W = rng.standard_normal(N * K).astype(np.float32)
+    g = rng.standard_normal(M * N).astype(np.float32)
+    gX0 = rng.standard_normal(M * K).astype(np.float32)
+    F.resetTape()
+    Xn, Wn = F.param(X), F.param(W)
+    Xn.grad = gX0.copy()                      # dX accumulates, dW overwrites
+    Y = F.matmulT(Xn, Wn, M, K, N)
+    Y.grad = g
+    Y._b(Y.grad)
+    torch.cuda.synchronize()
+    device_ok()
+    Xb = bf16_round(X).reshape(M, K).astype(np.float64)
+    Wb = bf16_round(W).reshape(N, K).astype(np.float64)
+    gb = bf16_round(g).reshape(M, N).astype(np.float64)
+    rows = np.arange(M) if M <= 1024 else np.random.default_rng(0).choice(M, 64, replace=False)
+    cols = np.arange(N) if N <= 1024 else np.random.default_rng(1).choice(N, 64, replace=False)
+    Yg = host(Y.data).reshape(M, N)
+    assert relf(Xb[rows] @ Wb.T, Yg[rows]) <= EXACT
+    dXg = host(Xn.grad).reshape(M, K)
+    assert relf(gX0.reshape(M, K)[rows] + gb[rows] @ Wb, dXg[rows]) <= EXACT
+    dWg = host(Wn.grad).reshape(N, K)
+    assert relf(gb[:, cols].T @ Xb, dWg[cols]) <= EXACT
+    # stated bf16 bound against the unrounded fp32 product
+    Xf, Wf = X.reshape(M, K).astype(np.float64), W.reshape(N, K).astype(np.float64)
+    assert relf(Xf[rows] @ Wf.T, Yg[rows]) <= BF16_BOUND
+
+
+def test_tc_fallback_for_unaligned_shapes():
+    """Row lengths that are not multiples of 8 elements cannot be TMA tiled;
+    they take the CUDA-core kernel (fp32 exact) instead."""
+    import forgellm as F
+    M, K, N = 33, 5, 7
+    rng = O.RNG(77)
+    X, W = rng.normals(M * K), rng.normals(N * K)
+    F.resetTape()
+    Y = F.matmulT(F.param(X), F.param(W), M, K, N)
+    assert O.rel_l2(O.matmulT_fwd(X, W, M, K, N), host(Y.data)) <= 1e-5
+
+
+def test_tc_repeated_calls_are_deterministic():
+    import forgellm as F
+    M, K, N = 512, 768, 2048
+    rng = np.random.default_rng(5)
+    X = rng.standard_normal(M * K).astype(np.float32)
+    W = rng.standard_normal(N * K).astype(np.float32)
+    outs = []
+    for _ in range(3):
+        F.resetTape()
+        outs.append(host(F.matmulT(F.param(X), F.param(W), M, K, N).data))
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
+    device_ok()
