@@ -67,16 +67,20 @@ def test_tc_matmulT_fwd_bwd(M, K, N):
     Y._b(Y.grad)
     torch.cuda.synchronize()
     device_ok()
-    Xb = bf16_round(X).reshape(M, K).astype(np.float64)
-    Wb = bf16_round(W).reshape(N, K).astype(np.float64)
-    gb = bf16_round(g).reshape(M, N).astype(np.float64)
+    # Which contractions the tensor cores take (16-byte TMA row strides);
+    # the others run the fp32 CUDA-core kernel on unrounded operands.
+    tc_fwd, tc_dx, tc_dw = K % 8 == 0, K % 8 == 0 and N % 8 == 0, N % 8 == 0 and K % 8 == 0
+    r = lambda a, on: bf16_round(a).astype(np.float64) if on else a.astype(np.float64)  # noqa: E731
     rows = np.arange(M) if M <= 1024 else np.random.default_rng(0).choice(M, 64, replace=False)
     cols = np.arange(N) if N <= 1024 else np.random.default_rng(1).choice(N, 64, replace=False)
     Yg = host(Y.data).reshape(M, N)
+    Xb, Wb = r(X, tc_fwd).reshape(M, K), r(W, tc_fwd).reshape(N, K)
     assert relf(Xb[rows] @ Wb.T, Yg[rows]) <= EXACT
     dXg = host(Xn.grad).reshape(M, K)
+    gb, Wb = r(g, tc_dx).reshape(M, N), r(W, tc_dx).reshape(N, K)
     assert relf(gX0.reshape(M, K)[rows] + gb[rows] @ Wb, dXg[rows]) <= EXACT
     dWg = host(Wn.grad).reshape(N, K)
+    gb, Xb = r(g, tc_dw).reshape(M, N), r(X, tc_dw).reshape(M, K)
     assert relf(gb[:, cols].T @ Xb, dWg[cols]) <= EXACT
     # stated bf16 bound against the unrounded fp32 product
     Xf, Wf = X.reshape(M, K).astype(np.float64), W.reshape(N, K).astype(np.float64)
