@@ -371,6 +371,8 @@ int fcu_attn_fwd(fcu_ctx *ctx, const float *Q, const float *K, const float *V, i
   if (rc) return rc;
   FCU_REQUIRE(Q && K && V && O && lse, "fcu_attn_fwd: null pointer");
   cudaStream_t st = ctx->stream;
+  if (ctx->precision == FCU_PREC_BF16 && fcu::attn_tc_supported(dH, Q, K, V))
+    return fcu::attn_fwd_tc(st, Q, K, V, B, T, nH, nKV, dH, O, lse);
   if (dH <= 16) return attn_fwd_launch<16>(st, Q, K, V, B, T, nH, nKV, dH, O, lse);
   if (dH <= 32) return attn_fwd_launch<32>(st, Q, K, V, B, T, nH, nKV, dH, O, lse);
   if (dH <= 64) return attn_fwd_launch<64>(st, Q, K, V, B, T, nH, nKV, dH, O, lse);
@@ -393,6 +395,9 @@ int fcu_attn_bwd(fcu_ctx *ctx, const float *dO, const float *Q, const float *K, 
                                                                                   delta);
   FCU_CHECK_LAUNCH();
   cudaStream_t st = ctx->stream;
+  if (ctx->precision == FCU_PREC_BF16 && fcu::attn_tc_supported(dH, Q, K, V) &&
+      (((uintptr_t)dO | (uintptr_t)dQ | (uintptr_t)dK | (uintptr_t)dV) & 15) == 0)
+    return fcu::attn_bwd_tc(st, dO, Q, K, V, lse, delta, B, T, nH, nKV, dH, dQ, dK, dV, accumulate);
   if (dH <= 16)
     return attn_bwd_launch<16>(st, dO, Q, K, V, lse, delta, B, T, nH, nKV, dH, dQ, dK, dV, accumulate);
   if (dH <= 32)

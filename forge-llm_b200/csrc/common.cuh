@@ -36,6 +36,15 @@ inline int div_up(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 // Number of kernels this library has launched (fcu_launch_count).
 void note_launch();
 
+// Tensor-core attention (attn_tc.cu): head dims 16/32/64/128, 16-byte
+// aligned operands.
+bool attn_tc_supported(int dH, const void *Q, const void *K, const void *V);
+int attn_fwd_tc(cudaStream_t st, const float *Q, const float *K, const float *V, int B, int T,
+                int nH, int nKV, int dH, float *O, float *lse);
+int attn_bwd_tc(cudaStream_t st, const float *dO, const float *Q, const float *K, const float *V,
+                const float *lse, const float *delta, int B, int T, int nH, int nKV, int dH,
+                float *dQ, float *dK, float *dV, int acc);
+
 }  // namespace fcu
 
 #define FCU_CHECK_CUDA(expr)                                                  \

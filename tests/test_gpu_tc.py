@@ -111,3 +111,41 @@ def test_tc_repeated_calls_are_deterministic():
         outs.append(host(F.matmulT(F.param(X), F.param(W), M, K, N).data))
     assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
     device_ok()
+
+
+# ------------------------------------------------------------------ attention (bf16 mode)
+ATTN_BF16_BOUND = 2e-2   # bf16 Q/K/V/P/dS operands, fp32 softmax and accumulation
+
+
+@pytest.mark.parametrize("B,T,nH,nKV,dH", [(1, 64, 4, 4, 16), (2, 130, 4, 1, 64), (3, 100, 6, 2, 32),
+                                          (1, 257, 2, 2, 128), (2, 1024, 12, 4, 64)])
+def test_tc_attention_bf16_bound(B, T, nH, nKV, dH):
+    import forgellm as F
+    rng = O.RNG(31 + B * T + dH)
+    Q = rng.normals(B * T * nH * dH)
+    K = rng.normals(B * T * nKV * dH)
+    V = rng.normals(B * T * nKV * dH)
+    g = rng.normals(B * T * nH * dH)
+    F.resetTape()
+    Qn, Kn, Vn = F.param(Q), F.param(K), F.param(V)
+    Out = F.causalAttnBatch(Qn, Kn, Vn, B, T, nH, nKV, dH)
+    Out.grad = g
+    Out._b(Out.grad)
+    torch.cuda.synchronize()
+    if B * T > 512:   # oracle on the first sequence only
+        sl = lambda a, h: a.reshape(B, T, h, dH)[0].ravel()  # noqa: E731
+        Qs, Ks, Vs, gs = sl(Q, nH), sl(K, nKV), sl(V, nKV), sl(g, nH)
+        Bo = 1
+    else:
+        Qs, Ks, Vs, gs, Bo = Q, K, V, g, B
+        sl = lambda a, h: a  # noqa: E731
+    Oo, P = O.attn_fwd(Qs, Ks, Vs, Bo, T, nH, nKV, dH)
+    gQ, gK, gV = O.attn_bwd(gs, Qs, Ks, Vs, P, Bo, T, nH, nKV, dH)
+    errs = {
+        "O": O.rel_l2(Oo, sl(host(Out.data), nH)),
+        "dQ": O.rel_l2(gQ, sl(host(Qn.grad), nH)),
+        "dK": O.rel_l2(gK, sl(host(Kn.grad), nKV)),
+        "dV": O.rel_l2(gV, sl(host(Vn.grad), nKV)),
+    }
+    assert max(errs.values()) <= ATTN_BF16_BOUND, errs
+    assert errs["O"] <= 1e-2, errs
