@@ -3,6 +3,8 @@
 // small helpers.  All are single-pass, coalesced, HBM-bound kernels.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace {
@@ -657,6 +659,73 @@ int fcu_ce_fwd(fcu_ctx *ctx, const float *logits, const int32_t *targets, int64_
   int rc = fcu::ctx_scratch(ctx, sizeof(float) * (size_t)T, &scr);
   if (rc) return rc;
   float *row_loss = (float *)scr;
+  bool aligned = ((uintptr_t)logits % 16 == 0) && ((uintptr_t)dunit % 16 == 0);
+  if (aligned && V % 4 == 0 && V <= (int64_t)kCeThreads * kCeVec * 4)
+    ce_fwd_kernel<true><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
+  else
+    ce_fwd_kernel<false><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
+  FCU_CHECK_LAUNCH();
+  mean_kernel<<<1, 1024, 0, ctx->stream>>>(row_loss, T, loss_out);
+  FCU_CHECK_LAUNCH();
+  return FCU_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- no-allocation CE
+// Scratch of fcu_ce_fwd_static: one float per logits row, in a fixed device
+// array instead of memory the context allocates.  It lives in every GPU that
+// loads this library, for the life of the process.
+namespace {
+
+constexpr int64_t kCeStaticMaxRows = 65536;  // 256 KiB per device
+static __device__ __align__(256) float g_ce_static_rows[kCeStaticMaxRows];
+
+std::mutex g_ce_static_mu;
+float *g_ce_static_ptr[64] = {nullptr};  // device address of the array, per device ordinal
+
+// The host-side name g_ce_static_rows is only a stand-in for the device
+// array, so its device address is looked up once per device, with that
+// device current, and cached.
+int ce_static_rows(int device, float **out) {
+  FCU_REQUIRE(device >= 0 && device < 64, "fcu_ce_fwd_static: device ordinal %d out of range", device);
+  std::lock_guard<std::mutex> lock(g_ce_static_mu);
+  if (!g_ce_static_ptr[device]) {
+    int cur = -1;
+    FCU_CHECK_CUDA(cudaGetDevice(&cur));
+    if (cur != device) FCU_CHECK_CUDA(cudaSetDevice(device));
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_ce_static_rows);
+    if (cur != device) {
+      cudaError_t e2 = cudaSetDevice(cur);
+      if (e == cudaSuccess) e = e2;
+    }
+    FCU_CHECK_CUDA(e);
+    g_ce_static_ptr[device] = (float *)p;
+  }
+  *out = g_ce_static_ptr[device];
+  return FCU_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fcu_ce_fwd_static(fcu_ctx *ctx, const float *logits, const int32_t *targets, int64_t T,
+                      int64_t V, float *loss_out, float *dunit) {
+  FCU_CTX(ctx);
+  FCU_REQUIRE(T > 0 && V > 0, "fcu_ce_fwd_static: bad shape T=%lld V=%lld", (long long)T,
+              (long long)V);
+  FCU_REQUIRE(T <= kCeStaticMaxRows,
+              "fcu_ce_fwd_static: T=%lld rows exceeds the fixed scratch of %lld rows; split the "
+              "rows across calls or use fcu_ce_fwd",
+              (long long)T, (long long)kCeStaticMaxRows);
+  FCU_REQUIRE(logits && targets && loss_out && dunit, "fcu_ce_fwd_static: null pointer");
+  float *row_loss = nullptr;
+  int rc = ce_static_rows(ctx->device, &row_loss);
+  if (rc) return rc;
+  // Every row writes its own slot before mean_kernel reads it, so nothing
+  // left over from an earlier call is ever read.
   bool aligned = ((uintptr_t)logits % 16 == 0) && ((uintptr_t)dunit % 16 == 0);
   if (aligned && V % 4 == 0 && V <= (int64_t)kCeThreads * kCeVec * 4)
     ce_fwd_kernel<true><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);

@@ -77,6 +77,7 @@ _SIGS = {
     "fcu_add_fwd": (_INT, [_P, _P, _P, _I64, _P]),
     "fcu_add_bwd": (_INT, [_P, _P, _I64, _P, _INT, _P, _INT]),
     "fcu_ce_fwd": (_INT, [_P, _P, _P, _I64, _I64, _P, _P]),
+    "fcu_ce_fwd_static": (_INT, [_P, _P, _P, _I64, _I64, _P, _P]),
     "fcu_axpy_dev": (_INT, [_P, _P, _P, _I64, _P, _INT]),
     "fcu_wsum_fwd": (_INT, [_P, _P, _P, _I64, _P]),
     "fcu_adam_step": (_INT, [_P, _P, _P, _P, _P, _I64, C.POINTER(AdamHyper), _P]),

@@ -161,6 +161,25 @@ int fcu_add_bwd(fcu_ctx *ctx, const float *g, int64_t n, float *da, int accumula
 int fcu_ce_fwd(fcu_ctx *ctx, const float *logits, const int32_t *targets, int64_t T, int64_t V,
                float *loss_out, float *dunit);
 
+/* fcu_ce_fwd for callers that must not allocate device memory.  No
+ * counterpart in the reference: it exists for hosts that plan every device
+ * byte up front (an embedding runtime with a fixed memory pool, or an
+ * N-API host whose buffers belong to another allocator), and for which a
+ * cudaMalloc inside a training step is not allowed (it can fail under memory
+ * pressure and it synchronises the whole device).  fcu_ce_fwd may allocate
+ * its per-row scratch through the context on first use or growth; this entry
+ * point never calls cudaMalloc, cudaFree or any allocating routine.
+ * Its scratch is a fixed array compiled into the library: T <= 65536 rows
+ * (256 KiB, held by every GPU that loads the library until the process
+ * exits).  Larger T is rejected with FCU_ERR_ARG.  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress, with that device
+ * current) and caches it; make that first call before any stream capture.
+ * All calls share the one array, so calls whose kernels overlap on the GPU
+ * (other streams, other threads) race; calls on one stream are ordered and
+ * safe.  Results equal fcu_ce_fwd's. */
+int fcu_ce_fwd_static(fcu_ctx *ctx, const float *logits, const int32_t *targets, int64_t T,
+                      int64_t V, float *loss_out, float *dunit);
+
 /* y (+)= alpha_dev[0] * x, alpha read from device memory (a loss gradient). */
 int fcu_axpy_dev(fcu_ctx *ctx, const float *alpha_dev, const float *x, int64_t n, float *y,
                  int accumulate);
