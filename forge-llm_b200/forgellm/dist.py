@@ -16,10 +16,18 @@ import torch.distributed as dist
 
 
 class DataParallel:
+    """Overlapped gradient averaging for one TrainableTransformer replica.
+
+    `model` needs `flat_grads` (flat gradient buffer), `layer_offsets`
+    ([(start, end)] per layer) and honours `grad_ready_hook`.  NCCL reduces
+    with AVG; backends without AVG (gloo, used by the CPU tests) reduce with
+    SUM and divide after the wait."""
+
     def __init__(self, model, group=None):
         self.model = model
         self.group = group
         self.world = dist.get_world_size(group)
+        self.native_avg = dist.get_backend(group) == "nccl"
         self.handles = []
         head_end = model.layer_offsets[0][0] if model.layer_offsets else model.flat_grads.numel()
         self.blocks = {"head": (0, head_end)}
@@ -33,8 +41,8 @@ class DataParallel:
             return
         a, b = self.blocks[key]
         buf = self.model.flat_grads[a:b]
-        self.handles.append(dist.all_reduce(buf, op=dist.ReduceOp.AVG, group=self.group,
-                                            async_op=True))
+        op = dist.ReduceOp.AVG if self.native_avg else dist.ReduceOp.SUM
+        self.handles.append((buf, dist.all_reduce(buf, op=op, group=self.group, async_op=True)))
         self.launched.add(key)
 
     def finish(self) -> None:
@@ -44,8 +52,10 @@ class DataParallel:
             for key in self.blocks:
                 if key not in self.launched:
                     self._ready(key)
-            for h in self.handles:
+            for buf, h in self.handles:
                 h.wait()
+                if not self.native_avg:
+                    buf.div_(self.world)
         self.handles.clear()
         self.launched.clear()
 
