@@ -5,6 +5,7 @@
 // one fused update pass that reads p, g, m, v once and writes p, m, v once
 // (28 bytes per parameter).  The per-element arithmetic is in double, like the
 // JS, with fp32 stores.
+#include <cuda_bf16.h>
 #include <math.h>
 
 #include "common.cuh"
@@ -56,7 +57,7 @@ __device__ __forceinline__ void adam_elem(float &p, float g, float &m, float &v,
 __global__ void adam_update_kernel(float *__restrict__ p, const float *__restrict__ g,
                                    float *__restrict__ m, float *__restrict__ v, int64_t n, Hyper h,
                                    const double *__restrict__ sumsq, double *__restrict__ info,
-                                   int vec) {
+                                   int vec, __nv_bfloat16 *__restrict__ shadow) {
   const double gnorm = sqrt(sumsq[0]);
   const double scale = gnorm > h.clip ? h.clip / gnorm : 1.0;
   if (info && blockIdx.x == 0 && threadIdx.x == 0) {
@@ -80,6 +81,13 @@ __global__ void adam_update_kernel(float *__restrict__ p, const float *__restric
       p4[i] = pp;
       m4[i] = mm;
       v4[i] = vv;
+      if (shadow) {
+        __nv_bfloat162 a = __floats2bfloat162_rn(pp.x, pp.y), b = __floats2bfloat162_rn(pp.z, pp.w);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t *>(&a);
+        u.y = *reinterpret_cast<uint32_t *>(&b);
+        reinterpret_cast<uint2 *>(shadow)[i] = u;
+      }
     }
     start = n4 << 2;
   }
@@ -89,6 +97,7 @@ __global__ void adam_update_kernel(float *__restrict__ p, const float *__restric
     p[i] = pp;
     m[i] = mm;
     v[i] = vv;
+    if (shadow) shadow[i] = __float2bfloat16_rn(pp);
   }
 }
 
@@ -107,15 +116,18 @@ int sumsq_impl(fcu_ctx *ctx, const float *g, int64_t n, double *out, int acc) {
 }
 
 int update_impl(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int64_t n,
-                const fcu_adam_hyper *hh, const double *sumsq, double *info) {
+                const fcu_adam_hyper *hh, const double *sumsq, double *info,
+                __nv_bfloat16 *shadow = nullptr) {
   Hyper h{hh->lr, hh->b1, hh->b2, hh->eps, hh->wd, hh->clip, hh->bc1, hh->bc2};
-  int vec = aligned16(p) && aligned16(g) && aligned16(m) && aligned16(v);
+  int vec = aligned16(p) && aligned16(g) && aligned16(m) && aligned16(v) &&
+            (shadow == nullptr || ((uintptr_t)shadow & 7) == 0);
   int64_t work = vec ? (n >> 2) : n;
   int64_t blocks = (work + kThreads - 1) / kThreads;
   int64_t cap = 16 * (int64_t)ctx->num_sms;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  adam_update_kernel<<<(int)blocks, kThreads, 0, ctx->stream>>>(p, g, m, v, n, h, sumsq, info, vec);
+  adam_update_kernel<<<(int)blocks, kThreads, 0, ctx->stream>>>(p, g, m, v, n, h, sumsq, info, vec,
+                                                                 shadow);
   FCU_CHECK_LAUNCH();
   return FCU_OK;
 }
@@ -155,6 +167,27 @@ int fcu_adam_step(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, in
   rc = sumsq_impl(ctx, g, n, ss, 0);
   if (rc) return rc;
   return update_impl(ctx, p, g, m, v, n, h, ss, info_dev);
+}
+
+int fcu_adam_step_shadow(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int64_t n,
+                         const fcu_adam_hyper *h, const double *sumsq_dev, double *info_dev,
+                         void *p_bf16) {
+  FCU_CTX(ctx);
+  FCU_REQUIRE(n >= 0 && p && g && m && v && h && p_bf16, "fcu_adam_step_shadow: bad args");
+  FCU_REQUIRE(h->bc1 > 0 && h->bc2 > 0, "fcu_adam_step_shadow: bias corrections must be > 0 (t >= 1)");
+  if (n == 0) return FCU_OK;
+  const double *ss = sumsq_dev;
+  if (!ss) {
+    const int nblk = 2 * ctx->num_sms;
+    void *scr = nullptr;
+    int rc = fcu::ctx_scratch(ctx, sizeof(double) * (nblk + 1), &scr);
+    if (rc) return rc;
+    double *own = (double *)scr + nblk;
+    rc = sumsq_impl(ctx, g, n, own, 0);
+    if (rc) return rc;
+    ss = own;
+  }
+  return update_impl(ctx, p, g, m, v, n, h, ss, info_dev, (__nv_bfloat16 *)p_bf16);
 }
 
 }  // extern "C"

@@ -1,18 +1,27 @@
 // Causal GQA flash attention on the tensor cores (bf16 operands, fp32
-// softmax and accumulation), used in FCU_PREC_BF16 mode.
+// softmax and accumulation).
 //
 // Same contract as attn.cu (causalAttn / causalAttnBatch, src/L2/tensor.js:
-// 191-268 and 299-376): fp32 Q/K/V/O in HBM, lse per score row kept for the
-// backward.  Operands are rounded to bf16 as they are staged in shared
-// memory; scores, the online softmax, P.V and all gradients accumulate in
-// fp32 registers through m16n8k16 tensor-core MMAs (FlashAttention-2 tiling:
-// 4 warps x 16 query rows, 64-key tiles; P and dS are re-used from the
-// accumulator registers as the A operand of the next product).
+// 191-268 and 299-376): lse per score row is kept for the backward instead of
+// the JS's P.  Operands are bf16 in shared memory; scores, the online softmax,
+// P.V and all gradients accumulate in fp32 registers through m16n8k16
+// tensor-core MMAs (FlashAttention-2 tiling: 4 warps x 16 rows, 64-key tiles;
+// P and dS are re-used from the accumulator registers as the A operand of the
+// next product).
+//
+// Two input flavours share the kernels:
+//   fp32 tensors (the op-level API): rounded to bf16 while staged;
+//   bf16 tensors (the fused model path): q, k, v read straight out of one
+//   [N, (nH+2nKV)*dH] qkv buffer by row stride + column offset, staged with
+//   cp.async into double-buffered tiles so the next tile loads during the
+//   current tile's MMAs.  There O is written in bf16, and dQ/dK/dV are
+//   written in bf16 into one dqkv buffer with the RoPE backward (R^T,
+//   src/L2/tensor.js:150-165) applied to dQ and dK on the way out.
 //
 // Backward is two deterministic kernels (no atomics):
 //   dK/dV: a CTA owns 64 keys of one kv head and sweeps the group's q heads
-//          and every later query tile, computing S^T, P^T, dP^T, dS^T with
-//          keys as rows; dV += P^T dO, dK += dS^T Q.
+//          and every later query tile (S^T, P^T, dP^T, dS^T with keys as
+//          rows); dV += P^T dO, dK += dS^T Q.
 //   dQ   : a CTA owns 64 queries and sweeps every earlier key tile; dQ += dS K.
 #include <cuda_bf16.h>
 #include <math.h>
@@ -31,6 +40,26 @@ template <int D>
 struct Smem {
   static constexpr int LD = D + 8;  // bf16 row stride: +16 B keeps ldmatrix conflict free
   static constexpr int TILE = kTile * LD;
+};
+
+// A [rows, heads*D] tensor inside a wider row-major buffer: element
+// (row r, head h, dim d) lives at p[r*ld + col + h*D + d].
+template <typename T>
+struct View {
+  T *p;
+  int64_t ld;
+  int64_t col;
+};
+
+struct Args {
+  View<const void> q, k, v, o_in, dO;   // inputs (o_in: the forward output, for delta)
+  View<void> o, dq, dk, dv;             // outputs
+  float *lse;
+  const float *delta;
+  const float2 *rope;                   // (cos, sin) [T][D/2] for the RoPE backward, or null
+  int T, nH, nKV;
+  float scale;
+  int acc;                              // fp32 outputs: accumulate
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -64,24 +93,54 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t *>(&v);
 }
 
-// Stage rows [r0, r0+64) of one head (columns [col0, col0+D)) of an fp32
-// matrix with row stride ld into a bf16 tile; rows >= nrows are zero.
-template <int D>
-__device__ __forceinline__ void stage_tile(__nv_bfloat16 *dst, const float *__restrict__ src,
-                                           int64_t row_base, int r0, int nrows, int64_t ld,
-                                           int64_t col0) {
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Stage rows [r0, r0+64) of head `h` of view `src` (rows of sequence base
+// `row_base`; rows >= nrows are zero) into a bf16 tile.  fp32 sources are
+// converted through registers; bf16 sources are copied with cp.async (the
+// caller commits and waits).
+template <int D, typename TI>
+__device__ __forceinline__ void stage(__nv_bfloat16 *dst, View<const void> src, int64_t row_base,
+                                      int r0, int nrows, int h) {
   constexpr int LD = Smem<D>::LD;
-  constexpr int V4 = D / 4;
-  for (int e = threadIdx.x; e < kTile * V4; e += kThreads) {
-    const int r = e / V4, c = (e % V4) * 4;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (r0 + r < nrows)
-      v = *reinterpret_cast<const float4 *>(src + (row_base + r0 + r) * ld + col0 + c);
-    uint2 o;
-    o.x = pack_bf16(v.x, v.y);
-    o.y = pack_bf16(v.z, v.w);
-    *reinterpret_cast<uint2 *>(dst + r * LD + c) = o;
+  if constexpr (sizeof(TI) == 4) {
+    const float *s = reinterpret_cast<const float *>(src.p);
+    constexpr int V4 = D / 4;
+    for (int e = threadIdx.x; e < kTile * V4; e += kThreads) {
+      const int r = e / V4, c = (e % V4) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (r0 + r < nrows)
+        v = *reinterpret_cast<const float4 *>(s + (row_base + r0 + r) * src.ld + src.col + (int64_t)h * D + c);
+      uint2 o;
+      o.x = pack_bf16(v.x, v.y);
+      o.y = pack_bf16(v.z, v.w);
+      *reinterpret_cast<uint2 *>(dst + r * LD + c) = o;
+    }
+  } else {
+    const __nv_bfloat16 *s = reinterpret_cast<const __nv_bfloat16 *>(src.p);
+    constexpr int C8 = D / 8;
+    for (int e = threadIdx.x; e < kTile * C8; e += kThreads) {
+      const int r = e / C8, c = (e % C8) * 8;
+      const bool ok = r0 + r < nrows;
+      const __nv_bfloat16 *g = ok ? s + (row_base + r0 + r) * src.ld + src.col + (int64_t)h * D + c : s;
+      cp_async16(dst + r * LD + c, g, ok);
+    }
   }
+}
+
+template <typename TI>
+__device__ __forceinline__ void stage_done() {
+  if constexpr (sizeof(TI) == 2) {
+    cp_async_commit();
+    cp_async_wait_all();
+  }
+  __syncthreads();
 }
 
 // A fragments (16 rows x D) of rows [row0, row0+16) of a staged tile.
@@ -142,25 +201,63 @@ __device__ __forceinline__ void mm_pt(float (&acc)[D / 8][4], const float (&p)[8
   }
 }
 
+// Store one accumulator row fragment (16 rows x D, this thread's two rows)
+// of head h: fp32 (optionally accumulating) or bf16, optionally rotated back
+// by R^T (pairs (2i, 2i+1) of the head, position row % T).
+template <int D, typename TO>
+__device__ __forceinline__ void store_rows(View<void> dst, const float (&a)[D / 8][4],
+                                           const int (&row)[2], int64_t base, int h, int T,
+                                           float mul, int acc, const float2 *rope, int t4) {
+#pragma unroll
+  for (int r = 0; r < 2; r++) {
+    if (row[r] >= T) continue;
+    const int64_t off = (base + row[r]) * dst.ld + dst.col + (int64_t)h * D;
+#pragma unroll
+    for (int j = 0; j < D / 8; j++) {
+      float x = a[j][2 * r] * mul, y = a[j][2 * r + 1] * mul;
+      if (rope) {
+        const float2 cs = rope[(int64_t)row[r] * (D / 2) + j * 4 + t4];
+        const float u = x * cs.x + y * cs.y, w = -x * cs.y + y * cs.x;
+        x = u;
+        y = w;
+      }
+      const int64_t e = off + j * 8 + 2 * t4;
+      if constexpr (sizeof(TO) == 4) {
+        float2 *p = reinterpret_cast<float2 *>(reinterpret_cast<float *>(dst.p) + e);
+        float2 v = make_float2(x, y);
+        if (acc) {
+          const float2 o = *p;
+          v.x += o.x;
+          v.y += o.y;
+        }
+        *p = v;
+      } else {
+        *reinterpret_cast<uint32_t *>(reinterpret_cast<__nv_bfloat16 *>(dst.p) + e) = pack_bf16(x, y);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ forward
-template <int D>
-__global__ void __launch_bounds__(kThreads) attn_fwd_tc_kernel(
-    const float *__restrict__ Q, const float *__restrict__ K, const float *__restrict__ V, int T,
-    int nH, int nKV, float scale, float *__restrict__ O, float *__restrict__ lse) {
+template <int D, typename TI, typename TO>
+__global__ void __launch_bounds__(kThreads) attn_fwd_tc_kernel(Args A) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  constexpr bool kAsync = sizeof(TI) == 2;
   __nv_bfloat16 *sQ = reinterpret_cast<__nv_bfloat16 *>(smem_raw);
-  __nv_bfloat16 *sK = sQ + Smem<D>::TILE;
-  __nv_bfloat16 *sV = sK + Smem<D>::TILE;
+  __nv_bfloat16 *sK[2] = {sQ + Smem<D>::TILE, sQ + 3 * Smem<D>::TILE};
+  __nv_bfloat16 *sV[2] = {sQ + 2 * Smem<D>::TILE, sQ + 4 * Smem<D>::TILE};
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int kvh = h / (nH / nKV);
+  const int T = A.T, kvh = h / (A.nH / A.nKV);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
-  const int64_t qD = (int64_t)nH * D, kvD = (int64_t)nKV * D, base = (int64_t)b * T;
+  const int64_t base = (int64_t)b * T;
   const int q0 = qt * kTile;
-  const float c = scale * kLog2e;
+  const float c = A.scale * kLog2e;
 
-  stage_tile<D>(sQ, Q, base, q0, T, qD, (int64_t)h * D);
-  __syncthreads();
+  stage<D, TI>(sQ, A.q, base, q0, T, h);
+  stage<D, TI>(sK[0], A.k, base, 0, T, kvh);
+  stage<D, TI>(sV[0], A.v, base, 0, T, kvh);
+  stage_done<TI>();
   uint32_t qf[D / 16][4];
   load_a_frags<D>(qf, sQ, warp * 16, lane);
 
@@ -173,13 +270,21 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_tc_kernel(
   const int row[2] = {q0 + warp * 16 + g, q0 + warp * 16 + g + 8};
 
   for (int kt = 0; kt <= qt; kt++) {
+    const int buf = kAsync ? (kt & 1) : 0;
+    if (kt > 0 && !kAsync) {
+      __syncthreads();
+      stage<D, TI>(sK[0], A.k, base, kt * kTile, T, kvh);
+      stage<D, TI>(sV[0], A.v, base, kt * kTile, T, kvh);
+      __syncthreads();
+    }
+    if (kAsync && kt < qt) {  // prefetch the next tile into the other buffer
+      stage<D, TI>(sK[buf ^ 1], A.k, base, (kt + 1) * kTile, T, kvh);
+      stage<D, TI>(sV[buf ^ 1], A.v, base, (kt + 1) * kTile, T, kvh);
+      cp_async_commit();
+    }
     const int k0 = kt * kTile;
-    __syncthreads();
-    stage_tile<D>(sK, K, base, k0, T, kvD, (int64_t)kvh * D);
-    stage_tile<D>(sV, V, base, k0, T, kvD, (int64_t)kvh * D);
-    __syncthreads();
     float s[8][4];
-    mm_abt<D>(s, qf, sK, lane);
+    mm_abt<D>(s, qf, sK[buf], lane);
     float mx[2] = {m[0], m[1]};
 #pragma unroll
     for (int j = 0; j < 8; j++) {
@@ -225,46 +330,64 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_tc_kernel(
       o[j][2] *= corr[1];
       o[j][3] *= corr[1];
     }
-    mm_pt<D>(o, s, sV, lane);
+    mm_pt<D>(o, s, sV[buf], lane);
+    if (kAsync) {
+      cp_async_wait_all();
+      __syncthreads();  // next tile landed; everyone is done with this one
+    }
   }
 #pragma unroll
   for (int r = 0; r < 2; r++) {
-    if (row[r] >= T) continue;
     const float il = 1.f / l[r];
-    float *orow = O + (base + row[r]) * qD + (int64_t)h * D;
 #pragma unroll
     for (int j = 0; j < D / 8; j++) {
-      float2 v = make_float2(o[j][2 * r] * il, o[j][2 * r + 1] * il);
-      *reinterpret_cast<float2 *>(orow + j * 8 + 2 * t4) = v;
+      o[j][2 * r] *= il;
+      o[j][2 * r + 1] *= il;
     }
-    if (t4 == 0) lse[((int64_t)b * nH + h) * T + row[r]] = (m[r] + log2f(l[r])) / kLog2e;
+    if (row[r] < T && t4 == 0)
+      A.lse[((int64_t)b * A.nH + h) * T + row[r]] = (m[r] + log2f(l[r])) / kLog2e;
   }
+  store_rows<D, TO>(A.o, o, row, base, h, T, 1.f, 0, nullptr, t4);
 }
 
 // ------------------------------------------------------------------ backward dK dV
-template <int D>
-__global__ void __launch_bounds__(kThreads) attn_bwd_dkdv_tc_kernel(
-    const float *__restrict__ Q, const float *__restrict__ K, const float *__restrict__ V,
-    const float *__restrict__ dO, const float *__restrict__ lse, const float *__restrict__ delta,
-    int T, int nH, int nKV, float scale, float *__restrict__ dK, float *__restrict__ dV, int acc) {
+template <int D, typename TI, typename TO>
+__global__ void __launch_bounds__(kThreads) attn_bwd_dkdv_tc_kernel(Args A) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  constexpr bool kAsync = sizeof(TI) == 2;
   __nv_bfloat16 *sK = reinterpret_cast<__nv_bfloat16 *>(smem_raw);
   __nv_bfloat16 *sV = sK + Smem<D>::TILE;
-  __nv_bfloat16 *sQ = sV + Smem<D>::TILE;
-  __nv_bfloat16 *sG = sQ + Smem<D>::TILE;
-  float *sL = reinterpret_cast<float *>(sG + Smem<D>::TILE);
-  float *sD = sL + kTile;
+  __nv_bfloat16 *sQ[2] = {sV + Smem<D>::TILE, sV + 3 * Smem<D>::TILE};
+  __nv_bfloat16 *sG[2] = {sV + 2 * Smem<D>::TILE, sV + 4 * Smem<D>::TILE};
+  float *sL = reinterpret_cast<float *>(sV + 5 * Smem<D>::TILE);  // [2][kTile]
+  float *sD = sL + 2 * kTile;                                     // [2][kTile]
   const int kt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-  const int group = nH / nKV;
+  const int T = A.T, nH = A.nH, group = nH / A.nKV;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
-  const int64_t qD = (int64_t)nH * D, kvD = (int64_t)nKV * D, base = (int64_t)b * T;
+  const int64_t base = (int64_t)b * T;
   const int k0 = kt * kTile;
-  const float c = scale * kLog2e;
+  const float c = A.scale * kLog2e;
+  const int ntiles = (T + kTile - 1) / kTile;
+  const int per_head = ntiles - kt;          // query tiles at or after this key tile
+  const int n_iter = group * per_head;
 
-  stage_tile<D>(sK, K, base, k0, T, kvD, (int64_t)kvh * D);
-  stage_tile<D>(sV, V, base, k0, T, kvD, (int64_t)kvh * D);
-  __syncthreads();
+  auto load_q = [&](int it, int bi) {        // stage query tile `it` into buffer bi
+    const int h = kvh * group + it / per_head;
+    const int q0 = (kt + it % per_head) * kTile;
+    stage<D, TI>(sQ[bi], A.q, base, q0, T, h);
+    stage<D, TI>(sG[bi], A.dO, base, q0, T, h);
+    for (int i = threadIdx.x; i < kTile; i += kThreads) {
+      const int q = q0 + i;
+      sL[bi * kTile + i] = q < T ? A.lse[((int64_t)b * nH + h) * T + q] * kLog2e : 0.f;
+      sD[bi * kTile + i] = q < T ? A.delta[((int64_t)b * nH + h) * T + q] : 0.f;
+    }
+  };
+
+  stage<D, TI>(sK, A.k, base, k0, T, kvh);
+  stage<D, TI>(sV, A.v, base, k0, T, kvh);
+  load_q(0, 0);
+  stage_done<TI>();
   uint32_t kf[D / 16][4], vf[D / 16][4];
   load_a_frags<D>(kf, sK, warp * 16, lane);
   load_a_frags<D>(vf, sV, warp * 16, lane);
@@ -274,85 +397,70 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_dkdv_tc_kernel(
 #pragma unroll
     for (int i = 0; i < 4; i++) dk[j][i] = dv[j][i] = 0.f;
   const int key[2] = {k0 + warp * 16 + g, k0 + warp * 16 + g + 8};
-  const int ntiles = (T + kTile - 1) / kTile;
 
-  for (int h = kvh * group; h < (kvh + 1) * group; h++) {
-    for (int qt = kt; qt < ntiles; qt++) {
-      const int q0 = qt * kTile;
+  for (int it = 0; it < n_iter; it++) {
+    const int buf = kAsync ? (it & 1) : 0;
+    if (it > 0 && !kAsync) {
       __syncthreads();
-      stage_tile<D>(sQ, Q, base, q0, T, qD, (int64_t)h * D);
-      stage_tile<D>(sG, dO, base, q0, T, qD, (int64_t)h * D);
-      for (int i = threadIdx.x; i < kTile; i += kThreads) {
-        const int q = q0 + i;
-        sL[i] = q < T ? lse[((int64_t)b * nH + h) * T + q] * kLog2e : 0.f;
-        sD[i] = q < T ? delta[((int64_t)b * nH + h) * T + q] : 0.f;
-      }
+      load_q(it, 0);
       __syncthreads();
-      float st[8][4], dpt[8][4];
-      mm_abt<D>(st, kf, sQ, lane);   // S^T: keys x queries
-      mm_abt<D>(dpt, vf, sG, lane);  // dP^T = V dO^T
+    }
+    if (kAsync && it + 1 < n_iter) {
+      load_q(it + 1, buf ^ 1);
+      cp_async_commit();
+    }
+    const int q0 = (kt + it % per_head) * kTile;
+    const float *L = sL + buf * kTile;
+    const float *Dd = sD + buf * kTile;
+    float st[8][4], dpt[8][4];
+    mm_abt<D>(st, kf, sQ[buf], lane);   // S^T: keys x queries
+    mm_abt<D>(dpt, vf, sG[buf], lane);  // dP^T = V dO^T
 #pragma unroll
-      for (int j = 0; j < 8; j++) {
+    for (int j = 0; j < 8; j++) {
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const int qi = j * 8 + 2 * t4 + (i & 1);
-          const int q = q0 + qi;
-          const int r = i >> 1;
-          float p = 0.f;
-          if (q < T && q >= key[r]) p = exp2f(st[j][i] * c - sL[qi]);
-          st[j][i] = p;
-          dpt[j][i] = p * (dpt[j][i] - sD[qi]);
-        }
+      for (int i = 0; i < 4; i++) {
+        const int qi = j * 8 + 2 * t4 + (i & 1);
+        const int q = q0 + qi;
+        const int r = i >> 1;
+        float p = 0.f;
+        if (q < T && q >= key[r]) p = exp2f(st[j][i] * c - L[qi]);
+        st[j][i] = p;
+        dpt[j][i] = p * (dpt[j][i] - Dd[qi]);
       }
-      mm_pt<D>(dv, st, sG, lane);   // dV += P^T dO
-      mm_pt<D>(dk, dpt, sQ, lane);  // dK += dS^T Q
+    }
+    mm_pt<D>(dv, st, sG[buf], lane);   // dV += P^T dO
+    mm_pt<D>(dk, dpt, sQ[buf], lane);  // dK += dS^T Q
+    if (kAsync) {
+      cp_async_wait_all();
+      __syncthreads();
     }
   }
-#pragma unroll
-  for (int r = 0; r < 2; r++) {
-    if (key[r] >= T) continue;
-    const int64_t off = (base + key[r]) * kvD + (int64_t)kvh * D;
-#pragma unroll
-    for (int j = 0; j < D / 8; j++) {
-      float2 *pk = reinterpret_cast<float2 *>(dK + off + j * 8 + 2 * t4);
-      float2 *pv = reinterpret_cast<float2 *>(dV + off + j * 8 + 2 * t4);
-      float2 vk = make_float2(dk[j][2 * r] * scale, dk[j][2 * r + 1] * scale);
-      float2 vv = make_float2(dv[j][2 * r], dv[j][2 * r + 1]);
-      if (acc) {
-        float2 ok = *pk, ov = *pv;
-        vk.x += ok.x;
-        vk.y += ok.y;
-        vv.x += ov.x;
-        vv.y += ov.y;
-      }
-      *pk = vk;
-      *pv = vv;
-    }
-  }
+  store_rows<D, TO>(A.dk, dk, key, base, kvh, T, A.scale, A.acc, A.rope, t4);
+  store_rows<D, TO>(A.dv, dv, key, base, kvh, T, 1.f, A.acc, nullptr, t4);
 }
 
 // ------------------------------------------------------------------ backward dQ
-template <int D>
-__global__ void __launch_bounds__(kThreads) attn_bwd_dq_tc_kernel(
-    const float *__restrict__ Q, const float *__restrict__ K, const float *__restrict__ V,
-    const float *__restrict__ dO, const float *__restrict__ lse, const float *__restrict__ delta,
-    int T, int nH, int nKV, float scale, float *__restrict__ dQ, int acc) {
+template <int D, typename TI, typename TO>
+__global__ void __launch_bounds__(kThreads) attn_bwd_dq_tc_kernel(Args A) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  constexpr bool kAsync = sizeof(TI) == 2;
   __nv_bfloat16 *sQ = reinterpret_cast<__nv_bfloat16 *>(smem_raw);
   __nv_bfloat16 *sG = sQ + Smem<D>::TILE;
-  __nv_bfloat16 *sK = sG + Smem<D>::TILE;
-  __nv_bfloat16 *sV = sK + Smem<D>::TILE;
+  __nv_bfloat16 *sK[2] = {sG + Smem<D>::TILE, sG + 3 * Smem<D>::TILE};
+  __nv_bfloat16 *sV[2] = {sG + 2 * Smem<D>::TILE, sG + 4 * Smem<D>::TILE};
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int kvh = h / (nH / nKV);
+  const int T = A.T, nH = A.nH, kvh = h / (nH / A.nKV);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
-  const int64_t qD = (int64_t)nH * D, kvD = (int64_t)nKV * D, base = (int64_t)b * T;
+  const int64_t base = (int64_t)b * T;
   const int q0 = qt * kTile;
-  const float c = scale * kLog2e;
+  const float c = A.scale * kLog2e;
 
-  stage_tile<D>(sQ, Q, base, q0, T, qD, (int64_t)h * D);
-  stage_tile<D>(sG, dO, base, q0, T, qD, (int64_t)h * D);
-  __syncthreads();
+  stage<D, TI>(sQ, A.q, base, q0, T, h);
+  stage<D, TI>(sG, A.dO, base, q0, T, h);
+  stage<D, TI>(sK[0], A.k, base, 0, T, kvh);
+  stage<D, TI>(sV[0], A.v, base, 0, T, kvh);
+  stage_done<TI>();
   uint32_t qf[D / 16][4], gf[D / 16][4];
   load_a_frags<D>(qf, sQ, warp * 16, lane);
   load_a_frags<D>(gf, sG, warp * 16, lane);
@@ -361,8 +469,8 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_dq_tc_kernel(
 #pragma unroll
   for (int r = 0; r < 2; r++) {
     const bool ok = row[r] < T;
-    L[r] = ok ? lse[((int64_t)b * nH + h) * T + row[r]] * kLog2e : 0.f;
-    Dl[r] = ok ? delta[((int64_t)b * nH + h) * T + row[r]] : 0.f;
+    L[r] = ok ? A.lse[((int64_t)b * nH + h) * T + row[r]] * kLog2e : 0.f;
+    Dl[r] = ok ? A.delta[((int64_t)b * nH + h) * T + row[r]] : 0.f;
   }
   float dq[D / 8][4];
 #pragma unroll
@@ -371,14 +479,22 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_dq_tc_kernel(
     for (int i = 0; i < 4; i++) dq[j][i] = 0.f;
 
   for (int kt = 0; kt <= qt; kt++) {
+    const int buf = kAsync ? (kt & 1) : 0;
+    if (kt > 0 && !kAsync) {
+      __syncthreads();
+      stage<D, TI>(sK[0], A.k, base, kt * kTile, T, kvh);
+      stage<D, TI>(sV[0], A.v, base, kt * kTile, T, kvh);
+      __syncthreads();
+    }
+    if (kAsync && kt < qt) {
+      stage<D, TI>(sK[buf ^ 1], A.k, base, (kt + 1) * kTile, T, kvh);
+      stage<D, TI>(sV[buf ^ 1], A.v, base, (kt + 1) * kTile, T, kvh);
+      cp_async_commit();
+    }
     const int k0 = kt * kTile;
-    __syncthreads();
-    stage_tile<D>(sK, K, base, k0, T, kvD, (int64_t)kvh * D);
-    stage_tile<D>(sV, V, base, k0, T, kvD, (int64_t)kvh * D);
-    __syncthreads();
     float s[8][4], dp[8][4];
-    mm_abt<D>(s, qf, sK, lane);
-    mm_abt<D>(dp, gf, sV, lane);
+    mm_abt<D>(s, qf, sK[buf], lane);
+    mm_abt<D>(dp, gf, sV[buf], lane);
 #pragma unroll
     for (int j = 0; j < 8; j++) {
 #pragma unroll
@@ -390,62 +506,101 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_dq_tc_kernel(
         dp[j][i] = p * (dp[j][i] - Dl[r]);
       }
     }
-    mm_pt<D>(dq, dp, sK, lane);  // dQ += dS K
-  }
-#pragma unroll
-  for (int r = 0; r < 2; r++) {
-    if (row[r] >= T) continue;
-    float *qrow = dQ + (base + row[r]) * qD + (int64_t)h * D;
-#pragma unroll
-    for (int j = 0; j < D / 8; j++) {
-      float2 *p = reinterpret_cast<float2 *>(qrow + j * 8 + 2 * t4);
-      float2 v = make_float2(dq[j][2 * r] * scale, dq[j][2 * r + 1] * scale);
-      if (acc) {
-        float2 o = *p;
-        v.x += o.x;
-        v.y += o.y;
-      }
-      *p = v;
+    mm_pt<D>(dq, dp, sK[buf], lane);  // dQ += dS K
+    if (kAsync) {
+      cp_async_wait_all();
+      __syncthreads();
     }
   }
+  store_rows<D, TO>(A.dq, dq, row, base, h, T, A.scale, A.acc, A.rope, t4);
 }
 
-template <int D>
-int fwd_launch(cudaStream_t st, const float *Q, const float *K, const float *V, int B, int T,
-               int nH, int nKV, float *O, float *lse) {
-  const size_t smem = 3 * sizeof(__nv_bfloat16) * Smem<D>::TILE;
+// delta[b,h,t] = sum_d dO[t,h,d] * O[t,h,d] (the rowsum(P * dP) of the JS), one warp per row.
+template <typename TI>
+__global__ void attn_delta_tc_kernel(Args A, int B, int D) {
+  const int64_t rows = (int64_t)B * A.T * A.nH;
+  const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= rows) return;
+  const int64_t bt = w / A.nH;
+  const int h = (int)(w % A.nH);
+  const TI *g = reinterpret_cast<const TI *>(A.dO.p) + bt * A.dO.ld + A.dO.col + (int64_t)h * D;
+  const TI *o = reinterpret_cast<const TI *>(A.o_in.p) + bt * A.o_in.ld + A.o_in.col + (int64_t)h * D;
+  float s = 0.f;
+  for (int d = lane; d < D; d += 32) s += (float)g[d] * (float)o[d];
+  s = warp_sum(s);
+  if (lane == 0) {
+    const int b = (int)(bt / A.T), t = (int)(bt % A.T);
+    ((float *)A.delta)[((int64_t)b * A.nH + h) * A.T + t] = s;
+  }
+}
+
+template <int D, typename TI, typename TO>
+int fwd_launch(cudaStream_t st, const Args &a, int B) {
+  const size_t smem = 5 * sizeof(__nv_bfloat16) * Smem<D>::TILE;
   if (smem > 48 * 1024)
-    FCU_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_tc_kernel<D>,
+    FCU_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_tc_kernel<D, TI, TO>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  dim3 grid(div_up(T, kTile), nH, B);
-  attn_fwd_tc_kernel<D><<<grid, kThreads, smem, st>>>(Q, K, V, T, nH, nKV,
-                                                      (float)(1.0 / sqrt((double)D)), O, lse);
+  dim3 grid(div_up(a.T, kTile), a.nH, B);
+  attn_fwd_tc_kernel<D, TI, TO><<<grid, kThreads, smem, st>>>(a);
   FCU_CHECK_LAUNCH();
   return FCU_OK;
 }
 
-template <int D>
-int bwd_launch(cudaStream_t st, const float *dO, const float *Q, const float *K, const float *V,
-               const float *lse, const float *delta, int B, int T, int nH, int nKV, float *dQ,
-               float *dK, float *dV, int acc) {
-  const float scale = (float)(1.0 / sqrt((double)D));
-  const size_t smem_kv = 4 * sizeof(__nv_bfloat16) * Smem<D>::TILE + 2 * kTile * sizeof(float);
-  const size_t smem_q = 4 * sizeof(__nv_bfloat16) * Smem<D>::TILE;
+template <int D, typename TI, typename TO>
+int bwd_launch(cudaStream_t st, const Args &a, int B) {
+  const size_t smem_kv = 6 * sizeof(__nv_bfloat16) * Smem<D>::TILE + 4 * kTile * sizeof(float);
+  const size_t smem_q = 6 * sizeof(__nv_bfloat16) * Smem<D>::TILE;
   if (smem_kv > 48 * 1024)
-    FCU_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel<D>,
+    FCU_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel<D, TI, TO>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_kv));
   if (smem_q > 48 * 1024)
-    FCU_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<D>,
+    FCU_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<D, TI, TO>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_q));
-  dim3 gkv(div_up(T, kTile), nKV, B);
-  attn_bwd_dkdv_tc_kernel<D><<<gkv, kThreads, smem_kv, st>>>(Q, K, V, dO, lse, delta, T, nH, nKV,
-                                                              scale, dK, dV, acc);
+  dim3 gkv(div_up(a.T, kTile), a.nKV, B);
+  attn_bwd_dkdv_tc_kernel<D, TI, TO><<<gkv, kThreads, smem_kv, st>>>(a);
   FCU_CHECK_LAUNCH();
-  dim3 gq(div_up(T, kTile), nH, B);
-  attn_bwd_dq_tc_kernel<D><<<gq, kThreads, smem_q, st>>>(Q, K, V, dO, lse, delta, T, nH, nKV, scale,
-                                                          dQ, acc);
+  dim3 gq(div_up(a.T, kTile), a.nH, B);
+  attn_bwd_dq_tc_kernel<D, TI, TO><<<gq, kThreads, smem_q, st>>>(a);
   FCU_CHECK_LAUNCH();
   return FCU_OK;
+}
+
+template <typename TI, typename TO>
+int fwd_dispatch(cudaStream_t st, const Args &a, int B, int dH) {
+  switch (dH) {
+    case 16: return fwd_launch<16, TI, TO>(st, a, B);
+    case 32: return fwd_launch<32, TI, TO>(st, a, B);
+    case 64: return fwd_launch<64, TI, TO>(st, a, B);
+    case 128: return fwd_launch<128, TI, TO>(st, a, B);
+  }
+  set_error("tensor-core attention: unsupported head dim %d", dH);
+  return FCU_ERR_ARG;
+}
+
+template <typename TI, typename TO>
+int bwd_dispatch(cudaStream_t st, const Args &a, int B, int dH) {
+  switch (dH) {
+    case 16: return bwd_launch<16, TI, TO>(st, a, B);
+    case 32: return bwd_launch<32, TI, TO>(st, a, B);
+    case 64: return bwd_launch<64, TI, TO>(st, a, B);
+    case 128: return bwd_launch<128, TI, TO>(st, a, B);
+  }
+  set_error("tensor-core attention: unsupported head dim %d", dH);
+  return FCU_ERR_ARG;
+}
+
+Args fp32_args(const float *Q, const float *K, const float *V, int T, int nH, int nKV, int dH) {
+  Args a{};
+  const int64_t qD = (int64_t)nH * dH, kvD = (int64_t)nKV * dH;
+  a.q = {Q, qD, 0};
+  a.k = {K, kvD, 0};
+  a.v = {V, kvD, 0};
+  a.T = T;
+  a.nH = nH;
+  a.nKV = nKV;
+  a.scale = (float)(1.0 / sqrt((double)dH));
+  return a;
 }
 
 }  // namespace
@@ -457,27 +612,99 @@ bool attn_tc_supported(int dH, const void *Q, const void *K, const void *V) {
 
 int attn_fwd_tc(cudaStream_t st, const float *Q, const float *K, const float *V, int B, int T,
                 int nH, int nKV, int dH, float *O, float *lse) {
-  switch (dH) {
-    case 16: return fwd_launch<16>(st, Q, K, V, B, T, nH, nKV, O, lse);
-    case 32: return fwd_launch<32>(st, Q, K, V, B, T, nH, nKV, O, lse);
-    case 64: return fwd_launch<64>(st, Q, K, V, B, T, nH, nKV, O, lse);
-    case 128: return fwd_launch<128>(st, Q, K, V, B, T, nH, nKV, O, lse);
-  }
-  set_error("attn_fwd_tc: unsupported head dim %d", dH);
-  return FCU_ERR_ARG;
+  Args a = fp32_args(Q, K, V, T, nH, nKV, dH);
+  a.o = {O, (int64_t)nH * dH, 0};
+  a.lse = lse;
+  return fwd_dispatch<float, float>(st, a, B, dH);
 }
 
 int attn_bwd_tc(cudaStream_t st, const float *dO, const float *Q, const float *K, const float *V,
                 const float *lse, const float *delta, int B, int T, int nH, int nKV, int dH,
                 float *dQ, float *dK, float *dV, int acc) {
-  switch (dH) {
-    case 16: return bwd_launch<16>(st, dO, Q, K, V, lse, delta, B, T, nH, nKV, dQ, dK, dV, acc);
-    case 32: return bwd_launch<32>(st, dO, Q, K, V, lse, delta, B, T, nH, nKV, dQ, dK, dV, acc);
-    case 64: return bwd_launch<64>(st, dO, Q, K, V, lse, delta, B, T, nH, nKV, dQ, dK, dV, acc);
-    case 128: return bwd_launch<128>(st, dO, Q, K, V, lse, delta, B, T, nH, nKV, dQ, dK, dV, acc);
-  }
-  set_error("attn_bwd_tc: unsupported head dim %d", dH);
-  return FCU_ERR_ARG;
+  Args a = fp32_args(Q, K, V, T, nH, nKV, dH);
+  const int64_t qD = (int64_t)nH * dH, kvD = (int64_t)nKV * dH;
+  a.dO = {dO, qD, 0};
+  a.dq = {dQ, qD, 0};
+  a.dk = {dK, kvD, 0};
+  a.dv = {dV, kvD, 0};
+  a.lse = const_cast<float *>(lse);
+  a.delta = delta;
+  a.acc = acc;
+  return bwd_dispatch<float, float>(st, a, B, dH);
 }
 
+int rope_table_f32(fcu_ctx *ctx, int T, int head_dim, double theta, const float2 **out);
+
 }  // namespace fcu
+
+extern "C" {
+
+int fcu_attn_fwd_bf16(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, int nH, int nKV,
+                      int dH, void *O, float *lse) {
+  using namespace fcu;
+  FCU_CTX(ctx);
+  FCU_REQUIRE(B > 0 && T > 0 && nH > 0 && nKV > 0 && nH % nKV == 0,
+              "fcu_attn_fwd_bf16: bad shape B=%d T=%d nH=%d nKV=%d", B, T, nH, nKV);
+  FCU_REQUIRE(dH == 16 || dH == 32 || dH == 64 || dH == 128, "fcu_attn_fwd_bf16: dH=%d", dH);
+  FCU_REQUIRE(ld_qkv >= (int64_t)(nH + 2 * nKV) * dH && ld_qkv % 8 == 0,
+              "fcu_attn_fwd_bf16: qkv row stride %lld", (long long)ld_qkv);
+  FCU_REQUIRE(qkv && O && lse && (((uintptr_t)qkv | (uintptr_t)O) & 15) == 0,
+              "fcu_attn_fwd_bf16: null or unaligned pointer");
+  const int64_t qD = (int64_t)nH * dH, kvD = (int64_t)nKV * dH;
+  Args a{};
+  a.q = {qkv, ld_qkv, 0};
+  a.k = {qkv, ld_qkv, qD};
+  a.v = {qkv, ld_qkv, qD + kvD};
+  a.o = {O, qD, 0};
+  a.lse = lse;
+  a.T = T;
+  a.nH = nH;
+  a.nKV = nKV;
+  a.scale = (float)(1.0 / sqrt((double)dH));
+  return fwd_dispatch<__nv_bfloat16, __nv_bfloat16>(ctx->stream, a, B, dH);
+}
+
+int fcu_attn_bwd_bf16(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv, const void *O,
+                      const float *lse, int B, int T, int nH, int nKV, int dH, double rope_theta,
+                      void *dqkv) {
+  using namespace fcu;
+  FCU_CTX(ctx);
+  FCU_REQUIRE(B > 0 && T > 0 && nH > 0 && nKV > 0 && nH % nKV == 0,
+              "fcu_attn_bwd_bf16: bad shape B=%d T=%d nH=%d nKV=%d", B, T, nH, nKV);
+  FCU_REQUIRE(dH == 16 || dH == 32 || dH == 64 || dH == 128, "fcu_attn_bwd_bf16: dH=%d", dH);
+  FCU_REQUIRE(ld_qkv >= (int64_t)(nH + 2 * nKV) * dH && ld_qkv % 8 == 0,
+              "fcu_attn_bwd_bf16: qkv row stride %lld", (long long)ld_qkv);
+  FCU_REQUIRE(dO && qkv && O && lse && dqkv &&
+                  (((uintptr_t)dO | (uintptr_t)qkv | (uintptr_t)O | (uintptr_t)dqkv) & 15) == 0,
+              "fcu_attn_bwd_bf16: null or unaligned pointer");
+  const int64_t qD = (int64_t)nH * dH, kvD = (int64_t)nKV * dH;
+  void *scr = nullptr;
+  int rc = ctx_scratch(ctx, sizeof(float) * (size_t)B * nH * T, &scr);
+  if (rc) return rc;
+  Args a{};
+  a.q = {qkv, ld_qkv, 0};
+  a.k = {qkv, ld_qkv, qD};
+  a.v = {qkv, ld_qkv, qD + kvD};
+  a.o_in = {O, qD, 0};
+  a.dO = {dO, qD, 0};
+  a.dq = {dqkv, ld_qkv, 0};
+  a.dk = {dqkv, ld_qkv, qD};
+  a.dv = {dqkv, ld_qkv, qD + kvD};
+  a.lse = const_cast<float *>(lse);
+  a.delta = (const float *)scr;
+  a.T = T;
+  a.nH = nH;
+  a.nKV = nKV;
+  a.scale = (float)(1.0 / sqrt((double)dH));
+  if (rope_theta > 0) {
+    rc = rope_table_f32(ctx, T, dH, rope_theta, &a.rope);
+    if (rc) return rc;
+  }
+  const int64_t rows = (int64_t)B * T * nH;
+  attn_delta_tc_kernel<__nv_bfloat16><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, ctx->stream>>>(
+      a, B, dH);
+  FCU_CHECK_LAUNCH();
+  return bwd_dispatch<__nv_bfloat16, __nv_bfloat16>(ctx->stream, a, B, dH);
+}
+
+}  // extern "C"

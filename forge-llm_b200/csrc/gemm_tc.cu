@@ -36,6 +36,15 @@ constexpr int GROUP_M = 16;                     // tile raster: GROUP_M m-blocks
 constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + (size_t)STAGES * STAGE_BYTES + 256;
 constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 2 GHz
 
+// Epilogue modes (what the epilogue warps do with one fp32 accumulator row):
+//   kOutF32      C[m,n] = acc            (beta = 1: C += acc)
+//   kOutF32Res   C[m,n] = R[m,n] + acc   (residual add fused, R and C fp32)
+//   kOutBF16     Cb[m,n] = bf16(acc)
+//   kOutBF16Rope Cb[m,n] = bf16(rope(acc)) for n < rope_cols, bf16(acc) after:
+//                interleaved pairs (2i, 2i+1) of each head_dim-wide head are
+//                rotated by the (cos, sin) of position m % rope_T.
+enum : int { kOutF32 = 0, kOutF32Res = 1, kOutBF16 = 2, kOutBF16Rope = 3 };
+
 struct TcParams {
   int M, N, K;
   float *C;
@@ -44,6 +53,11 @@ struct TcParams {
   int a_mn, b_mn;
   int tiles_m, tiles_n;
   int *err;
+  int mode;
+  const float *R;          // kOutF32Res (row stride ldc)
+  __nv_bfloat16 *Cb;       // kOutBF16* (row stride ldc)
+  const float2 *rope;      // [rope_T][head_dim/2] (cos, sin)
+  int rope_T, rope_cols, head_dim;
 };
 
 // ------------------------------------------------------------------ PTX helpers
@@ -175,6 +189,82 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   const int r = t - g * per_group;
   tm = first + r % gm;
   tn = r / gm;
+}
+
+__device__ __forceinline__ uint32_t pack2_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// Writes columns [nb, nb+32) of output row gm from one TMEM load.
+__device__ __forceinline__ void store_chunk(const TcParams &p, int64_t gm, int nb,
+                                            const uint32_t (&r)[32]) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+  const bool full = nb + 32 <= p.N;
+  if (p.mode == kOutF32 || p.mode == kOutF32Res) {
+    float *crow = p.C + gm * p.ldc;
+    const float *rrow = p.mode == kOutF32Res ? p.R + gm * p.ldc : nullptr;
+    const bool vec = full && ((p.ldc & 3) == 0) && (((uintptr_t)p.C & 15) == 0) &&
+                     (rrow == nullptr || ((uintptr_t)p.R & 15) == 0);
+    if (vec) {
+      float4 *dst = reinterpret_cast<float4 *>(crow + nb);
+      const float4 *src = rrow ? reinterpret_cast<const float4 *>(rrow + nb) : nullptr;
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        float4 o = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        if (src || p.beta) {
+          const float4 a = src ? src[i] : dst[i];
+          o.x += a.x;
+          o.y += a.y;
+          o.z += a.z;
+          o.w += a.w;
+        }
+        dst[i] = o;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; i++) {
+        if (nb + i < p.N) {
+          float o = v[i];
+          if (rrow) o += rrow[nb + i];
+          else if (p.beta) o += crow[nb + i];
+          crow[nb + i] = o;
+        }
+      }
+    }
+    return;
+  }
+  if (p.mode == kOutBF16Rope && nb < p.rope_cols) {
+    const int64_t pos = gm % p.rope_T;
+    const int half = p.head_dim >> 1;
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const int pi = ((nb + 2 * i) % p.head_dim) >> 1;
+      const float2 cs = p.rope[pos * half + pi];
+      const float a = v[2 * i], b = v[2 * i + 1];
+      v[2 * i] = a * cs.x - b * cs.y;
+      v[2 * i + 1] = a * cs.y + b * cs.x;
+    }
+  }
+  __nv_bfloat16 *brow = p.Cb + gm * p.ldc;
+  if (full && ((p.ldc & 7) == 0) && (((uintptr_t)p.Cb & 15) == 0)) {
+    uint4 *dst = reinterpret_cast<uint4 *>(brow + nb);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      uint4 o;
+      o.x = pack2_bf16(v[8 * i], v[8 * i + 1]);
+      o.y = pack2_bf16(v[8 * i + 2], v[8 * i + 3]);
+      o.z = pack2_bf16(v[8 * i + 4], v[8 * i + 5]);
+      o.w = pack2_bf16(v[8 * i + 6], v[8 * i + 7]);
+      dst[i] = o;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; i++)
+      if (nb + i < p.N) brow[nb + i] = __float2bfloat16_rn(v[i]);
+  }
 }
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -317,39 +407,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const int64_t gm = (int64_t)tm * BM + row;
       const int n0 = tn * BN;
-      float *crow = p.C + gm * p.ldc;
-      const bool vec = ((p.ldc & 3) == 0) && (((uintptr_t)p.C & 15) == 0);
 #pragma unroll 1
       for (int c = 0; c < BN / 32; c++) {
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
-        if (gm < p.M) {
-          const int nb = n0 + c * 32;
-          if (vec && nb + 32 <= p.N) {
-            float4 *dst = reinterpret_cast<float4 *>(crow + nb);
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-              float4 v = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
-                                     __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
-              if (p.beta) {
-                float4 o = dst[i];
-                v.x += o.x;
-                v.y += o.y;
-                v.z += o.z;
-                v.w += o.w;
-              }
-              dst[i] = v;
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; i++) {
-              if (nb + i < p.N) {
-                float v = __uint_as_float(r[i]);
-                crow[nb + i] = p.beta ? crow[nb + i] + v : v;
-              }
-            }
-          }
-        }
+        if (gm < p.M) store_chunk(p, gm, n0 + c * 32, r);
       }
       tc_fence_before();
       __syncwarp();
@@ -480,9 +542,19 @@ bool gemm_tc_supported(GemmOp op, int64_t M, int64_t N, int64_t K) {
   return false;
 }
 
-// C[M,N] (+)= A . B in the layouts of `op`, operands already bf16.
-int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfloat16 *B, float *C,
-                 int64_t M, int64_t N, int64_t K, int beta, int *err) {
+struct TcOut {
+  int mode = kOutF32;
+  float *C = nullptr;
+  int beta = 0;
+  const float *R = nullptr;
+  __nv_bfloat16 *Cb = nullptr;
+  const float2 *rope = nullptr;
+  int rope_T = 1, rope_cols = 0, head_dim = 2;
+};
+
+// out[M,N] = A . B in the layouts of `op` (bf16 operands), written as `o` says.
+int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfloat16 *B,
+                 int64_t M, int64_t N, int64_t K, const TcOut &o, int *err) {
   int rc = get_encode();
   if (rc) return rc;
   CUtensorMap ta, tb;
@@ -508,9 +580,16 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
-  p.C = C;
+  p.C = o.C;
   p.ldc = N;
-  p.beta = beta;
+  p.beta = o.beta;
+  p.mode = o.mode;
+  p.R = o.R;
+  p.Cb = o.Cb;
+  p.rope = o.rope;
+  p.rope_T = o.rope_T;
+  p.rope_cols = o.rope_cols;
+  p.head_dim = o.head_dim;
   p.a_mn = a_mn;
   p.b_mn = b_mn;
   p.tiles_m = (int)((M + BM - 1) / BM);
@@ -549,9 +628,113 @@ int gemm_tc(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float *C, i
   __nv_bfloat16 *Bb = (__nv_bfloat16 *)((uint8_t *)ws + off_b);
   rc = convert(ctx, A, na, Ab);
   if (!rc) rc = convert(ctx, B, nb, Bb);
-  if (!rc) rc = gemm_bf16_tc(ctx, op, Ab, Bb, C, M, N, K, beta, err);
+  TcOut o;
+  o.C = C;
+  o.beta = beta;
+  if (!rc) rc = gemm_bf16_tc(ctx, op, Ab, Bb, M, N, K, o, err);
   return rc;
 }
+
+// (cos, sin) table [T][head_dim/2] in fp32 for the RoPE epilogue, rounded
+// once from the double angles of ropeRows (src/L2/tensor.js:141-143).
+__global__ void rope_table_f32_kernel(float2 *tab, int T, int half, int head_dim, double theta) {
+  const int64_t n = (int64_t)T * half;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t pos = e / half, i = e % half;
+    const double ang = (double)pos / pow(theta, (double)(2 * i) / (double)head_dim);
+    double s, c;
+    sincos(ang, &s, &c);
+    tab[e] = make_float2((float)c, (float)s);
+  }
+}
+
+int rope_table_f32(fcu_ctx *ctx, int T, int head_dim, double theta, const float2 **out) {
+  struct Tab {
+    float2 *p = nullptr;
+    int T = 0, head_dim = 0;
+    double theta = 0;
+  };
+  static thread_local Tab tabs[64];
+  Tab &t = tabs[ctx->device & 63];
+  if (!t.p || t.T < T || t.head_dim != head_dim || t.theta != theta) {
+    if (t.p) {
+      FCU_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
+      FCU_CHECK_CUDA(cudaFree(t.p));
+      t.p = nullptr;
+    }
+    const int half = head_dim / 2;
+    FCU_CHECK_CUDA(cudaMalloc(&t.p, sizeof(float2) * (size_t)T * half));
+    rope_table_f32_kernel<<<256, 256, 0, ctx->stream>>>(t.p, T, half, head_dim, theta);
+    FCU_CHECK_LAUNCH();
+    t.T = T;
+    t.head_dim = head_dim;
+    t.theta = theta;
+  }
+  *out = t.p;
+  return FCU_OK;
+}
+
+}  // namespace fcu
+
+extern "C" int fcu_gemm_bf16(fcu_ctx *ctx, int op, const void *A, const void *B, int64_t M,
+                             int64_t N, int64_t K, const fcu_gemm_out *out) {
+  using namespace fcu;
+  FCU_CTX(ctx);
+  FCU_REQUIRE(out != nullptr && A && B, "fcu_gemm_bf16: null argument");
+  FCU_REQUIRE(op >= 0 && op <= 2, "fcu_gemm_bf16: unknown op %d", op);
+  const GemmOp gop = (GemmOp)op;
+  FCU_REQUIRE(gemm_tc_supported(gop, M, N, K),
+              "fcu_gemm_bf16: shape M=%lld N=%lld K=%lld has a row length that is not a multiple "
+              "of 8 elements (TMA needs 16-byte rows)",
+              (long long)M, (long long)N, (long long)K);
+  FCU_REQUIRE((((uintptr_t)A | (uintptr_t)B) & 15) == 0, "fcu_gemm_bf16: operands must be 16-byte aligned");
+  FCU_REQUIRE(out->out != nullptr, "fcu_gemm_bf16: null output");
+  TcOut o;
+  switch (out->mode) {
+    case FCU_OUT_F32:
+      o.mode = kOutF32;
+      o.C = (float *)out->out;
+      o.beta = out->accumulate ? 1 : 0;
+      break;
+    case FCU_OUT_F32_RESIDUAL:
+      FCU_REQUIRE(out->residual != nullptr, "fcu_gemm_bf16: FCU_OUT_F32_RESIDUAL needs a residual");
+      o.mode = kOutF32Res;
+      o.C = (float *)out->out;
+      o.R = out->residual;
+      break;
+    case FCU_OUT_BF16:
+      o.mode = kOutBF16;
+      o.Cb = (__nv_bfloat16 *)out->out;
+      break;
+    case FCU_OUT_BF16_ROPE: {
+      FCU_REQUIRE(out->rope_T > 0 && out->head_dim > 0 && out->head_dim % 2 == 0,
+                  "fcu_gemm_bf16: RoPE needs rope_T > 0 and an even head_dim (got %d, %d)",
+                  out->rope_T, out->head_dim);
+      FCU_REQUIRE(out->rope_cols >= 0 && out->rope_cols % 32 == 0 && out->rope_cols % out->head_dim == 0 &&
+                      out->rope_cols <= N,
+                  "fcu_gemm_bf16: rope_cols %d must be a multiple of 32 and of head_dim", out->rope_cols);
+      o.mode = kOutBF16Rope;
+      o.Cb = (__nv_bfloat16 *)out->out;
+      o.rope_T = out->rope_T;
+      o.rope_cols = out->rope_cols;
+      o.head_dim = out->head_dim;
+      int rc = rope_table_f32(ctx, out->rope_T, out->head_dim, out->rope_theta, &o.rope);
+      if (rc) return rc;
+      break;
+    }
+    default:
+      set_error("fcu_gemm_bf16: unknown output mode %d", out->mode);
+      return FCU_ERR_ARG;
+  }
+  void *ws = nullptr;
+  int *err = nullptr;
+  int rc = workspace(ctx, 0, &ws, &err);
+  if (rc) return rc;
+  return gemm_bf16_tc(ctx, gop, (const __nv_bfloat16 *)A, (const __nv_bfloat16 *)B, M, N, K, o, err);
+}
+
+namespace fcu {
 
 int gemm_tc_error(fcu_ctx *ctx) {
   void *ws = nullptr;

@@ -1,6 +1,7 @@
 // Row-wise and elementwise kernels of the training hot path: embedding,
 // rmsNorm, ropeRows, sliceCols, swiglu, residual add, fused cross-entropy and
 // small helpers.  All are single-pass, coalesced, HBM-bound kernels.
+#include <cuda_bf16.h>
 #include <math.h>
 
 #include <mutex>
@@ -340,15 +341,28 @@ __device__ __forceinline__ void ce_block_reduce(float &m, float &s, float *shm, 
   }
 }
 
-template <bool CACHED>
+__device__ __forceinline__ void ce_store4(float *p, float4 o) { *reinterpret_cast<float4 *>(p) = o; }
+__device__ __forceinline__ void ce_store4(__nv_bfloat16 *p, float4 o) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(o.x, o.y), b = __floats2bfloat162_rn(o.z, o.w);
+  uint2 u;
+  u.x = *reinterpret_cast<uint32_t *>(&a);
+  u.y = *reinterpret_cast<uint32_t *>(&b);
+  *reinterpret_cast<uint2 *>(p) = u;
+}
+__device__ __forceinline__ void ce_store1(float *p, float v) { *p = v; }
+__device__ __forceinline__ void ce_store1(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
+
+// TO = float: the op-level gradient; TO = bf16: the fused path, where the
+// gradient is the next tensor-core GEMM's operand.
+template <bool CACHED, typename TO = float>
 __global__ void __launch_bounds__(kCeThreads) ce_fwd_kernel(const float *logits,
                                                             const int32_t *__restrict__ targets,
                                                             int64_t T, int64_t V,
-                                                            float *row_loss, float *dunit) {
+                                                            float *row_loss, TO *dunit) {
   __shared__ float shm[32], shs[32];
   const int64_t row = blockIdx.x;
   const float *l = logits + row * V;
-  float *du = dunit + row * V;
+  TO *du = dunit + row * V;
   const float invT = (float)(1.0 / (double)T);
   const int32_t tgt = targets[row];
   float m = -INFINITY, s = 0.f;
@@ -384,7 +398,6 @@ __global__ void __launch_bounds__(kCeThreads) ce_fwd_kernel(const float *logits,
   const float lt = (tgt >= 0 && tgt < V) ? l[tgt] : __int_as_float(0x7fc00000);
   __syncthreads();  // every thread has read l[tgt] before any in-place write
   if (CACHED) {
-    float4 *d4 = reinterpret_cast<float4 *>(du);
     const int64_t V4 = V >> 2;
 #pragma unroll
     for (int k = 0; k < kCeVec; k++) {
@@ -397,13 +410,13 @@ __global__ void __launch_bounds__(kCeThreads) ce_fwd_kernel(const float *logits,
         o.y = (expf(v.y - lse) - (i + 1 == tgt ? 1.f : 0.f)) * invT;
         o.z = (expf(v.z - lse) - (i + 2 == tgt ? 1.f : 0.f)) * invT;
         o.w = (expf(v.w - lse) - (i + 3 == tgt ? 1.f : 0.f)) * invT;
-        d4[i4] = o;
+        ce_store4(du + i, o);
       }
     }
   } else {
     for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
       float v = l[i];
-      du[i] = (expf(v - lse) - (i == tgt ? 1.f : 0.f)) * invT;
+      ce_store1(du + i, (expf(v - lse) - (i == tgt ? 1.f : 0.f)) * invT);
     }
   }
   if (threadIdx.x == 0) row_loss[row] = lse - lt;
@@ -664,6 +677,29 @@ int fcu_ce_fwd(fcu_ctx *ctx, const float *logits, const int32_t *targets, int64_
     ce_fwd_kernel<true><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
   else
     ce_fwd_kernel<false><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
+  FCU_CHECK_LAUNCH();
+  mean_kernel<<<1, 1024, 0, ctx->stream>>>(row_loss, T, loss_out);
+  FCU_CHECK_LAUNCH();
+  return FCU_OK;
+}
+
+int fcu_ce_fwd_bf16grad(fcu_ctx *ctx, const float *logits, const int32_t *targets, int64_t T,
+                        int64_t V, float *loss_out, void *dlogits_bf16) {
+  FCU_CTX(ctx);
+  FCU_REQUIRE(T > 0 && V > 0 && T < (1ll << 31), "fcu_ce_fwd_bf16grad: bad shape");
+  FCU_REQUIRE(logits && targets && loss_out && dlogits_bf16, "fcu_ce_fwd_bf16grad: null pointer");
+  void *scr = nullptr;
+  int rc = fcu::ctx_scratch(ctx, sizeof(float) * (size_t)T, &scr);
+  if (rc) return rc;
+  float *row_loss = (float *)scr;
+  __nv_bfloat16 *du = (__nv_bfloat16 *)dlogits_bf16;
+  bool aligned = ((uintptr_t)logits % 16 == 0) && ((uintptr_t)du % 8 == 0);
+  if (aligned && V % 4 == 0 && V <= (int64_t)kCeThreads * kCeVec * 4)
+    ce_fwd_kernel<true, __nv_bfloat16><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V,
+                                                                               row_loss, du);
+  else
+    ce_fwd_kernel<false, __nv_bfloat16><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V,
+                                                                                row_loss, du);
   FCU_CHECK_LAUNCH();
   mean_kernel<<<1, 1024, 0, ctx->stream>>>(row_loss, T, loss_out);
   FCU_CHECK_LAUNCH();

@@ -31,6 +31,17 @@ class ModelCfg(C.Structure):
                 ("norm_eps", C.c_double), ("rope_theta", C.c_double)]
 
 
+class GemmOut(C.Structure):
+    """fcu_gemm_out."""
+    _fields_ = [("mode", C.c_int), ("out", C.c_void_p), ("accumulate", C.c_int),
+                ("residual", C.c_void_p), ("rope_T", C.c_int), ("rope_cols", C.c_int),
+                ("head_dim", C.c_int), ("rope_theta", C.c_double)]
+
+
+GEMM_FWD, GEMM_DX, GEMM_DW = 0, 1, 2
+OUT_F32, OUT_F32_RESIDUAL, OUT_BF16, OUT_BF16_ROPE = 0, 1, 2, 3
+
+
 class AdamHyper(C.Structure):
     _fields_ = [("lr", C.c_double), ("b1", C.c_double), ("b2", C.c_double),
                 ("eps", C.c_double), ("wd", C.c_double), ("clip", C.c_double),
@@ -84,6 +95,17 @@ _SIGS = {
     "fcu_adam_step_sumsq": (_INT, [_P, _P, _P, _P, _P, _I64, C.POINTER(AdamHyper), _P, _P]),
     "fcu_sumsq": (_INT, [_P, _P, _I64, _P, _INT]),
     "fcu_scale": (_INT, [_P, _P, _I64, C.c_float]),
+    "fcu_gemm_bf16": (_INT, [_P, _INT, _P, _P, _I64, _I64, _I64, _P]),
+    "fcu_rmsnorm_fwd_bf16": (_INT, [_P, _P, _P, _I64, _I64, _D, _P, _P]),
+    "fcu_rmsnorm_bwd_fused": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _P, _INT, _P, _P, _INT]),
+    "fcu_swiglu_fwd_bf16": (_INT, [_P, _P, _I64, _I64, _P]),
+    "fcu_swiglu_bwd_bf16": (_INT, [_P, _P, _P, _I64, _I64, _P]),
+    "fcu_ce_fwd_bf16grad": (_INT, [_P, _P, _P, _I64, _I64, _P, _P]),
+    "fcu_attn_fwd_bf16": (_INT, [_P, _P, _I64, _INT, _INT, _INT, _INT, _INT, _P, _P]),
+    "fcu_attn_bwd_bf16": (_INT, [_P, _P, _P, _I64, _P, _P, _INT, _INT, _INT, _INT, _INT, _D, _P]),
+    "fcu_adam_step_shadow": (_INT, [_P, _P, _P, _P, _P, _I64, C.POINTER(AdamHyper), _P, _P, _P]),
+    "fcu_to_bf16": (_INT, [_P, _P, _I64, _P]),
+    "fcu_scale_bf16_dev": (_INT, [_P, _P, _I64, _P]),
     "fcu_rng_init": (None, [C.POINTER(RngState), C.c_uint32]),
     "fcu_rng_next": (_D, [C.POINTER(RngState)]),
     "fcu_rng_normal": (_D, [C.POINTER(RngState)]),

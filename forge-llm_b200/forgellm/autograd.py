@@ -29,6 +29,14 @@ from ._lib import AdamHyper, Context, call
 
 RETAIN_OP_GRADS = False
 
+# bf16 copies of flat parameter buffers that Adam keeps current:
+# flat fp32 data_ptr -> owner with `.flat_params_bf16` and `._shadow_stale`.
+_SHADOWS: dict = {}
+
+
+def register_shadow(flat_params: torch.Tensor, owner) -> None:
+    _SHADOWS[flat_params.data_ptr()] = owner
+
 
 # ----------------------------------------------------------------- device helpers
 def ctx() -> Context:
@@ -94,7 +102,8 @@ def noGrad(fn):
 class Node:
     """A tensor on the tape (autograd.js:25-34)."""
 
-    __slots__ = ("data", "_grad", "_gzero", "_gslot", "_b", "isParam", "__weakref__")
+    __slots__ = ("data", "_grad", "_gzero", "_gslot", "_b", "isParam", "_seeded_one",
+                 "__weakref__")
 
     def __init__(self, data, requiresGrad: bool = True):
         self.data = data if (isinstance(data, torch.Tensor) and data.is_cuda
@@ -104,6 +113,7 @@ class Node:
         self._gslot = None   # preallocated storage for the gradient (flat buffers)
         self._b = None
         self.isParam = False
+        self._seeded_one = False
         if requiresGrad and _tape.enabled:
             _tape.nodes.append(self)
 
@@ -161,6 +171,7 @@ def op(out, bwd) -> Node:
 def backward(loss: Node) -> None:
     """autograd.js:126-133."""
     loss.grad = torch.ones(loss.n, dtype=torch.float32, device=loss.data.device)
+    loss._seeded_one = True           # the loss gradient is the constant 1
     nodes = _tape.nodes
     after = _tape.after
     for i in range(len(nodes) - 1, -1, -1):
@@ -289,6 +300,13 @@ class Adam:
             for p in self.p:          # materialise zeroed-but-unwritten grads
                 if p._gzero:
                     p.grad  # noqa: B018  (property zero-fills)
+            owner = _SHADOWS.get(pf.data_ptr())
+            if (owner is not None and getattr(owner, "flat_params_bf16", None) is not None
+                    and owner.flat_params_bf16.numel() == pf.numel()):
+                call("fcu_adam_step_shadow", c.handle, ptr(pf), ptr(gf), ptr(self.m_flat),
+                     ptr(self.v_flat), pf.numel(), h, ptr(sumsq_dev), ptr(info),
+                     ptr(owner.flat_params_bf16))
+                return AdamInfo(h.lr, info.clone())
             if sumsq_dev is None:
                 call("fcu_adam_step", c.handle, ptr(pf), ptr(gf), ptr(self.m_flat),
                      ptr(self.v_flat), pf.numel(), h, ptr(info))
@@ -314,6 +332,8 @@ class Adam:
                 continue
             call("fcu_adam_step_sumsq", c.handle, ptr(p.data), ptr(g), ptr(self.m[j]),
                  ptr(self.v[j]), p.n, h, ptr(ss), ptr(info))
+        for owner in _SHADOWS.values():   # a bf16 weight copy may now be out of date
+            owner._shadow_stale = True
         return AdamInfo(h.lr, info.clone())
 
 

@@ -15,7 +15,7 @@ import numpy as np
 import torch
 
 from . import autograd as AD
-from ._lib import ModelCfg, RngState, call, lib
+from ._lib import ModelCfg, RngState, call, lib  # noqa: F401
 from .autograd import Adam, Node, backward, resetTape
 from .tensor import (addTensors, causalAttn, causalAttnBatch, crossEntropyMean, embedLookup,
                      matmulT, rmsNorm, ropeRows, sliceCols, swigluRows)
@@ -162,8 +162,81 @@ class TrainableTransformer:
             else:
                 self.params[name] = p
         self.layer_offsets = self._layer_offsets()
+        self.offsets = {}
+        off = 0
+        for name, n in param_shapes(c):
+            self.offsets[name] = (off, off + n)
+            off += n
         self.w = None
+        # bf16 fused step: None = automatic (bf16 precision and supported
+        # shapes), True / False to force.
+        self.fused = None
+        self._fused_steps = {}
+        self.flat_params_bf16 = None
+        self._shadow_stale = True
+        self._shadow_version = -1
+        self._bf16_views = None
         self._build()
+
+    # ------------------------------------------------------------ bf16 fused path
+    def _use_fused(self) -> bool:
+        from ._lib import FCU_PREC_BF16
+        from .fused import fused_supported
+        if self.fused is False:
+            return False
+        ok = AD.ctx().precision == FCU_PREC_BF16 and fused_supported(self.cfg)
+        if self.fused is True and not ok:
+            raise ValueError("fused step needs bf16 precision and supported shapes")
+        return ok
+
+    def bf16_weights(self) -> dict:
+        """bf16 views of the weights the fused GEMMs read (re-converted from
+        the fp32 parameters when host code or a per-tensor optimizer changed
+        them; Adam's flat step keeps them current itself)."""
+        if self.flat_params_bf16 is None:
+            self.flat_params_bf16 = torch.empty(self.flat_params.numel(), dtype=torch.bfloat16,
+                                                device=self.flat_params.device)
+            AD.register_shadow(self.flat_params, self)
+        if self._shadow_stale or self._shadow_version != self.flat_params._version:
+            call("fcu_to_bf16", AD.ctx().handle, self.flat_params.data_ptr(),
+                 self.flat_params.numel(), self.flat_params_bf16.data_ptr())
+            self._shadow_stale = False
+            self._shadow_version = self.flat_params._version
+        if self._bf16_views is None:
+            s, o = self.flat_params_bf16, self.offsets
+            v = lambda name: s[o[name][0]:o[name][1]]  # noqa: E731
+            layers = []
+            for l in range(self.cfg.nLayers):
+                p = f"layer.{l}."
+                layers.append({"wqkv": v(p + "wqkv"), "wo": v(p + "wo"),
+                               "ffn_gu": s[o[p + "ffn_gate"][0]:o[p + "ffn_up"][1]],
+                               "ffn_down": v(p + "ffn_down")})
+            self._bf16_views = {"tok_emb": v("tok_emb"), "layers": layers}
+        return self._bf16_views
+
+    def grad_block(self, l: int, which: str) -> torch.Tensor:
+        """Gradient view of ffn_gate followed by ffn_up of layer l."""
+        assert which == "ffn_gu"
+        o = self.offsets
+        return self.flat_grads[o[f"layer.{l}.ffn_gate"][0]:o[f"layer.{l}.ffn_up"][1]]
+
+    def _fused_loss(self, ids, tgt, B: int, T: int) -> Node:
+        from .fused import FusedStep
+        key = (B, T)
+        fs = self._fused_steps.get(key)
+        if fs is None:
+            self._fused_steps.clear()           # one shape's buffers at a time
+            fs = self._fused_steps[key] = FusedStep(self, B, T)
+        idt = AD.as_device(ids, torch.int32)
+        tgt = AD.as_device(tgt, torch.int32)
+        loss = fs.forward(idt, tgt)
+        node = None
+
+        def bwd(g):
+            fs.backward(None if getattr(node, "_seeded_one", False) else g)
+
+        node = AD.op(loss, bwd)
+        return node
 
     def _layer_offsets(self):
         """(start, end) of each layer's block in the flat buffers."""
@@ -218,7 +291,10 @@ class TrainableTransformer:
     def loss(self, ids, targets) -> Node:
         """Forward + mean cross-entropy, next-token targets (train.js:166-171)."""
         T = len(targets)
-        logits = self.forward(list(ids)[:T] if not isinstance(ids, torch.Tensor) else ids[:T])
+        ids_t = list(ids)[:T] if not isinstance(ids, torch.Tensor) else ids[:T]
+        if self._use_fused():
+            return self._fused_loss(ids_t, targets, 1, T)
+        logits = self.forward(ids_t)
         return crossEntropyMean(logits, targets, T, self.cfg.vocabSize)
 
     def lossBatch(self, batchIds) -> Node:
@@ -232,6 +308,8 @@ class TrainableTransformer:
             B, T = len(batchIds), len(batchIds[0]) - 1
             ids = [r[i] for r in batchIds for i in range(T)]
             tgt = [r[i + 1] for r in batchIds for i in range(T)]
+        if self._use_fused():
+            return self._fused_loss(ids, tgt, B, T)
         logits = self._forward(ids, B, T, 0)
         return crossEntropyMean(logits, tgt, B * T, self.cfg.vocabSize)
 

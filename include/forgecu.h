@@ -91,6 +91,72 @@ int fcu_matmulT_bwd(fcu_ctx *ctx, const float *dY, const float *X, const float *
                     int accumulate_dx, float *dW, int accumulate_dw, int64_t M, int64_t K,
                     int64_t N);
 
+/* ---------------------------------------------------------------- fused bf16 path */
+/* The building blocks TrainableTransformer's step uses in FCU_PREC_BF16 mode.
+ * They compute the same contractions as the matmulT / causalAttn /
+ * rmsNorm / swigluRows / crossEntropyMean entries above, but take bf16
+ * operands produced directly by the previous kernel and fuse the glue the JS
+ * does as separate ops (residual add, RoPE, bf16 copies of gradients), so no
+ * fp32 -> bf16 conversion pass or column slice is ever run. */
+enum { FCU_GEMM_FWD = 0, FCU_GEMM_DX = 1, FCU_GEMM_DW = 2 };
+enum { FCU_OUT_F32 = 0, FCU_OUT_F32_RESIDUAL = 1, FCU_OUT_BF16 = 2, FCU_OUT_BF16_ROPE = 3 };
+
+typedef struct {
+  int mode;               /* FCU_OUT_* */
+  void *out;              /* [M, N] fp32 (F32*) or bf16 (BF16*) */
+  int accumulate;         /* FCU_OUT_F32: out += A.B */
+  const float *residual;  /* FCU_OUT_F32_RESIDUAL: out = residual + A.B (addTensors, train.js:230) */
+  int rope_T;             /* FCU_OUT_BF16_ROPE: position = row % rope_T (ropeRows posStride) */
+  int rope_cols;          /* columns [0, rope_cols) are rotated (q and k of a fused qkv) */
+  int head_dim;
+  double rope_theta;
+} fcu_gemm_out;
+
+/* One tcgen05 contraction on bf16 operands (fp32 accumulate) in the layouts
+ * of matmulT: FCU_GEMM_FWD C = A[M,K].B[N,K]^T; FCU_GEMM_DX C = A[M,K].B[K,N];
+ * FCU_GEMM_DW C = A[K,M]^T.B[K,N].  Every operand row length must be a multiple
+ * of 8 elements and both operands 16-byte aligned. */
+int fcu_gemm_bf16(fcu_ctx *ctx, int op, const void *A, const void *B, int64_t M, int64_t N,
+                  int64_t K, const fcu_gemm_out *out);
+
+/* rmsNorm forward (src/L2/tensor.js:103-113) writing bf16 out[T,D] and fp32
+ * inv[T].  D % 4 == 0. */
+int fcu_rmsnorm_fwd_bf16(fcu_ctx *ctx, const float *X, const float *w, int64_t T, int64_t D,
+                         double eps, void *out_bf16, float *inv);
+/* rmsNorm backward (src/L2/tensor.js:114-127) fused with the residual
+ * gradient: dX (+)= the rmsNorm input gradient (fp32, in place); if dX_bf16
+ * is not NULL it receives bf16 of the final dX (the next GEMM's operand);
+ * dw (+)= sum_t g*x*inv (deterministic).  D % 4 == 0, D <= 2048. */
+int fcu_rmsnorm_bwd_fused(fcu_ctx *ctx, const float *dY, const float *X, const float *w,
+                          const float *inv, int64_t T, int64_t D, float *dX, int accumulate_dx,
+                          void *dX_bf16, float *dw, int accumulate_dw);
+/* swigluRows (src/L2/tensor.js:272-290) over one bf16 [N, 2H] buffer whose
+ * columns [0,H) are the gate and [H,2H) the up projection (the layout of
+ * ffn_gate followed by ffn_up in paramList order): act[N,H] = silu(g)*u, and
+ * backward dgu[N,2H] = (dact*u*silu'(g), dact*silu(g)).  H % 8 == 0. */
+int fcu_swiglu_fwd_bf16(fcu_ctx *ctx, const void *gu, int64_t N, int64_t H, void *act);
+int fcu_swiglu_bwd_bf16(fcu_ctx *ctx, const void *dact, const void *gu, int64_t N, int64_t H,
+                        void *dgu);
+/* crossEntropyMean forward (src/L2/tensor.js:393-407) whose unit gradient
+ * (P - onehot)/T is written in bf16 (the LM-head backward's operand). */
+int fcu_ce_fwd_bf16grad(fcu_ctx *ctx, const float *logits, const int32_t *targets, int64_t T,
+                        int64_t V, float *loss_out, void *dlogits_bf16);
+/* Causal GQA attention on bf16 operands read from one qkv buffer [B*T, ld]
+ * (q heads at columns [0, nH*dH), k at [nH*dH, ..+nKV*dH), v after), O bf16
+ * [B*T, nH*dH], lse fp32 [B, nH, T] (causalAttnBatch, src/L2/tensor.js:299-337). */
+int fcu_attn_fwd_bf16(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, int nH, int nKV,
+                      int dH, void *O, float *lse);
+/* Its backward (src/L2/tensor.js:339-375): dq, dk, dv written in bf16 into
+ * dqkv (same layout as qkv); when rope_theta > 0 the RoPE backward R^T
+ * (src/L2/tensor.js:150-165, position = row % T) is applied to dq and dk. */
+int fcu_attn_bwd_bf16(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv, const void *O,
+                      const float *lse, int B, int T, int nH, int nKV, int dH, double rope_theta,
+                      void *dqkv);
+/* y[i] = bf16(x[i]). */
+int fcu_to_bf16(fcu_ctx *ctx, const float *x, int64_t n, void *y);
+/* y[i] = bf16(y[i] * alpha_dev[0]) (a loss gradient other than 1). */
+int fcu_scale_bf16_dev(fcu_ctx *ctx, void *y, int64_t n, const float *alpha_dev);
+
 /* ---------------------------------------------------------------- embedding */
 /* out[T,D] = W[ids[t], :].  Replaces embedLookup, src/L2/tensor.js:85-91. */
 int fcu_embed_fwd(fcu_ctx *ctx, const float *W, const int32_t *ids, int64_t T, int64_t V,
@@ -213,6 +279,12 @@ int fcu_adam_step_sumsq(fcu_ctx *ctx, float *p, const float *g, float *m, float 
 
 /* sumsq_dev[0] (+)= sum g[i]^2 in double, deterministic. */
 int fcu_sumsq(fcu_ctx *ctx, const float *g, int64_t n, double *sumsq_dev, int accumulate);
+
+/* Adam (fcu_adam_step semantics) that also writes bf16(p) into p_bf16, the
+ * weight copy the bf16 GEMMs read.  sumsq_dev may be NULL (computed here). */
+int fcu_adam_step_shadow(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int64_t n,
+                         const fcu_adam_hyper *h, const double *sumsq_dev, double *info_dev,
+                         void *p_bf16);
 
 /* ---------------------------------------------------------------- RNG / init (host) */
 /* xorshift128+ with splitmix32 seeding, Box-Muller normals: the seeded
