@@ -163,6 +163,8 @@ def main():
                     choices=["fp32", "tf32x3", "bf16"])
     ap.add_argument("--batch", type=int, default=GLOBAL_BATCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true",
+                    help="launch the step op by op instead of replaying its CUDA graph")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -196,15 +198,28 @@ def main():
     batch_dev = torch.from_numpy(np.ascontiguousarray(local_rows)).cuda()
     batch_host = torch.from_numpy(np.ascontiguousarray(local_rows)).pin_memory()
 
-    def step(batch):
-        F.resetTape()
-        model.zeroGrad()
-        loss = model.lossBatch(batch)
-        AD.backward(loss)
-        if dp is not None:
-            dp.finish()
-        opt.step()
-        return loss
+    use_graph = args.precision == "bf16" and not args.eager
+    if use_graph:
+        # The whole step (fused fwd + bwd, all-reduces, Adam) as one CUDA graph.
+        from forgellm.graph import CapturedStep
+        cs = CapturedStep(model, opt, local_rows.shape[0], SEQ, dp=dp, time_gemms=True)
+
+        def step(batch):
+            return cs(batch)
+    else:
+        cs = None
+
+        def step(batch):
+            if batch.device.type != "cuda":
+                batch = batch.to("cuda", non_blocking=True)
+            F.resetTape()
+            model.zeroGrad()
+            loss = model.lossBatch(batch)
+            AD.backward(loss)
+            if dp is not None:
+                dp.finish()
+            opt.step()
+            return loss.data
 
     def barrier():
         if world > 1:
@@ -219,7 +234,7 @@ def main():
     # ---------------- timed region 1: inputs resident in HBM
     sampler = ClockSampler(local)
     sampler.start()
-    TS.GEMM_TIMER = []
+    TS.GEMM_TIMER = None if use_graph else []
     launches0 = lib().fcu_launch_count()
     stream = torch.cuda.current_stream()
     barrier()
@@ -229,17 +244,23 @@ def main():
         step(batch_dev)
     ev1.record(stream)
     torch.cuda.synchronize()
-    launches = lib().fcu_launch_count() - launches0
     ms = ev0.elapsed_time(ev1)
-    gemm = TS.GEMM_TIMER
-    TS.GEMM_TIMER = None
     clocks = sampler.stop()
-    gemm_ms = sum(a.elapsed_time(b) for _, a, b in gemm)
-    gemm_flops = sum(f for f, _, _ in gemm)
+    if use_graph:
+        launches = cs.launches_per_step * args.steps     # kernel nodes replayed
+        gemm_flops, gemm_ms = cs.gemm_time_ms()          # last replay's GEMMs
+        gemm_flops *= args.steps
+        gemm_ms *= args.steps
+    else:
+        launches = lib().fcu_launch_count() - launches0
+        gemm = TS.GEMM_TIMER
+        TS.GEMM_TIMER = None
+        gemm_ms = sum(a.elapsed_time(b) for _, a, b in gemm)
+        gemm_flops = sum(f for f, _, _ in gemm)
     t = torch.tensor([ms, gemm_ms], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, gemm_ms_max = float(t[0]), float(t[1])
+    ms = float(t[0])
     tokens_per_step = args.batch * SEQ
     value = tokens_per_step * args.steps / (ms / 1e3)
 
@@ -248,15 +269,8 @@ def main():
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        b = batch_host.to("cuda", non_blocking=True)
-        F.resetTape()
-        model.zeroGrad()
-        loss = model.lossBatch(b)
-        AD.backward(loss)
-        if dp is not None:
-            dp.finish()
-        opt.step()
-        _ = float(loss.data[0].item())          # device -> host read of the loss
+        loss = step(batch_host)                  # host -> device copy of the batch inside
+        _ = float(loss[0].item())                # device -> host read of the loss
     e1.record(stream)
     torch.cuda.synchronize()
     te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")

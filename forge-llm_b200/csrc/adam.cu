@@ -57,12 +57,15 @@ __device__ __forceinline__ void adam_elem(float &p, float g, float &m, float &v,
 __global__ void adam_update_kernel(float *__restrict__ p, const float *__restrict__ g,
                                    float *__restrict__ m, float *__restrict__ v, int64_t n, Hyper h,
                                    const double *__restrict__ sumsq, double *__restrict__ info,
-                                   int vec, __nv_bfloat16 *__restrict__ shadow) {
+                                   int vec, __nv_bfloat16 *__restrict__ shadow,
+                                   const Hyper *__restrict__ hdev) {
+  if (hdev) h = *hdev;  // the on-device schedule of fcu_adam_step_sched
   const double gnorm = sqrt(sumsq[0]);
   const double scale = gnorm > h.clip ? h.clip / gnorm : 1.0;
   if (info && blockIdx.x == 0 && threadIdx.x == 0) {
     info[0] = gnorm;
     info[1] = scale;
+    if (hdev) info[2] = h.lr;
   }
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   int64_t start = 0;
@@ -115,10 +118,34 @@ int sumsq_impl(fcu_ctx *ctx, const float *g, int64_t n, double *out, int acc) {
   return FCU_OK;
 }
 
+// The cosine lr and bias corrections of step t = ++(*t_dev), computed on the
+// device so a captured step replays with the right schedule
+// (src/L2/autograd.js:222,229,237-238).
+__global__ void adam_sched_kernel(double lr0, double b1, double b2, double eps, double wd,
+                                  double clip, double total, int32_t *__restrict__ t_dev,
+                                  Hyper *__restrict__ out) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    const int t = ++t_dev[0];
+    double tt = (double)t / total;
+    if (tt > 1) tt = 1;
+    Hyper h;
+    h.lr = lr0 * 0.5 * (1.0 + cos(M_PI * tt));
+    h.b1 = b1;
+    h.b2 = b2;
+    h.eps = eps;
+    h.wd = wd;
+    h.clip = clip;
+    h.bc1 = 1.0 - pow(b1, (double)t);
+    h.bc2 = 1.0 - pow(b2, (double)t);
+    *out = h;
+  }
+}
+
 int update_impl(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int64_t n,
                 const fcu_adam_hyper *hh, const double *sumsq, double *info,
-                __nv_bfloat16 *shadow = nullptr) {
-  Hyper h{hh->lr, hh->b1, hh->b2, hh->eps, hh->wd, hh->clip, hh->bc1, hh->bc2};
+                __nv_bfloat16 *shadow = nullptr, const Hyper *hdev = nullptr) {
+  Hyper h{0, 0, 0, 0, 0, 0, 1, 1};
+  if (hh) h = Hyper{hh->lr, hh->b1, hh->b2, hh->eps, hh->wd, hh->clip, hh->bc1, hh->bc2};
   int vec = aligned16(p) && aligned16(g) && aligned16(m) && aligned16(v) &&
             (shadow == nullptr || ((uintptr_t)shadow & 7) == 0);
   int64_t work = vec ? (n >> 2) : n;
@@ -127,7 +154,7 @@ int update_impl(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int6
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   adam_update_kernel<<<(int)blocks, kThreads, 0, ctx->stream>>>(p, g, m, v, n, h, sumsq, info, vec,
-                                                                 shadow);
+                                                                 shadow, hdev);
   FCU_CHECK_LAUNCH();
   return FCU_OK;
 }
@@ -188,6 +215,27 @@ int fcu_adam_step_shadow(fcu_ctx *ctx, float *p, const float *g, float *m, float
     ss = own;
   }
   return update_impl(ctx, p, g, m, v, n, h, ss, info_dev, (__nv_bfloat16 *)p_bf16);
+}
+
+int fcu_adam_step_sched(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int64_t n,
+                        const fcu_adam_sched *s, int32_t *t_dev, double *info_dev, void *p_bf16) {
+  FCU_CTX(ctx);
+  FCU_REQUIRE(n >= 0 && p && g && m && v && s && t_dev, "fcu_adam_step_sched: bad args");
+  FCU_REQUIRE(s->total_steps > 0, "fcu_adam_step_sched: total_steps must be > 0");
+  if (n == 0) return FCU_OK;
+  // scratch: [nblk partial sums][sum of squares][Hyper]
+  const int nblk = 2 * ctx->num_sms;
+  void *scr = nullptr;
+  int rc = fcu::ctx_scratch(ctx, sizeof(double) * (nblk + 1) + sizeof(Hyper) + 64, &scr);
+  if (rc) return rc;
+  double *ss = (double *)scr + nblk;
+  Hyper *hdev = (Hyper *)(((uintptr_t)(ss + 1) + 63) & ~(uintptr_t)63);
+  adam_sched_kernel<<<1, 32, 0, ctx->stream>>>(s->lr, s->b1, s->b2, s->eps, s->wd, s->clip,
+                                               s->total_steps, t_dev, hdev);
+  FCU_CHECK_LAUNCH();
+  rc = sumsq_impl(ctx, g, n, ss, 0);
+  if (rc) return rc;
+  return update_impl(ctx, p, g, m, v, n, nullptr, ss, info_dev, (__nv_bfloat16 *)p_bf16, hdev);
 }
 
 }  // extern "C"

@@ -48,6 +48,12 @@ class AdamHyper(C.Structure):
                 ("bc1", C.c_double), ("bc2", C.c_double)]
 
 
+class AdamSched(C.Structure):
+    _fields_ = [("lr", C.c_double), ("b1", C.c_double), ("b2", C.c_double),
+                ("eps", C.c_double), ("wd", C.c_double), ("clip", C.c_double),
+                ("total_steps", C.c_double)]
+
+
 _P = C.c_void_p
 _I64 = C.c_int64
 _INT = C.c_int
@@ -104,6 +110,7 @@ _SIGS = {
     "fcu_attn_fwd_bf16": (_INT, [_P, _P, _I64, _INT, _INT, _INT, _INT, _INT, _P, _P]),
     "fcu_attn_bwd_bf16": (_INT, [_P, _P, _P, _I64, _P, _P, _INT, _INT, _INT, _INT, _INT, _D, _P]),
     "fcu_adam_step_shadow": (_INT, [_P, _P, _P, _P, _P, _I64, C.POINTER(AdamHyper), _P, _P, _P]),
+    "fcu_adam_step_sched": (_INT, [_P, _P, _P, _P, _P, _I64, C.POINTER(AdamSched), _P, _P, _P]),
     "fcu_to_bf16": (_INT, [_P, _P, _I64, _P]),
     "fcu_scale_bf16_dev": (_INT, [_P, _P, _I64, _P]),
     "fcu_rng_init": (None, [C.POINTER(RngState), C.c_uint32]),

@@ -288,10 +288,39 @@ class Adam:
         return AdamHyper(lr, self.b1, self.b2, self.eps, self.wd, self.clip,
                          1 - math.pow(self.b1, self.t), 1 - math.pow(self.b2, self.t))
 
+    def step_device(self) -> torch.Tensor:
+        """Adam.step with the step counter and the lr schedule on the device
+        (fcu_adam_step_sched): nothing in it depends on host values that
+        change between steps, so it can be captured in a CUDA graph and
+        replayed.  Needs the flat parameter layout (TrainableTransformer).
+        Returns the device tensor {gnorm, scale, lr} of this step."""
+        if self._flat is None:
+            raise ValueError("step_device needs parameters that share one flat buffer")
+        from ._lib import AdamSched
+        pf, gf = self._flat
+        if getattr(self, "_t_dev", None) is None:
+            self._t_dev = torch.full((1,), self.t, dtype=torch.int32, device=pf.device)
+            self._info3 = torch.zeros(3, dtype=torch.float64, device=pf.device)
+            self._sched = AdamSched(self.lr, self.b1, self.b2, self.eps, self.wd, self.clip,
+                                    float(self.total))
+        for p in self.p:
+            if p._gzero:
+                p.grad  # noqa: B018  (property zero-fills)
+        owner = _SHADOWS.get(pf.data_ptr())
+        shadow = (owner.flat_params_bf16 if owner is not None
+                  and getattr(owner, "flat_params_bf16", None) is not None else None)
+        call("fcu_adam_step_sched", ctx().handle, ptr(pf), ptr(gf), ptr(self.m_flat),
+             ptr(self.v_flat), pf.numel(), self._sched, ptr(self._t_dev), ptr(self._info3),
+             ptr(shadow))
+        self.t += 1
+        return self._info3
+
     def step(self, sumsq_dev: torch.Tensor | None = None) -> AdamInfo:
         """One step.  `sumsq_dev` (device double [1]) overrides the local sum
         of squared gradients, e.g. after a data-parallel all-reduce."""
         self.t += 1
+        if getattr(self, "_t_dev", None) is not None:
+            self._t_dev.fill_(self.t)          # keep the device counter in step
         h = self.hyper()
         c = ctx()
         info = self._info

@@ -280,6 +280,21 @@ int fcu_adam_step_sumsq(fcu_ctx *ctx, float *p, const float *g, float *m, float 
 /* sumsq_dev[0] (+)= sum g[i]^2 in double, deterministic. */
 int fcu_sumsq(fcu_ctx *ctx, const float *g, int64_t n, double *sumsq_dev, int accumulate);
 
+/* The constants of one Adam optimizer (the constructor options of
+ * src/L2/autograd.js:215). */
+typedef struct {
+  double lr, b1, b2, eps, wd, clip, total_steps;
+} fcu_adam_sched;
+
+/* One Adam.step whose step counter lives on the device: t = ++t_dev[0], then
+ * the cosine lr and bias corrections of step t are computed on the device
+ * (src/L2/autograd.js:222,229,237-238), so a captured CUDA graph of a whole
+ * training step replays with the right schedule.  Global-norm clipping as
+ * fcu_adam_step.  info_dev (3 doubles) receives {gnorm, scale, lr}; p_bf16
+ * may be NULL or the bf16 weight copy to refresh. */
+int fcu_adam_step_sched(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int64_t n,
+                        const fcu_adam_sched *s, int32_t *t_dev, double *info_dev, void *p_bf16);
+
 /* Adam (fcu_adam_step semantics) that also writes bf16(p) into p_bf16, the
  * weight copy the bf16 GEMMs read.  sumsq_dev may be NULL (computed here). */
 int fcu_adam_step_shadow(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int64_t n,
