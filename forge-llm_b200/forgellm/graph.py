@@ -24,8 +24,7 @@ from . import tensor as TS
 
 
 class CapturedStep:
-    def __init__(self, model, opt, B: int, T: int, dp=None, warmup: int = 2,
-                 time_gemms: bool = False):
+    def __init__(self, model, opt, B: int, T: int, dp=None, warmup: int = 2):
         if not model._use_fused():
             raise ValueError("CapturedStep needs the fused bf16 path (precision bf16, supported shapes)")
         if opt._flat is None:
@@ -43,16 +42,15 @@ class CapturedStep:
                 self._body()
         torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
-        self.gemm_events = [] if time_gemms else None
         self.graph = torch.cuda.CUDAGraph()
-        TS.GEMM_TIMER = self.gemm_events
         from ._lib import lib
         n0 = lib().fcu_launch_count()
+        saved_timer, TS.GEMM_TIMER = TS.GEMM_TIMER, None   # no host events inside the graph
         try:
             with torch.cuda.graph(self.graph):
                 self.loss, self.info = self._body()
         finally:
-            TS.GEMM_TIMER = None
+            TS.GEMM_TIMER = saved_timer
         self.launches_per_step = int(lib().fcu_launch_count() - n0)   # this library's kernels
         for dst, src in zip((model.flat_params, opt.m_flat, opt.v_flat), saved):
             dst.copy_(src)
@@ -80,12 +78,3 @@ class CapturedStep:
         self.graph.replay()
         self.opt.t += 1
         return self.loss
-
-    def gemm_time_ms(self):
-        """(GEMM FLOPs, GEMM milliseconds) of the most recent replay, from the
-        CUDA events captured around every GEMM (time_gemms=True)."""
-        if not self.gemm_events:
-            return None
-        flops = sum(f for f, _, _ in self.gemm_events)
-        ms = sum(a.elapsed_time(b) for _, a, b in self.gemm_events)
-        return flops, ms
