@@ -159,8 +159,9 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--precision", default=os.environ.get("FORGECU_PRECISION", "fp32"),
-                    choices=["fp32", "tf32x3", "bf16"])
+    ap.add_argument("--precision", default=os.environ.get("FORGECU_PRECISION", "bf16"),
+                    choices=["fp32", "tf32x3", "bf16"],
+                    help="bf16: tensor-core fused step (default); fp32: CUDA-core parity mode")
     ap.add_argument("--batch", type=int, default=GLOBAL_BATCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true",
@@ -180,7 +181,7 @@ def main():
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     import forgellm as F
     from forgellm import autograd as AD
@@ -332,6 +333,14 @@ def main():
                                     "sample": "1 sequence x 16 tokens of the config-5 model, "
                                               f"fwd+bwd+Adam over all 100M params ({sec:.1f} s)"}
         print(json.dumps(line), flush=True)
+    # A CUDA graph that holds NCCL calls must be released before the process
+    # group is destroyed, or the exit waits on it forever.
+    torch.cuda.synchronize()
+    if cs is not None:
+        cs.graph.reset()
+        del cs
+    import gc
+    gc.collect()
     if dp is not None:
         dp.detach()
     if world > 1:
