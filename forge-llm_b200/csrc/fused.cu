@@ -139,13 +139,22 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_bwd_fused_kernel(
   }
 }
 
+// out[c] (+)= sum_b part[b][c]: a (32 x 8) block per 32 columns, each row of
+// threads summing every 8th partial, then a fixed-order sum of the 8.
 __global__ void colsum_kernel(const float *__restrict__ part, int nblk, int64_t D,
                               float *__restrict__ out, int acc) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < D;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    float s = 0.f;
-    for (int b = 0; b < nblk; b++) s += part[(int64_t)b * D + i];
-    out[i] = acc ? out[i] + s : s;
+  __shared__ float sh[8][33];
+  const int64_t c = (int64_t)blockIdx.x * 32 + threadIdx.x;
+  float s = 0.f;
+  if (c < D)
+    for (int b = threadIdx.y; b < nblk; b += 8) s += part[(int64_t)b * D + c];
+  sh[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && c < D) {
+    float t = 0.f;
+#pragma unroll
+    for (int y = 0; y < 8; y++) t += sh[y][threadIdx.x];
+    out[c] = acc ? out[c] + t : t;
   }
 }
 
@@ -238,8 +247,8 @@ int rms_bwd_launch(fcu_ctx *ctx, const float *dY, const float *X, const float *w
   rmsnorm_bwd_fused_kernel<NC><<<(int)nblk, kThreads, smem, ctx->stream>>>(
       dY, X, w, inv, T, D, rpb, dX, acc_dx, dXb, (float *)scr);
   FCU_CHECK_LAUNCH();
-  colsum_kernel<<<grid_for(D, kThreads, 4096), kThreads, 0, ctx->stream>>>((float *)scr, (int)nblk,
-                                                                           D, dw, acc_dw);
+  colsum_kernel<<<(unsigned)((D + 31) / 32), dim3(32, 8), 0, ctx->stream>>>((float *)scr, (int)nblk,
+                                                                            D, dw, acc_dw);
   FCU_CHECK_LAUNCH();
   return FCU_OK;
 }

@@ -58,6 +58,8 @@ struct TcParams {
   __nv_bfloat16 *Cb;       // kOutBF16* (row stride ldc)
   const float2 *rope;      // [rope_T][head_dim/2] (cos, sin)
   int rope_T, rope_cols, head_dim;
+  int splits;              // K slices per output tile (1 = no split)
+  float *ws;               // split-K partial tiles [splits][M][ldc]
 };
 
 // ------------------------------------------------------------------ PTX helpers
@@ -307,18 +309,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // Work units: (output tile, K slice).  With split-K (p.splits > 1) unit u
+  // covers k-blocks [kb0, kb1) of tile u / splits; its partial tile goes to
+  // the workspace and a reduction kernel adds the slices in order.
   const int num_tiles = p.tiles_m * p.tiles_n;
   const int nk = (p.K + BK - 1) / BK;
+  const int units = num_tiles * p.splits;
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer
     int it = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const int t = u / p.splits, sp = u - t * p.splits;
+      const int kb0 = (int)((int64_t)nk * sp / p.splits);
+      const int kb1 = (int)((int64_t)nk * (sp + 1) / p.splits);
       int tm, tn;
       tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
       const int m0 = tm * BM, n0 = tn * BN;
-      for (int kb = 0; kb < nk; kb++, it++) {
+      for (int kb = kb0; kb < kb1; kb++, it++) {
         const int s = it % STAGES;
         const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
@@ -355,7 +364,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t idesc = instr_desc_bf16(p.a_mn, p.b_mn);
     int it = 0, ti = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ti++) {
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ti++) {
+      const int sp = u % p.splits;
+      const int kb0 = (int)((int64_t)nk * sp / p.splits);
+      const int kb1 = (int)((int64_t)nk * (sp + 1) / p.splits);
       const int acc = ti & 1;
       const uint32_t aph = (uint32_t)(ti >> 1) & 1u;
       if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag)) {
@@ -364,7 +376,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-      for (int kb = 0; kb < nk; kb++, it++) {
+      for (int kb = kb0; kb < kb1; kb++, it++) {
         const int s = it % STAGES;
         const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
         if (!mbar_wait(&full[s], ph, abort_flag)) {
@@ -377,7 +389,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int k = 0; k < BK / UMMA_K; k++)
           umma_bf16(d_tmem, operand_desc(a, k, p.a_mn), operand_desc(b, k, p.b_mn), idesc,
-                    (kb | k) != 0 ? 1u : 0u);
+                    (kb != kb0 || k != 0) ? 1u : 0u);
         umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
       }
       if (!ok) break;
@@ -395,7 +407,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int row = q * 32 + lane;
     int ti = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ti++) {
+    TcParams part = p;   // split-K: plain fp32 stores of this slice's partial tile
+    part.mode = kOutF32;
+    part.beta = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ti++) {
+      const int t = u / p.splits, sp = u - t * p.splits;
       int tm, tn;
       tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
       const int acc = ti & 1;
@@ -407,11 +423,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const int64_t gm = (int64_t)tm * BM + row;
       const int n0 = tn * BN;
+      if (p.splits > 1) part.C = p.ws + (int64_t)sp * p.M * p.ldc;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; c++) {
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
-        if (gm < p.M) store_chunk(p, gm, n0 + c * 32, r);
+        if (gm < p.M) store_chunk(p.splits > 1 ? part : p, gm, n0 + c * 32, r);
       }
       tc_fence_before();
       __syncwarp();
@@ -515,6 +532,60 @@ int workspace(fcu_ctx *ctx, size_t bytes, void **out, int **err) {
   return FCU_OK;
 }
 
+// Split-K partial tiles (grown on demand, never shrunk).
+int partials(fcu_ctx *ctx, size_t bytes, void **out) {
+  struct Buf {
+    void *p = nullptr;
+    size_t n = 0;
+  };
+  static thread_local Buf bufs[64];
+  Buf &b = bufs[ctx->device & 63];
+  if (bytes > b.n) {
+    if (b.p) {
+      FCU_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
+      FCU_CHECK_CUDA(cudaFree(b.p));
+      b.p = nullptr;
+      b.n = 0;
+    }
+    FCU_CHECK_CUDA(cudaMalloc(&b.p, bytes));
+    b.n = bytes;
+  }
+  *out = b.p;
+  return FCU_OK;
+}
+
+// C = (beta ? C : 0) + sum over slices s = 0..splits-1 of ws[s] (fixed order).
+__global__ void splitk_reduce_kernel(const float *__restrict__ ws, int splits, int64_t mn,
+                                     float *__restrict__ C, int beta) {
+  const int64_t n4 = (mn & 3) == 0 && (((uintptr_t)C & 15) == 0) ? mn >> 2 : 0;
+  const float4 *w4 = reinterpret_cast<const float4 *>(ws);
+  float4 *c4 = reinterpret_cast<float4 *>(C);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    float4 s = w4[i];
+    for (int k = 1; k < splits; k++) {
+      const float4 v = w4[(int64_t)k * n4 + i];
+      s.x += v.x;
+      s.y += v.y;
+      s.z += v.z;
+      s.w += v.w;
+    }
+    if (beta) {
+      const float4 v = c4[i];
+      s.x += v.x;
+      s.y += v.y;
+      s.z += v.z;
+      s.w += v.w;
+    }
+    c4[i] = s;
+  }
+  for (int64_t i = (n4 << 2) + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < mn; i += stride) {
+    float s = ws[i];
+    for (int k = 1; k < splits; k++) s += ws[(int64_t)k * mn + i];
+    C[i] = beta ? C[i] + s : s;
+  }
+}
+
 int convert(fcu_ctx *ctx, const float *x, int64_t n, __nv_bfloat16 *y) {
   FCU_REQUIRE(((uintptr_t)x & 15) == 0, "tensor-core path: fp32 operand must be 16-byte aligned");
   int64_t work = (n >> 2) > 0 ? (n >> 2) : 1;
@@ -595,16 +666,45 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
   p.tiles_m = (int)((M + BM - 1) / BM);
   p.tiles_n = (int)((N + BN - 1) / BN);
   p.err = err;
+  // Split-K when an fp32 product has too few output tiles to fill the GPU
+  // twice over (the weight gradients, whose contraction runs over every
+  // token): each slice keeps at least 4 k-blocks.
+  p.splits = 1;
+  p.ws = nullptr;
+  {
+    const int tiles = p.tiles_m * p.tiles_n;
+    const int nk = (int)((K + BK - 1) / BK);
+    if (o.mode == kOutF32 && tiles < 2 * ctx->num_sms) {
+      int s = (2 * ctx->num_sms + tiles - 1) / tiles;
+      s = s > 16 ? 16 : s;
+      s = s > nk / 4 ? nk / 4 : s;
+      if (s >= 2) {
+        void *w = nullptr;
+        rc = partials(ctx, sizeof(float) * (size_t)s * (size_t)M * (size_t)N, &w);
+        if (rc) return rc;
+        p.splits = s;
+        p.ws = (float *)w;
+      }
+    }
+  }
   static bool attr_set = false;
   if (!attr_set) {
     FCU_CHECK_CUDA(cudaFuncSetAttribute(gemm_bf16_tc_kernel,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
     attr_set = true;
   }
-  const int tiles = p.tiles_m * p.tiles_n;
-  const int grid = tiles < ctx->num_sms ? tiles : ctx->num_sms;
+  const int units = p.tiles_m * p.tiles_n * p.splits;
+  const int grid = units < ctx->num_sms ? units : ctx->num_sms;
   gemm_bf16_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, ctx->stream>>>(ta, tb, p);
   FCU_CHECK_LAUNCH();
+  if (p.splits > 1) {
+    const int64_t mn = M * N;
+    int blocks = (int)((mn / 4 + 255) / 256);
+    if (blocks > 8 * ctx->num_sms) blocks = 8 * ctx->num_sms;
+    if (blocks < 1) blocks = 1;
+    splitk_reduce_kernel<<<blocks, 256, 0, ctx->stream>>>(p.ws, p.splits, mn, o.C, o.beta);
+    FCU_CHECK_LAUNCH();
+  }
   return FCU_OK;
 }
 
