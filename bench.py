@@ -153,6 +153,46 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_micro_gemm(args):
+    """One tcgen05 contraction of the train step, timed alone (profiling aid):
+    `--micro gemm --shape M,N,K --op fwd|dx|dw`.  Prints TFLOP/s."""
+    import torch
+    import ctypes
+    import forgellm as F
+    from forgellm import autograd as AD
+    from forgellm._lib import GemmOut, OUT_F32, call
+    F.set_precision("bf16")
+    M, N, K = (int(x) for x in args.shape.split(","))
+    op = {"fwd": 0, "dx": 1, "dw": 2}[args.op]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    na = M * K if op != 2 else K * M
+    nb = N * K if op == 0 else K * N
+    A = torch.randn(na, device="cuda", generator=g).to(torch.bfloat16)
+    Bm = torch.randn(nb, device="cuda", generator=g).to(torch.bfloat16)
+    C = torch.empty(M * N, device="cuda")
+    o = GemmOut(OUT_F32, C.data_ptr(), 0, None, 0, 0, 0, 0.0)
+    h = AD.ctx().handle
+
+    def run():
+        call("fcu_gemm_bf16", h, op, A.data_ptr(), Bm.data_ptr(), M, N, K, ctypes.byref(o))
+
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+    pk, kind = peaks()
+    print(json.dumps({"micro": "gemm_bf16_tc", "op": args.op, "M": M, "N": N, "K": K,
+                      "ms": ms, "tflops": tf, "frac_of_burst_peak": tf / pk["bf16_tflops"],
+                      "peak_kind": kind}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -166,7 +206,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true",
                     help="launch the step op by op instead of replaying its CUDA graph")
+    ap.add_argument("--micro", choices=["gemm"], help="time one kernel alone (profiling)")
+    ap.add_argument("--shape", default="8192,2048,768")
+    ap.add_argument("--op", default="fwd", choices=["fwd", "dx", "dw"])
     args = ap.parse_args()
+    if args.micro == "gemm":
+        run_micro_gemm(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

@@ -60,6 +60,12 @@ struct Args {
   int T, nH, nKV;
   float scale;
   int acc;                              // fp32 outputs: accumulate
+  // dK/dV with one CTA per (key tile, q head) instead of per (key tile, kv
+  // head): each writes fp32 partials pk/pv [group][B*T][nKV*D] that
+  // attn_kv_reduce_kernel sums over the group in order (small grids only).
+  int split_heads;
+  float *pk, *pv;
+  int64_t rows;                         // B*T
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -361,8 +367,11 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_dkdv_tc_kernel(Args A) {
   __nv_bfloat16 *sG[2] = {sV + 2 * Smem<D>::TILE, sV + 4 * Smem<D>::TILE};
   float *sL = reinterpret_cast<float *>(sV + 5 * Smem<D>::TILE);  // [2][kTile]
   float *sD = sL + 2 * kTile;                                     // [2][kTile]
-  const int kt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int kt = blockIdx.x, b = blockIdx.z;
   const int T = A.T, nH = A.nH, group = nH / A.nKV;
+  const int kvh = A.split_heads ? (int)blockIdx.y / group : (int)blockIdx.y;
+  const int h_begin = A.split_heads ? (int)blockIdx.y : kvh * group;
+  const int n_heads = A.split_heads ? 1 : group;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
   const int64_t base = (int64_t)b * T;
@@ -370,10 +379,10 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_dkdv_tc_kernel(Args A) {
   const float c = A.scale * kLog2e;
   const int ntiles = (T + kTile - 1) / kTile;
   const int per_head = ntiles - kt;          // query tiles at or after this key tile
-  const int n_iter = group * per_head;
+  const int n_iter = n_heads * per_head;
 
   auto load_q = [&](int it, int bi) {        // stage query tile `it` into buffer bi
-    const int h = kvh * group + it / per_head;
+    const int h = h_begin + it / per_head;
     const int q0 = (kt + it % per_head) * kTile;
     stage<D, TI>(sQ[bi], A.q, base, q0, T, h);
     stage<D, TI>(sG[bi], A.dO, base, q0, T, h);
@@ -435,8 +444,51 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_dkdv_tc_kernel(Args A) {
       __syncthreads();
     }
   }
+  if (A.split_heads) {
+    const int64_t kvD = (int64_t)A.nKV * D;
+    const int g = h_begin - kvh * group;
+    View<void> pk{A.pk + (int64_t)g * A.rows * kvD, kvD, 0};
+    View<void> pv{A.pv + (int64_t)g * A.rows * kvD, kvD, 0};
+    store_rows<D, float>(pk, dk, key, base, kvh, T, A.scale, 0, nullptr, t4);
+    store_rows<D, float>(pv, dv, key, base, kvh, T, 1.f, 0, nullptr, t4);
+    return;
+  }
   store_rows<D, TO>(A.dk, dk, key, base, kvh, T, A.scale, A.acc, A.rope, t4);
   store_rows<D, TO>(A.dv, dv, key, base, kvh, T, 1.f, A.acc, nullptr, t4);
+}
+
+// dK/dV of the head-split backward: sum the group's fp32 partials in order,
+// rotate dK back (R^T) and store bf16 into the dqkv buffer.  One thread per
+// (row, kv head, element pair).
+template <int D>
+__global__ void attn_kv_reduce_kernel(Args A, int group) {
+  const int64_t kvD = (int64_t)A.nKV * D;
+  const int64_t pairs = A.rows * (kvD / 2);
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < pairs;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = e / (kvD / 2);
+    const int64_t c = (e - row * (kvD / 2)) * 2;   // column within [0, kvD)
+    float k0 = 0.f, k1 = 0.f, v0 = 0.f, v1 = 0.f;
+    for (int g = 0; g < group; g++) {
+      const int64_t o = (int64_t)g * A.rows * kvD + row * kvD + c;
+      const float2 pk = *reinterpret_cast<const float2 *>(A.pk + o);
+      const float2 pv = *reinterpret_cast<const float2 *>(A.pv + o);
+      k0 += pk.x;
+      k1 += pk.y;
+      v0 += pv.x;
+      v1 += pv.y;
+    }
+    if (A.rope) {
+      const float2 cs = A.rope[(row % A.T) * (D / 2) + (c % D) / 2];
+      const float u = k0 * cs.x + k1 * cs.y, w = -k0 * cs.y + k1 * cs.x;
+      k0 = u;
+      k1 = w;
+    }
+    __nv_bfloat16 *dk = reinterpret_cast<__nv_bfloat16 *>(A.dk.p) + row * A.dk.ld + A.dk.col + c;
+    __nv_bfloat16 *dv = reinterpret_cast<__nv_bfloat16 *>(A.dv.p) + row * A.dv.ld + A.dv.col + c;
+    *reinterpret_cast<uint32_t *>(dk) = pack_bf16(k0, k1);
+    *reinterpret_cast<uint32_t *>(dv) = pack_bf16(v0, v1);
+  }
 }
 
 // ------------------------------------------------------------------ backward dQ
@@ -557,9 +609,16 @@ int bwd_launch(cudaStream_t st, const Args &a, int B) {
   if (smem_q > 48 * 1024)
     FCU_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<D, TI, TO>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_q));
-  dim3 gkv(div_up(a.T, kTile), a.nKV, B);
+  dim3 gkv(div_up(a.T, kTile), a.split_heads ? a.nH : a.nKV, B);
   attn_bwd_dkdv_tc_kernel<D, TI, TO><<<gkv, kThreads, smem_kv, st>>>(a);
   FCU_CHECK_LAUNCH();
+  if (a.split_heads) {
+    const int64_t pairs = a.rows * ((int64_t)a.nKV * D / 2);
+    int blocks = (int)((pairs + 255) / 256);
+    if (blocks > 65535) blocks = 65535;
+    attn_kv_reduce_kernel<D><<<blocks, 256, 0, st>>>(a, a.nH / a.nKV);
+    FCU_CHECK_LAUNCH();
+  }
   dim3 gq(div_up(a.T, kTile), a.nH, B);
   attn_bwd_dq_tc_kernel<D, TI, TO><<<gq, kThreads, smem_q, st>>>(a);
   FCU_CHECK_LAUNCH();
@@ -678,10 +737,22 @@ int fcu_attn_bwd_bf16(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_
                   (((uintptr_t)dO | (uintptr_t)qkv | (uintptr_t)O | (uintptr_t)dqkv) & 15) == 0,
               "fcu_attn_bwd_bf16: null or unaligned pointer");
   const int64_t qD = (int64_t)nH * dH, kvD = (int64_t)nKV * dH;
+  // Small grids (few sequences per GPU) balance the causal work better with
+  // one dK/dV CTA per q head and a reduction over each GQA group.
+  const int64_t kv_ctas = (int64_t)div_up(T, kTile) * nKV * B;
+  const int split = (nH > nKV && kv_ctas < 8 * (int64_t)ctx->num_sms) ? 1 : 0;
+  const size_t delta_bytes = (sizeof(float) * (size_t)B * nH * T + 255) & ~(size_t)255;
+  const size_t part_bytes = split ? sizeof(float) * (size_t)(nH / nKV) * B * T * kvD : 0;
   void *scr = nullptr;
-  int rc = ctx_scratch(ctx, sizeof(float) * (size_t)B * nH * T, &scr);
+  int rc = ctx_scratch(ctx, delta_bytes + 2 * part_bytes, &scr);
   if (rc) return rc;
   Args a{};
+  a.split_heads = split;
+  a.rows = (int64_t)B * T;
+  if (split) {
+    a.pk = (float *)((uint8_t *)scr + delta_bytes);
+    a.pv = (float *)((uint8_t *)scr + delta_bytes + part_bytes);
+  }
   a.q = {qkv, ld_qkv, 0};
   a.k = {qkv, ld_qkv, qD};
   a.v = {qkv, ld_qkv, qD + kvD};

@@ -32,7 +32,11 @@ class CapturedStep:
         self.model, self.opt, self.dp = model, opt, dp
         self.B, self.T = B, T
         dev = model.flat_params.device
-        self.batch = torch.zeros(B, T + 1, dtype=torch.int32, device=dev)
+        # warm up on ids spread like real batches (a constant batch would make
+        # every token share one embedding row and time a degenerate backward)
+        gen = torch.Generator(device=dev).manual_seed(0)
+        self.batch = torch.randint(0, model.cfg.vocabSize, (B, T + 1), dtype=torch.int32,
+                                   device=dev, generator=gen)
         saved = [t.clone() for t in (model.flat_params, opt.m_flat, opt.v_flat)]
         t0 = opt.t
         side = torch.cuda.Stream(device=dev)
