@@ -33,9 +33,7 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
 constexpr int NUM_THREADS = 192;
 constexpr uint32_t TMEM_COLS = 2 * BN;          // 512
 constexpr int GROUP_M = 16;                     // tile raster: GROUP_M m-blocks per n sweep
-constexpr size_t STAGE_TILE_BYTES = 4 * 32 * 33 * sizeof(float);  // epilogue transpose tiles
-constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + (size_t)STAGES * STAGE_BYTES + 256 +
-                              STAGE_TILE_BYTES;
+constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + (size_t)STAGES * STAGE_BYTES + 256;
 constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 2 GHz
 
 // Epilogue modes (what the epilogue warps do with one fp32 accumulator row):
@@ -200,15 +198,48 @@ __device__ __forceinline__ uint32_t pack2_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t *>(&v);
 }
 
-// Writes one warp's 32 x 32 block of the output: rows gm0 .. gm0+31 (row
-// gm0+lane arrives in this lane's v[]), columns nb .. nb+31.  RoPE is applied
-// by the row owner (it holds both members of each pair); the block is then
-// transposed through a padded shared-memory tile so that every global access
-// covers one contiguous row segment (128 B of fp32 or 2 x 64 B of bf16).
-__device__ __forceinline__ void store_block(const TcParams &p, int64_t gm0, int nb, float (&v)[32],
-                                            float *stage, int lane) {
+// Writes columns [nb, nb+32) of output row gm from one TMEM load.
+__device__ __forceinline__ void store_chunk(const TcParams &p, int64_t gm, int nb,
+                                            const uint32_t (&r)[32]) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+  const bool full = nb + 32 <= p.N;
+  if (p.mode == kOutF32 || p.mode == kOutF32Res) {
+    float *crow = p.C + gm * p.ldc;
+    const float *rrow = p.mode == kOutF32Res ? p.R + gm * p.ldc : nullptr;
+    const bool vec = full && ((p.ldc & 3) == 0) && (((uintptr_t)p.C & 15) == 0) &&
+                     (rrow == nullptr || ((uintptr_t)p.R & 15) == 0);
+    if (vec) {
+      float4 *dst = reinterpret_cast<float4 *>(crow + nb);
+      const float4 *src = rrow ? reinterpret_cast<const float4 *>(rrow + nb) : nullptr;
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        float4 o = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        if (src || p.beta) {
+          const float4 a = src ? src[i] : dst[i];
+          o.x += a.x;
+          o.y += a.y;
+          o.z += a.z;
+          o.w += a.w;
+        }
+        dst[i] = o;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; i++) {
+        if (nb + i < p.N) {
+          float o = v[i];
+          if (rrow) o += rrow[nb + i];
+          else if (p.beta) o += crow[nb + i];
+          crow[nb + i] = o;
+        }
+      }
+    }
+    return;
+  }
   if (p.mode == kOutBF16Rope && nb < p.rope_cols) {
-    const int64_t pos = (gm0 + lane) % p.rope_T;
+    const int64_t pos = gm % p.rope_T;
     const int half = p.head_dim >> 1;
 #pragma unroll
     for (int i = 0; i < 16; i++) {
@@ -219,46 +250,23 @@ __device__ __forceinline__ void store_block(const TcParams &p, int64_t gm0, int 
       v[2 * i + 1] = a * cs.y + b * cs.x;
     }
   }
-  __syncwarp();
+  __nv_bfloat16 *brow = p.Cb + gm * p.ldc;
+  if (full && ((p.ldc & 7) == 0) && (((uintptr_t)p.Cb & 15) == 0)) {
+    uint4 *dst = reinterpret_cast<uint4 *>(brow + nb);
 #pragma unroll
-  for (int i = 0; i < 32; i++) stage[lane * 33 + i] = v[i];
-  __syncwarp();
-  if (p.mode == kOutF32 || p.mode == kOutF32Res) {
-    const int col = nb + lane;
-    const bool res = p.mode == kOutF32Res;
-#pragma unroll 4
-    for (int r = 0; r < 32; r++) {
-      const int64_t gm = gm0 + r;
-      if (gm >= p.M) break;
-      if (col < p.N) {
-        const int64_t off = gm * p.ldc + col;
-        float o = stage[r * 33 + lane];
-        if (res) o += p.R[off];
-        else if (p.beta) o += p.C[off];
-        p.C[off] = o;
-      }
+    for (int i = 0; i < 4; i++) {
+      uint4 o;
+      o.x = pack2_bf16(v[8 * i], v[8 * i + 1]);
+      o.y = pack2_bf16(v[8 * i + 2], v[8 * i + 3]);
+      o.z = pack2_bf16(v[8 * i + 4], v[8 * i + 5]);
+      o.w = pack2_bf16(v[8 * i + 6], v[8 * i + 7]);
+      dst[i] = o;
     }
   } else {
-    const int sub = lane >> 4, cp = (lane & 15) * 2;
-    const bool pairs = (p.ldc & 1) == 0 && (((uintptr_t)p.Cb & 3) == 0);
-#pragma unroll 4
-    for (int r = 0; r < 32; r += 2) {
-      const int rr = r + sub;
-      const int64_t gm = gm0 + rr;
-      const int col = nb + cp;
-      if (gm < p.M && col < p.N) {
-        const float a = stage[rr * 33 + cp], b = stage[rr * 33 + cp + 1];
-        __nv_bfloat16 *dst = p.Cb + gm * p.ldc + col;
-        if (pairs && col + 1 < p.N) {
-          *reinterpret_cast<uint32_t *>(dst) = pack2_bf16(a, b);
-        } else {
-          dst[0] = __float2bfloat16_rn(a);
-          if (col + 1 < p.N) dst[1] = __float2bfloat16_rn(b);
-        }
-      }
-    }
+#pragma unroll
+    for (int i = 0; i < 32; i++)
+      if (nb + i < p.N) brow[nb + i] = __float2bfloat16_rn(v[i]);
   }
-  __syncwarp();  // the stage tile is rewritten by the next block
 }
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -275,7 +283,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t *mma_done = tempty + 2;    // [1]
   uint32_t *tmem_slot = (uint32_t *)(mma_done + 1);
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
-  float *stage_base = (float *)(sB + STAGES * B_BYTES + 256);  // [4 warps][32][33]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -417,15 +424,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int64_t gm = (int64_t)tm * BM + row;
       const int n0 = tn * BN;
       if (p.splits > 1) part.C = p.ws + (int64_t)sp * p.M * p.ldc;
-      float *stage = stage_base + (warp - 2) * 32 * 33;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; c++) {
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
-        store_block(p.splits > 1 ? part : p, gm - lane, n0 + c * 32, v, stage, lane);
+        if (gm < p.M) store_chunk(p.splits > 1 ? part : p, gm, n0 + c * 32, r);
       }
       tc_fence_before();
       __syncwarp();
