@@ -554,35 +554,41 @@ int partials(fcu_ctx *ctx, size_t bytes, void **out) {
   return FCU_OK;
 }
 
-// C = (beta ? C : 0) + sum over slices s = 0..splits-1 of ws[s] (fixed order).
-__global__ void splitk_reduce_kernel(const float *__restrict__ ws, int splits, int64_t mn,
-                                     float *__restrict__ C, int beta) {
-  const int64_t n4 = (mn & 3) == 0 && (((uintptr_t)C & 15) == 0) ? mn >> 2 : 0;
-  const float4 *w4 = reinterpret_cast<const float4 *>(ws);
-  float4 *c4 = reinterpret_cast<float4 *>(C);
+// Split-K epilogue: out = mode(sum over slices s = 0..splits-1 of ws[s]),
+// summed in slice order (deterministic), for every output mode of the GEMM
+// epilogue.  One thread per pair of adjacent columns (RoPE rotates pairs).
+__global__ void splitk_reduce_kernel(TcParams p) {
+  const int64_t hp = (p.N + 1) / 2;  // column pairs per row
+  const int64_t pairs = (int64_t)p.M * hp, mn = (int64_t)p.M * p.N;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
-    float4 s = w4[i];
-    for (int k = 1; k < splits; k++) {
-      const float4 v = w4[(int64_t)k * n4 + i];
-      s.x += v.x;
-      s.y += v.y;
-      s.z += v.z;
-      s.w += v.w;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < pairs; e += stride) {
+    const int64_t row = e / hp;
+    const int c = (int)(e - row * hp) * 2;
+    const bool two = c + 1 < p.N;
+    const int64_t o = row * p.ldc + c;
+    float s0 = 0.f, s1 = 0.f;
+    for (int k = 0; k < p.splits; k++) {
+      s0 += p.ws[(int64_t)k * mn + o];
+      if (two) s1 += p.ws[(int64_t)k * mn + o + 1];
     }
-    if (beta) {
-      const float4 v = c4[i];
-      s.x += v.x;
-      s.y += v.y;
-      s.z += v.z;
-      s.w += v.w;
+    if (p.mode == kOutF32 || p.mode == kOutF32Res) {
+      const float *add = p.mode == kOutF32Res ? p.R : (p.beta ? p.C : nullptr);
+      if (add) {
+        s0 += add[o];
+        if (two) s1 += add[o + 1];
+      }
+      p.C[o] = s0;
+      if (two) p.C[o + 1] = s1;
+    } else {
+      if (p.mode == kOutBF16Rope && c < p.rope_cols && two) {
+        const float2 cs = p.rope[(row % p.rope_T) * (p.head_dim >> 1) + ((c % p.head_dim) >> 1)];
+        const float a = s0, b = s1;
+        s0 = a * cs.x - b * cs.y;
+        s1 = a * cs.y + b * cs.x;
+      }
+      p.Cb[o] = __float2bfloat16_rn(s0);
+      if (two) p.Cb[o + 1] = __float2bfloat16_rn(s1);
     }
-    c4[i] = s;
-  }
-  for (int64_t i = (n4 << 2) + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < mn; i += stride) {
-    float s = ws[i];
-    for (int k = 1; k < splits; k++) s += ws[(int64_t)k * mn + i];
-    C[i] = beta ? C[i] + s : s;
   }
 }
 
@@ -666,18 +672,19 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
   p.tiles_m = (int)((M + BM - 1) / BM);
   p.tiles_n = (int)((N + BN - 1) / BN);
   p.err = err;
-  // Split-K when an fp32 product has too few output tiles to fill the GPU
-  // twice over (the weight gradients, whose contraction runs over every
-  // token): each slice keeps at least 4 k-blocks.
+  // Split-K when a product has too few output tiles to fill the GPU twice
+  // over and a long contraction (the weight gradients, whose contraction runs
+  // over every token; the LM-head input gradient): each slice keeps at least
+  // 16 k-blocks, so the partial-tile traffic stays small next to the MMAs.
   p.splits = 1;
   p.ws = nullptr;
   {
     const int tiles = p.tiles_m * p.tiles_n;
     const int nk = (int)((K + BK - 1) / BK);
-    if (o.mode == kOutF32 && tiles < 2 * ctx->num_sms) {
+    if (tiles < 2 * ctx->num_sms && nk >= 32) {
       int s = (2 * ctx->num_sms + tiles - 1) / tiles;
       s = s > 16 ? 16 : s;
-      s = s > nk / 4 ? nk / 4 : s;
+      s = s > nk / 16 ? nk / 16 : s;
       if (s >= 2) {
         void *w = nullptr;
         rc = partials(ctx, sizeof(float) * (size_t)s * (size_t)M * (size_t)N, &w);
@@ -698,11 +705,11 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
   gemm_bf16_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, ctx->stream>>>(ta, tb, p);
   FCU_CHECK_LAUNCH();
   if (p.splits > 1) {
-    const int64_t mn = M * N;
-    int blocks = (int)((mn / 4 + 255) / 256);
+    const int64_t pairs = M * ((N + 1) / 2);
+    int blocks = (int)((pairs + 255) / 256);
     if (blocks > 8 * ctx->num_sms) blocks = 8 * ctx->num_sms;
     if (blocks < 1) blocks = 1;
-    splitk_reduce_kernel<<<blocks, 256, 0, ctx->stream>>>(p.ws, p.splits, mn, o.C, o.beta);
+    splitk_reduce_kernel<<<blocks, 256, 0, ctx->stream>>>(p);
     FCU_CHECK_LAUNCH();
   }
   return FCU_OK;

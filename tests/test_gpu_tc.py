@@ -113,6 +113,59 @@ def test_tc_repeated_calls_are_deterministic():
     device_ok()
 
 
+# ------------------------------------------------------------------ fcu_gemm_bf16 output modes
+@pytest.mark.parametrize("op,M,N,K", [(0, 128, 256, 4096),     # 1 tile, K long: split-K
+                                      (0, 300, 520, 768),      # no split, ragged tiles
+                                      (2, 256, 128, 8192),     # dW layout, split-K
+                                      (1, 200, 256, 4096)])    # dX layout, split-K
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+def test_gemm_bf16_output_modes(op, M, N, K, mode):
+    """Every epilogue (fp32 / fp32 + residual / bf16 / bf16 + RoPE), with and
+    without split-K, against a float64 product of the same bf16 operands."""
+    import ctypes
+    from forgellm import _lib
+    from forgellm.autograd import ctx
+    g = torch.Generator(device="cuda").manual_seed(op * 100 + mode)
+    na = M * K if op != 2 else K * M
+    nb = N * K if op == 0 else K * N
+    A = torch.randn(na, device="cuda", generator=g).to(torch.bfloat16)
+    B = torch.randn(nb, device="cuda", generator=g).to(torch.bfloat16)
+    Ad, Bd = A.double().cpu(), B.double().cpu()
+    if op == 0:
+        ref = Ad.view(M, K) @ Bd.view(N, K).T
+    elif op == 1:
+        ref = Ad.view(M, K) @ Bd.view(K, N)
+    else:
+        ref = Ad.view(K, M).T @ Bd.view(K, N)
+    R = torch.randn(M * N, device="cuda", generator=g)
+    out = torch.zeros(M * N, device="cuda", dtype=torch.float32 if mode < 2 else torch.bfloat16)
+    T_rope, hd, rc = 64, 64, 128
+    o = _lib.GemmOut(mode, out.data_ptr(), 0, R.data_ptr() if mode == 1 else None,
+                     T_rope if mode == 3 else 0, rc if mode == 3 else 0, hd if mode == 3 else 0,
+                     10000.0 if mode == 3 else 0.0)
+    _lib.call("fcu_gemm_bf16", ctx().handle, op, A.data_ptr(), B.data_ptr(), M, N, K, ctypes.byref(o))
+    torch.cuda.synchronize()
+    device_ok()
+    want = ref.clone()
+    if mode == 1:
+        want += R.double().cpu().view(M, N)
+    if mode == 3:
+        import math
+        w = want.numpy()
+        for m in range(M):
+            pos = m % T_rope
+            for c in range(0, min(rc, N), 2):
+                i = (c % hd) // 2
+                ang = pos / math.pow(10000.0, 2 * i / hd)
+                cs, sn = math.cos(ang), math.sin(ang)
+                a, b = w[m, c], w[m, c + 1]
+                w[m, c], w[m, c + 1] = a * cs - b * sn, a * sn + b * cs
+        want = torch.from_numpy(w)
+    got = out.double().cpu().view(M, N)
+    tol = EXACT if mode < 2 else 5e-3          # bf16 outputs carry their own rounding
+    assert relf(want.numpy(), got.numpy()) <= tol
+
+
 # ------------------------------------------------------------------ attention (bf16 mode)
 ATTN_BF16_BOUND = 2e-2   # bf16 Q/K/V/P/dS operands, fp32 softmax and accumulation
 
