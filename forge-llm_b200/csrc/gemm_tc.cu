@@ -25,16 +25,25 @@
 namespace fcu {
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int BM = 128, BK = 64;
 constexpr int UMMA_K = 16;
 constexpr int A_BYTES = BM * BK * 2;            // 16 KB
-constexpr int B_BYTES = BN * BK * 2;            // 32 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
 constexpr int NUM_THREADS = 192;
-constexpr uint32_t TMEM_COLS = 2 * BN;          // 512
 constexpr int GROUP_M = 16;                     // tile raster: GROUP_M m-blocks per n sweep
-constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + (size_t)STAGES * STAGE_BYTES + 256;
 constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 2 GHz
+
+// Output tile width.  128 x 256 is the main tile; 128 x 128 doubles the tile
+// count of narrow products that would otherwise leave SMs idle in the last
+// wave (few tokens per GPU), at the same operand traffic per FLOP on A.
+template <int BN_>
+struct TileCfg {
+  static constexpr int BN = BN_;
+  static constexpr int STAGES = BN_ == 256 ? 4 : 6;
+  static constexpr int B_BYTES = BN_ * BK * 2;            // 32 / 16 KB
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 48 / 32 KB
+  static constexpr uint32_t TMEM_COLS = 2 * BN_;          // 512 / 256
+  static constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + (size_t)STAGES * STAGE_BYTES + 256;
+};
 
 // Epilogue modes (what the epilogue warps do with one fp32 accumulator row):
 //   kOutF32      C[m,n] = acc            (beta = 1: C += acc)
@@ -178,9 +187,9 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t tile, int k, int mn_ma
 
 // Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A/B bf16 (bits
 // 7-9 / 10-12 = 1), majors (bits 15/16), N>>3 (bits 17-22), M>>4 (bits 24-28).
-__device__ __forceinline__ uint32_t instr_desc_bf16(int a_mn, int b_mn) {
+__device__ __forceinline__ uint32_t instr_desc_bf16(int a_mn, int b_mn, int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
-         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &tm, int &tn) {
@@ -269,9 +278,15 @@ __device__ __forceinline__ void store_chunk(const TcParams &p, int64_t gm, int n
   }
 }
 
+template <int BN_>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, TcParams p) {
+  constexpr int BN = TileCfg<BN_>::BN;
+  constexpr int STAGES = TileCfg<BN_>::STAGES;
+  constexpr int B_BYTES = TileCfg<BN_>::B_BYTES;
+  constexpr int STAGE_BYTES = TileCfg<BN_>::STAGE_BYTES;
+  constexpr uint32_t TMEM_COLS = TileCfg<BN_>::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *sA = smem;
@@ -361,7 +376,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_wait(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u, abort_flag);
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer
-    const uint32_t idesc = instr_desc_bf16(p.a_mn, p.b_mn);
+    const uint32_t idesc = instr_desc_bf16(p.a_mn, p.b_mn, BN);
     int it = 0, ti = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ti++) {
@@ -634,12 +649,28 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
                  int64_t M, int64_t N, int64_t K, const TcOut &o, int *err) {
   int rc = get_encode();
   if (rc) return rc;
+  // Split-K when a product has too few output tiles to fill the GPU twice
+  // over and a long contraction (the weight gradients, whose contraction runs
+  // over every token; the LM-head input gradient): each slice keeps at least
+  // 16 k-blocks, so the partial-tile traffic stays small next to the MMAs.
+  // Otherwise a product that would leave SMs idle in its last wave takes the
+  // 128-wide tile (twice the tiles).
+  const int nk = (int)((K + BK - 1) / BK);
+  const int64_t tiles256 = ((M + BM - 1) / BM) * ((N + 255) / 256);
+  int splits = 1;
+  if (tiles256 < 2 * ctx->num_sms && nk >= 32) {
+    int s = (int)((2 * ctx->num_sms + tiles256 - 1) / tiles256);
+    s = s > 16 ? 16 : s;
+    s = s > nk / 16 ? nk / 16 : s;
+    if (s >= 2) splits = s;
+  }
+  const int bn = (splits == 1 && tiles256 < 2 * ctx->num_sms && N > 128) ? 128 : 256;
   CUtensorMap ta, tb;
   int a_mn = 0, b_mn = 0;
   switch (op) {
     case GemmOp::kFwd:
       rc = make_map(&ta, A, M, K, 64, BM);
-      if (!rc) rc = make_map(&tb, B, N, K, 64, BN);
+      if (!rc) rc = make_map(&tb, B, N, K, 64, (uint32_t)bn);
       break;
     case GemmOp::kDx:
       b_mn = 1;
@@ -670,39 +701,34 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
   p.a_mn = a_mn;
   p.b_mn = b_mn;
   p.tiles_m = (int)((M + BM - 1) / BM);
-  p.tiles_n = (int)((N + BN - 1) / BN);
+  p.tiles_n = (int)((N + bn - 1) / bn);
   p.err = err;
-  // Split-K when a product has too few output tiles to fill the GPU twice
-  // over and a long contraction (the weight gradients, whose contraction runs
-  // over every token; the LM-head input gradient): each slice keeps at least
-  // 16 k-blocks, so the partial-tile traffic stays small next to the MMAs.
-  p.splits = 1;
+  p.splits = splits;
   p.ws = nullptr;
-  {
-    const int tiles = p.tiles_m * p.tiles_n;
-    const int nk = (int)((K + BK - 1) / BK);
-    if (tiles < 2 * ctx->num_sms && nk >= 32) {
-      int s = (2 * ctx->num_sms + tiles - 1) / tiles;
-      s = s > 16 ? 16 : s;
-      s = s > nk / 16 ? nk / 16 : s;
-      if (s >= 2) {
-        void *w = nullptr;
-        rc = partials(ctx, sizeof(float) * (size_t)s * (size_t)M * (size_t)N, &w);
-        if (rc) return rc;
-        p.splits = s;
-        p.ws = (float *)w;
-      }
-    }
+  if (splits > 1) {
+    void *w = nullptr;
+    rc = partials(ctx, sizeof(float) * (size_t)splits * (size_t)M * (size_t)N, &w);
+    if (rc) return rc;
+    p.ws = (float *)w;
   }
-  static bool attr_set = false;
-  if (!attr_set) {
-    FCU_CHECK_CUDA(cudaFuncSetAttribute(gemm_bf16_tc_kernel,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
-    attr_set = true;
+  static bool attr_set[2] = {false, false};
+  if (!attr_set[bn == 128]) {
+    if (bn == 256)
+      FCU_CHECK_CUDA(cudaFuncSetAttribute(gemm_bf16_tc_kernel<256>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)TileCfg<256>::SMEM_BYTES));
+    else
+      FCU_CHECK_CUDA(cudaFuncSetAttribute(gemm_bf16_tc_kernel<128>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)TileCfg<128>::SMEM_BYTES));
+    attr_set[bn == 128] = true;
   }
   const int units = p.tiles_m * p.tiles_n * p.splits;
   const int grid = units < ctx->num_sms ? units : ctx->num_sms;
-  gemm_bf16_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, ctx->stream>>>(ta, tb, p);
+  if (bn == 256)
+    gemm_bf16_tc_kernel<256><<<grid, NUM_THREADS, TileCfg<256>::SMEM_BYTES, ctx->stream>>>(ta, tb, p);
+  else
+    gemm_bf16_tc_kernel<128><<<grid, NUM_THREADS, TileCfg<128>::SMEM_BYTES, ctx->stream>>>(ta, tb, p);
   FCU_CHECK_LAUNCH();
   if (p.splits > 1) {
     const int64_t pairs = M * ((N + 1) / 2);
