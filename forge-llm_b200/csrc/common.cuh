@@ -45,6 +45,11 @@ int attn_bwd_tc(cudaStream_t st, const float *dO, const float *Q, const float *K
                 const float *lse, const float *delta, int B, int T, int nH, int nKV, int dH,
                 float *dQ, float *dK, float *dV, int acc);
 
+// tcgen05 attention (attn_tmem.cu): head dim 64, bf16 qkv buffer.
+bool attn_tmem_supported(int dH);
+int attn_fwd_tmem(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, int nH, int nKV,
+                  void *O, float *lse);
+
 }  // namespace fcu
 
 #define FCU_CHECK_CUDA(expr)                                                  \

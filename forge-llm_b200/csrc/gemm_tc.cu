@@ -21,6 +21,7 @@
 #include <cudaTypedefs.h>
 
 #include "gemm.cuh"
+#include "tc_ptx.cuh"
 
 namespace fcu {
 namespace {
@@ -30,7 +31,6 @@ constexpr int UMMA_K = 16;
 constexpr int A_BYTES = BM * BK * 2;            // 16 KB
 constexpr int NUM_THREADS = 192;
 constexpr int GROUP_M = 16;                     // tile raster: GROUP_M m-blocks per n sweep
-constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 2 GHz
 
 // Output tile width.  128 x 256 is the main tile; 128 x 128 doubles the tile
 // count of narrow products that would otherwise leave SMs idle in the last
@@ -71,126 +71,7 @@ struct TcParams {
   float *ws;               // split-K partial tiles [splits][M][ldc]
 };
 
-// ------------------------------------------------------------------ PTX helpers
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: false if the phase did not complete within kWaitCycles or
-// another role of this CTA has already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) return false;
-  }
-}
-
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1,
-                                            uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-      "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                          uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32"
-      " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15,"
-      " %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31},"
-      " [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Shared-memory matrix descriptor (sm_100 "version 1" format), 128B swizzle:
-// bits 0-13 start>>4, 16-29 LBO>>4, 32-45 SBO>>4, 46-47 version=1,
-// 61-63 layout (2 = SWIZZLE_128B).
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
-  return d;
-}
-
-// Descriptor of the k-th 16-deep slice of a staged operand tile.
-//   K-major : rows of 64 elements (128 B), 8-row swizzle atoms 1024 B apart;
-//             the slice starts k*32 B into each row.
-//   MN-major: boxes of 64 (MN) x BK (K) elements, one 128-B row per k,
-//             box j at j*BK*128 B (LBO), 8-row K groups 1024 B apart (SBO);
-//             the slice starts 16 rows = 2048 B further.
-__device__ __forceinline__ uint64_t operand_desc(uint32_t tile, int k, int mn_major) {
-  if (!mn_major) return smem_desc(tile + (uint32_t)k * 32u, 16u, 1024u);
-  return smem_desc(tile + (uint32_t)k * 2048u, (uint32_t)BK * 128u, 1024u);
-}
-
-// Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A/B bf16 (bits
-// 7-9 / 10-12 = 1), majors (bits 15/16), N>>3 (bits 17-22), M>>4 (bits 24-28).
-__device__ __forceinline__ uint32_t instr_desc_bf16(int a_mn, int b_mn, int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
-         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-}
+using namespace tc;
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &tm, int &tn) {
   const int per_group = GROUP_M * tiles_n;
@@ -200,11 +81,6 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   const int r = t - g * per_group;
   tm = first + r % gm;
   tn = r / gm;
-}
-
-__device__ __forceinline__ uint32_t pack2_bf16(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t *>(&v);
 }
 
 // Writes columns [nb, nb+32) of output row gm from one TMEM load.
@@ -314,10 +190,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    tmem_alloc(tmem_slot, TMEM_COLS);
   }
   tc_fence_before();
   __syncthreads();
@@ -376,7 +249,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_wait(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u, abort_flag);
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer
-    const uint32_t idesc = instr_desc_bf16(p.a_mn, p.b_mn, BN);
+    const uint32_t idesc = instr_desc_bf16(p.a_mn, p.b_mn, BM, BN);
     int it = 0, ti = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ti++) {
@@ -403,7 +276,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t b = smem_u32(sB + s * B_BYTES);
 #pragma unroll
         for (int k = 0; k < BK / UMMA_K; k++)
-          umma_bf16(d_tmem, operand_desc(a, k, p.a_mn), operand_desc(b, k, p.b_mn), idesc,
+          umma_bf16(d_tmem, operand_desc(a, k, p.a_mn, BK), operand_desc(b, k, p.b_mn, BK), idesc,
                     (kb != kb0 || k != 0) ? 1u : 0u);
         umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
       }
@@ -431,7 +304,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
       const int acc = ti & 1;
       const uint32_t aph = (uint32_t)(ti >> 1) & 1u;
-      if (!mbar_wait(&tfull[acc], aph, abort_flag)) {
+      if (!warp_wait(&tfull[acc], aph, abort_flag)) {
         ok = false;
         break;
       }
@@ -458,8 +331,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(TMEM_COLS));
+    tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -484,7 +356,9 @@ __global__ void to_bf16_kernel(const float *__restrict__ x, int64_t n, __nv_bflo
 // ------------------------------------------------------------------ host side
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
-int get_encode() {
+}  // namespace
+
+int tc_get_encode() {
   if (g_encode) return FCU_OK;
   cudaDriverEntryPointQueryResult q;
   void *fn = nullptr;
@@ -497,12 +371,10 @@ int get_encode() {
   return FCU_OK;
 }
 
-// 2-D bf16 tensor map over a row-major [rows, cols] matrix with a
-// {box_cols, box_rows} box and 128-byte swizzle (box_cols * 2 == 128).
-int make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols, uint32_t box_cols,
-             uint32_t box_rows) {
+int tc_make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                uint64_t row_stride, uint32_t box_cols, uint32_t box_rows) {
   cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {cols * 2};
+  cuuint64_t strides[1] = {row_stride * 2};
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims,
@@ -510,12 +382,15 @@ int make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols, u
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
-    set_error("cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu box=%ux%u", (int)r,
-              (unsigned long long)rows, (unsigned long long)cols, box_cols, box_rows);
+    set_error("cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu stride=%llu box=%ux%u", (int)r,
+              (unsigned long long)rows, (unsigned long long)cols, (unsigned long long)row_stride,
+              box_cols, box_rows);
     return FCU_ERR_CUDA;
   }
   return FCU_OK;
 }
+
+namespace {
 
 struct Workspace {
   void *ptr = nullptr;
@@ -647,7 +522,7 @@ struct TcOut {
 // out[M,N] = A . B in the layouts of `op` (bf16 operands), written as `o` says.
 int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfloat16 *B,
                  int64_t M, int64_t N, int64_t K, const TcOut &o, int *err) {
-  int rc = get_encode();
+  int rc = tc_get_encode();
   if (rc) return rc;
   // Split-K when a product has too few output tiles to fill the GPU twice
   // over and a long contraction (the weight gradients, whose contraction runs
@@ -669,18 +544,18 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
   int a_mn = 0, b_mn = 0;
   switch (op) {
     case GemmOp::kFwd:
-      rc = make_map(&ta, A, M, K, 64, BM);
-      if (!rc) rc = make_map(&tb, B, N, K, 64, (uint32_t)bn);
+      rc = tc_make_map(&ta, A, M, K, K, 64, BM);
+      if (!rc) rc = tc_make_map(&tb, B, N, K, K, 64, (uint32_t)bn);
       break;
     case GemmOp::kDx:
       b_mn = 1;
-      rc = make_map(&ta, A, M, K, 64, BM);
-      if (!rc) rc = make_map(&tb, B, K, N, 64, BK);
+      rc = tc_make_map(&ta, A, M, K, K, 64, BM);
+      if (!rc) rc = tc_make_map(&tb, B, K, N, N, 64, BK);
       break;
     case GemmOp::kDw:
       a_mn = b_mn = 1;
-      rc = make_map(&ta, A, K, M, 64, BK);
-      if (!rc) rc = make_map(&tb, B, K, N, 64, BK);
+      rc = tc_make_map(&ta, A, K, M, M, 64, BK);
+      if (!rc) rc = tc_make_map(&tb, B, K, N, N, 64, BK);
       break;
   }
   if (rc) return rc;
@@ -869,6 +744,11 @@ extern "C" int fcu_gemm_bf16(fcu_ctx *ctx, int op, const void *A, const void *B,
 
 namespace fcu {
 
+int tc_error_word(fcu_ctx *ctx, int **err) {
+  void *ws = nullptr;
+  return workspace(ctx, 0, &ws, err);
+}
+
 int gemm_tc_error(fcu_ctx *ctx) {
   void *ws = nullptr;
   int *err = nullptr;
@@ -878,7 +758,7 @@ int gemm_tc_error(fcu_ctx *ctx) {
   FCU_CHECK_CUDA(cudaMemcpyAsync(&h, err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
   FCU_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
   if (h) {
-    set_error("tensor-core GEMM: a bounded wait ran out (role %d)", h);
+    set_error("tensor-core kernel: a bounded wait ran out (code %d)", h);
     return FCU_ERR_TIMEOUT;
   }
   return FCU_OK;

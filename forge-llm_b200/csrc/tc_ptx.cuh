@@ -1,0 +1,253 @@
+// PTX wrappers shared by the sm_100a tensor-core kernels (GEMM, attention):
+// mbarriers with bounded waits, 2-D TMA loads, tcgen05 MMA / commit / TMEM
+// loads and stores, and the shared-memory matrix descriptors for tiles that
+// TMA writes with the 128-byte swizzle.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace fcu {
+namespace tc {
+
+constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 2 GHz
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: false if the phase did not complete within kWaitCycles or
+// another role of this CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) return false;
+  }
+}
+
+// mbar_wait by all 32 lanes of a warp with one warp-uniform result, so a warp
+// that goes on to warp-collective tcgen05.ld / tcgen05.st never diverges
+// (those .sync.aligned instructions need every lane).
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+  const bool ok = mbar_wait(bar, parity, abort_flag);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Bounded wait that ignores the abort flag: for draining copies and MMAs this
+// CTA issued before it exits (they always complete; the bound is a backstop).
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity))
+    if (clock64() - t0 > kWaitCycles) return false;
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Generic-proxy shared-memory writes (st.shared) made visible to the async
+// proxy (tcgen05.mma operand reads, TMA).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot)),
+               "r"(cols));
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols));
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane (32x32b shape: warp
+// q of a warpgroup reads lanes 32q..32q+31).  The _nw form issues the load
+// only; tmem_wait_ld() completes every load issued before it.
+__device__ __forceinline__ void tmem_ld32_nw(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32"
+      " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15,"
+      " %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31},"
+      " [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  tmem_ld32_nw(taddr, r);
+  tmem_wait_ld();
+}
+
+// 64 consecutive fp32 columns of this thread's TMEM lane, waited for.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float *f) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32"
+      " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15,"
+      " %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31,"
+      " %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47,"
+      " %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63},"
+      " [%64];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=f"(f[0]), "=f"(f[1]), "=f"(f[2]), "=f"(f[3]), "=f"(f[4]), "=f"(f[5]), "=f"(f[6]),
+        "=f"(f[7]), "=f"(f[8]), "=f"(f[9]), "=f"(f[10]), "=f"(f[11]), "=f"(f[12]), "=f"(f[13]),
+        "=f"(f[14]), "=f"(f[15]), "=f"(f[16]), "=f"(f[17]), "=f"(f[18]), "=f"(f[19]),
+        "=f"(f[20]), "=f"(f[21]), "=f"(f[22]), "=f"(f[23]), "=f"(f[24]), "=f"(f[25]),
+        "=f"(f[26]), "=f"(f[27]), "=f"(f[28]), "=f"(f[29]), "=f"(f[30]), "=f"(f[31]),
+        "=f"(f[32]), "=f"(f[33]), "=f"(f[34]), "=f"(f[35]), "=f"(f[36]), "=f"(f[37]),
+        "=f"(f[38]), "=f"(f[39]), "=f"(f[40]), "=f"(f[41]), "=f"(f[42]), "=f"(f[43]),
+        "=f"(f[44]), "=f"(f[45]), "=f"(f[46]), "=f"(f[47]), "=f"(f[48]), "=f"(f[49]),
+        "=f"(f[50]), "=f"(f[51]), "=f"(f[52]), "=f"(f[53]), "=f"(f[54]), "=f"(f[55]),
+        "=f"(f[56]), "=f"(f[57]), "=f"(f[58]), "=f"(f[59]), "=f"(f[60]), "=f"(f[61]),
+        "=f"(f[62]), "=f"(f[63])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0],"
+      " {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16,"
+      " %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor (sm_100 "version 1" format), 128B swizzle:
+// bits 0-13 start>>4, 16-29 LBO>>4, 32-45 SBO>>4, 46-47 version=1,
+// 61-63 layout (2 = SWIZZLE_128B).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Descriptor of the k-th 16-deep slice of a staged operand tile whose K depth
+// is `kdepth` elements.
+//   K-major : rows of 64 elements (128 B), 8-row swizzle atoms 1024 B apart;
+//             the slice starts k*32 B into each row (k < 4: one 64-deep block).
+//   MN-major: boxes of 64 (MN) x kdepth (K) elements, one 128-B row per k,
+//             box j at j*kdepth*128 B (LBO), 8-row K groups 1024 B apart
+//             (SBO); the slice starts 16 rows = 2048 B further.
+__device__ __forceinline__ uint64_t operand_desc(uint32_t tile, int k, int mn_major, int kdepth) {
+  if (!mn_major) return smem_desc(tile + (uint32_t)k * 32u, 16u, 1024u);
+  return smem_desc(tile + (uint32_t)k * 2048u, (uint32_t)kdepth * 128u, 1024u);
+}
+
+// Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A/B bf16 (bits
+// 7-9 / 10-12 = 1), majors (bits 15/16), N>>3 (bits 17-22), M>>4 (bits 24-28).
+__device__ __forceinline__ uint32_t instr_desc_bf16(int a_mn, int b_mn, int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t pack2_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// Byte offset of the 16-byte chunk `c` (elements 8c..8c+7) of row `r` in a
+// K-major tile of 64-element rows written with the 128-byte swizzle (the
+// layout TMA produces and operand_desc describes).  The tile base must be
+// 1024-byte aligned.
+__device__ __forceinline__ uint32_t sw128_offset(int r, int c) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+}  // namespace tc
+
+// Host side (defined in gemm_tc.cu): the driver's tensor-map encoder and a
+// 2-D bf16 map over a row-major [rows, cols] matrix with row stride
+// `row_stride` elements, a {box_cols, box_rows} box and 128-byte swizzle.
+int tc_get_encode();
+// Device word the tensor-core kernels set when a bounded wait runs out
+// (read and reported by fcu_check_device_error).
+int tc_error_word(fcu_ctx *ctx, int **err);
+int tc_make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                uint64_t row_stride, uint32_t box_cols, uint32_t box_rows);
+
+}  // namespace fcu

@@ -202,3 +202,48 @@ def test_tc_attention_bf16_bound(B, T, nH, nKV, dH):
     }
     assert max(errs.values()) <= ATTN_BF16_BOUND, errs
     assert errs["O"] <= 1e-2, errs
+
+
+# ------------------------------------------------------------------ fcu_attn_fwd_bf16 (fused-path entry)
+def _attn_ref64(qkv, B, T, nH, nKV, dH):
+    """float64 causal GQA attention of the same bf16 q/k/v: (O [B*T, nH*dH], lse [B, nH, T])."""
+    x = qkv.double().view(B, T, -1)
+    q = x[..., :nH * dH].view(B, T, nH, dH).permute(0, 2, 1, 3)
+    k = x[..., nH * dH:(nH + nKV) * dH].view(B, T, nKV, dH).permute(0, 2, 1, 3)
+    v = x[..., (nH + nKV) * dH:(nH + 2 * nKV) * dH].view(B, T, nKV, dH).permute(0, 2, 1, 3)
+    g = nH // nKV
+    k, v = k.repeat_interleave(g, 1), v.repeat_interleave(g, 1)
+    s = q @ k.transpose(-1, -2) / dH ** 0.5
+    s = s.masked_fill(torch.triu(torch.ones(T, T, dtype=torch.bool, device=s.device), 1), float("-inf"))
+    lse = torch.logsumexp(s, -1)
+    o = torch.softmax(s, -1) @ v
+    return o.permute(0, 2, 1, 3).reshape(B * T, nH * dH), lse
+
+
+@pytest.mark.parametrize("B,T,nH,nKV,extra", [(1, 64, 2, 2, 0), (2, 130, 4, 1, 0), (3, 300, 6, 2, 64),
+                                              (2, 1024, 12, 4, 0), (1, 2048, 32, 8, 0)])
+def test_attn_fwd_bf16_entry(B, T, nH, nKV, extra):
+    """The fused path's attention forward (bf16 qkv in, bf16 O + fp32 lse out)
+    against float64 attention of the same bf16 inputs: only P's and O's bf16
+    rounding differ (relL2 <= 1e-2), the log-sum-exp to 1e-5."""
+    from forgellm import _lib
+    from forgellm.autograd import ctx
+    dH = 64
+    width = (nH + 2 * nKV) * dH
+    ld = width + extra
+    g = torch.Generator(device="cuda").manual_seed(B * 1000 + T)
+    qkv = (torch.randn(B * T, ld, device="cuda", generator=g) * 1.5).to(torch.bfloat16)
+    O = torch.full((B * T, nH * dH), float("nan"), device="cuda").to(torch.bfloat16)
+    lse = torch.full((B * nH * T,), float("nan"), device="cuda")
+    outs = []
+    for _ in range(2):
+        _lib.call("fcu_attn_fwd_bf16", ctx().handle, qkv.data_ptr(), ld, B, T, nH, nKV, dH,
+                  O.data_ptr(), lse.data_ptr())
+        torch.cuda.synchronize()
+        outs.append((O.clone(), lse.clone()))
+    device_ok()
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    o_ref, lse_ref = _attn_ref64(qkv[:, :width], B, T, nH, nKV, dH)
+    assert torch.isfinite(O.float()).all() and torch.isfinite(lse).all()
+    assert relf(o_ref.cpu().numpy(), O.double().cpu().numpy()) <= 1e-2
+    assert float((lse.double().view(B, nH, T) - lse_ref).abs().max()) <= 1e-4
