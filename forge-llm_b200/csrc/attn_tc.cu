@@ -738,6 +738,26 @@ int fcu_attn_bwd_bf16(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_
                   (((uintptr_t)dO | (uintptr_t)qkv | (uintptr_t)O | (uintptr_t)dqkv) & 15) == 0,
               "fcu_attn_bwd_bf16: null or unaligned pointer");
   const int64_t qD = (int64_t)nH * dH, kvD = (int64_t)nKV * dH;
+  if (attn_tmem_supported(dH)) {
+    // tcgen05 kernels, one CTA per SM: split dK/dV per q head when one CTA
+    // per kv head would leave the GPU with fewer than 4 CTAs per SM.
+    const int64_t ctas = (int64_t)div_up(T, 128) * nKV * B;
+    const int split = (nH > nKV && ctas < 4 * (int64_t)ctx->num_sms) ? 1 : 0;
+    const size_t delta_bytes = (sizeof(float) * (size_t)B * nH * T + 255) & ~(size_t)255;
+    const size_t part_bytes = split ? sizeof(float) * (size_t)(nH / nKV) * B * T * kvD : 0;
+    void *scr = nullptr;
+    int rc = ctx_scratch(ctx, delta_bytes + 2 * part_bytes, &scr);
+    if (rc) return rc;
+    const float2 *rope = nullptr;
+    if (rope_theta > 0) {
+      rc = rope_table_f32(ctx, T, dH, rope_theta, &rope);
+      if (rc) return rc;
+    }
+    float *pk = split ? (float *)((uint8_t *)scr + delta_bytes) : nullptr;
+    float *pv = split ? (float *)((uint8_t *)scr + delta_bytes + part_bytes) : nullptr;
+    return attn_bwd_tmem(ctx, dO, qkv, ld_qkv, O, lse, (float *)scr, B, T, nH, nKV, rope, dqkv, split,
+                         pk, pv);
+  }
   // Small grids (few sequences per GPU) balance the causal work better with
   // one dK/dV CTA per q head and a reduction over each GQA group.
   const int64_t kv_ctas = (int64_t)div_up(T, kTile) * nKV * B;

@@ -187,8 +187,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (!warp_wait(s_full, (uint32_t)j & 1u, abort_flag)) { ok = false; break; }
       tc_fence_after();
       float s[kBN];
-      tmem_ld64(tS + lane_addr, s);
-      tmem_ld64(tS + lane_addr + 64, s + 64);
+      tmem_ld128(tS + lane_addr, s);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free);
@@ -198,25 +197,33 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int c = 0; c < kBN; c++)
           if (c > lim) s[c] = -INFINITY;
       }
-      float mx = s[0];
+      // Row max and sum over 8 independent chains (short dependency chains).
+      float mx8[8];
 #pragma unroll
-      for (int c = 1; c < kBN; c++) mx = fmaxf(mx, s[c]);
+      for (int u = 0; u < 8; u++) mx8[u] = s[u];
+#pragma unroll
+      for (int c = 8; c < kBN; c++) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
+      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       mx *= p.scale_log2;
       float alpha = 1.f;
       bool rescale_o = false;
       if (mx > m + kRescaleLog2) {
-        alpha = exp2f(m - mx);                  // 0 on the first block
+        alpha = ex2_ftz(m - mx);                // 0 on the first block
         rescale_o = j > 0;
         m = mx;
       }
       const float neg_m = -m;
-      float rs = 0.f;
+      float rs8[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) rs8[u] = 0.f;
 #pragma unroll
       for (int c = 0; c < kBN; c++) {
-        const float e = exp2f(fmaf(s[c], p.scale_log2, neg_m));
+        const float e = ex2_ftz(fmaf(s[c], p.scale_log2, neg_m));
         s[c] = e;
-        rs += e;
+        rs8[c & 7] += e;
       }
+      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       l = l * alpha + rs;
       // PV_{j-1} must be done with P and O before P is overwritten / O rescaled.
       if (j > 0 && !warp_wait(o_done, (uint32_t)(j - 1) & 1u, abort_flag)) { ok = false; break; }
@@ -278,6 +285,583 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
+// ------------------------------------------------------------------ backward
+//
+// Two kernels, both deterministic (every gradient element is summed by one
+// CTA in a fixed order), with the softmax probabilities recomputed from the
+// forward's log-sum-exp:
+//
+// dK/dV, per CTA one 128-key tile of one kv head (or, head-split, of one q
+// head), looping over the query tiles at or after it of every q head of the
+// GQA group:
+//   warp 0      TMA: K, V once; a 3-deep ring of (Q, dO) tiles plus the
+//               tile's log-sum-exp and delta = rowsum(dO * O) rows
+//   warp 1      MMA (one thread):  S^T = K Q^T, dP^T = V dO^T (128x128x64,
+//               TMEM cols [0,128), [128,256)), then for the previous tile
+//               dV += P^T dO, dK += dS^T Q (128x64x128, cols [256,320),
+//               [320,384))
+//   warps 2..9  thread = key row, two warps per TMEM lane quarter splitting
+//               the 128 query columns: P^T = exp2(S^T c - L), dS^T =
+//               P^T (dP^T - delta), both to shared memory as bf16 K-major
+//               tiles; at the end dV, and dK * scale rotated back by RoPE.
+// dQ, per CTA one 128-row query tile of one q head, looping over the key
+// tiles at or before it: S = Q K^T, dP = dO V^T, dS = P (dP - delta),
+// dQ += dS K; at the end dQ * scale rotated back by RoPE.
+constexpr int kBwdThreads = 320;
+constexpr uint32_t kBwdTmemCols = 512;
+constexpr int kStages = 3;
+
+struct BwdParams {
+  int B, T, nH, nKV, n_t, group, split;
+  float scale, scale_log2;
+  const float *lse, *delta;         // [B][nH][T]
+  const float2 *rope;               // (cos, sin) [T][32], or null: no RoPE backward
+  __nv_bfloat16 *dqkv;              // dq | dk | dv columns, row stride ld
+  int64_t ld;
+  float *pk, *pv;                   // head-split: fp32 partials [group][B*T][nKV*64]
+  int *err;
+};
+
+// dK/dV kernel shared memory (byte offsets)
+constexpr int kKV_K = 0;
+constexpr int kKV_V = kKV_K + kTile;
+constexpr int kKV_Q = kKV_V + kTile;                  // kStages tiles
+constexpr int kKV_G = kKV_Q + kStages * kTile;        // kStages tiles (dO)
+constexpr int kKV_P = kKV_G + kStages * kTile;        // P^T, 2 halves
+constexpr int kKV_S = kKV_P + 2 * kTile;              // dS^T, 2 halves
+constexpr int kKV_L = kKV_S + 2 * kTile;              // [kStages][128] f32
+constexpr int kKV_D = kKV_L + kStages * 128 * 4;      // [kStages][128] f32
+constexpr int kKV_Bar = kKV_D + kStages * 128 * 4;
+constexpr int kKVSmem = kKV_Bar + 16 * 8 + 16;
+
+// dQ kernel shared memory
+constexpr int kQ_Q = 0;
+constexpr int kQ_G = kQ_Q + kTile;
+constexpr int kQ_K = kQ_G + kTile;                    // kStages tiles
+constexpr int kQ_V = kQ_K + kStages * kTile;          // kStages tiles
+constexpr int kQ_S = kQ_V + kStages * kTile;          // dS, 2 halves
+constexpr int kQ_Bar = kQ_S + 2 * kTile;
+constexpr int kQSmem = kQ_Bar + 16 * 8 + 16;
+
+// Stores 64 consecutive bf16 pairs' worth of packed values (one 128-byte
+// row half) into a K-major swizzled tile at row r.
+__device__ __forceinline__ void store_row_half(uint8_t *tile, int r, const uint32_t (&v)[32]) {
+#pragma unroll
+  for (int c8 = 0; c8 < 8; c8++)
+    *reinterpret_cast<uint4 *>(tile + sw128_offset(r, c8)) =
+        make_uint4(v[4 * c8], v[4 * c8 + 1], v[4 * c8 + 2], v[4 * c8 + 3]);
+}
+
+// Rotates interleaved pairs back by R^T: (x, y) -> (x c + y s, -x s + y c).
+__device__ __forceinline__ void rope_back(float &x, float &y, float2 cs) {
+  const float u = x * cs.x + y * cs.y, w = -x * cs.y + y * cs.x;
+  x = u;
+  y = w;
+}
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_dkdv_tmem_kernel(const __grid_constant__ CUtensorMap tm_qkv,
+                              const __grid_constant__ CUtensorMap tm_do, BwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t *sK = smem + kKV_K, *sV = smem + kKV_V, *sQ = smem + kKV_Q, *sG = smem + kKV_G;
+  uint8_t *sPt = smem + kKV_P, *sDt = smem + kKV_S;
+  float *sL = (float *)(smem + kKV_L), *sDl = (float *)(smem + kKV_D);
+  uint64_t *bars = (uint64_t *)(smem + kKV_Bar);
+  uint64_t *kv_full = bars, *q_full = bars + 1, *q_empty = bars + 4;   // q_*: [kStages]
+  uint64_t *st_full = bars + 7, *st_free = bars + 8, *pds_full = bars + 9, *pds_free = bars + 10;
+  uint64_t *acc_done = bars + 11, *mma_done = bars + 12;
+  uint32_t *tmem_slot = (uint32_t *)(bars + 13);
+  volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Work item: early key tiles (most query tiles after them) first.
+  const int heads_cta = p.split ? p.nH : p.nKV;
+  const int per = heads_cta * p.B;
+  const int kt = (int)(blockIdx.x / per);
+  const int rest = (int)(blockIdx.x % per);
+  const int hx = rest % heads_cta, b = rest / heads_cta;
+  const int kvh = p.split ? hx / p.group : hx;
+  const int h_begin = p.split ? hx : kvh * p.group;
+  const int n_heads = p.split ? 1 : p.group;
+  const int per_head = p.n_t - kt;              // query tiles kt..n_t-1
+  const int n_iter = n_heads * per_head;
+  const int k0 = kt * kBN;
+  const int row0 = b * p.T;
+  const bool aligned = (smem_u32(smem) & 1023u) == 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < kStages; s++) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1);
+    }
+    mbar_init(st_full, 1);
+    mbar_init(st_free, 8);
+    mbar_init(pds_full, 8);
+    mbar_init(pds_free, 1);
+    mbar_init(acc_done, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    if (!aligned) atomicExch(p.err, 20);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kBwdTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 320;
+
+  if (!aligned) {
+  } else if (warp == 0) {
+    // ---------------- producer (lane 0 issues TMA; the warp stages lse / delta)
+    bool ok = true;
+    int issued = 0;
+    if (lane == 0) {
+      mbar_expect_tx(kv_full, 2 * kTile);
+      tma_load_2d(sK, &tm_qkv, (p.nH + kvh) * kD, row0 + k0, kv_full);
+      tma_load_2d(sV, &tm_qkv, (p.nH + p.nKV + kvh) * kD, row0 + k0, kv_full);
+    }
+    for (int it = 0; it < n_iter; it++) {
+      const int s = it % kStages;
+      if (!warp_wait(&q_empty[s], ((uint32_t)(it / kStages) & 1u) ^ 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const int h = h_begin + it / per_head;
+      const int q0 = (kt + it % per_head) * kBM;
+      const int64_t lrow = ((int64_t)b * p.nH + h) * p.T;
+#pragma unroll
+      for (int e = lane; e < kBM; e += 32) {
+        const int q = q0 + e;
+        sL[s * kBM + e] = q < p.T ? p.lse[lrow + q] * kLog2e : 0.f;
+        sDl[s * kBM + e] = q < p.T ? p.delta[lrow + q] : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_expect_tx(&q_full[s], 2 * kTile);
+        tma_load_2d(sQ + s * kTile, &tm_qkv, h * kD, row0 + q0, &q_full[s]);
+        tma_load_2d(sG + s * kTile, &tm_do, h * kD, row0 + q0, &q_full[s]);
+      }
+      issued++;
+    }
+    if (lane == 0) {
+      if (!ok) {
+        *abort_flag = 1;
+        atomicExch(p.err, 21);
+      }
+      mbar_wait_drain(kv_full, 0);
+      for (int i = issued - kStages < 0 ? 0 : issued - kStages; i < issued; i++)
+        mbar_wait_drain(&q_full[i % kStages], (uint32_t)(i / kStages) & 1u);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t id_n128 = instr_desc_bf16(0, 0, kBM, kBN);
+      const uint32_t id_n64 = instr_desc_bf16(0, 1, kBM, kD);
+      bool ok = mbar_wait(kv_full, 0, abort_flag);
+      const uint32_t ak = smem_u32(sK), av = smem_u32(sV), ap = smem_u32(sPt), ad = smem_u32(sDt);
+      for (int it = 0; it <= n_iter && ok; it++) {
+        if (it < n_iter) {
+          const int s = it % kStages;
+          if (!mbar_wait(&q_full[s], (uint32_t)(it / kStages) & 1u, abort_flag) ||
+              (it > 0 && !mbar_wait(st_free, (uint32_t)(it - 1) & 1u, abort_flag))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t bq = smem_u32(sQ + s * kTile), bg = smem_u32(sG + s * kTile);
+#pragma unroll
+          for (int k = 0; k < kD / 16; k++)
+            umma_bf16(tS, operand_desc(ak, k, 0, kD), operand_desc(bq, k, 0, kD), id_n128, k > 0 ? 1u : 0u);
+#pragma unroll
+          for (int k = 0; k < kD / 16; k++)
+            umma_bf16(tdP, operand_desc(av, k, 0, kD), operand_desc(bg, k, 0, kD), id_n128, k > 0 ? 1u : 0u);
+          umma_commit(st_full);
+        }
+        if (it > 0) {
+          const int i = it - 1, s = i % kStages;
+          if (!mbar_wait(pds_full, (uint32_t)i & 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t bq = smem_u32(sQ + s * kTile), bg = smem_u32(sG + s * kTile);
+#pragma unroll
+          for (int k = 0; k < kBM / 16; k++)
+            umma_bf16(tdV, operand_desc(ap + (uint32_t)(k >> 2) * kTile, k & 3, 0, kD),
+                      operand_desc(bg, k, 1, kBM), id_n64, (i > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+          for (int k = 0; k < kBM / 16; k++)
+            umma_bf16(tdK, operand_desc(ad + (uint32_t)(k >> 2) * kTile, k & 3, 0, kD),
+                      operand_desc(bq, k, 1, kBM), id_n64, (i > 0 || k > 0) ? 1u : 0u);
+          umma_commit(pds_free);
+          umma_commit(&q_empty[s]);
+        }
+      }
+      if (ok) {
+        umma_commit(acc_done);
+      } else {
+        *abort_flag = 1;
+        atomicExch(p.err, 22);
+      }
+      umma_commit(mma_done);
+      mbar_wait_drain(mma_done, 0);
+    }
+  } else {
+    // ---------------- P^T / dS^T (warps 2..9)
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const int r = quarter * 32 + lane;          // key row == TMEM lane
+    const int key = k0 + r;
+    const uint32_t la = (uint32_t)(quarter * 32) << 16;
+    const int cb = half * 64;                   // this warp's 64 query columns
+    bool ok = true;
+    for (int it = 0; it < n_iter; it++) {
+      const int s = it % kStages;
+      const int q0 = (kt + it % per_head) * kBM;
+      if (!warp_wait(&q_full[s], (uint32_t)(it / kStages) & 1u, abort_flag) ||
+          !warp_wait(st_full, (uint32_t)it & 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sv[64], dp[64];
+      tmem_ld64(tS + la + cb, sv);
+      tmem_ld64(tdP + la + cb, dp);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(st_free);
+      const float *L = sL + s * kBM + cb, *Dl = sDl + s * kBM + cb;
+      const int qc = q0 + cb;                   // first query of these columns
+      const bool mask = qc < key || qc + 64 > p.T;
+      uint32_t pp[32], dd[32];
+#pragma unroll
+      for (int c = 0; c < 32; c++) {
+        float p0 = ex2_ftz(fmaf(sv[2 * c], p.scale_log2, -L[2 * c]));
+        float p1 = ex2_ftz(fmaf(sv[2 * c + 1], p.scale_log2, -L[2 * c + 1]));
+        if (mask) {
+          const int q = qc + 2 * c;
+          if (q < key || q >= p.T) p0 = 0.f;
+          if (q + 1 < key || q + 1 >= p.T) p1 = 0.f;
+        }
+        pp[c] = pack2_bf16(p0, p1);
+        dd[c] = pack2_bf16(p0 * (dp[2 * c] - Dl[2 * c]), p1 * (dp[2 * c + 1] - Dl[2 * c + 1]));
+      }
+      // dV/dK of the previous tile must be done reading P^T / dS^T.
+      if (it > 0 && !warp_wait(pds_free, (uint32_t)(it - 1) & 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      store_row_half(sPt + half * kTile, r, pp);
+      store_row_half(sDt + half * kTile, r, dd);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pds_full);
+    }
+    if (ok && warp_wait(acc_done, 0, abort_flag)) {
+      tc_fence_after();
+      float v[64];
+      tmem_ld64((half ? tdK : tdV) + la, v);
+      if (key < p.T) {
+        const float mul = half ? p.scale : 1.f;
+        if (p.split) {
+          const int g = h_begin - kvh * p.group;
+          float *dst = (half ? p.pk : p.pv) +
+                       ((int64_t)g * p.B * p.T + row0 + key) * ((int64_t)p.nKV * kD) + kvh * kD;
+#pragma unroll
+          for (int c4 = 0; c4 < 16; c4++)
+            reinterpret_cast<float4 *>(dst)[c4] =
+                make_float4(v[4 * c4] * mul, v[4 * c4 + 1] * mul, v[4 * c4 + 2] * mul, v[4 * c4 + 3] * mul);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; c++) v[c] *= mul;
+          if (half && p.rope) {
+#pragma unroll
+            for (int i = 0; i < 32; i++) rope_back(v[2 * i], v[2 * i + 1], p.rope[(int64_t)key * 32 + i]);
+          }
+          uint4 *dst = reinterpret_cast<uint4 *>(p.dqkv + (int64_t)(row0 + key) * p.ld +
+                                                 (int64_t)(p.nH + (half ? 0 : p.nKV) + kvh) * kD);
+#pragma unroll
+          for (int c8 = 0; c8 < 8; c8++)
+            dst[c8] = make_uint4(pack2_bf16(v[8 * c8], v[8 * c8 + 1]), pack2_bf16(v[8 * c8 + 2], v[8 * c8 + 3]),
+                                 pack2_bf16(v[8 * c8 + 4], v[8 * c8 + 5]), pack2_bf16(v[8 * c8 + 6], v[8 * c8 + 7]));
+        }
+      }
+    } else {
+      ok = false;
+    }
+    if (!ok && lane == 0) {
+      *abort_flag = 1;
+      atomicExch(p.err, 23);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kBwdTmemCols);
+}
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_dq_tmem_kernel(const __grid_constant__ CUtensorMap tm_qkv,
+                            const __grid_constant__ CUtensorMap tm_do, BwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t *sQ = smem + kQ_Q, *sG = smem + kQ_G, *sK = smem + kQ_K, *sV = smem + kQ_V;
+  uint8_t *sDs = smem + kQ_S;
+  uint64_t *bars = (uint64_t *)(smem + kQ_Bar);
+  uint64_t *qg_full = bars, *kv_full = bars + 1, *kv_empty = bars + 4;   // kv_*: [kStages]
+  uint64_t *sp_full = bars + 7, *sp_free = bars + 8, *ds_full = bars + 9, *ds_free = bars + 10;
+  uint64_t *acc_done = bars + 11, *mma_done = bars + 12;
+  uint32_t *tmem_slot = (uint32_t *)(bars + 13);
+  volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int per = p.nH * p.B;
+  const int qt = p.n_t - 1 - (int)(blockIdx.x / per);   // latest query tiles first
+  const int rest = (int)(blockIdx.x % per);
+  const int h = rest % p.nH, b = rest / p.nH;
+  const int kvh = h / p.group;
+  const int q0 = qt * kBM;
+  const int nkv = qt + 1;
+  const int row0 = b * p.T;
+  const bool aligned = (smem_u32(smem) & 1023u) == 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(qg_full, 1);
+    for (int s = 0; s < kStages; s++) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(sp_full, 1);
+    mbar_init(sp_free, 8);
+    mbar_init(ds_full, 8);
+    mbar_init(ds_free, 1);
+    mbar_init(acc_done, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    if (!aligned) atomicExch(p.err, 30);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kBwdTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tdP = tmem + 128, tdQ = tmem + 256;
+
+  if (!aligned) {
+  } else if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      bool ok = true;
+      int issued = 0;
+      mbar_expect_tx(qg_full, 2 * kTile);
+      tma_load_2d(sQ, &tm_qkv, h * kD, row0 + q0, qg_full);
+      tma_load_2d(sG, &tm_do, h * kD, row0 + q0, qg_full);
+      for (int j = 0; j < nkv; j++) {
+        const int s = j % kStages;
+        if (!mbar_wait(&kv_empty[s], ((uint32_t)(j / kStages) & 1u) ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(&kv_full[s], 2 * kTile);
+        tma_load_2d(sK + s * kTile, &tm_qkv, (p.nH + kvh) * kD, row0 + j * kBN, &kv_full[s]);
+        tma_load_2d(sV + s * kTile, &tm_qkv, (p.nH + p.nKV + kvh) * kD, row0 + j * kBN, &kv_full[s]);
+        issued++;
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicExch(p.err, 31);
+      }
+      mbar_wait_drain(qg_full, 0);
+      for (int i = issued - kStages < 0 ? 0 : issued - kStages; i < issued; i++)
+        mbar_wait_drain(&kv_full[i % kStages], (uint32_t)(i / kStages) & 1u);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t id_n128 = instr_desc_bf16(0, 0, kBM, kBN);
+      const uint32_t id_n64 = instr_desc_bf16(0, 1, kBM, kD);
+      bool ok = mbar_wait(qg_full, 0, abort_flag);
+      const uint32_t aq = smem_u32(sQ), ag = smem_u32(sG), ads = smem_u32(sDs);
+      for (int j = 0; j <= nkv && ok; j++) {
+        if (j < nkv) {
+          const int s = j % kStages;
+          if (!mbar_wait(&kv_full[s], (uint32_t)(j / kStages) & 1u, abort_flag) ||
+              (j > 0 && !mbar_wait(sp_free, (uint32_t)(j - 1) & 1u, abort_flag))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t bk = smem_u32(sK + s * kTile), bv = smem_u32(sV + s * kTile);
+#pragma unroll
+          for (int k = 0; k < kD / 16; k++)
+            umma_bf16(tS, operand_desc(aq, k, 0, kD), operand_desc(bk, k, 0, kD), id_n128, k > 0 ? 1u : 0u);
+#pragma unroll
+          for (int k = 0; k < kD / 16; k++)
+            umma_bf16(tdP, operand_desc(ag, k, 0, kD), operand_desc(bv, k, 0, kD), id_n128, k > 0 ? 1u : 0u);
+          umma_commit(sp_full);
+        }
+        if (j > 0) {
+          const int i = j - 1, s = i % kStages;
+          if (!mbar_wait(ds_full, (uint32_t)i & 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t bk = smem_u32(sK + s * kTile);
+#pragma unroll
+          for (int k = 0; k < kBN / 16; k++)
+            umma_bf16(tdQ, operand_desc(ads + (uint32_t)(k >> 2) * kTile, k & 3, 0, kD),
+                      operand_desc(bk, k, 1, kBN), id_n64, (i > 0 || k > 0) ? 1u : 0u);
+          umma_commit(ds_free);
+          umma_commit(&kv_empty[s]);
+        }
+      }
+      if (ok) {
+        umma_commit(acc_done);
+      } else {
+        *abort_flag = 1;
+        atomicExch(p.err, 32);
+      }
+      umma_commit(mma_done);
+      mbar_wait_drain(mma_done, 0);
+    }
+  } else {
+    // ---------------- dS (warps 2..9)
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const int r = quarter * 32 + lane;          // query row == TMEM lane
+    const int q = q0 + r;
+    const uint32_t la = (uint32_t)(quarter * 32) << 16;
+    const int cb = half * 64;                   // this warp's 64 key columns
+    const int64_t li = ((int64_t)b * p.nH + h) * p.T + q;
+    const float L = q < p.T ? p.lse[li] * kLog2e : 0.f;
+    const float Dq = q < p.T ? p.delta[li] : 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; j++) {
+      if (!warp_wait(sp_full, (uint32_t)j & 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sv[64], dp[64];
+      tmem_ld64(tS + la + cb, sv);
+      tmem_ld64(tdP + la + cb, dp);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sp_free);
+      const int lim = j == nkv - 1 ? r - cb : 1 << 30;   // diagonal tile: key column c valid if c <= lim
+      uint32_t dd[32];
+#pragma unroll
+      for (int c = 0; c < 32; c++) {
+        float p0 = ex2_ftz(fmaf(sv[2 * c], p.scale_log2, -L));
+        float p1 = ex2_ftz(fmaf(sv[2 * c + 1], p.scale_log2, -L));
+        if (2 * c > lim) p0 = 0.f;
+        if (2 * c + 1 > lim) p1 = 0.f;
+        dd[c] = pack2_bf16(p0 * (dp[2 * c] - Dq), p1 * (dp[2 * c + 1] - Dq));
+      }
+      if (j > 0 && !warp_wait(ds_free, (uint32_t)(j - 1) & 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      store_row_half(sDs + half * kTile, r, dd);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_full);
+    }
+    if (ok && warp_wait(acc_done, 0, abort_flag)) {
+      tc_fence_after();
+      uint32_t u[32];
+      tmem_ld32(tdQ + la + half * 32, u);
+      if (q < p.T) {
+        float v[32];
+#pragma unroll
+        for (int c = 0; c < 32; c++) v[c] = __uint_as_float(u[c]) * p.scale;
+        if (p.rope) {
+#pragma unroll
+          for (int i = 0; i < 16; i++) rope_back(v[2 * i], v[2 * i + 1], p.rope[(int64_t)q * 32 + half * 16 + i]);
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(p.dqkv + (int64_t)(row0 + q) * p.ld + (int64_t)h * kD + half * 32);
+#pragma unroll
+        for (int c8 = 0; c8 < 4; c8++)
+          dst[c8] = make_uint4(pack2_bf16(v[8 * c8], v[8 * c8 + 1]), pack2_bf16(v[8 * c8 + 2], v[8 * c8 + 3]),
+                               pack2_bf16(v[8 * c8 + 4], v[8 * c8 + 5]), pack2_bf16(v[8 * c8 + 6], v[8 * c8 + 7]));
+      }
+    } else {
+      ok = false;
+    }
+    if (!ok && lane == 0) {
+      *abort_flag = 1;
+      atomicExch(p.err, 33);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kBwdTmemCols);
+}
+
+// delta[b][h][t] = sum_d dO[bt, h*64 + d] * O[bt, h*64 + d]; 8 threads per
+// (token, head), one 16-byte load of each operand per thread.
+__global__ void attn_delta64_kernel(const __nv_bfloat16 *__restrict__ dO,
+                                    const __nv_bfloat16 *__restrict__ O, int64_t units, int nH, int T,
+                                    float *__restrict__ delta) {
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t unit = t >> 3;                  // token row * nH + head
+  float s = 0.f;
+  if (unit < units) {
+    const uint4 g = reinterpret_cast<const uint4 *>(dO)[t];
+    const uint4 o = reinterpret_cast<const uint4 *>(O)[t];
+    const __nv_bfloat162 *g2 = reinterpret_cast<const __nv_bfloat162 *>(&g);
+    const __nv_bfloat162 *o2 = reinterpret_cast<const __nv_bfloat162 *>(&o);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float2 a = __bfloat1622float2(g2[i]), c = __bfloat1622float2(o2[i]);
+      s = fmaf(a.x, c.x, s);
+      s = fmaf(a.y, c.y, s);
+    }
+  }
+  s += __shfl_xor_sync(0xffffffffu, s, 4);
+  s += __shfl_xor_sync(0xffffffffu, s, 2);
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  if (unit < units && (t & 7) == 0) {
+    const int64_t row = unit / nH;
+    const int h = (int)(unit - row * nH);
+    const int64_t b = row / T, tt = row - b * T;
+    delta[(b * nH + h) * T + tt] = s;
+  }
+}
+
+// Head-split dK/dV: sums the group's fp32 partials in order, rotates dK back
+// and stores both as bf16 into the dqkv buffer.  One thread per 4 columns.
+__global__ void attn_kv_reduce64_kernel(const float *__restrict__ pk, const float *__restrict__ pv,
+                                        int group, int64_t rows, int nH, int nKV, int T,
+                                        const float2 *__restrict__ rope, __nv_bfloat16 *dqkv, int64_t ld) {
+  const int64_t kvD = (int64_t)nKV * kD, q4 = kvD / 4, n = rows * q4;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = e / q4;
+    const int64_t c = (e - row * q4) * 4;
+    float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
+    for (int g = 0; g < group; g++) {
+      const int64_t o = ((int64_t)g * rows + row) * kvD + c;
+      const float4 a = *reinterpret_cast<const float4 *>(pk + o);
+      const float4 d = *reinterpret_cast<const float4 *>(pv + o);
+      k.x += a.x; k.y += a.y; k.z += a.z; k.w += a.w;
+      v.x += d.x; v.y += d.y; v.z += d.z; v.w += d.w;
+    }
+    if (rope) {
+      const float2 *cs = rope + (row % T) * 32 + (c % kD) / 2;
+      rope_back(k.x, k.y, cs[0]);
+      rope_back(k.z, k.w, cs[1]);
+    }
+    __nv_bfloat16 *dk = dqkv + row * ld + (int64_t)nH * kD + c;
+    __nv_bfloat16 *dv = dk + kvD;
+    *reinterpret_cast<uint2 *>(dk) = make_uint2(pack2_bf16(k.x, k.y), pack2_bf16(k.z, k.w));
+    *reinterpret_cast<uint2 *>(dv) = make_uint2(pack2_bf16(v.x, v.y), pack2_bf16(v.z, v.w));
+  }
+}
+
 }  // namespace
 
 bool attn_tmem_supported(int dH) { return dH == kD; }
@@ -314,6 +898,72 @@ int attn_fwd_tmem(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, i
   const int64_t grid = (int64_t)p.n_qt * nH * B;
   FCU_REQUIRE(grid <= INT32_MAX, "attention: grid too large");
   attn_fwd_tmem_kernel<<<(unsigned)grid, kThreads, kSmemBytes, ctx->stream>>>(map, p);
+  FCU_CHECK_LAUNCH();
+  return FCU_OK;
+}
+
+// Backward from the bf16 qkv buffer, dO and O ([B*T, nH*64] bf16) and the
+// forward's lse: dq | dk | dv (RoPE rotated back when `rope` is given) into
+// the bf16 dqkv buffer (same layout and row stride as qkv).  `delta` is
+// scratch of B*nH*T floats; `pk`, `pv` are the head-split partial buffers
+// (group * B*T * nKV*64 floats each), used when `split` is set.
+int attn_bwd_tmem(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv, const void *O,
+                  const float *lse, float *delta, int B, int T, int nH, int nKV, const float2 *rope,
+                  void *dqkv, int split, float *pk, float *pv) {
+  int rc = tc_get_encode();
+  if (rc) return rc;
+  int *err = nullptr;
+  rc = tc_error_word(ctx, &err);
+  if (rc) return rc;
+  CUtensorMap map_qkv, map_do;
+  rc = tc_make_map(&map_qkv, qkv, (uint64_t)B * T, (uint64_t)(nH + 2 * nKV) * kD, (uint64_t)ld_qkv, 64,
+                   kBM);
+  if (!rc) rc = tc_make_map(&map_do, dO, (uint64_t)B * T, (uint64_t)nH * kD, (uint64_t)nH * kD, 64, kBM);
+  if (rc) return rc;
+  const int64_t units = (int64_t)B * T * nH;
+  attn_delta64_kernel<<<(unsigned)((units * 8 + 255) / 256), 256, 0, ctx->stream>>>(
+      (const __nv_bfloat16 *)dO, (const __nv_bfloat16 *)O, units, nH, T, delta);
+  FCU_CHECK_LAUNCH();
+  BwdParams p{};
+  p.B = B;
+  p.T = T;
+  p.nH = nH;
+  p.nKV = nKV;
+  p.n_t = div_up(T, kBM);
+  p.group = nH / nKV;
+  p.split = split;
+  p.scale = (float)(1.0 / sqrt((double)kD));
+  p.scale_log2 = p.scale * kLog2e;
+  p.lse = lse;
+  p.delta = delta;
+  p.rope = rope;
+  p.dqkv = (__nv_bfloat16 *)dqkv;
+  p.ld = ld_qkv;
+  p.pk = pk;
+  p.pv = pv;
+  p.err = err;
+  static bool attr_set[64] = {false};
+  if (!attr_set[ctx->device & 63]) {
+    FCU_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd_dkdv_tmem_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kKVSmem));
+    FCU_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd_dq_tmem_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kQSmem));
+    attr_set[ctx->device & 63] = true;
+  }
+  const int64_t grid_kv = (int64_t)p.n_t * (split ? nH : nKV) * B;
+  const int64_t grid_q = (int64_t)p.n_t * nH * B;
+  FCU_REQUIRE(grid_q <= INT32_MAX, "attention backward: grid too large");
+  attn_bwd_dkdv_tmem_kernel<<<(unsigned)grid_kv, kBwdThreads, kKVSmem, ctx->stream>>>(map_qkv, map_do, p);
+  FCU_CHECK_LAUNCH();
+  if (split) {
+    const int64_t n = (int64_t)B * T * nKV * kD / 4;
+    int blocks = (int)((n + 255) / 256);
+    if (blocks > 16 * ctx->num_sms) blocks = 16 * ctx->num_sms;
+    attn_kv_reduce64_kernel<<<blocks, 256, 0, ctx->stream>>>(pk, pv, p.group, (int64_t)B * T, nH, nKV, T,
+                                                            rope, (__nv_bfloat16 *)dqkv, ld_qkv);
+    FCU_CHECK_LAUNCH();
+  }
+  attn_bwd_dq_tmem_kernel<<<(unsigned)grid_q, kBwdThreads, kQSmem, ctx->stream>>>(map_qkv, map_do, p);
   FCU_CHECK_LAUNCH();
   return FCU_OK;
 }

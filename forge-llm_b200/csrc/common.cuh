@@ -49,6 +49,9 @@ int attn_bwd_tc(cudaStream_t st, const float *dO, const float *Q, const float *K
 bool attn_tmem_supported(int dH);
 int attn_fwd_tmem(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, int nH, int nKV,
                   void *O, float *lse);
+int attn_bwd_tmem(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv, const void *O,
+                  const float *lse, float *delta, int B, int T, int nH, int nKV, const float2 *rope,
+                  void *dqkv, int split, float *pk, float *pv);
 
 }  // namespace fcu
 

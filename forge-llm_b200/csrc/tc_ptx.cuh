@@ -175,6 +175,23 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float *f) {
       : "memory");
 }
 
+// 128 consecutive fp32 columns of this thread's TMEM lane, waited for.
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, float *f) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, %64, %65, %66, %67, %68, %69, %70, %71, %72, %73, %74, %75, %76, %77, %78, %79, %80, %81, %82, %83, %84, %85, %86, %87, %88, %89, %90, %91, %92, %93, %94, %95, %96, %97, %98, %99, %100, %101, %102, %103, %104, %105, %106, %107, %108, %109, %110, %111, %112, %113, %114, %115, %116, %117, %118, %119, %120, %121, %122, %123, %124, %125, %126, %127}, [%128];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=f"(f[0]), "=f"(f[1]), "=f"(f[2]), "=f"(f[3]), "=f"(f[4]), "=f"(f[5]), "=f"(f[6]), "=f"(f[7]), "=f"(f[8]), "=f"(f[9]), "=f"(f[10]), "=f"(f[11]), "=f"(f[12]), "=f"(f[13]), "=f"(f[14]), "=f"(f[15]), "=f"(f[16]), "=f"(f[17]), "=f"(f[18]), "=f"(f[19]), "=f"(f[20]), "=f"(f[21]), "=f"(f[22]), "=f"(f[23]), "=f"(f[24]), "=f"(f[25]), "=f"(f[26]), "=f"(f[27]), "=f"(f[28]), "=f"(f[29]), "=f"(f[30]), "=f"(f[31]), "=f"(f[32]), "=f"(f[33]), "=f"(f[34]), "=f"(f[35]), "=f"(f[36]), "=f"(f[37]), "=f"(f[38]), "=f"(f[39]), "=f"(f[40]), "=f"(f[41]), "=f"(f[42]), "=f"(f[43]), "=f"(f[44]), "=f"(f[45]), "=f"(f[46]), "=f"(f[47]), "=f"(f[48]), "=f"(f[49]), "=f"(f[50]), "=f"(f[51]), "=f"(f[52]), "=f"(f[53]), "=f"(f[54]), "=f"(f[55]), "=f"(f[56]), "=f"(f[57]), "=f"(f[58]), "=f"(f[59]), "=f"(f[60]), "=f"(f[61]), "=f"(f[62]), "=f"(f[63]), "=f"(f[64]), "=f"(f[65]), "=f"(f[66]), "=f"(f[67]), "=f"(f[68]), "=f"(f[69]), "=f"(f[70]), "=f"(f[71]), "=f"(f[72]), "=f"(f[73]), "=f"(f[74]), "=f"(f[75]), "=f"(f[76]), "=f"(f[77]), "=f"(f[78]), "=f"(f[79]), "=f"(f[80]), "=f"(f[81]), "=f"(f[82]), "=f"(f[83]), "=f"(f[84]), "=f"(f[85]), "=f"(f[86]), "=f"(f[87]), "=f"(f[88]), "=f"(f[89]), "=f"(f[90]), "=f"(f[91]), "=f"(f[92]), "=f"(f[93]), "=f"(f[94]), "=f"(f[95]), "=f"(f[96]), "=f"(f[97]), "=f"(f[98]), "=f"(f[99]), "=f"(f[100]), "=f"(f[101]), "=f"(f[102]), "=f"(f[103]), "=f"(f[104]), "=f"(f[105]), "=f"(f[106]), "=f"(f[107]), "=f"(f[108]), "=f"(f[109]), "=f"(f[110]), "=f"(f[111]), "=f"(f[112]), "=f"(f[113]), "=f"(f[114]), "=f"(f[115]), "=f"(f[116]), "=f"(f[117]), "=f"(f[118]), "=f"(f[119]), "=f"(f[120]), "=f"(f[121]), "=f"(f[122]), "=f"(f[123]), "=f"(f[124]), "=f"(f[125]), "=f"(f[126]), "=f"(f[127])
+      : "r"(taddr)
+      : "memory");
+}
+
+// 2^x on the MUFU unit; subnormal results flush to zero.
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0],"

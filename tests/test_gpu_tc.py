@@ -247,3 +247,57 @@ def test_attn_fwd_bf16_entry(B, T, nH, nKV, extra):
     assert torch.isfinite(O.float()).all() and torch.isfinite(lse).all()
     assert relf(o_ref.cpu().numpy(), O.double().cpu().numpy()) <= 1e-2
     assert float((lse.double().view(B, nH, T) - lse_ref).abs().max()) <= 1e-4
+
+
+def _rope_back64(d, B, T, heads, dH, theta):
+    """Rotate per-head interleaved pairs of d [B*T, heads*dH] back by R^T (float64)."""
+    pos = torch.arange(T, dtype=torch.float64, device=d.device).repeat(B)
+    i = torch.arange(dH // 2, dtype=torch.float64, device=d.device)
+    ang = pos[:, None] / theta ** (2 * i / dH)[None, :]
+    c, s = torch.cos(ang)[:, None, :], torch.sin(ang)[:, None, :]
+    x = d.view(B * T, heads, dH // 2, 2)
+    a, b = x[..., 0], x[..., 1]
+    return torch.stack((a * c + b * s, -a * s + b * c), -1).reshape(B * T, heads * dH)
+
+
+@pytest.mark.parametrize("B,T,nH,nKV,theta", [(1, 64, 2, 2, 0.0), (2, 130, 4, 1, 10000.0),
+                                              (3, 300, 6, 2, 10000.0), (2, 1024, 12, 4, 10000.0),
+                                              (16, 1024, 12, 4, 10000.0), (40, 512, 12, 4, 10000.0),
+                                              (1, 2048, 32, 8, 10000.0)])
+def test_attn_bwd_bf16_entry(B, T, nH, nKV, theta):
+    """The fused path's attention backward (dq | dk | dv into the bf16 dqkv
+    buffer, RoPE rotated back) against float64 autograd of the same bf16
+    inputs: relL2 <= 2e-2 (P and dS are bf16 operands), every gradient finite."""
+    from forgellm import _lib
+    from forgellm.autograd import ctx
+    dH = 64
+    width = (nH + 2 * nKV) * dH
+    g = torch.Generator(device="cuda").manual_seed(B * 77 + T)
+    qkv = torch.randn(B * T, width, device="cuda", generator=g).to(torch.bfloat16)
+    dO = torch.randn(B * T, nH * dH, device="cuda", generator=g).to(torch.bfloat16)
+    O = torch.empty(B * T, nH * dH, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B * nH * T, device="cuda")
+    h = ctx().handle
+    _lib.call("fcu_attn_fwd_bf16", h, qkv.data_ptr(), width, B, T, nH, nKV, dH, O.data_ptr(), lse.data_ptr())
+    dqkv = torch.full((B * T, width), float("nan"), device="cuda").to(torch.bfloat16)
+    outs = []
+    for _ in range(2):
+        _lib.call("fcu_attn_bwd_bf16", h, dO.data_ptr(), qkv.data_ptr(), width, O.data_ptr(),
+                  lse.data_ptr(), B, T, nH, nKV, dH, theta, dqkv.data_ptr())
+        torch.cuda.synchronize()
+        outs.append(dqkv.clone())
+    device_ok()
+    assert torch.equal(outs[0], outs[1])                     # deterministic
+    x = qkv.double().requires_grad_(True)
+    o_ref, _ = _attn_ref64(x, B, T, nH, nKV, dH)
+    o_ref.backward(dO.double())
+    ref = x.grad
+    qD, kD = nH * dH, nKV * dH
+    if theta > 0:
+        ref = torch.cat((_rope_back64(ref[:, :qD], B, T, nH, dH, theta),
+                         _rope_back64(ref[:, qD:qD + kD], B, T, nKV, dH, theta), ref[:, qD + kD:]), 1)
+    got = dqkv.double()
+    assert torch.isfinite(got).all()
+    for name, sl in (("dq", slice(0, qD)), ("dk", slice(qD, qD + kD)), ("dv", slice(qD + kD, width))):
+        err = relf(ref[:, sl].cpu().numpy(), got[:, sl].cpu().numpy())
+        assert err <= 2e-2, (name, err)
