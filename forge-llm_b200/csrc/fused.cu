@@ -22,14 +22,38 @@ __device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
   return __bfloat1622float2(v);
 }
 
+inline int grid_for(int64_t n, int per_block, int cap) {
+  int64_t g = (n + per_block - 1) / per_block;
+  return (int)(g < 1 ? 1 : (g > cap ? cap : g));
+}
+
 // ---------------------------------------------------------------- rmsNorm fwd -> bf16
 // One warp per row; out = bf16(x * inv * w), inv[t] = 1/sqrt(mean(x^2) + eps).
+// With ADD, x = X + A is formed first and stored to Xout (any D % 4 == 0).
+template <bool ADD>
 __global__ void rmsnorm_fwd_bf16_kernel(const float *__restrict__ X, const float *__restrict__ w,
                                         int64_t T, int64_t D, float eps,
-                                        __nv_bfloat16 *__restrict__ out, float *__restrict__ inv) {
+                                        __nv_bfloat16 *__restrict__ out, float *__restrict__ inv,
+                                        const float *__restrict__ A, float *__restrict__ Xout) {
   const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
+  if (ADD) {
+    const float4 *a4 = reinterpret_cast<const float4 *>(A + row * D);
+    const float4 *s4 = reinterpret_cast<const float4 *>(X + row * D);
+    float4 *d4 = reinterpret_cast<float4 *>(Xout + row * D);
+    for (int64_t c = lane; c < (D >> 2); c += 32) {
+      float4 v = s4[c];
+      const float4 a = a4[c];
+      v.x += a.x;
+      v.y += a.y;
+      v.z += a.z;
+      v.w += a.w;
+      d4[c] = v;
+    }
+    __syncwarp();
+    X = Xout;
+  }
   const float4 *x4 = reinterpret_cast<const float4 *>(X + row * D);
   const float4 *w4 = reinterpret_cast<const float4 *>(w);
   const int64_t D4 = D >> 2;
@@ -49,6 +73,73 @@ __global__ void rmsnorm_fwd_bf16_kernel(const float *__restrict__ X, const float
     o.y = pack_bf16(v.z * iv * ww.z, v.w * iv * ww.w);
     o2[c] = o;
   }
+}
+
+// Row cached in registers (D = 128 * NC): one HBM read of x.  With ADD the
+// row is x = X + A (the residual add of the branch that produced A), stored
+// to Xout before it is normalised.
+template <int NC, bool ADD>
+__global__ void rmsnorm_fwd_bf16_rc_kernel(const float *__restrict__ X, const float *__restrict__ A,
+                                           const float *__restrict__ w, int64_t T, float eps,
+                                           float *__restrict__ Xout, __nv_bfloat16 *__restrict__ out,
+                                           float *__restrict__ inv) {
+  constexpr int D = 128 * NC;
+  const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  const float4 *x4 = reinterpret_cast<const float4 *>(X + row * D);
+  float4 v[NC];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NC; i++) {
+    v[i] = x4[lane + 32 * i];
+    if (ADD) {
+      const float4 a = reinterpret_cast<const float4 *>(A + row * D)[lane + 32 * i];
+      v[i].x += a.x;
+      v[i].y += a.y;
+      v[i].z += a.z;
+      v[i].w += a.w;
+      reinterpret_cast<float4 *>(Xout + row * D)[lane + 32 * i] = v[i];
+    }
+    ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+  }
+  ss = warp_sum(ss);
+  const float iv = rsqrtf(ss / (float)D + eps);
+  if (lane == 0) inv[row] = iv;
+  const float4 *w4 = reinterpret_cast<const float4 *>(w);
+  uint2 *o2 = reinterpret_cast<uint2 *>(out + row * D);
+#pragma unroll
+  for (int i = 0; i < NC; i++) {
+    const float4 ww = w4[lane + 32 * i];
+    uint2 o;
+    o.x = pack_bf16(v[i].x * iv * ww.x, v[i].y * iv * ww.y);
+    o.y = pack_bf16(v[i].z * iv * ww.z, v[i].w * iv * ww.w);
+    o2[lane + 32 * i] = o;
+  }
+}
+
+template <bool ADD>
+int rmsnorm_fwd_rc_launch(cudaStream_t st, const float *X, const float *A, const float *w, int64_t T,
+                          int64_t D, float eps, float *Xout, __nv_bfloat16 *out, float *inv) {
+  const int blocks = grid_for(T * 32, kThreads, 1 << 30);
+  switch (D / 128) {
+#define FCU_RMS_CASE(nc)                                                                       \
+  case nc:                                                                                     \
+    rmsnorm_fwd_bf16_rc_kernel<nc, ADD><<<blocks, kThreads, 0, st>>>(X, A, w, T, eps, Xout, out, inv); \
+    break;
+    FCU_RMS_CASE(1)
+    FCU_RMS_CASE(2)
+    FCU_RMS_CASE(3)
+    FCU_RMS_CASE(4)
+    FCU_RMS_CASE(5)
+    FCU_RMS_CASE(6)
+    FCU_RMS_CASE(7)
+    FCU_RMS_CASE(8)
+#undef FCU_RMS_CASE
+    default: return FCU_ERR_ARG;
+  }
+  FCU_CHECK_LAUNCH();
+  return FCU_OK;
 }
 
 // ---------------------------------------------------------------- rmsNorm bwd, fused
@@ -221,11 +312,6 @@ __global__ void scale_bf16_dev_kernel(__nv_bfloat16 *__restrict__ y, int64_t n,
     y[i] = __float2bfloat16_rn(__bfloat162float(y[i]) * a);
 }
 
-inline int grid_for(int64_t n, int per_block, int cap) {
-  int64_t g = (n + per_block - 1) / per_block;
-  return (int)(g < 1 ? 1 : (g > cap ? cap : g));
-}
-
 inline bool al16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
 template <int NC>
@@ -265,8 +351,29 @@ int fcu_rmsnorm_fwd_bf16(fcu_ctx *ctx, const float *X, const float *w, int64_t T
   if (T == 0) return FCU_OK;
   FCU_REQUIRE(X && w && out && inv && al16(X) && al16(w) && ((uintptr_t)out & 7) == 0,
               "fcu_rmsnorm_fwd_bf16: null or unaligned pointer");
-  rmsnorm_fwd_bf16_kernel<<<grid_for(T * 32, kThreads, 1 << 30), kThreads, 0, ctx->stream>>>(
-      X, w, T, D, (float)eps, (__nv_bfloat16 *)out, inv);
+  if (D % 128 == 0 && D <= 1024)
+    return rmsnorm_fwd_rc_launch<false>(ctx->stream, X, nullptr, w, T, D, (float)eps, nullptr,
+                                        (__nv_bfloat16 *)out, inv);
+  rmsnorm_fwd_bf16_kernel<false><<<grid_for(T * 32, kThreads, 1 << 30), kThreads, 0, ctx->stream>>>(
+      X, w, T, D, (float)eps, (__nv_bfloat16 *)out, inv, nullptr, nullptr);
+  FCU_CHECK_LAUNCH();
+  return FCU_OK;
+}
+
+int fcu_rmsnorm_fwd_bf16_add(fcu_ctx *ctx, const float *X, const float *A, const float *w, int64_t T,
+                             int64_t D, double eps, float *Xout, void *out, float *inv) {
+  FCU_CTX(ctx);
+  FCU_REQUIRE(T >= 0 && D > 0 && D % 4 == 0,
+              "fcu_rmsnorm_fwd_bf16_add: D=%lld must be a multiple of 4", (long long)D);
+  if (T == 0) return FCU_OK;
+  FCU_REQUIRE(X && A && w && Xout && out && inv && al16(X) && al16(A) && al16(w) && al16(Xout) &&
+                  ((uintptr_t)out & 7) == 0,
+              "fcu_rmsnorm_fwd_bf16_add: null or unaligned pointer");
+  if (D % 128 == 0 && D <= 1024)
+    return rmsnorm_fwd_rc_launch<true>(ctx->stream, X, A, w, T, D, (float)eps, Xout,
+                                       (__nv_bfloat16 *)out, inv);
+  rmsnorm_fwd_bf16_kernel<true><<<grid_for(T * 32, kThreads, 1 << 30), kThreads, 0, ctx->stream>>>(
+      X, w, T, D, (float)eps, (__nv_bfloat16 *)out, inv, A, Xout);
   FCU_CHECK_LAUNCH();
   return FCU_OK;
 }

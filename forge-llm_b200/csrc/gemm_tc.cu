@@ -19,6 +19,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
+#include <string.h>
 
 #include "gemm.cuh"
 #include "tc_ptx.cuh"
@@ -30,6 +31,10 @@ constexpr int BM = 128, BK = 64;
 constexpr int UMMA_K = 16;
 constexpr int A_BYTES = BM * BK * 2;            // 16 KB
 constexpr int NUM_THREADS = 192;
+// Epilogue staging: per epilogue warp two 32-row x 128-byte boxes (32 fp32
+// or 64 bf16 columns), 128B-swizzled, written out by TMA stores.
+constexpr int EPI_BOX = 32 * 128;
+constexpr int EPI_BYTES = 4 * 2 * EPI_BOX;
 constexpr int GROUP_M = 16;                     // tile raster: GROUP_M m-blocks per n sweep
 
 // Output tile width.  128 x 256 is the main tile; 128 x 128 doubles the tile
@@ -42,7 +47,8 @@ struct TileCfg {
   static constexpr int B_BYTES = BN_ * BK * 2;            // 32 / 16 KB
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 48 / 32 KB
   static constexpr uint32_t TMEM_COLS = 2 * BN_;          // 512 / 256
-  static constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + (size_t)STAGES * STAGE_BYTES + 256;
+  static constexpr size_t SMEM_BYTES =
+      1024 /*align slack*/ + (size_t)STAGES * STAGE_BYTES + EPI_BYTES + 256;
 };
 
 // Epilogue modes (what the epilogue warps do with one fp32 accumulator row):
@@ -68,7 +74,9 @@ struct TcParams {
   const float2 *rope;      // [rope_T][head_dim/2] (cos, sin)
   int rope_T, rope_cols, head_dim;
   int splits;              // K slices per output tile (1 = no split)
-  float *ws;               // split-K partial tiles [splits][M][ldc]
+  float *ws;               // split-K partial tiles [splits][ws_rows][ldc]
+  int ws_rows;             // M rounded up to the 128-row tile
+  int tma_out;             // 1: epilogue stores through shared memory + TMA (tmC)
 };
 
 using namespace tc;
@@ -157,7 +165,8 @@ __device__ __forceinline__ void store_chunk(const TcParams &p, int64_t gm, int n
 template <int BN_>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, TcParams p) {
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, TcParams p) {
   constexpr int BN = TileCfg<BN_>::BN;
   constexpr int STAGES = TileCfg<BN_>::STAGES;
   constexpr int B_BYTES = TileCfg<BN_>::B_BYTES;
@@ -167,7 +176,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *sA = smem;
   uint8_t *sB = smem + STAGES * A_BYTES;
-  uint64_t *full = (uint64_t *)(sB + STAGES * B_BYTES);
+  uint8_t *sEpi = sB + STAGES * B_BYTES;
+  uint64_t *full = (uint64_t *)(sEpi + EPI_BYTES);
   uint64_t *empty = full + STAGES;
   uint64_t *tfull = empty + STAGES;   // [2]
   uint64_t *tempty = tfull + 2;       // [2]
@@ -298,6 +308,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     TcParams part = p;   // split-K: plain fp32 stores of this slice's partial tile
     part.mode = kOutF32;
     part.beta = 0;
+    // TMA epilogue: fp32 outputs in 32-column boxes, bf16 in 64-column boxes.
+    const bool bf16_out = p.splits == 1 && p.mode >= kOutBF16;
+    const int cw = bf16_out ? 64 : 32;
+    uint8_t *stg = sEpi + q * 2 * EPI_BOX;
+    int seq = 0;                        // boxes this warp has stored (staging buffer = seq & 1)
     for (int u = blockIdx.x; u < units; u += gridDim.x, ti++) {
       const int t = u / p.splits, sp = u - t * p.splits;
       int tm, tn;
@@ -311,17 +326,82 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const int64_t gm = (int64_t)tm * BM + row;
       const int n0 = tn * BN;
-      if (p.splits > 1) part.C = p.ws + (int64_t)sp * p.M * p.ldc;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      if (!p.tma_out) {
+        if (p.splits > 1) part.C = p.ws + (int64_t)sp * p.ws_rows * p.ldc;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; c++) {
-        uint32_t r[32];
-        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
-        if (gm < p.M) store_chunk(p.splits > 1 ? part : p, gm, n0 + c * 32, r);
+        for (int c = 0; c < BN / 32; c++) {
+          uint32_t r[32];
+          tmem_ld32(tbase + (uint32_t)(c * 32), r);
+          if (gm < p.M) store_chunk(p.splits > 1 ? part : p, gm, n0 + c * 32, r);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        continue;
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      const int m_box = tm * BM + q * 32;          // first output row of this warp's boxes
+      const int nbox = min(BN, p.N - n0) > 0 ? (min(BN, p.N - n0) + cw - 1) / cw : 0;
+#pragma unroll 1
+      for (int c = 0; c < nbox; c++) {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(tbase + (uint32_t)(c * cw), r0);
+        if (bf16_out) tmem_ld32(tbase + (uint32_t)(c * cw + 32), r1);
+        float v[64];
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          v[i] = __uint_as_float(r0[i]);
+          v[32 + i] = bf16_out ? __uint_as_float(r1[i]) : 0.f;
+        }
+        if (c == nbox - 1) {                       // accumulator no longer needed
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+        uint8_t *box = stg + (seq & 1) * EPI_BOX;
+        if (lane == 0) bulk_wait_read<1>();        // the store that last used this buffer has read it
+        __syncwarp();
+        const int n = n0 + c * cw;
+        if (!bf16_out) {
+#pragma unroll
+          for (int j = 0; j < 8; j++)
+            *reinterpret_cast<float4 *>(box + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        } else {
+          if (p.mode == kOutBF16Rope && n < p.rope_cols && gm < p.M) {
+            const int64_t pos = gm % p.rope_T;
+            const int half = p.head_dim >> 1;
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+              const float2 cs = p.rope[pos * half + ((n + 2 * i) % p.head_dim) / 2];
+              const float a = v[2 * i], b = v[2 * i + 1];
+              v[2 * i] = a * cs.x - b * cs.y;
+              v[2 * i + 1] = a * cs.y + b * cs.x;
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 8; j++)
+            *reinterpret_cast<uint4 *>(box + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                make_uint4(pack2_bf16(v[8 * j], v[8 * j + 1]), pack2_bf16(v[8 * j + 2], v[8 * j + 3]),
+                           pack2_bf16(v[8 * j + 4], v[8 * j + 5]), pack2_bf16(v[8 * j + 6], v[8 * j + 7]));
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && m_box < p.M) {
+          const int y = p.splits > 1 ? sp * p.ws_rows + m_box : m_box;
+          if (p.splits == 1 && p.beta) tma_reduce_add_2d(&tmC, box, n, y);
+          else tma_store_2d(&tmC, box, n, y);
+          bulk_commit();
+        }
+        seq++;
+      }
+      if (nbox == 0) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+      }
     }
+    if (lane == 0) bulk_wait_all();
     if (!ok) {
       *abort_flag = 1;
       atomicExch(p.err, 3);
@@ -371,16 +451,16 @@ int tc_get_encode() {
   return FCU_OK;
 }
 
-int tc_make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
-                uint64_t row_stride, uint32_t box_cols, uint32_t box_rows) {
+static int make_map_dt(CUtensorMap *map, CUtensorMapDataType dt, int esize, const void *base,
+                       uint64_t rows, uint64_t cols, uint64_t row_stride, uint32_t box_cols,
+                       uint32_t box_rows) {
   cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {row_stride * 2};
+  cuuint64_t strides[1] = {row_stride * (uint64_t)esize};
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims,
-                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = g_encode(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu stride=%llu box=%ux%u", (int)r,
               (unsigned long long)rows, (unsigned long long)cols, (unsigned long long)row_stride,
@@ -388,6 +468,18 @@ int tc_make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols
     return FCU_ERR_CUDA;
   }
   return FCU_OK;
+}
+
+int tc_make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                uint64_t row_stride, uint32_t box_cols, uint32_t box_rows) {
+  return make_map_dt(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, rows, cols, row_stride, box_cols,
+                     box_rows);
+}
+
+int tc_make_map_f32(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                    uint64_t row_stride, uint32_t box_cols, uint32_t box_rows) {
+  return make_map_dt(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, rows, cols, row_stride, box_cols,
+                     box_rows);
 }
 
 namespace {
@@ -449,7 +541,7 @@ int partials(fcu_ctx *ctx, size_t bytes, void **out) {
 // epilogue.  One thread per pair of adjacent columns (RoPE rotates pairs).
 __global__ void splitk_reduce_kernel(TcParams p) {
   const int64_t hp = (p.N + 1) / 2;  // column pairs per row
-  const int64_t pairs = (int64_t)p.M * hp, mn = (int64_t)p.M * p.N;
+  const int64_t pairs = (int64_t)p.M * hp, mn = (int64_t)p.ws_rows * p.ldc;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < pairs; e += stride) {
     const int64_t row = e / hp;
@@ -580,11 +672,36 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
   p.err = err;
   p.splits = splits;
   p.ws = nullptr;
+  p.ws_rows = (int)(p.tiles_m * BM);
   if (splits > 1) {
     void *w = nullptr;
-    rc = partials(ctx, sizeof(float) * (size_t)splits * (size_t)M * (size_t)N, &w);
+    rc = partials(ctx, sizeof(float) * (size_t)splits * (size_t)p.ws_rows * (size_t)N, &w);
     if (rc) return rc;
     p.ws = (float *)w;
+  }
+  // TMA epilogue: needs 16-byte aligned output rows; the fp32 + residual
+  // epilogue keeps the direct stores.
+  CUtensorMap tc;
+  memset(&tc, 0, sizeof(tc));
+  p.tma_out = 0;
+  if (splits > 1) {
+    if (N % 4 == 0) {
+      rc = tc_make_map_f32(&tc, p.ws, (uint64_t)splits * p.ws_rows, N, N, 32, 32);
+      if (rc) return rc;
+      p.tma_out = 1;
+    }
+  } else if (o.mode == kOutF32) {
+    if (N % 4 == 0 && ((uintptr_t)o.C & 15) == 0) {
+      rc = tc_make_map_f32(&tc, o.C, M, N, N, 32, 32);
+      if (rc) return rc;
+      p.tma_out = 1;
+    }
+  } else if (o.mode == kOutBF16 || o.mode == kOutBF16Rope) {
+    if (N % 8 == 0 && ((uintptr_t)o.Cb & 15) == 0 && (o.mode == kOutBF16 || o.head_dim % 64 == 0)) {
+      rc = tc_make_map(&tc, o.Cb, M, N, N, 64, 32);
+      if (rc) return rc;
+      p.tma_out = 1;
+    }
   }
   static bool attr_set[2] = {false, false};
   if (!attr_set[bn == 128]) {
@@ -601,9 +718,9 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
   const int units = p.tiles_m * p.tiles_n * p.splits;
   const int grid = units < ctx->num_sms ? units : ctx->num_sms;
   if (bn == 256)
-    gemm_bf16_tc_kernel<256><<<grid, NUM_THREADS, TileCfg<256>::SMEM_BYTES, ctx->stream>>>(ta, tb, p);
+    gemm_bf16_tc_kernel<256><<<grid, NUM_THREADS, TileCfg<256>::SMEM_BYTES, ctx->stream>>>(ta, tb, tc, p);
   else
-    gemm_bf16_tc_kernel<128><<<grid, NUM_THREADS, TileCfg<128>::SMEM_BYTES, ctx->stream>>>(ta, tb, p);
+    gemm_bf16_tc_kernel<128><<<grid, NUM_THREADS, TileCfg<128>::SMEM_BYTES, ctx->stream>>>(ta, tb, tc, p);
   FCU_CHECK_LAUNCH();
   if (p.splits > 1) {
     const int64_t pairs = M * ((N + 1) / 2);

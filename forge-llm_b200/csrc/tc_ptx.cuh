@@ -84,6 +84,35 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
       : "memory");
 }
 
+// 2-D TMA store / reduce-add of a shared-memory box to global memory, as a
+// bulk async-group (commit with bulk_commit, reuse the source after
+// bulk_wait_read).  The start coordinates must not be negative.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   (uint64_t)map),
+               "r"(c0), "r"(c1), "r"(smem_u32(src))
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const void *src, int c0, int c1) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+          (uint64_t)map),
+      "r"(c0), "r"(c1), "r"(smem_u32(src))
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Waits until at most N committed bulk groups still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Waits until every committed bulk group has completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -266,5 +295,8 @@ int tc_get_encode();
 int tc_error_word(fcu_ctx *ctx, int **err);
 int tc_make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
                 uint64_t row_stride, uint32_t box_cols, uint32_t box_rows);
+// The same for fp32 (box_cols * 4 == 128).
+int tc_make_map_f32(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                    uint64_t row_stride, uint32_t box_cols, uint32_t box_rows);
 
 }  // namespace fcu

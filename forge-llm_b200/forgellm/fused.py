@@ -75,6 +75,7 @@ class FusedStep:
             L.gu = e(N * 2 * H, dt=BF16)
             L.act = e(N * H, dt=BF16)
             self.layers.append(L)
+        self.br = e(N * D)          # branch output (wo / down GEMM) before its residual add
         self.xL = e(N * D)
         self.invf = e(N)
         self.xf = e(N * D, dt=BF16)
@@ -113,23 +114,37 @@ class FusedStep:
         self.ids = ids
         call("fcu_embed_fwd", h, P["tok_emb"].data.data_ptr(), ids.data_ptr(), N, V, D,
              self.layers[0].x.data_ptr() if c.nLayers else self.xL.data_ptr())
+        eps = float(c.normEps)
+        if c.nLayers:
+            L0 = self.layers[0]
+            call("fcu_rmsnorm_fwd_bf16", h, L0.x.data_ptr(), P["layers"][0]["ln1"].data.data_ptr(), N, D,
+                 eps, L0.xn.data_ptr(), L0.inv1.data_ptr())
+        else:
+            call("fcu_rmsnorm_fwd_bf16", h, self.xL.data_ptr(), P["ln_f"].data.data_ptr(), N, D, eps,
+                 self.xf.data_ptr(), self.invf.data_ptr())
         for l, L in enumerate(self.layers):
             Lp, Lw = P["layers"][l], W["layers"][l]
-            x_next = self.layers[l + 1].x if l + 1 < c.nLayers else self.xL
-            call("fcu_rmsnorm_fwd_bf16", h, L.x.data_ptr(), Lp["ln1"].data.data_ptr(), N, D,
-                 float(c.normEps), L.xn.data_ptr(), L.inv1.data_ptr())
             self._gemm(h, GEMM_FWD, L.xn, Lw["wqkv"], N, c.qkvOut, D, OUT_BF16_ROPE, L.qkv, rope=True)
             call("fcu_attn_fwd_bf16", h, L.qkv.data_ptr(), c.qkvOut, B, T, c.nHeads, c.nKvHeads,
                  c.dHead, L.o.data_ptr(), L.lse.data_ptr())
-            self._gemm(h, GEMM_FWD, L.o, Lw["wo"], N, D, qD, OUT_F32_RESIDUAL, L.x1, residual=L.x)
-            call("fcu_rmsnorm_fwd_bf16", h, L.x1.data_ptr(), Lp["ln2"].data.data_ptr(), N, D,
-                 float(c.normEps), L.xn2.data_ptr(), L.inv2.data_ptr())
+            # x1 = x + o.wo^T, added inside the ln2 normalisation
+            self._gemm(h, GEMM_FWD, L.o, Lw["wo"], N, D, qD, OUT_F32, self.br)
+            call("fcu_rmsnorm_fwd_bf16_add", h, L.x.data_ptr(), self.br.data_ptr(),
+                 Lp["ln2"].data.data_ptr(), N, D, eps, L.x1.data_ptr(), L.xn2.data_ptr(),
+                 L.inv2.data_ptr())
             self._gemm(h, GEMM_FWD, L.xn2, Lw["ffn_gu"], N, 2 * H, D, OUT_BF16, L.gu)
             call("fcu_swiglu_fwd_bf16", h, L.gu.data_ptr(), N, H, L.act.data_ptr())
-            self._gemm(h, GEMM_FWD, L.act, Lw["ffn_down"], N, D, H, OUT_F32_RESIDUAL, x_next,
-                       residual=L.x1)
-        call("fcu_rmsnorm_fwd_bf16", h, self.xL.data_ptr(), P["ln_f"].data.data_ptr(), N, D,
-             float(c.normEps), self.xf.data_ptr(), self.invf.data_ptr())
+            # x_next = x1 + act.down^T, added inside the next ln1 (or ln_f)
+            self._gemm(h, GEMM_FWD, L.act, Lw["ffn_down"], N, D, H, OUT_F32, self.br)
+            if l + 1 < c.nLayers:
+                Ln = self.layers[l + 1]
+                call("fcu_rmsnorm_fwd_bf16_add", h, L.x1.data_ptr(), self.br.data_ptr(),
+                     P["layers"][l + 1]["ln1"].data.data_ptr(), N, D, eps, Ln.x.data_ptr(),
+                     Ln.xn.data_ptr(), Ln.inv1.data_ptr())
+            else:
+                call("fcu_rmsnorm_fwd_bf16_add", h, L.x1.data_ptr(), self.br.data_ptr(),
+                     P["ln_f"].data.data_ptr(), N, D, eps, self.xL.data_ptr(), self.xf.data_ptr(),
+                     self.invf.data_ptr())
         self._gemm(h, GEMM_FWD, self.xf, W["tok_emb"], N, V, D, OUT_F32, self.logits)
         call("fcu_ce_fwd_bf16grad", h, self.logits.data_ptr(), targets.data_ptr(), N, V,
              self.loss.data_ptr(), self.dlogits.data_ptr())

@@ -123,6 +123,13 @@ int fcu_gemm_bf16(fcu_ctx *ctx, int op, const void *A, const void *B, int64_t M,
  * inv[T].  D % 4 == 0. */
 int fcu_rmsnorm_fwd_bf16(fcu_ctx *ctx, const float *X, const float *w, int64_t T, int64_t D,
                          double eps, void *out_bf16, float *inv);
+
+// Residual add fused into the next normalisation: Xout = X + A (fp32; the
+// residual stream plus the branch output a GEMM wrote), then out / inv as
+// fcu_rmsnorm_fwd_bf16 computes them from Xout.  D a multiple of 4.  Replaces an `addTensors(x, branch)` + `rmsNorm(x)` pair of the
+// block (src/L6/train.js:145-147, 153 with the next block's :130 or :156).
+int fcu_rmsnorm_fwd_bf16_add(fcu_ctx *ctx, const float *X, const float *A, const float *w, int64_t T,
+                             int64_t D, double eps, float *Xout, void *out, float *inv);
 /* rmsNorm backward (src/L2/tensor.js:114-127) fused with the residual
  * gradient: dX (+)= the rmsNorm input gradient (fp32, in place); if dX_bf16
  * is not NULL it receives bf16 of the final dX (the next GEMM's operand);

@@ -121,3 +121,27 @@ def test_fused_overfit_I71():
         last = m.backward(m.loss(data, data[1:]))
         opt.step()
     assert last < first * 0.6 and last < 0.05, (first, last)
+
+
+@pytest.mark.parametrize("T,D", [(1000, 768), (257, 100), (64, 1024)])
+def test_rmsnorm_fwd_bf16_add(T, D):
+    """Residual add fused into the normalisation: Xout is exactly X + A
+    (fp32), inv and the bf16 output follow from Xout."""
+    from forgellm import _lib
+    from forgellm.autograd import ctx
+    g = torch.Generator(device="cuda").manual_seed(T + D)
+    X = torch.randn(T, D, device="cuda", generator=g)
+    A = torch.randn(T, D, device="cuda", generator=g)
+    w = torch.randn(D, device="cuda", generator=g)
+    Xout = torch.empty(T, D, device="cuda")
+    out = torch.empty(T, D, device="cuda", dtype=torch.bfloat16)
+    inv = torch.empty(T, device="cuda")
+    _lib.call("fcu_rmsnorm_fwd_bf16_add", ctx().handle, X.data_ptr(), A.data_ptr(), w.data_ptr(), T, D,
+              1e-5, Xout.data_ptr(), out.data_ptr(), inv.data_ptr())
+    torch.cuda.synchronize()
+    assert torch.equal(Xout, X + A)
+    x = Xout.double()
+    iv = 1.0 / torch.sqrt((x * x).mean(1) + 1e-5)
+    assert float(((inv.double() - iv).abs() / iv).max()) <= 1e-5
+    ref = x * iv[:, None] * w.double()[None, :]
+    assert float(((out.double() - ref).abs() - 2 ** -8 * ref.abs()).max()) <= 1e-6

@@ -118,10 +118,13 @@ def test_tc_repeated_calls_are_deterministic():
                                       (0, 300, 520, 768),      # no split, ragged tiles
                                       (2, 256, 128, 8192),     # dW layout, split-K
                                       (1, 200, 256, 4096)])    # dX layout, split-K
-@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+@pytest.mark.parametrize("mode", [0, 1, 2, 3, 4])
 def test_gemm_bf16_output_modes(op, M, N, K, mode):
-    """Every epilogue (fp32 / fp32 + residual / bf16 / bf16 + RoPE), with and
-    without split-K, against a float64 product of the same bf16 operands."""
+    """Every epilogue (fp32 / fp32 + residual / bf16 / bf16 + RoPE, and fp32
+    accumulating into the output as mode 4), with and without split-K,
+    against a float64 product of the same bf16 operands."""
+    accumulate = 1 if mode == 4 else 0
+    mode = 0 if mode == 4 else mode
     import ctypes
     from forgellm import _lib
     from forgellm.autograd import ctx
@@ -139,14 +142,19 @@ def test_gemm_bf16_output_modes(op, M, N, K, mode):
         ref = Ad.view(K, M).T @ Bd.view(K, N)
     R = torch.randn(M * N, device="cuda", generator=g)
     out = torch.zeros(M * N, device="cuda", dtype=torch.float32 if mode < 2 else torch.bfloat16)
+    if accumulate:
+        out.normal_(generator=g)
+    out0 = out.double().cpu().view(M, N)
     T_rope, hd, rc = 64, 64, 128
-    o = _lib.GemmOut(mode, out.data_ptr(), 0, R.data_ptr() if mode == 1 else None,
+    o = _lib.GemmOut(mode, out.data_ptr(), accumulate, R.data_ptr() if mode == 1 else None,
                      T_rope if mode == 3 else 0, rc if mode == 3 else 0, hd if mode == 3 else 0,
                      10000.0 if mode == 3 else 0.0)
     _lib.call("fcu_gemm_bf16", ctx().handle, op, A.data_ptr(), B.data_ptr(), M, N, K, ctypes.byref(o))
     torch.cuda.synchronize()
     device_ok()
     want = ref.clone()
+    if accumulate:
+        want += out0
     if mode == 1:
         want += R.double().cpu().view(M, N)
     if mode == 3:
