@@ -4,7 +4,7 @@
 //
 // Forward, per CTA: one 128-row query tile of one head, looping over the
 // 128-key blocks at or before its diagonal.
-//   warp 0      TMA: Q once, then a 2-deep ring of (K, V) blocks
+//   warp 0      TMA: Q once, then a 3-deep ring of (K, V) blocks
 //   warp 1      TMEM owner + MMA issuer (one thread):
 //                 S_j = Q K_j^T        128x128x64  -> TMEM cols [0, 128)
 //                 O  += P_j V_j        128x64x128  -> TMEM cols [128, 192)
@@ -12,9 +12,9 @@
 //               score tile is computed while the softmax works on this one
 //   warps 2..5  softmax: thread = query row = TMEM lane.  Reads its S row,
 //               applies the causal mask, keeps the running max / sum, writes
-//               P = exp2(S*scale*log2e - m) as bf16 into shared memory in the
-//               128B-swizzled K-major layout the PV MMA reads, and at the end
-//               normalises O and stores it with the log-sum-exp.
+//               P = exp2(S*scale*log2e - m) as bf16 pairs into TMEM (cols
+//               [192, 256)), where the PV MMA reads it as its A operand, and
+//               at the end normalises O and stores it with the log-sum-exp.
 // The running max used for P is only moved when the block max exceeds it by
 // more than 2^8: P then stays <= 256, and O (in TMEM) and the row sum are
 // rescaled rarely, by the same factor, so O / l is unchanged.
@@ -36,17 +36,17 @@ constexpr int kBN = 128;                       // keys per block
 constexpr int kD = 64;                         // head dim
 constexpr int kTile = kBM * kD * 2;            // one [128][64] bf16 tile: 16 KB
 constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 256;            // S [0,128), O [128,192)
+constexpr uint32_t kTmemCols = 256;            // S [0,128), O [128,192), P [192,256) (bf16 pairs)
+constexpr int kFwdStages = 3;                  // K/V ring depth
 constexpr float kRescaleLog2 = 8.f;
 constexpr float kLog2e = 1.4426950408889634f;
 
 // Shared memory map (byte offsets; tiles 1024-byte aligned for the swizzle).
 constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTile;           // 2 stages
-constexpr int kOffV = kOffK + 2 * kTile;       // 2 stages
-constexpr int kOffP = kOffV + 2 * kTile;       // 2 halves (keys 0-63, 64-127)
-constexpr int kOffBar = kOffP + 2 * kTile;
-constexpr int kSmemBytes = kOffBar + 16 * 8 + 16;
+constexpr int kOffK = kOffQ + kTile;           // kFwdStages tiles
+constexpr int kOffV = kOffK + kFwdStages * kTile;
+constexpr int kOffBar = kOffV + kFwdStages * kTile;
+constexpr int kSmemBytes = kOffBar + (6 + 4 * kFwdStages) * 8 + 16;
 
 struct FwdParams {
   int B, T, nH, nKV, n_qt;
@@ -59,14 +59,15 @@ struct FwdParams {
 __global__ void __launch_bounds__(kThreads, 2)
     attn_fwd_tmem_kernel(const __grid_constant__ CUtensorMap tm, FwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  uint8_t *sQ = smem + kOffQ, *sK = smem + kOffK, *sV = smem + kOffV, *sP = smem + kOffP;
+  uint8_t *sQ = smem + kOffQ, *sK = smem + kOffK, *sV = smem + kOffV;
   uint64_t *bars = (uint64_t *)(smem + kOffBar);
+  constexpr int S = kFwdStages;
   uint64_t *q_full = bars + 0;
-  uint64_t *k_full = bars + 1, *k_empty = bars + 3;   // [2] each
-  uint64_t *v_full = bars + 5, *v_empty = bars + 7;   // [2] each
-  uint64_t *s_full = bars + 9, *s_free = bars + 10;
-  uint64_t *p_full = bars + 11, *o_done = bars + 12, *mma_done = bars + 13;
-  uint32_t *tmem_slot = (uint32_t *)(bars + 14);
+  uint64_t *k_full = bars + 1, *k_empty = bars + 1 + S;         // [S] each
+  uint64_t *v_full = bars + 1 + 2 * S, *v_empty = bars + 1 + 3 * S;
+  uint64_t *s_full = bars + 1 + 4 * S, *s_free = s_full + 1;
+  uint64_t *p_full = s_full + 2, *o_done = s_full + 3, *mma_done = s_full + 4;
+  uint32_t *tmem_slot = (uint32_t *)(s_full + 5);
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -83,7 +84,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < 2; s++) {
+    for (int s = 0; s < S; s++) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
@@ -103,7 +104,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 128;
+  const uint32_t tS = tmem, tO = tmem + 128, tP = tmem + 192;
 
   if (!aligned) {
     // nothing issued; fall through to the dealloc
@@ -114,8 +115,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_expect_tx(q_full, kTile);
     tma_load_2d(sQ, &tm, h * kD, row0 + q0, q_full);
     for (int j = 0; j < nkv; j++) {
-      const int s = j & 1;
-      const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+      const int s = j % S;
+      const uint32_t ph = (uint32_t)(j / S) & 1u;
       if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
       mbar_expect_tx(&k_full[s], kTile);
       tma_load_2d(sK + s * kTile, &tm, (p.nH + kvh) * kD, row0 + j * kBN, &k_full[s]);
@@ -131,40 +132,41 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     // Every copy issued has landed before the CTA exits.
     mbar_wait_drain(q_full, 0);
-    for (int i = nk - 2 < 0 ? 0 : nk - 2; i < nk; i++) mbar_wait_drain(&k_full[i & 1], (uint32_t)(i >> 1) & 1u);
-    for (int i = nv - 2 < 0 ? 0 : nv - 2; i < nv; i++) mbar_wait_drain(&v_full[i & 1], (uint32_t)(i >> 1) & 1u);
+    for (int i = nk - S < 0 ? 0 : nk - S; i < nk; i++) mbar_wait_drain(&k_full[i % S], (uint32_t)(i / S) & 1u);
+    for (int i = nv - S < 0 ? 0 : nv - S; i < nv; i++) mbar_wait_drain(&v_full[i % S], (uint32_t)(i / S) & 1u);
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer
     const uint32_t id_s = instr_desc_bf16(0, 0, kBM, kBN);   // Q, K both K-major
     const uint32_t id_o = instr_desc_bf16(0, 1, kBM, kD);    // P K-major, V MN-major
     bool ok = mbar_wait(q_full, 0, abort_flag);
-    const uint32_t aq = smem_u32(sQ), ap = smem_u32(sP);
+    const uint64_t dQ = desc_k(smem_u32(sQ));
+    const uint64_t dK0 = desc_k(smem_u32(sK)), dV0 = desc_mn(smem_u32(sV), kBN);
+    constexpr uint64_t kTileStep = kTile >> 4;
     for (int j = 0; j <= nkv && ok; j++) {
       if (j < nkv) {
-        const int s = j & 1;
-        if (!mbar_wait(&k_full[s], (uint32_t)(j >> 1) & 1u, abort_flag)) { ok = false; break; }
+        const int s = j % S;
+        if (!mbar_wait(&k_full[s], (uint32_t)(j / S) & 1u, abort_flag)) { ok = false; break; }
         if (j > 0 && !mbar_wait(s_free, (uint32_t)(j - 1) & 1u, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t bk = smem_u32(sK + s * kTile);
+        const uint64_t dK = dK0 + (uint64_t)s * kTileStep;
 #pragma unroll
         for (int k = 0; k < kD / 16; k++)
-          umma_bf16(tS, operand_desc(aq, k, 0, kD), operand_desc(bk, k, 0, kD), id_s, k > 0 ? 1u : 0u);
+          umma_bf16(tS, dQ + k * kDescKStep, dK + k * kDescKStep, id_s, k > 0 ? 1u : 0u);
         umma_commit(s_full);
         umma_commit(&k_empty[s]);
       }
       if (j > 0) {
-        const int i = j - 1, s = i & 1;
-        if (!mbar_wait(&v_full[s], (uint32_t)(i >> 1) & 1u, abort_flag) ||
+        const int i = j - 1, s = i % S;
+        if (!mbar_wait(&v_full[s], (uint32_t)(i / S) & 1u, abort_flag) ||
             !mbar_wait(p_full, (uint32_t)i & 1u, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t bv = smem_u32(sV + s * kTile);
+        const uint64_t dV = dV0 + (uint64_t)s * kTileStep;
 #pragma unroll
         for (int k = 0; k < kBN / 16; k++)
-          umma_bf16(tO, operand_desc(ap + (uint32_t)(k >> 2) * kTile, k & 3, 0, kD),
-                    operand_desc(bv, k, 1, kBN), id_o, (i > 0 || k > 0) ? 1u : 0u);
+          umma_bf16_ts(tO, tP + (uint32_t)(8 * k), dV + k * kDescMNStep, id_o, (i > 0 || k > 0) ? 1u : 0u);
         umma_commit(o_done);
         umma_commit(&v_empty[s]);
       }
@@ -214,28 +216,21 @@ __global__ void __launch_bounds__(kThreads, 2)
         m = mx;
       }
       const float neg_m = -m;
-      float rs8[8];
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[kBN / 2];                     // P as bf16 pairs
 #pragma unroll
-      for (int u = 0; u < 8; u++) rs8[u] = 0.f;
-#pragma unroll
-      for (int c = 0; c < kBN; c++) {
-        const float e = ex2_ftz(fmaf(s[c], p.scale_log2, neg_m));
-        s[c] = e;
-        rs8[c & 7] += e;
+      for (int c = 0; c < kBN; c += 2) {
+        const float e0 = ex2_ftz(fmaf(s[c], p.scale_log2, neg_m));
+        const float e1 = ex2_ftz(fmaf(s[c + 1], p.scale_log2, neg_m));
+        rs4[(c >> 1) & 3] += e0 + e1;
+        pk[c / 2] = pack2_bf16(e0, e1);
       }
-      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+      const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       l = l * alpha + rs;
       // PV_{j-1} must be done with P and O before P is overwritten / O rescaled.
       if (j > 0 && !warp_wait(o_done, (uint32_t)(j - 1) & 1u, abort_flag)) { ok = false; break; }
-#pragma unroll
-      for (int c8 = 0; c8 < kBN / 8; c8++) {
-        uint4 v;
-        v.x = pack2_bf16(s[8 * c8 + 0], s[8 * c8 + 1]);
-        v.y = pack2_bf16(s[8 * c8 + 2], s[8 * c8 + 3]);
-        v.z = pack2_bf16(s[8 * c8 + 4], s[8 * c8 + 5]);
-        v.w = pack2_bf16(s[8 * c8 + 6], s[8 * c8 + 7]);
-        *reinterpret_cast<uint4 *>(sP + (c8 >> 3) * kTile + sw128_offset(r, c8 & 7)) = v;
-      }
+      tmem_st32(tP + lane_addr, pk);
+      tmem_st32(tP + lane_addr + 32, pk + 32);
       if (__any_sync(0xffffffffu, rescale_o)) {   // warp-collective: alpha = 1 on other rows
         tc_fence_after();
 #pragma unroll
@@ -246,9 +241,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int c = 0; c < 32; c++) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
           tmem_st32(tO + lane_addr + half * 32, o);
         }
-        tmem_wait_st();
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
@@ -294,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 // dK/dV, per CTA one 128-key tile of one kv head (or, head-split, of one q
 // head), looping over the query tiles at or after it of every q head of the
 // GQA group:
-//   warp 0      TMA: K, V once; a 3-deep ring of (Q, dO) tiles plus the
+//   warp 0      TMA: K, V once; a 5-deep ring of (Q, dO) tiles plus the
 //               tile's log-sum-exp and delta = rowsum(dO * O) rows
 //   warp 1      MMA (one thread):  S^T = K Q^T, dP^T = V dO^T (128x128x64,
 //               TMEM cols [0,128), [128,256)), then for the previous tile
@@ -302,14 +296,16 @@ __global__ void __launch_bounds__(kThreads, 2)
 //               [320,384))
 //   warps 2..9  thread = key row, two warps per TMEM lane quarter splitting
 //               the 128 query columns: P^T = exp2(S^T c - L), dS^T =
-//               P^T (dP^T - delta), both to shared memory as bf16 K-major
-//               tiles; at the end dV, and dK * scale rotated back by RoPE.
+//               P^T (dP^T - delta), both into TMEM as bf16 pairs (cols
+//               [384,448), [448,512)), the A operands of the dV / dK MMAs;
+//               at the end dV, and dK * scale rotated back by RoPE.
 // dQ, per CTA one 128-row query tile of one q head, looping over the key
-// tiles at or before it: S = Q K^T, dP = dO V^T, dS = P (dP - delta),
-// dQ += dS K; at the end dQ * scale rotated back by RoPE.
+// tiles at or before it: S = Q K^T, dP = dO V^T, dS = P (dP - delta) (into
+// TMEM cols [320,384) as the A operand), dQ += dS K; at the end dQ * scale
+// rotated back by RoPE.
 constexpr int kBwdThreads = 320;
 constexpr uint32_t kBwdTmemCols = 512;
-constexpr int kStages = 3;
+constexpr int kStages = 5;                   // Q/dO (dK/dV) and K/V (dQ) ring depth
 
 struct BwdParams {
   int B, T, nH, nKV, n_t, group, split;
@@ -327,30 +323,18 @@ constexpr int kKV_K = 0;
 constexpr int kKV_V = kKV_K + kTile;
 constexpr int kKV_Q = kKV_V + kTile;                  // kStages tiles
 constexpr int kKV_G = kKV_Q + kStages * kTile;        // kStages tiles (dO)
-constexpr int kKV_P = kKV_G + kStages * kTile;        // P^T, 2 halves
-constexpr int kKV_S = kKV_P + 2 * kTile;              // dS^T, 2 halves
-constexpr int kKV_L = kKV_S + 2 * kTile;              // [kStages][128] f32
+constexpr int kKV_L = kKV_G + kStages * kTile;        // [kStages][128] f32
 constexpr int kKV_D = kKV_L + kStages * 128 * 4;      // [kStages][128] f32
 constexpr int kKV_Bar = kKV_D + kStages * 128 * 4;
-constexpr int kKVSmem = kKV_Bar + 16 * 8 + 16;
+constexpr int kKVSmem = kKV_Bar + (7 + 2 * kStages) * 8 + 16;
 
 // dQ kernel shared memory
 constexpr int kQ_Q = 0;
 constexpr int kQ_G = kQ_Q + kTile;
 constexpr int kQ_K = kQ_G + kTile;                    // kStages tiles
 constexpr int kQ_V = kQ_K + kStages * kTile;          // kStages tiles
-constexpr int kQ_S = kQ_V + kStages * kTile;          // dS, 2 halves
-constexpr int kQ_Bar = kQ_S + 2 * kTile;
-constexpr int kQSmem = kQ_Bar + 16 * 8 + 16;
-
-// Stores 64 consecutive bf16 pairs' worth of packed values (one 128-byte
-// row half) into a K-major swizzled tile at row r.
-__device__ __forceinline__ void store_row_half(uint8_t *tile, int r, const uint32_t (&v)[32]) {
-#pragma unroll
-  for (int c8 = 0; c8 < 8; c8++)
-    *reinterpret_cast<uint4 *>(tile + sw128_offset(r, c8)) =
-        make_uint4(v[4 * c8], v[4 * c8 + 1], v[4 * c8 + 2], v[4 * c8 + 3]);
-}
+constexpr int kQ_Bar = kQ_V + kStages * kTile;
+constexpr int kQSmem = kQ_Bar + (7 + 2 * kStages) * 8 + 16;
 
 // Rotates interleaved pairs back by R^T: (x, y) -> (x c + y s, -x s + y c).
 __device__ __forceinline__ void rope_back(float &x, float &y, float2 cs) {
@@ -364,13 +348,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                               const __grid_constant__ CUtensorMap tm_do, BwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t *sK = smem + kKV_K, *sV = smem + kKV_V, *sQ = smem + kKV_Q, *sG = smem + kKV_G;
-  uint8_t *sPt = smem + kKV_P, *sDt = smem + kKV_S;
   float *sL = (float *)(smem + kKV_L), *sDl = (float *)(smem + kKV_D);
   uint64_t *bars = (uint64_t *)(smem + kKV_Bar);
-  uint64_t *kv_full = bars, *q_full = bars + 1, *q_empty = bars + 4;   // q_*: [kStages]
-  uint64_t *st_full = bars + 7, *st_free = bars + 8, *pds_full = bars + 9, *pds_free = bars + 10;
-  uint64_t *acc_done = bars + 11, *mma_done = bars + 12;
-  uint32_t *tmem_slot = (uint32_t *)(bars + 13);
+  uint64_t *kv_full = bars, *q_full = bars + 1, *q_empty = bars + 1 + kStages;   // q_*: [kStages]
+  uint64_t *st_full = bars + 1 + 2 * kStages, *st_free = st_full + 1, *pds_full = st_full + 2;
+  uint64_t *pds_free = st_full + 3, *acc_done = st_full + 4, *mma_done = st_full + 5;
+  uint32_t *tmem_slot = (uint32_t *)(st_full + 6);
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -392,7 +375,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     for (int s = 0; s < kStages; s++) {
-      mbar_init(&q_full[s], 1);
+      mbar_init(&q_full[s], 2);               // TMA bytes + lse / delta staged
       mbar_init(&q_empty[s], 1);
     }
     mbar_init(st_full, 1);
@@ -411,6 +394,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 320;
+  const uint32_t tPt = tmem + 384, tDt = tmem + 448;   // P^T, dS^T as bf16 pairs
 
   if (!aligned) {
   } else if (warp == 0) {
@@ -430,6 +414,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       const int h = h_begin + it / per_head;
       const int q0 = (kt + it % per_head) * kBM;
+      if (lane == 0) {                        // copies first: their latency overlaps the loads below
+        mbar_expect_tx(&q_full[s], 2 * kTile);
+        tma_load_2d(sQ + s * kTile, &tm_qkv, h * kD, row0 + q0, &q_full[s]);
+        tma_load_2d(sG + s * kTile, &tm_do, h * kD, row0 + q0, &q_full[s]);
+      }
+      issued++;
       const int64_t lrow = ((int64_t)b * p.nH + h) * p.T;
 #pragma unroll
       for (int e = lane; e < kBM; e += 32) {
@@ -438,12 +428,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         sDl[s * kBM + e] = q < p.T ? p.delta[lrow + q] : 0.f;
       }
       __syncwarp();
-      if (lane == 0) {
-        mbar_expect_tx(&q_full[s], 2 * kTile);
-        tma_load_2d(sQ + s * kTile, &tm_qkv, h * kD, row0 + q0, &q_full[s]);
-        tma_load_2d(sG + s * kTile, &tm_do, h * kD, row0 + q0, &q_full[s]);
-      }
-      issued++;
+      if (lane == 0) mbar_arrive(&q_full[s]);
     }
     if (lane == 0) {
       if (!ok) {
@@ -460,7 +445,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t id_n128 = instr_desc_bf16(0, 0, kBM, kBN);
       const uint32_t id_n64 = instr_desc_bf16(0, 1, kBM, kD);
       bool ok = mbar_wait(kv_full, 0, abort_flag);
-      const uint32_t ak = smem_u32(sK), av = smem_u32(sV), ap = smem_u32(sPt), ad = smem_u32(sDt);
+      const uint64_t dK = desc_k(smem_u32(sK)), dV = desc_k(smem_u32(sV));
+      const uint64_t dQk0 = desc_k(smem_u32(sQ)), dGk0 = desc_k(smem_u32(sG));
+      const uint64_t dQm0 = desc_mn(smem_u32(sQ), kBM), dGm0 = desc_mn(smem_u32(sG), kBM);
+      constexpr uint64_t kTileStep = kTile >> 4;
       for (int it = 0; it <= n_iter && ok; it++) {
         if (it < n_iter) {
           const int s = it % kStages;
@@ -470,13 +458,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t bq = smem_u32(sQ + s * kTile), bg = smem_u32(sG + s * kTile);
+          const uint64_t bq = dQk0 + (uint64_t)s * kTileStep, bg = dGk0 + (uint64_t)s * kTileStep;
 #pragma unroll
           for (int k = 0; k < kD / 16; k++)
-            umma_bf16(tS, operand_desc(ak, k, 0, kD), operand_desc(bq, k, 0, kD), id_n128, k > 0 ? 1u : 0u);
+            umma_bf16(tS, dK + k * kDescKStep, bq + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
 #pragma unroll
           for (int k = 0; k < kD / 16; k++)
-            umma_bf16(tdP, operand_desc(av, k, 0, kD), operand_desc(bg, k, 0, kD), id_n128, k > 0 ? 1u : 0u);
+            umma_bf16(tdP, dV + k * kDescKStep, bg + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
           umma_commit(st_full);
         }
         if (it > 0) {
@@ -486,15 +474,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t bq = smem_u32(sQ + s * kTile), bg = smem_u32(sG + s * kTile);
+          const uint64_t bq = dQm0 + (uint64_t)s * kTileStep, bg = dGm0 + (uint64_t)s * kTileStep;
 #pragma unroll
           for (int k = 0; k < kBM / 16; k++)
-            umma_bf16(tdV, operand_desc(ap + (uint32_t)(k >> 2) * kTile, k & 3, 0, kD),
-                      operand_desc(bg, k, 1, kBM), id_n64, (i > 0 || k > 0) ? 1u : 0u);
+            umma_bf16_ts(tdV, tPt + (uint32_t)(8 * k), bg + k * kDescMNStep, id_n64, (i > 0 || k > 0) ? 1u : 0u);
 #pragma unroll
           for (int k = 0; k < kBM / 16; k++)
-            umma_bf16(tdK, operand_desc(ad + (uint32_t)(k >> 2) * kTile, k & 3, 0, kD),
-                      operand_desc(bq, k, 1, kBM), id_n64, (i > 0 || k > 0) ? 1u : 0u);
+            umma_bf16_ts(tdK, tDt + (uint32_t)(8 * k), bq + k * kDescMNStep, id_n64, (i > 0 || k > 0) ? 1u : 0u);
           umma_commit(pds_free);
           umma_commit(&q_empty[s]);
         }
@@ -526,35 +512,41 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tc_fence_after();
       float sv[64], dp[64];
-      tmem_ld64(tS + la + cb, sv);
-      tmem_ld64(tdP + la + cb, dp);
+      tmem_ld64x2(tS + la + cb, tdP + la + cb, sv, dp);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(st_free);
-      const float *L = sL + s * kBM + cb, *Dl = sDl + s * kBM + cb;
+      const float4 *L4 = reinterpret_cast<const float4 *>(sL + s * kBM + cb);
+      const float4 *D4 = reinterpret_cast<const float4 *>(sDl + s * kBM + cb);
       const int qc = q0 + cb;                   // first query of these columns
       const bool mask = qc < key || qc + 64 > p.T;
       uint32_t pp[32], dd[32];
 #pragma unroll
-      for (int c = 0; c < 32; c++) {
-        float p0 = ex2_ftz(fmaf(sv[2 * c], p.scale_log2, -L[2 * c]));
-        float p1 = ex2_ftz(fmaf(sv[2 * c + 1], p.scale_log2, -L[2 * c + 1]));
-        if (mask) {
-          const int q = qc + 2 * c;
-          if (q < key || q >= p.T) p0 = 0.f;
-          if (q + 1 < key || q + 1 >= p.T) p1 = 0.f;
+      for (int c4 = 0; c4 < 16; c4++) {
+        const float4 l4 = L4[c4], d4 = D4[c4];
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
+        float pr[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          pr[u] = ex2_ftz(fmaf(sv[4 * c4 + u], p.scale_log2, -lv[u]));
+          if (mask) {
+            const int q = qc + 4 * c4 + u;
+            if (q < key || q >= p.T) pr[u] = 0.f;
+          }
         }
-        pp[c] = pack2_bf16(p0, p1);
-        dd[c] = pack2_bf16(p0 * (dp[2 * c] - Dl[2 * c]), p1 * (dp[2 * c + 1] - Dl[2 * c + 1]));
+        pp[2 * c4] = pack2_bf16(pr[0], pr[1]);
+        pp[2 * c4 + 1] = pack2_bf16(pr[2], pr[3]);
+        dd[2 * c4] = pack2_bf16(pr[0] * (dp[4 * c4] - dv[0]), pr[1] * (dp[4 * c4 + 1] - dv[1]));
+        dd[2 * c4 + 1] = pack2_bf16(pr[2] * (dp[4 * c4 + 2] - dv[2]), pr[3] * (dp[4 * c4 + 3] - dv[3]));
       }
       // dV/dK of the previous tile must be done reading P^T / dS^T.
       if (it > 0 && !warp_wait(pds_free, (uint32_t)(it - 1) & 1u, abort_flag)) {
         ok = false;
         break;
       }
-      store_row_half(sPt + half * kTile, r, pp);
-      store_row_half(sDt + half * kTile, r, dd);
-      fence_proxy_async_smem();
+      tmem_st32(tPt + la + (uint32_t)(32 * half), pp);
+      tmem_st32(tDt + la + (uint32_t)(32 * half), dd);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(pds_full);
@@ -607,12 +599,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                             const __grid_constant__ CUtensorMap tm_do, BwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t *sQ = smem + kQ_Q, *sG = smem + kQ_G, *sK = smem + kQ_K, *sV = smem + kQ_V;
-  uint8_t *sDs = smem + kQ_S;
   uint64_t *bars = (uint64_t *)(smem + kQ_Bar);
-  uint64_t *qg_full = bars, *kv_full = bars + 1, *kv_empty = bars + 4;   // kv_*: [kStages]
-  uint64_t *sp_full = bars + 7, *sp_free = bars + 8, *ds_full = bars + 9, *ds_free = bars + 10;
-  uint64_t *acc_done = bars + 11, *mma_done = bars + 12;
-  uint32_t *tmem_slot = (uint32_t *)(bars + 13);
+  uint64_t *qg_full = bars, *kv_full = bars + 1, *kv_empty = bars + 1 + kStages;   // kv_*: [kStages]
+  uint64_t *sp_full = bars + 1 + 2 * kStages, *sp_free = sp_full + 1, *ds_full = sp_full + 2;
+  uint64_t *ds_free = sp_full + 3, *acc_done = sp_full + 4, *mma_done = sp_full + 5;
+  uint32_t *tmem_slot = (uint32_t *)(sp_full + 6);
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -647,7 +638,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tdP = tmem + 128, tdQ = tmem + 256;
+  const uint32_t tS = tmem, tdP = tmem + 128, tdQ = tmem + 256, tdS = tmem + 320;
 
   if (!aligned) {
   } else if (warp == 0) {
@@ -683,7 +674,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t id_n128 = instr_desc_bf16(0, 0, kBM, kBN);
       const uint32_t id_n64 = instr_desc_bf16(0, 1, kBM, kD);
       bool ok = mbar_wait(qg_full, 0, abort_flag);
-      const uint32_t aq = smem_u32(sQ), ag = smem_u32(sG), ads = smem_u32(sDs);
+      const uint64_t dQ = desc_k(smem_u32(sQ)), dG = desc_k(smem_u32(sG));
+      const uint64_t dKk0 = desc_k(smem_u32(sK)), dVk0 = desc_k(smem_u32(sV));
+      const uint64_t dKm0 = desc_mn(smem_u32(sK), kBN);
+      constexpr uint64_t kTileStep = kTile >> 4;
       for (int j = 0; j <= nkv && ok; j++) {
         if (j < nkv) {
           const int s = j % kStages;
@@ -693,13 +687,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t bk = smem_u32(sK + s * kTile), bv = smem_u32(sV + s * kTile);
+          const uint64_t bk = dKk0 + (uint64_t)s * kTileStep, bv = dVk0 + (uint64_t)s * kTileStep;
 #pragma unroll
           for (int k = 0; k < kD / 16; k++)
-            umma_bf16(tS, operand_desc(aq, k, 0, kD), operand_desc(bk, k, 0, kD), id_n128, k > 0 ? 1u : 0u);
+            umma_bf16(tS, dQ + k * kDescKStep, bk + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
 #pragma unroll
           for (int k = 0; k < kD / 16; k++)
-            umma_bf16(tdP, operand_desc(ag, k, 0, kD), operand_desc(bv, k, 0, kD), id_n128, k > 0 ? 1u : 0u);
+            umma_bf16(tdP, dG + k * kDescKStep, bv + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
           umma_commit(sp_full);
         }
         if (j > 0) {
@@ -709,11 +703,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t bk = smem_u32(sK + s * kTile);
+          const uint64_t bk = dKm0 + (uint64_t)s * kTileStep;
 #pragma unroll
           for (int k = 0; k < kBN / 16; k++)
-            umma_bf16(tdQ, operand_desc(ads + (uint32_t)(k >> 2) * kTile, k & 3, 0, kD),
-                      operand_desc(bk, k, 1, kBN), id_n64, (i > 0 || k > 0) ? 1u : 0u);
+            umma_bf16_ts(tdQ, tdS + (uint32_t)(8 * k), bk + k * kDescMNStep, id_n64, (i > 0 || k > 0) ? 1u : 0u);
           umma_commit(ds_free);
           umma_commit(&kv_empty[s]);
         }
@@ -745,8 +738,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tc_fence_after();
       float sv[64], dp[64];
-      tmem_ld64(tS + la + cb, sv);
-      tmem_ld64(tdP + la + cb, dp);
+      tmem_ld64x2(tS + la + cb, tdP + la + cb, sv, dp);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(sp_free);
@@ -764,8 +756,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         ok = false;
         break;
       }
-      store_row_half(sDs + half * kTile, r, dd);
-      fence_proxy_async_smem();
+      tmem_st32(tdS + la + (uint32_t)(32 * half), dd);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_full);

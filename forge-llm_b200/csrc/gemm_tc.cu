@@ -260,6 +260,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer
     const uint32_t idesc = instr_desc_bf16(p.a_mn, p.b_mn, BM, BN);
+    const uint64_t dA0 = p.a_mn ? desc_mn(smem_u32(sA), BK) : desc_k(smem_u32(sA));
+    const uint64_t dB0 = p.b_mn ? desc_mn(smem_u32(sB), BK) : desc_k(smem_u32(sB));
+    const uint64_t kA = p.a_mn ? kDescMNStep : kDescKStep, kB = p.b_mn ? kDescMNStep : kDescKStep;
     int it = 0, ti = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ti++) {
@@ -282,12 +285,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t a = smem_u32(sA + s * A_BYTES);
-        const uint32_t b = smem_u32(sB + s * B_BYTES);
+        const uint64_t a = dA0 + (uint64_t)s * (A_BYTES >> 4);
+        const uint64_t b = dB0 + (uint64_t)s * (B_BYTES >> 4);
 #pragma unroll
         for (int k = 0; k < BK / UMMA_K; k++)
-          umma_bf16(d_tmem, operand_desc(a, k, p.a_mn, BK), operand_desc(b, k, p.b_mn, BK), idesc,
-                    (kb != kb0 || k != 0) ? 1u : 0u);
+          umma_bf16(d_tmem, a + k * kA, b + k * kB, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
         umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
       }
       if (!ok) break;

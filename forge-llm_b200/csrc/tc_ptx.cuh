@@ -135,6 +135,17 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint6
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
+// The same with A read from TMEM (M rows on lanes, K packed two bf16 per
+// 32-bit column, lower k in the low half): a_tmem is the column of k = 0.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -214,6 +225,17 @@ __device__ __forceinline__ void tmem_ld128(uint32_t taddr, float *f) {
       : "memory");
 }
 
+// Two 64-column TMEM loads (this thread's lane) completed by one wait.
+__device__ __forceinline__ void tmem_ld64x2(uint32_t ta, uint32_t tb, float *a, float *b) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%128];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%64, %65, %66, %67, %68, %69, %70, %71, %72, %73, %74, %75, %76, %77, %78, %79, %80, %81, %82, %83, %84, %85, %86, %87, %88, %89, %90, %91, %92, %93, %94, %95, %96, %97, %98, %99, %100, %101, %102, %103, %104, %105, %106, %107, %108, %109, %110, %111, %112, %113, %114, %115, %116, %117, %118, %119, %120, %121, %122, %123, %124, %125, %126, %127}, [%129];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=f"(a[0]), "=f"(a[1]), "=f"(a[2]), "=f"(a[3]), "=f"(a[4]), "=f"(a[5]), "=f"(a[6]), "=f"(a[7]), "=f"(a[8]), "=f"(a[9]), "=f"(a[10]), "=f"(a[11]), "=f"(a[12]), "=f"(a[13]), "=f"(a[14]), "=f"(a[15]), "=f"(a[16]), "=f"(a[17]), "=f"(a[18]), "=f"(a[19]), "=f"(a[20]), "=f"(a[21]), "=f"(a[22]), "=f"(a[23]), "=f"(a[24]), "=f"(a[25]), "=f"(a[26]), "=f"(a[27]), "=f"(a[28]), "=f"(a[29]), "=f"(a[30]), "=f"(a[31]), "=f"(a[32]), "=f"(a[33]), "=f"(a[34]), "=f"(a[35]), "=f"(a[36]), "=f"(a[37]), "=f"(a[38]), "=f"(a[39]), "=f"(a[40]), "=f"(a[41]), "=f"(a[42]), "=f"(a[43]), "=f"(a[44]), "=f"(a[45]), "=f"(a[46]), "=f"(a[47]), "=f"(a[48]), "=f"(a[49]), "=f"(a[50]), "=f"(a[51]), "=f"(a[52]), "=f"(a[53]), "=f"(a[54]), "=f"(a[55]), "=f"(a[56]), "=f"(a[57]), "=f"(a[58]), "=f"(a[59]), "=f"(a[60]), "=f"(a[61]), "=f"(a[62]), "=f"(a[63]), "=f"(b[0]), "=f"(b[1]), "=f"(b[2]), "=f"(b[3]), "=f"(b[4]), "=f"(b[5]), "=f"(b[6]), "=f"(b[7]), "=f"(b[8]), "=f"(b[9]), "=f"(b[10]), "=f"(b[11]), "=f"(b[12]), "=f"(b[13]), "=f"(b[14]), "=f"(b[15]), "=f"(b[16]), "=f"(b[17]), "=f"(b[18]), "=f"(b[19]), "=f"(b[20]), "=f"(b[21]), "=f"(b[22]), "=f"(b[23]), "=f"(b[24]), "=f"(b[25]), "=f"(b[26]), "=f"(b[27]), "=f"(b[28]), "=f"(b[29]), "=f"(b[30]), "=f"(b[31]), "=f"(b[32]), "=f"(b[33]), "=f"(b[34]), "=f"(b[35]), "=f"(b[36]), "=f"(b[37]), "=f"(b[38]), "=f"(b[39]), "=f"(b[40]), "=f"(b[41]), "=f"(b[42]), "=f"(b[43]), "=f"(b[44]), "=f"(b[45]), "=f"(b[46]), "=f"(b[47]), "=f"(b[48]), "=f"(b[49]), "=f"(b[50]), "=f"(b[51]), "=f"(b[52]), "=f"(b[53]), "=f"(b[54]), "=f"(b[55]), "=f"(b[56]), "=f"(b[57]), "=f"(b[58]), "=f"(b[59]), "=f"(b[60]), "=f"(b[61]), "=f"(b[62]), "=f"(b[63])
+      : "r"(ta), "r"(tb)
+      : "memory");
+}
+
 // 2^x on the MUFU unit; subnormal results flush to zero.
 __device__ __forceinline__ float ex2_ftz(float x) {
   float y;
@@ -221,7 +243,7 @@ __device__ __forceinline__ float ex2_ftz(float x) {
   return y;
 }
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t *r) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0],"
       " {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16,"
@@ -262,6 +284,16 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
 __device__ __forceinline__ uint64_t operand_desc(uint32_t tile, int k, int mn_major, int kdepth) {
   if (!mn_major) return smem_desc(tile + (uint32_t)k * 32u, 16u, 1024u);
   return smem_desc(tile + (uint32_t)k * 2048u, (uint32_t)kdepth * 128u, 1024u);
+}
+
+// Descriptor arithmetic without rebuilding: the start-address field counts
+// 16-byte units in the low bits, so a k-slice or a later tile of the same
+// layout is the base descriptor plus a constant.
+constexpr uint64_t kDescKStep = 32 >> 4;       // K-major: next 16-deep slice
+constexpr uint64_t kDescMNStep = 2048 >> 4;    // MN-major: next 16-deep slice
+__device__ __forceinline__ uint64_t desc_k(uint32_t tile) { return smem_desc(tile, 16u, 1024u); }
+__device__ __forceinline__ uint64_t desc_mn(uint32_t tile, int kdepth) {
+  return smem_desc(tile, (uint32_t)kdepth * 128u, 1024u);
 }
 
 // Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A/B bf16 (bits
