@@ -431,6 +431,98 @@ __global__ void __launch_bounds__(kCeThreads) ce_fwd_kernel(const float *logits,
   if (threadIdx.x == 0) row_loss[row] = lse - lt;
 }
 
+// Fused-path CE: bf16 gradient, loss per row.  Online max / sum in the
+// log2 domain (one FMA + one ex2 per logit), one block reduction, then a
+// second pass that re-reads the row (from L2: two 512-thread CTAs per SM keep
+// ~300 rows, under 40 MB, in flight) and writes (softmax - onehot) / T.
+__device__ __forceinline__ float ex2_approx(float x) {   // 2^x on the MUFU unit (ftz)
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+
+constexpr int kCe2Threads = 512;
+constexpr int kCe2Unroll = 4;
+
+__global__ void __launch_bounds__(kCe2Threads, 2)
+    ce_bf16_kernel(const float *__restrict__ logits, const int32_t *__restrict__ targets, int64_t T,
+                   int64_t V, float *__restrict__ row_loss, __nv_bfloat16 *__restrict__ du) {
+  __shared__ float shm[32], shs[32];
+  constexpr float kL2e = 1.4426950408889634f;
+  const int64_t row = blockIdx.x;
+  const float4 *l4 = reinterpret_cast<const float4 *>(logits + row * V);
+  const int64_t V4 = V >> 2;
+  const int32_t tgt = targets[row];
+  float lt = 0.f;
+  if (threadIdx.x == 0) lt = (tgt >= 0 && tgt < V) ? logits[row * V + tgt] : __int_as_float(0x7fc00000);
+  float m = -INFINITY, s = 0.f;                 // log2 domain: m = max(x log2e), s = sum 2^(x log2e - m)
+  for (int64_t base = threadIdx.x; base < V4; base += (int64_t)kCe2Threads * kCe2Unroll) {
+    float4 v[kCe2Unroll];
+#pragma unroll
+    for (int u = 0; u < kCe2Unroll; u++) {
+      const int64_t i4 = base + (int64_t)u * kCe2Threads;
+      v[u] = i4 < V4 ? l4[i4] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    }
+#pragma unroll
+    for (int u = 0; u < kCe2Unroll; u++) {
+      const float mx = fmaxf(fmaxf(v[u].x, v[u].y), fmaxf(v[u].z, v[u].w)) * kL2e;
+      if (mx > m) {
+        s *= ex2_approx(m - mx);                // 0 while m is -inf
+        m = mx;
+      }
+      if (mx != -INFINITY)
+        s += ex2_approx(fmaf(v[u].x, kL2e, -m)) + ex2_approx(fmaf(v[u].y, kL2e, -m)) +
+             ex2_approx(fmaf(v[u].z, kL2e, -m)) + ex2_approx(fmaf(v[u].w, kL2e, -m));
+    }
+  }
+  // combine (m, s) over the block
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    const float mm = fmaxf(m, m2);
+    s = (m == -INFINITY ? 0.f : s * ex2_approx(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * ex2_approx(m2 - mm));
+    m = mm;
+  }
+  if (lane == 0) {
+    shm[wid] = m;
+    shs[wid] = s;
+  }
+  __syncthreads();
+  float M = -INFINITY;
+  for (int w = 0; w < kCe2Threads / 32; w++) M = fmaxf(M, shm[w]);
+  float S = 0.f;
+  for (int w = 0; w < kCe2Threads / 32; w++) S += shm[w] == -INFINITY ? 0.f : shs[w] * ex2_approx(shm[w] - M);
+  const float lse2 = M + __log2f(S);            // log2-domain log-sum-exp
+  const float invT = (float)(1.0 / (double)T);
+  uint2 *d2 = reinterpret_cast<uint2 *>(du + row * V);
+  for (int64_t base = threadIdx.x; base < V4; base += (int64_t)kCe2Threads * kCe2Unroll) {
+    float4 v[kCe2Unroll];
+#pragma unroll
+    for (int u = 0; u < kCe2Unroll; u++) {
+      const int64_t i4 = base + (int64_t)u * kCe2Threads;
+      if (i4 < V4) v[u] = l4[i4];
+    }
+#pragma unroll
+    for (int u = 0; u < kCe2Unroll; u++) {
+      const int64_t i4 = base + (int64_t)u * kCe2Threads;
+      if (i4 >= V4) continue;
+      const int64_t i = i4 * 4;
+      const float o0 = (ex2_approx(fmaf(v[u].x, kL2e, -lse2)) - (i + 0 == tgt ? 1.f : 0.f)) * invT;
+      const float o1 = (ex2_approx(fmaf(v[u].y, kL2e, -lse2)) - (i + 1 == tgt ? 1.f : 0.f)) * invT;
+      const float o2 = (ex2_approx(fmaf(v[u].z, kL2e, -lse2)) - (i + 2 == tgt ? 1.f : 0.f)) * invT;
+      const float o3 = (ex2_approx(fmaf(v[u].w, kL2e, -lse2)) - (i + 3 == tgt ? 1.f : 0.f)) * invT;
+      d2[i4] = make_uint2(pack_bf16(o0, o1), pack_bf16(o2, o3));
+    }
+  }
+  if (threadIdx.x == 0) row_loss[row] = lse2 * 0.6931471805599453f - lt;
+}
+
 // loss = sum(row_loss) / T, summed in double in row order by one CTA.
 __global__ void mean_kernel(const float *__restrict__ v, int64_t n, float *__restrict__ out) {
   __shared__ double sh[32];
@@ -703,7 +795,9 @@ int fcu_ce_fwd_bf16grad(fcu_ctx *ctx, const float *logits, const int32_t *target
   float *row_loss = (float *)scr;
   __nv_bfloat16 *du = (__nv_bfloat16 *)dlogits_bf16;
   bool aligned = ((uintptr_t)logits % 16 == 0) && ((uintptr_t)du % 8 == 0);
-  if (aligned && V % 4 == 0 && V <= (int64_t)kCeThreads * kCeVec * 4)
+  if (aligned && V % 4 == 0)
+    ce_bf16_kernel<<<(int)T, kCe2Threads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, du);
+  else if (aligned && V % 4 == 0 && V <= (int64_t)kCeThreads * kCeVec * 4)
     ce_fwd_kernel<true, __nv_bfloat16><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V,
                                                                                row_loss, du);
   else

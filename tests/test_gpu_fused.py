@@ -145,3 +145,29 @@ def test_rmsnorm_fwd_bf16_add(T, D):
     assert float(((inv.double() - iv).abs() / iv).max()) <= 1e-5
     ref = x * iv[:, None] * w.double()[None, :]
     assert float(((out.double() - ref).abs() - 2 ** -8 * ref.abs()).max()) <= 1e-6
+
+
+@pytest.mark.parametrize("T,V", [(8192, 32000), (300, 1000), (7, 1001)])
+def test_ce_fwd_bf16grad(T, V):
+    """Fused-path cross-entropy: mean loss against float64 to 1e-5 relative,
+    dLogits = (softmax - onehot) / T within bf16 rounding (plus 2^-20 of the
+    row's largest probability for the fast exp)."""
+    from forgellm import _lib
+    from forgellm.autograd import ctx
+    g = torch.Generator(device="cuda").manual_seed(T + V)
+    logits = torch.randn(T, V, device="cuda", generator=g) * 2.0
+    targets = torch.randint(0, V, (T,), device="cuda", generator=g, dtype=torch.int32)
+    loss = torch.empty(1, device="cuda")
+    d = torch.empty(T, V, device="cuda", dtype=torch.bfloat16)
+    _lib.call("fcu_ce_fwd_bf16grad", ctx().handle, logits.data_ptr(), targets.data_ptr(), T, V,
+              loss.data_ptr(), d.data_ptr())
+    torch.cuda.synchronize()
+    x = logits.double()
+    lse = torch.logsumexp(x, 1)
+    ref_loss = float((lse - x.gather(1, targets.long()[:, None])[:, 0]).mean())
+    assert abs(float(loss) - ref_loss) <= 1e-5 * abs(ref_loss)
+    ref = torch.softmax(x, 1)
+    ref[torch.arange(T), targets.long()] -= 1.0
+    ref /= T
+    err = (d.double() - ref).abs() - 2 ** -8 * ref.abs()
+    assert float(err.max()) <= 2 ** -20 / T
