@@ -328,13 +328,14 @@ constexpr int kKV_D = kKV_L + kStages * 128 * 4;      // [kStages][128] f32
 constexpr int kKV_Bar = kKV_D + kStages * 128 * 4;
 constexpr int kKVSmem = kKV_Bar + (7 + 2 * kStages) * 8 + 16;
 
-// dQ kernel shared memory
-constexpr int kQ_Q = 0;
-constexpr int kQ_G = kQ_Q + kTile;
-constexpr int kQ_K = kQ_G + kTile;                    // kStages tiles
-constexpr int kQ_V = kQ_K + kStages * kTile;          // kStages tiles
-constexpr int kQ_Bar = kQ_V + kStages * kTile;
-constexpr int kQSmem = kQ_Bar + (7 + 2 * kStages) * 8 + 16;
+// dQ kernel shared memory: Q / dO double-buffered per item, a K/V ring
+constexpr int kQStages = 4;
+constexpr int kQ_Q = 0;                               // [2] Q tiles
+constexpr int kQ_G = kQ_Q + 2 * kTile;                // [2] dO tiles
+constexpr int kQ_K = kQ_G + 2 * kTile;                // kQStages tiles
+constexpr int kQ_V = kQ_K + kQStages * kTile;         // kQStages tiles
+constexpr int kQ_Bar = kQ_V + kQStages * kTile;
+constexpr int kQSmem = kQ_Bar + (13 + 2 * kQStages) * 8 + 16;
 
 // Rotates interleaved pairs back by R^T: (x, y) -> (x c + y s, -x s + y c).
 __device__ __forceinline__ void rope_back(float &x, float &y, float2 cs) {
@@ -594,32 +595,41 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, kBwdTmemCols);
 }
 
+// dQ, persistent: one CTA per SM walks the (query tile, head) items, latest
+// query tiles first, strided over the grid.  Per item it loops over the key
+// tiles at or before its query tile: S = Q K^T, dP = dO V^T, dS = P (dP -
+// delta) into TMEM cols [256,320) as the A operand, dQ += dS K into one of
+// two TMEM accumulators (cols [320,384), [384,448)), so one item's epilogue
+// (dQ * scale rotated back by RoPE) overlaps the next item's first MMAs.
+// Q/dO tiles are double-buffered per item; the K/V ring runs across items.
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_dq_tmem_kernel(const __grid_constant__ CUtensorMap tm_qkv,
                             const __grid_constant__ CUtensorMap tm_do, BwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t *sQ = smem + kQ_Q, *sG = smem + kQ_G, *sK = smem + kQ_K, *sV = smem + kQ_V;
   uint64_t *bars = (uint64_t *)(smem + kQ_Bar);
-  uint64_t *qg_full = bars, *kv_full = bars + 1, *kv_empty = bars + 1 + kStages;   // kv_*: [kStages]
-  uint64_t *sp_full = bars + 1 + 2 * kStages, *sp_free = sp_full + 1, *ds_full = sp_full + 2;
-  uint64_t *ds_free = sp_full + 3, *acc_done = sp_full + 4, *mma_done = sp_full + 5;
-  uint32_t *tmem_slot = (uint32_t *)(sp_full + 6);
+  uint64_t *qg_full = bars, *qg_empty = bars + 2;                       // [2]
+  uint64_t *kv_full = bars + 4, *kv_empty = bars + 4 + kQStages;        // [kQStages]
+  uint64_t *sp_full = bars + 4 + 2 * kQStages, *sp_free = sp_full + 1;
+  uint64_t *ds_full = sp_full + 2, *ds_free = sp_full + 3;
+  uint64_t *acc_full = sp_full + 4, *acc_free = sp_full + 6;            // [2]
+  uint64_t *mma_done = sp_full + 8;
+  uint32_t *tmem_slot = (uint32_t *)(mma_done + 1);
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int per = p.nH * p.B;
-  const int qt = p.n_t - 1 - (int)(blockIdx.x / per);   // latest query tiles first
-  const int rest = (int)(blockIdx.x % per);
-  const int h = rest % p.nH, b = rest / p.nH;
-  const int kvh = h / p.group;
-  const int q0 = qt * kBM;
-  const int nkv = qt + 1;
-  const int row0 = b * p.T;
+  const int n_items = p.n_t * per;
   const bool aligned = (smem_u32(smem) & 1023u) == 0;
 
   if (threadIdx.x == 0) {
-    mbar_init(qg_full, 1);
-    for (int s = 0; s < kStages; s++) {
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&qg_full[i], 1);
+      mbar_init(&qg_empty[i], 1);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_free[i], 8);
+    }
+    for (int s = 0; s < kQStages; s++) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
@@ -627,7 +637,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(sp_free, 8);
     mbar_init(ds_full, 8);
     mbar_init(ds_free, 1);
-    mbar_init(acc_done, 1);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     if (!aligned) atomicExch(p.err, 30);
@@ -638,51 +647,83 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tdP = tmem + 128, tdQ = tmem + 256, tdS = tmem + 320;
+  const uint32_t tS = tmem, tdP = tmem + 128, tdS = tmem + 256, tdQ0 = tmem + 320;
 
   if (!aligned) {
   } else if (warp == 0) {
     // ---------------- TMA producer
     if (lane == 0) {
       bool ok = true;
-      int issued = 0;
-      mbar_expect_tx(qg_full, 2 * kTile);
-      tma_load_2d(sQ, &tm_qkv, h * kD, row0 + q0, qg_full);
-      tma_load_2d(sG, &tm_do, h * kD, row0 + q0, qg_full);
-      for (int j = 0; j < nkv; j++) {
-        const int s = j % kStages;
-        if (!mbar_wait(&kv_empty[s], ((uint32_t)(j / kStages) & 1u) ^ 1u, abort_flag)) {
+      int u = 0, nq = 0;
+      for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+        const int qt = p.n_t - 1 - idx / per, rest = idx % per;
+        const int h = rest % p.nH, b = rest / p.nH, kvh = h / p.group;
+        const int row0 = b * p.T, qb = nq & 1;
+        if (!mbar_wait(&qg_empty[qb], ((uint32_t)(nq >> 1) & 1u) ^ 1u, abort_flag)) {
           ok = false;
           break;
         }
-        mbar_expect_tx(&kv_full[s], 2 * kTile);
-        tma_load_2d(sK + s * kTile, &tm_qkv, (p.nH + kvh) * kD, row0 + j * kBN, &kv_full[s]);
-        tma_load_2d(sV + s * kTile, &tm_qkv, (p.nH + p.nKV + kvh) * kD, row0 + j * kBN, &kv_full[s]);
-        issued++;
+        mbar_expect_tx(&qg_full[qb], 2 * kTile);
+        tma_load_2d(sQ + qb * kTile, &tm_qkv, h * kD, row0 + qt * kBM, &qg_full[qb]);
+        tma_load_2d(sG + qb * kTile, &tm_do, h * kD, row0 + qt * kBM, &qg_full[qb]);
+        nq++;
+        for (int j = 0; j <= qt; j++, u++) {
+          const int s = u % kQStages;
+          if (!mbar_wait(&kv_empty[s], ((uint32_t)(u / kQStages) & 1u) ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&kv_full[s], 2 * kTile);
+          tma_load_2d(sK + s * kTile, &tm_qkv, (p.nH + kvh) * kD, row0 + j * kBN, &kv_full[s]);
+          tma_load_2d(sV + s * kTile, &tm_qkv, (p.nH + p.nKV + kvh) * kD, row0 + j * kBN, &kv_full[s]);
+        }
       }
       if (!ok) {
         *abort_flag = 1;
         atomicExch(p.err, 31);
       }
-      mbar_wait_drain(qg_full, 0);
-      for (int i = issued - kStages < 0 ? 0 : issued - kStages; i < issued; i++)
-        mbar_wait_drain(&kv_full[i % kStages], (uint32_t)(i / kStages) & 1u);
+      for (int i = nq - 2 < 0 ? 0 : nq - 2; i < nq; i++) mbar_wait_drain(&qg_full[i & 1], (uint32_t)(i >> 1) & 1u);
+      for (int i = u - kQStages < 0 ? 0 : u - kQStages; i < u; i++)
+        mbar_wait_drain(&kv_full[i % kQStages], (uint32_t)(i / kQStages) & 1u);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
       const uint32_t id_n128 = instr_desc_bf16(0, 0, kBM, kBN);
       const uint32_t id_n64 = instr_desc_bf16(0, 1, kBM, kD);
-      bool ok = mbar_wait(qg_full, 0, abort_flag);
-      const uint64_t dQ = desc_k(smem_u32(sQ)), dG = desc_k(smem_u32(sG));
+      const uint64_t dQ0 = desc_k(smem_u32(sQ)), dG0 = desc_k(smem_u32(sG));
       const uint64_t dKk0 = desc_k(smem_u32(sK)), dVk0 = desc_k(smem_u32(sV));
       const uint64_t dKm0 = desc_mn(smem_u32(sK), kBN);
       constexpr uint64_t kTileStep = kTile >> 4;
-      for (int j = 0; j <= nkv && ok; j++) {
-        if (j < nkv) {
-          const int s = j % kStages;
-          if (!mbar_wait(&kv_full[s], (uint32_t)(j / kStages) & 1u, abort_flag) ||
-              (j > 0 && !mbar_wait(sp_free, (uint32_t)(j - 1) & 1u, abort_flag))) {
+      bool ok = true, have_prev = false, prev_first = false, prev_last = false;
+      int u = 0, ii = 0, prev_u = 0, prev_s = 0, prev_qb = 0;
+      // dQ += dS K for the previous unit (one unit behind its S / dP MMAs)
+      auto issue_dq = [&]() -> bool {
+        if (!mbar_wait(ds_full, (uint32_t)prev_u & 1u, abort_flag)) return false;
+        tc_fence_after();
+        const uint64_t bk = dKm0 + (uint64_t)prev_s * kTileStep;
+        const uint32_t acc = tdQ0 + (uint32_t)(prev_qb * kD);
+#pragma unroll
+        for (int k = 0; k < kBN / 16; k++)
+          umma_bf16_ts(acc, tdS + (uint32_t)(8 * k), bk + k * kDescMNStep, id_n64, (!prev_first || k > 0) ? 1u : 0u);
+        umma_commit(ds_free);
+        umma_commit(&kv_empty[prev_s]);
+        if (prev_last) umma_commit(&acc_full[prev_qb]);
+        return true;
+      };
+      for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x, ii++) {
+        const int qt = p.n_t - 1 - idx / per;
+        const int qb = ii & 1;
+        if (!mbar_wait(&qg_full[qb], (uint32_t)(ii >> 1) & 1u, abort_flag) ||
+            !mbar_wait(&acc_free[qb], ((uint32_t)(ii >> 1) & 1u) ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint64_t aq = dQ0 + (uint64_t)qb * kTileStep, ag = dG0 + (uint64_t)qb * kTileStep;
+        for (int j = 0; j <= qt; j++, u++) {
+          const int s = u % kQStages;
+          if (!mbar_wait(&kv_full[s], (uint32_t)(u / kQStages) & 1u, abort_flag) ||
+              (u > 0 && !mbar_wait(sp_free, (uint32_t)(u - 1) & 1u, abort_flag))) {
             ok = false;
             break;
           }
@@ -690,30 +731,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const uint64_t bk = dKk0 + (uint64_t)s * kTileStep, bv = dVk0 + (uint64_t)s * kTileStep;
 #pragma unroll
           for (int k = 0; k < kD / 16; k++)
-            umma_bf16(tS, dQ + k * kDescKStep, bk + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
+            umma_bf16(tS, aq + k * kDescKStep, bk + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
 #pragma unroll
           for (int k = 0; k < kD / 16; k++)
-            umma_bf16(tdP, dG + k * kDescKStep, bv + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
+            umma_bf16(tdP, ag + k * kDescKStep, bv + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
           umma_commit(sp_full);
-        }
-        if (j > 0) {
-          const int i = j - 1, s = i % kStages;
-          if (!mbar_wait(ds_full, (uint32_t)i & 1u, abort_flag)) {
+          if (j == qt) umma_commit(&qg_empty[qb]);   // this item's Q / dO are read
+          if (have_prev && !issue_dq()) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          const uint64_t bk = dKm0 + (uint64_t)s * kTileStep;
-#pragma unroll
-          for (int k = 0; k < kBN / 16; k++)
-            umma_bf16_ts(tdQ, tdS + (uint32_t)(8 * k), bk + k * kDescMNStep, id_n64, (i > 0 || k > 0) ? 1u : 0u);
-          umma_commit(ds_free);
-          umma_commit(&kv_empty[s]);
+          have_prev = true;
+          prev_u = u;
+          prev_s = s;
+          prev_qb = qb;
+          prev_first = j == 0;
+          prev_last = j == qt;
         }
       }
-      if (ok) {
-        umma_commit(acc_done);
-      } else {
+      if (ok && have_prev && !issue_dq()) ok = false;
+      if (!ok) {
         *abort_flag = 1;
         atomicExch(p.err, 32);
       }
@@ -721,67 +758,75 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_wait_drain(mma_done, 0);
     }
   } else {
-    // ---------------- dS (warps 2..9)
+    // ---------------- dS and the dQ epilogue (warps 2..9)
     const int quarter = warp & 3, half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;          // query row == TMEM lane
-    const int q = q0 + r;
     const uint32_t la = (uint32_t)(quarter * 32) << 16;
     const int cb = half * 64;                   // this warp's 64 key columns
-    const int64_t li = ((int64_t)b * p.nH + h) * p.T + q;
-    const float L = q < p.T ? p.lse[li] * kLog2e : 0.f;
-    const float Dq = q < p.T ? p.delta[li] : 0.f;
     bool ok = true;
-    for (int j = 0; j < nkv; j++) {
-      if (!warp_wait(sp_full, (uint32_t)j & 1u, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float sv[64], dp[64];
-      tmem_ld64x2(tS + la + cb, tdP + la + cb, sv, dp);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(sp_free);
-      const int lim = j == nkv - 1 ? r - cb : 1 << 30;   // diagonal tile: key column c valid if c <= lim
-      uint32_t dd[32];
+    int u = 0, ii = 0;
+    for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x, ii++) {
+      const int qt = p.n_t - 1 - idx / per, rest = idx % per;
+      const int h = rest % p.nH, b = rest / p.nH;
+      const int q = qt * kBM + r, qb = ii & 1;
+      const int64_t li = ((int64_t)b * p.nH + h) * p.T + q;
+      const float L = q < p.T ? p.lse[li] * kLog2e : 0.f;
+      const float Dq = q < p.T ? p.delta[li] : 0.f;
+      for (int j = 0; j <= qt; j++, u++) {
+        if (!warp_wait(sp_full, (uint32_t)u & 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float sv[64], dp[64];
+        tmem_ld64x2(tS + la + cb, tdP + la + cb, sv, dp);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sp_free);
+        const int lim = j == qt ? r - cb : 1 << 30;   // diagonal tile: key column c valid if c <= lim
+        uint32_t dd[32];
 #pragma unroll
-      for (int c = 0; c < 32; c++) {
-        float p0 = ex2_ftz(fmaf(sv[2 * c], p.scale_log2, -L));
-        float p1 = ex2_ftz(fmaf(sv[2 * c + 1], p.scale_log2, -L));
-        if (2 * c > lim) p0 = 0.f;
-        if (2 * c + 1 > lim) p1 = 0.f;
-        dd[c] = pack2_bf16(p0 * (dp[2 * c] - Dq), p1 * (dp[2 * c + 1] - Dq));
+        for (int c = 0; c < 32; c++) {
+          float p0 = ex2_ftz(fmaf(sv[2 * c], p.scale_log2, -L));
+          float p1 = ex2_ftz(fmaf(sv[2 * c + 1], p.scale_log2, -L));
+          if (2 * c > lim) p0 = 0.f;
+          if (2 * c + 1 > lim) p1 = 0.f;
+          dd[c] = pack2_bf16(p0 * (dp[2 * c] - Dq), p1 * (dp[2 * c + 1] - Dq));
+        }
+        if (u > 0 && !warp_wait(ds_free, (uint32_t)(u - 1) & 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tmem_st32(tdS + la + (uint32_t)(32 * half), dd);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ds_full);
       }
-      if (j > 0 && !warp_wait(ds_free, (uint32_t)(j - 1) & 1u, abort_flag)) {
+      if (!ok || !warp_wait(&acc_full[qb], (uint32_t)(ii >> 1) & 1u, abort_flag)) {
         ok = false;
         break;
       }
-      tmem_st32(tdS + la + (uint32_t)(32 * half), dd);
-      tmem_wait_st();
+      tc_fence_after();
+      uint32_t uq[32];
+      tmem_ld32(tdQ0 + (uint32_t)(qb * kD) + la + (uint32_t)(half * 32), uq);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(ds_full);
-    }
-    if (ok && warp_wait(acc_done, 0, abort_flag)) {
-      tc_fence_after();
-      uint32_t u[32];
-      tmem_ld32(tdQ + la + half * 32, u);
+      if (lane == 0) mbar_arrive(&acc_free[qb]);
       if (q < p.T) {
         float v[32];
 #pragma unroll
-        for (int c = 0; c < 32; c++) v[c] = __uint_as_float(u[c]) * p.scale;
+        for (int c = 0; c < 32; c++) v[c] = __uint_as_float(uq[c]) * p.scale;
         if (p.rope) {
 #pragma unroll
           for (int i = 0; i < 16; i++) rope_back(v[2 * i], v[2 * i + 1], p.rope[(int64_t)q * 32 + half * 16 + i]);
         }
-        uint4 *dst = reinterpret_cast<uint4 *>(p.dqkv + (int64_t)(row0 + q) * p.ld + (int64_t)h * kD + half * 32);
+        uint4 *dst = reinterpret_cast<uint4 *>(p.dqkv + (int64_t)(b * p.T + q) * p.ld + (int64_t)h * kD + half * 32);
 #pragma unroll
         for (int c8 = 0; c8 < 4; c8++)
           dst[c8] = make_uint4(pack2_bf16(v[8 * c8], v[8 * c8 + 1]), pack2_bf16(v[8 * c8 + 2], v[8 * c8 + 3]),
                                pack2_bf16(v[8 * c8 + 4], v[8 * c8 + 5]), pack2_bf16(v[8 * c8 + 6], v[8 * c8 + 7]));
       }
-    } else {
-      ok = false;
     }
     if (!ok && lane == 0) {
       *abort_flag = 1;
@@ -943,8 +988,9 @@ int attn_bwd_tmem(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv,
     attr_set[ctx->device & 63] = true;
   }
   const int64_t grid_kv = (int64_t)p.n_t * (split ? nH : nKV) * B;
-  const int64_t grid_q = (int64_t)p.n_t * nH * B;
-  FCU_REQUIRE(grid_q <= INT32_MAX, "attention backward: grid too large");
+  const int64_t items_q = (int64_t)p.n_t * nH * B;
+  const int64_t grid_q = items_q < ctx->num_sms ? items_q : ctx->num_sms;   // persistent
+  FCU_REQUIRE(items_q <= INT32_MAX, "attention backward: grid too large");
   attn_bwd_dkdv_tmem_kernel<<<(unsigned)grid_kv, kBwdThreads, kKVSmem, ctx->stream>>>(map_qkv, map_do, p);
   FCU_CHECK_LAUNCH();
   if (split) {

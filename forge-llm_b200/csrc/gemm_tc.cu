@@ -371,11 +371,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         } else {
           if (p.mode == kOutBF16Rope && n < p.rope_cols && gm < p.M) {
-            const int64_t pos = gm % p.rope_T;
+            // the box's 64 columns lie inside one head (head_dim % 64 == 0)
             const int half = p.head_dim >> 1;
+            const float2 *cs_row = p.rope + (gm % p.rope_T) * half + (n % p.head_dim) / 2;
 #pragma unroll
             for (int i = 0; i < 32; i++) {
-              const float2 cs = p.rope[pos * half + ((n + 2 * i) % p.head_dim) / 2];
+              const float2 cs = cs_row[i];
               const float a = v[2 * i], b = v[2 * i + 1];
               v[2 * i] = a * cs.x - b * cs.y;
               v[2 * i + 1] = a * cs.y + b * cs.x;
