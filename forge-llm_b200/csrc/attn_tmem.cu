@@ -305,7 +305,6 @@ __global__ void __launch_bounds__(kThreads, 2)
 // rotated back by RoPE.
 constexpr int kBwdThreads = 320;
 constexpr uint32_t kBwdTmemCols = 512;
-constexpr int kStages = 5;                   // Q/dO (dK/dV) and K/V (dQ) ring depth
 
 struct BwdParams {
   int B, T, nH, nKV, n_t, group, split;
@@ -318,15 +317,17 @@ struct BwdParams {
   int *err;
 };
 
-// dK/dV kernel shared memory (byte offsets)
-constexpr int kKV_K = 0;
-constexpr int kKV_V = kKV_K + kTile;
-constexpr int kKV_Q = kKV_V + kTile;                  // kStages tiles
-constexpr int kKV_G = kKV_Q + kStages * kTile;        // kStages tiles (dO)
-constexpr int kKV_L = kKV_G + kStages * kTile;        // [kStages][128] f32
-constexpr int kKV_D = kKV_L + kStages * 128 * 4;      // [kStages][128] f32
-constexpr int kKV_Bar = kKV_D + kStages * 128 * 4;
-constexpr int kKVSmem = kKV_Bar + (7 + 2 * kStages) * 8 + 16;
+// dK/dV kernel shared memory: K / V double-buffered per item, a (Q, dO, lse,
+// delta) ring across items
+constexpr int kKStages = 4;
+constexpr int kKV_K = 0;                              // [2]
+constexpr int kKV_V = kKV_K + 2 * kTile;              // [2]
+constexpr int kKV_Q = kKV_V + 2 * kTile;              // kKStages tiles
+constexpr int kKV_G = kKV_Q + kKStages * kTile;       // kKStages tiles (dO)
+constexpr int kKV_L = kKV_G + kKStages * kTile;       // [kKStages][128] f32
+constexpr int kKV_D = kKV_L + kKStages * 128 * 4;     // [kKStages][128] f32
+constexpr int kKV_Bar = kKV_D + kKStages * 128 * 4;
+constexpr int kKVSmem = kKV_Bar + (13 + 2 * kKStages) * 8 + 16;
 
 // dQ kernel shared memory: Q / dO double-buffered per item, a K/V ring
 constexpr int kQStages = 4;
@@ -351,31 +352,43 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t *sK = smem + kKV_K, *sV = smem + kKV_V, *sQ = smem + kKV_Q, *sG = smem + kKV_G;
   float *sL = (float *)(smem + kKV_L), *sDl = (float *)(smem + kKV_D);
   uint64_t *bars = (uint64_t *)(smem + kKV_Bar);
-  uint64_t *kv_full = bars, *q_full = bars + 1, *q_empty = bars + 1 + kStages;   // q_*: [kStages]
-  uint64_t *st_full = bars + 1 + 2 * kStages, *st_free = st_full + 1, *pds_full = st_full + 2;
-  uint64_t *pds_free = st_full + 3, *acc_done = st_full + 4, *mma_done = st_full + 5;
-  uint32_t *tmem_slot = (uint32_t *)(st_full + 6);
+  uint64_t *kv_full = bars, *kv_empty = bars + 2;                        // [2]
+  uint64_t *q_full = bars + 4, *q_empty = bars + 4 + kKStages;           // [kKStages]
+  uint64_t *st_full = bars + 4 + 2 * kKStages, *st_free = st_full + 1;
+  uint64_t *pds_full = st_full + 2, *pds_free = st_full + 3;
+  uint64_t *acc_full = st_full + 4, *acc_free = st_full + 5, *mma_done = st_full + 6;
+  uint32_t *tmem_slot = (uint32_t *)(st_full + 7);
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Work item: early key tiles (most query tiles after them) first.
+  // Work items (key tile, head, sequence), early key tiles (most query tiles
+  // after them) first, strided over the persistent grid.
   const int heads_cta = p.split ? p.nH : p.nKV;
   const int per = heads_cta * p.B;
-  const int kt = (int)(blockIdx.x / per);
-  const int rest = (int)(blockIdx.x % per);
-  const int hx = rest % heads_cta, b = rest / heads_cta;
-  const int kvh = p.split ? hx / p.group : hx;
-  const int h_begin = p.split ? hx : kvh * p.group;
+  const int n_items = p.n_t * per;
   const int n_heads = p.split ? 1 : p.group;
-  const int per_head = p.n_t - kt;              // query tiles kt..n_t-1
-  const int n_iter = n_heads * per_head;
-  const int k0 = kt * kBN;
-  const int row0 = b * p.T;
   const bool aligned = (smem_u32(smem) & 1023u) == 0;
+  struct Item {
+    int kt, kvh, h_begin, b, per_head, n_iter;
+  };
+  auto item = [&](int idx) {
+    Item w;
+    w.kt = idx / per;
+    const int rest = idx % per, hx = rest % heads_cta;
+    w.b = rest / heads_cta;
+    w.kvh = p.split ? hx / p.group : hx;
+    w.h_begin = p.split ? hx : w.kvh * p.group;
+    w.per_head = p.n_t - w.kt;                  // query tiles kt..n_t-1
+    w.n_iter = n_heads * w.per_head;
+    return w;
+  };
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
-    for (int s = 0; s < kStages; s++) {
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int s = 0; s < kKStages; s++) {
       mbar_init(&q_full[s], 2);               // TMA bytes + lse / delta staged
       mbar_init(&q_empty[s], 1);
     }
@@ -383,7 +396,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(st_free, 8);
     mbar_init(pds_full, 8);
     mbar_init(pds_free, 1);
-    mbar_init(acc_done, 1);
+    mbar_init(acc_full, 1);
+    mbar_init(acc_free, 8);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     if (!aligned) atomicExch(p.err, 20);
@@ -401,60 +415,96 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   } else if (warp == 0) {
     // ---------------- producer (lane 0 issues TMA; the warp stages lse / delta)
     bool ok = true;
-    int issued = 0;
-    if (lane == 0) {
-      mbar_expect_tx(kv_full, 2 * kTile);
-      tma_load_2d(sK, &tm_qkv, (p.nH + kvh) * kD, row0 + k0, kv_full);
-      tma_load_2d(sV, &tm_qkv, (p.nH + p.nKV + kvh) * kD, row0 + k0, kv_full);
-    }
-    for (int it = 0; it < n_iter; it++) {
-      const int s = it % kStages;
-      if (!warp_wait(&q_empty[s], ((uint32_t)(it / kStages) & 1u) ^ 1u, abort_flag)) {
+    int u = 0, nk = 0;
+    for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+      const Item w = item(idx);
+      const int row0 = w.b * p.T, kb = nk & 1;
+      if (!warp_wait(&kv_empty[kb], ((uint32_t)(nk >> 1) & 1u) ^ 1u, abort_flag)) {
         ok = false;
         break;
       }
-      const int h = h_begin + it / per_head;
-      const int q0 = (kt + it % per_head) * kBM;
-      if (lane == 0) {                        // copies first: their latency overlaps the loads below
-        mbar_expect_tx(&q_full[s], 2 * kTile);
-        tma_load_2d(sQ + s * kTile, &tm_qkv, h * kD, row0 + q0, &q_full[s]);
-        tma_load_2d(sG + s * kTile, &tm_do, h * kD, row0 + q0, &q_full[s]);
+      if (lane == 0) {
+        mbar_expect_tx(&kv_full[kb], 2 * kTile);
+        tma_load_2d(sK + kb * kTile, &tm_qkv, (p.nH + w.kvh) * kD, row0 + w.kt * kBN, &kv_full[kb]);
+        tma_load_2d(sV + kb * kTile, &tm_qkv, (p.nH + p.nKV + w.kvh) * kD, row0 + w.kt * kBN, &kv_full[kb]);
       }
-      issued++;
-      const int64_t lrow = ((int64_t)b * p.nH + h) * p.T;
+      nk++;
+      for (int it = 0; it < w.n_iter; it++, u++) {
+        const int s = u % kKStages;
+        if (!warp_wait(&q_empty[s], ((uint32_t)(u / kKStages) & 1u) ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int h = w.h_begin + it / w.per_head;
+        const int q0 = (w.kt + it % w.per_head) * kBM;
+        if (lane == 0) {                      // copies first: their latency overlaps the loads below
+          mbar_expect_tx(&q_full[s], 2 * kTile);
+          tma_load_2d(sQ + s * kTile, &tm_qkv, h * kD, row0 + q0, &q_full[s]);
+          tma_load_2d(sG + s * kTile, &tm_do, h * kD, row0 + q0, &q_full[s]);
+        }
+        const int64_t lrow = ((int64_t)w.b * p.nH + h) * p.T;
 #pragma unroll
-      for (int e = lane; e < kBM; e += 32) {
-        const int q = q0 + e;
-        sL[s * kBM + e] = q < p.T ? p.lse[lrow + q] * kLog2e : 0.f;
-        sDl[s * kBM + e] = q < p.T ? p.delta[lrow + q] : 0.f;
+        for (int e = lane; e < kBM; e += 32) {
+          const int q = q0 + e;
+          sL[s * kBM + e] = q < p.T ? p.lse[lrow + q] * kLog2e : 0.f;
+          sDl[s * kBM + e] = q < p.T ? p.delta[lrow + q] : 0.f;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&q_full[s]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&q_full[s]);
     }
     if (lane == 0) {
       if (!ok) {
         *abort_flag = 1;
         atomicExch(p.err, 21);
       }
-      mbar_wait_drain(kv_full, 0);
-      for (int i = issued - kStages < 0 ? 0 : issued - kStages; i < issued; i++)
-        mbar_wait_drain(&q_full[i % kStages], (uint32_t)(i / kStages) & 1u);
+      for (int i = nk - 2 < 0 ? 0 : nk - 2; i < nk; i++) mbar_wait_drain(&kv_full[i & 1], (uint32_t)(i >> 1) & 1u);
+      for (int i = u - kKStages < 0 ? 0 : u - kKStages; i < u; i++)
+        mbar_wait_drain(&q_full[i % kKStages], (uint32_t)(i / kKStages) & 1u);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
       const uint32_t id_n128 = instr_desc_bf16(0, 0, kBM, kBN);
       const uint32_t id_n64 = instr_desc_bf16(0, 1, kBM, kD);
-      bool ok = mbar_wait(kv_full, 0, abort_flag);
-      const uint64_t dK = desc_k(smem_u32(sK)), dV = desc_k(smem_u32(sV));
+      constexpr uint64_t kTileStep = kTile >> 4;
+      const uint64_t dK0 = desc_k(smem_u32(sK)), dV0 = desc_k(smem_u32(sV));
       const uint64_t dQk0 = desc_k(smem_u32(sQ)), dGk0 = desc_k(smem_u32(sG));
       const uint64_t dQm0 = desc_mn(smem_u32(sQ), kBM), dGm0 = desc_mn(smem_u32(sG), kBM);
-      constexpr uint64_t kTileStep = kTile >> 4;
-      for (int it = 0; it <= n_iter && ok; it++) {
-        if (it < n_iter) {
-          const int s = it % kStages;
-          if (!mbar_wait(&q_full[s], (uint32_t)(it / kStages) & 1u, abort_flag) ||
-              (it > 0 && !mbar_wait(st_free, (uint32_t)(it - 1) & 1u, abort_flag))) {
+      bool ok = true, have_prev = false, prev_first = false, prev_last = false;
+      int u = 0, ii = 0, prev_u = 0, prev_s = 0, prev_kb = 0, prev_ii = 0;
+      // dV += P^T dO, dK += dS^T Q for the previous unit (one unit behind its S / dP MMAs)
+      auto issue_dvdk = [&]() -> bool {
+        if (!mbar_wait(pds_full, (uint32_t)prev_u & 1u, abort_flag)) return false;
+        if (prev_first && !mbar_wait(acc_free, ((uint32_t)prev_ii & 1u) ^ 1u, abort_flag)) return false;
+        tc_fence_after();
+        const uint64_t bq = dQm0 + (uint64_t)prev_s * kTileStep, bg = dGm0 + (uint64_t)prev_s * kTileStep;
+#pragma unroll
+        for (int k = 0; k < kBM / 16; k++)
+          umma_bf16_ts(tdV, tPt + (uint32_t)(8 * k), bg + k * kDescMNStep, id_n64, (!prev_first || k > 0) ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < kBM / 16; k++)
+          umma_bf16_ts(tdK, tDt + (uint32_t)(8 * k), bq + k * kDescMNStep, id_n64, (!prev_first || k > 0) ? 1u : 0u);
+        umma_commit(pds_free);
+        umma_commit(&q_empty[prev_s]);
+        if (prev_last) {
+          umma_commit(acc_full);
+          umma_commit(&kv_empty[prev_kb]);
+        }
+        return true;
+      };
+      for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x, ii++) {
+        const Item w = item(idx);
+        const int kb = ii & 1;
+        if (!mbar_wait(&kv_full[kb], (uint32_t)(ii >> 1) & 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint64_t ak = dK0 + (uint64_t)kb * kTileStep, av = dV0 + (uint64_t)kb * kTileStep;
+        for (int it = 0; it < w.n_iter; it++, u++) {
+          const int s = u % kKStages;
+          if (!mbar_wait(&q_full[s], (uint32_t)(u / kKStages) & 1u, abort_flag) ||
+              (u > 0 && !mbar_wait(st_free, (uint32_t)(u - 1) & 1u, abort_flag))) {
             ok = false;
             break;
           }
@@ -462,33 +512,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const uint64_t bq = dQk0 + (uint64_t)s * kTileStep, bg = dGk0 + (uint64_t)s * kTileStep;
 #pragma unroll
           for (int k = 0; k < kD / 16; k++)
-            umma_bf16(tS, dK + k * kDescKStep, bq + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
+            umma_bf16(tS, ak + k * kDescKStep, bq + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
 #pragma unroll
           for (int k = 0; k < kD / 16; k++)
-            umma_bf16(tdP, dV + k * kDescKStep, bg + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
+            umma_bf16(tdP, av + k * kDescKStep, bg + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
           umma_commit(st_full);
-        }
-        if (it > 0) {
-          const int i = it - 1, s = i % kStages;
-          if (!mbar_wait(pds_full, (uint32_t)i & 1u, abort_flag)) {
+          if (have_prev && !issue_dvdk()) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          const uint64_t bq = dQm0 + (uint64_t)s * kTileStep, bg = dGm0 + (uint64_t)s * kTileStep;
-#pragma unroll
-          for (int k = 0; k < kBM / 16; k++)
-            umma_bf16_ts(tdV, tPt + (uint32_t)(8 * k), bg + k * kDescMNStep, id_n64, (i > 0 || k > 0) ? 1u : 0u);
-#pragma unroll
-          for (int k = 0; k < kBM / 16; k++)
-            umma_bf16_ts(tdK, tDt + (uint32_t)(8 * k), bq + k * kDescMNStep, id_n64, (i > 0 || k > 0) ? 1u : 0u);
-          umma_commit(pds_free);
-          umma_commit(&q_empty[s]);
+          have_prev = true;
+          prev_u = u;
+          prev_s = s;
+          prev_kb = kb;
+          prev_ii = ii;
+          prev_first = it == 0;
+          prev_last = it == w.n_iter - 1;
         }
       }
-      if (ok) {
-        umma_commit(acc_done);
-      } else {
+      if (ok && have_prev && !issue_dvdk()) ok = false;
+      if (!ok) {
         *abort_flag = 1;
         atomicExch(p.err, 22);
       }
@@ -496,72 +539,82 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_wait_drain(mma_done, 0);
     }
   } else {
-    // ---------------- P^T / dS^T (warps 2..9)
+    // ---------------- P^T / dS^T and the dK / dV epilogue (warps 2..9)
     const int quarter = warp & 3, half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;          // key row == TMEM lane
-    const int key = k0 + r;
     const uint32_t la = (uint32_t)(quarter * 32) << 16;
     const int cb = half * 64;                   // this warp's 64 query columns
     bool ok = true;
-    for (int it = 0; it < n_iter; it++) {
-      const int s = it % kStages;
-      const int q0 = (kt + it % per_head) * kBM;
-      if (!warp_wait(&q_full[s], (uint32_t)(it / kStages) & 1u, abort_flag) ||
-          !warp_wait(st_full, (uint32_t)it & 1u, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float sv[64], dp[64];
-      tmem_ld64x2(tS + la + cb, tdP + la + cb, sv, dp);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(st_free);
-      const float4 *L4 = reinterpret_cast<const float4 *>(sL + s * kBM + cb);
-      const float4 *D4 = reinterpret_cast<const float4 *>(sDl + s * kBM + cb);
-      const int qc = q0 + cb;                   // first query of these columns
-      const bool mask = qc < key || qc + 64 > p.T;
-      uint32_t pp[32], dd[32];
-#pragma unroll
-      for (int c4 = 0; c4 < 16; c4++) {
-        const float4 l4 = L4[c4], d4 = D4[c4];
-        const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
-        float pr[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-          pr[u] = ex2_ftz(fmaf(sv[4 * c4 + u], p.scale_log2, -lv[u]));
-          if (mask) {
-            const int q = qc + 4 * c4 + u;
-            if (q < key || q >= p.T) pr[u] = 0.f;
-          }
+    int u = 0, ii = 0;
+    for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x, ii++) {
+      const Item w = item(idx);
+      const int key = w.kt * kBN + r;
+      for (int it = 0; it < w.n_iter; it++, u++) {
+        const int s = u % kKStages;
+        const int q0 = (w.kt + it % w.per_head) * kBM;
+        if (!warp_wait(&q_full[s], (uint32_t)(u / kKStages) & 1u, abort_flag) ||
+            !warp_wait(st_full, (uint32_t)u & 1u, abort_flag)) {
+          ok = false;
+          break;
         }
-        pp[2 * c4] = pack2_bf16(pr[0], pr[1]);
-        pp[2 * c4 + 1] = pack2_bf16(pr[2], pr[3]);
-        dd[2 * c4] = pack2_bf16(pr[0] * (dp[4 * c4] - dv[0]), pr[1] * (dp[4 * c4 + 1] - dv[1]));
-        dd[2 * c4 + 1] = pack2_bf16(pr[2] * (dp[4 * c4 + 2] - dv[2]), pr[3] * (dp[4 * c4 + 3] - dv[3]));
+        tc_fence_after();
+        float sv[64], dp[64];
+        tmem_ld64x2(tS + la + cb, tdP + la + cb, sv, dp);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(st_free);
+        const float4 *L4 = reinterpret_cast<const float4 *>(sL + s * kBM + cb);
+        const float4 *D4 = reinterpret_cast<const float4 *>(sDl + s * kBM + cb);
+        const int qc = q0 + cb;                 // first query of these columns
+        const bool mask = qc < key || qc + 64 > p.T;
+        uint32_t pp[32], dd[32];
+#pragma unroll
+        for (int c4 = 0; c4 < 16; c4++) {
+          const float4 l4 = L4[c4], d4 = D4[c4];
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
+          float pr[4];
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            pr[e] = ex2_ftz(fmaf(sv[4 * c4 + e], p.scale_log2, -lv[e]));
+            if (mask) {
+              const int q = qc + 4 * c4 + e;
+              if (q < key || q >= p.T) pr[e] = 0.f;
+            }
+          }
+          pp[2 * c4] = pack2_bf16(pr[0], pr[1]);
+          pp[2 * c4 + 1] = pack2_bf16(pr[2], pr[3]);
+          dd[2 * c4] = pack2_bf16(pr[0] * (dp[4 * c4] - dv[0]), pr[1] * (dp[4 * c4 + 1] - dv[1]));
+          dd[2 * c4 + 1] = pack2_bf16(pr[2] * (dp[4 * c4 + 2] - dv[2]), pr[3] * (dp[4 * c4 + 3] - dv[3]));
+        }
+        // dV/dK of the previous unit must be done reading P^T / dS^T.
+        if (u > 0 && !warp_wait(pds_free, (uint32_t)(u - 1) & 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tmem_st32(tPt + la + (uint32_t)(32 * half), pp);
+        tmem_st32(tDt + la + (uint32_t)(32 * half), dd);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pds_full);
       }
-      // dV/dK of the previous tile must be done reading P^T / dS^T.
-      if (it > 0 && !warp_wait(pds_free, (uint32_t)(it - 1) & 1u, abort_flag)) {
+      if (!ok || !warp_wait(acc_full, (uint32_t)ii & 1u, abort_flag)) {
         ok = false;
         break;
       }
-      tmem_st32(tPt + la + (uint32_t)(32 * half), pp);
-      tmem_st32(tDt + la + (uint32_t)(32 * half), dd);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(pds_full);
-    }
-    if (ok && warp_wait(acc_done, 0, abort_flag)) {
       tc_fence_after();
       float v[64];
       tmem_ld64((half ? tdK : tdV) + la, v);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_free);
       if (key < p.T) {
+        const int row0 = w.b * p.T;
         const float mul = half ? p.scale : 1.f;
         if (p.split) {
-          const int g = h_begin - kvh * p.group;
+          const int g = w.h_begin - w.kvh * p.group;
           float *dst = (half ? p.pk : p.pv) +
-                       ((int64_t)g * p.B * p.T + row0 + key) * ((int64_t)p.nKV * kD) + kvh * kD;
+                       ((int64_t)g * p.B * p.T + row0 + key) * ((int64_t)p.nKV * kD) + w.kvh * kD;
 #pragma unroll
           for (int c4 = 0; c4 < 16; c4++)
             reinterpret_cast<float4 *>(dst)[c4] =
@@ -574,15 +627,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             for (int i = 0; i < 32; i++) rope_back(v[2 * i], v[2 * i + 1], p.rope[(int64_t)key * 32 + i]);
           }
           uint4 *dst = reinterpret_cast<uint4 *>(p.dqkv + (int64_t)(row0 + key) * p.ld +
-                                                 (int64_t)(p.nH + (half ? 0 : p.nKV) + kvh) * kD);
+                                                 (int64_t)(p.nH + (half ? 0 : p.nKV) + w.kvh) * kD);
 #pragma unroll
           for (int c8 = 0; c8 < 8; c8++)
             dst[c8] = make_uint4(pack2_bf16(v[8 * c8], v[8 * c8 + 1]), pack2_bf16(v[8 * c8 + 2], v[8 * c8 + 3]),
                                  pack2_bf16(v[8 * c8 + 4], v[8 * c8 + 5]), pack2_bf16(v[8 * c8 + 6], v[8 * c8 + 7]));
         }
       }
-    } else {
-      ok = false;
     }
     if (!ok && lane == 0) {
       *abort_flag = 1;
@@ -987,7 +1038,8 @@ int attn_bwd_tmem(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kQSmem));
     attr_set[ctx->device & 63] = true;
   }
-  const int64_t grid_kv = (int64_t)p.n_t * (split ? nH : nKV) * B;
+  const int64_t items_kv = (int64_t)p.n_t * (split ? nH : nKV) * B;
+  const int64_t grid_kv = items_kv < ctx->num_sms ? items_kv : ctx->num_sms;   // persistent
   const int64_t items_q = (int64_t)p.n_t * nH * B;
   const int64_t grid_q = items_q < ctx->num_sms ? items_q : ctx->num_sms;   // persistent
   FCU_REQUIRE(items_q <= INT32_MAX, "attention backward: grid too large");
