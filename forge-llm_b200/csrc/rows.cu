@@ -117,6 +117,41 @@ __global__ void embed_segsum_kernel(const unsigned long long *__restrict__ keys,
   }
 }
 
+// The same for D = 128 * NC: each lane keeps NC float4 of the row in
+// registers and every token row is one round of independent 16-byte loads.
+// Per element the order is unchanged: the existing dW value, then the tokens
+// in ascending t.
+template <int NC>
+__global__ void embed_segsum4_kernel(const unsigned long long *__restrict__ keys, int64_t T, int64_t V,
+                                     const float *__restrict__ dX, float *__restrict__ dW) {
+  constexpr int D = 128 * NC;
+  const int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= T) return;
+  const uint32_t id = (uint32_t)(keys[i] >> 32);
+  if (i > 0 && (uint32_t)(keys[i - 1] >> 32) == id) return;
+  if ((int32_t)id < 0 || (int64_t)(int32_t)id >= V) return;  // JS: out-of-range store is a no-op
+  float4 *row = reinterpret_cast<float4 *>(dW + (int64_t)id * D);
+  float4 acc[NC];
+#pragma unroll
+  for (int k = 0; k < NC; k++) acc[k] = row[lane + 32 * k];
+  for (int64_t s = i; s < T; s++) {
+    const unsigned long long key = keys[s];
+    if ((uint32_t)(key >> 32) != id) break;
+    const float4 *x = reinterpret_cast<const float4 *>(dX + (int64_t)(uint32_t)(key & 0xffffffffull) * D);
+#pragma unroll
+    for (int k = 0; k < NC; k++) {
+      const float4 v = x[lane + 32 * k];
+      acc[k].x += v.x;
+      acc[k].y += v.y;
+      acc[k].z += v.z;
+      acc[k].w += v.w;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NC; k++) row[lane + 32 * k] = acc[k];
+}
+
 // ---------------------------------------------------------------- rmsNorm
 // One warp per row.  inv[t] = 1/sqrt(sum(x^2)/D + eps) (double reduction,
 // stored fp32 as the JS Float32Array does); out = x * inv * w.
@@ -623,8 +658,22 @@ int fcu_embed_bwd(fcu_ctx *ctx, const float *dX, const int32_t *ids, int64_t T, 
     bitonic_smem_kernel<<<nchunks, 1024, 0, ctx->stream>>>(keys, k, k);
     FCU_CHECK_LAUNCH();
   }
-  embed_segsum_kernel<<<grid_for(T * 32, kThreads, 1 << 30), kThreads, 0, ctx->stream>>>(keys, T, V,
-                                                                                          D, dX, dW);
+  const int blocks = grid_for(T * 32, kThreads, 1 << 30);
+  const bool vec = D % 128 == 0 && D <= 1024 && (((uintptr_t)dX | (uintptr_t)dW) & 15) == 0;
+  switch (vec ? D / 128 : 0) {
+#define FCU_SEGSUM_CASE(nc) \
+  case nc: embed_segsum4_kernel<nc><<<blocks, kThreads, 0, ctx->stream>>>(keys, T, V, dX, dW); break;
+    FCU_SEGSUM_CASE(1)
+    FCU_SEGSUM_CASE(2)
+    FCU_SEGSUM_CASE(3)
+    FCU_SEGSUM_CASE(4)
+    FCU_SEGSUM_CASE(5)
+    FCU_SEGSUM_CASE(6)
+    FCU_SEGSUM_CASE(7)
+    FCU_SEGSUM_CASE(8)
+#undef FCU_SEGSUM_CASE
+    default: embed_segsum_kernel<<<blocks, kThreads, 0, ctx->stream>>>(keys, T, V, D, dX, dW);
+  }
   FCU_CHECK_LAUNCH();
   return FCU_OK;
 }

@@ -214,8 +214,12 @@ OR_API void or_embed_fwd(const float *W, const int32_t *ids, int64_t T, int64_t 
   for (int64_t t = 0; t < T; t++) memcpy(out + t * D, W + (int64_t)ids[t] * D, D * sizeof(float));
 }
 
-OR_API void or_embed_bwd(const float *g, const int32_t *ids, int64_t T, int64_t D, float *gW) {
+OR_API void or_embed_bwd(const float *g, const int32_t *ids, int64_t T, int64_t V, int64_t D,
+                         float *gW) {
   for (int64_t t = 0; t < T; t++) {
+    /* tensor.js:94-96: an out-of-range id indexes outside the Float32Array,
+     * whose store is a no-op. */
+    if (ids[t] < 0 || (int64_t)ids[t] >= V) continue;
     float *o = gW + (int64_t)ids[t] * D;
     const float *gr = g + t * D;
     for (int64_t d = 0; d < D; d++) o[d] = (float)((double)o[d] + (double)gr[d]);
@@ -808,7 +812,7 @@ OR_API float or_model_step(const or_cfg *c, const float *P, float *G, const int3
       gx = gxin;
     }
     /* x = embedLookup(tok_emb, ids) */
-    or_embed_bwd(gx, ids, N, D, G + Lo.tok_emb);
+    or_embed_bwd(gx, ids, N, c->vocab, D, G + Lo.tok_emb);
     free(gx);
   }
 

@@ -72,7 +72,7 @@ def _declare(L):
         "or_matmulT_bwd_dw": (None, [_f, _f, _f, _i64, _i64, _i64, _i64, _i64]),
         "or_matmulT_bwd": (None, [_f, _f, _f, _f, _f, _i64, _i64, _i64]),
         "or_embed_fwd": (None, [_f, _i, _i64, _i64, _f]),
-        "or_embed_bwd": (None, [_f, _i, _i64, _i64, _f]),
+        "or_embed_bwd": (None, [_f, _i, _i64, _i64, _i64, _f]),
         "or_rmsnorm_fwd": (None, [_f, _f, _i64, _i64, C.c_double, _f, _f]),
         "or_rmsnorm_bwd": (None, [_f, _f, _f, _f, _i64, _i64, _f, _f]),
         "or_rope_fwd": (None, [_f, _i64, C.c_int, C.c_int, C.c_int, C.c_double, C.c_int, _f]),
@@ -197,7 +197,7 @@ def embed_fwd(W, ids, V, D):
 def embed_bwd(g, ids, V, D, gW=None):
     ids = np.ascontiguousarray(ids, np.int32)
     gW = np.zeros(V * D, np.float32) if gW is None else gW
-    lib().or_embed_bwd(_fp(f32(g)), _ip(ids), ids.size, D, _fp(gW))
+    lib().or_embed_bwd(_fp(f32(g)), _ip(ids), ids.size, V, D, _fp(gW))
     return gW
 
 

@@ -387,3 +387,26 @@ def test_adam_clips_global_norm():
     b.grad = np.array([0, 4.0], np.float32)
     info = f.Adam([a, b], lr=0.1).step()
     assert abs(info["gnorm"] - 5.0) < 1e-12 and abs(info["scale"] - 0.2) < 1e-12
+
+
+@pytest.mark.parametrize("V,D,T", [(50, 128, 700), (3000, 768, 4096)])
+def test_embed_bwd_vectorized_bit_exact(V, D, T):
+    """Widths that take the register-cached segmented sum (D a multiple of
+    128): still bit-exact against the oracle's token-order scatter-add, with
+    a heavy id, accumulation into an existing gradient and out-of-range ids."""
+    f = F()
+    rng = O.RNG(V + D)
+    E = rng.normals(V * D)
+    ids = rng.ints(T, V)
+    ids[: T // 5] = 7
+    ids[3] = -1
+    ids[11] = V
+    g = rng.normals(T * D)
+    gE0 = rng.normals(V * D)
+    f.resetTape()
+    En = f.param(E)
+    En.grad = gE0.copy()
+    X = f.embedLookup(En, ids, V, D)
+    X.grad = g
+    X._b(X.grad)
+    assert np.array_equal(host(En.grad), O.embed_bwd(g, ids, V, D, gE0.copy()))
