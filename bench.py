@@ -62,17 +62,46 @@ class ClockSampler:
         self.proc = None
         self.lines = []
         self.t = None
+        self.mid_thread = None
+        self.mid_lines = []
 
     def start(self):
+        """Start sampling every 100 ms; returns once the sampler produces
+        output, with that pre-region sample discarded."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 3.0:
+                time.sleep(0.01)
+            self.lines.clear()
         except Exception:
             self.proc = None
+
+    def mid(self):
+        """One extra query while the GPU works through the steps just
+        enqueued, so a region shorter than the sampling period still has a
+        sample taken under load."""
+        self.mid_lines = []
+
+        def run():
+            self.mid_lines = self._one_shot()
+
+        self.mid_thread = threading.Thread(target=run, daemon=True)
+        self.mid_thread.start()
+
+    def _one_shot(self):
+        try:
+            r = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                               timeout=5)
+            return [ln.strip() for ln in r.stdout.splitlines() if ln.strip()]
+        except Exception:
+            return []
 
     def _read(self):
         for line in self.proc.stdout:
@@ -81,6 +110,10 @@ class ClockSampler:
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        end = []
+        if self.mid_thread is not None:
+            self.mid_thread.join(timeout=6)
+            end = self.mid_lines
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -90,7 +123,7 @@ class ClockSampler:
             self.t.join(timeout=2)
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines + end:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -193,6 +226,114 @@ def run_micro_gemm(args):
                       "peak_kind": kind}), flush=True)
 
 
+def _time_ms(fn, steps, warmup):
+    """Mean CUDA-event milliseconds of fn() over `steps` calls after `warmup`."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_config(args):
+    """The operator configs C1-C4 of the hot path, each on its seeded inputs
+    through the public API, one JSON line each (`--config c1|c2|c3|c4`)."""
+    import torch
+    import forgellm as F
+    from forgellm import autograd as AD
+    from forgellm._lib import call
+    F.set_precision(args.precision)
+    pk, kind = peaks()
+    dev = "cuda"
+    out = {"config": args.config, "precision": args.precision, "data": "synthetic (forge-llm RNG)"}
+    if args.config == "c2":                      # matmulT fwd + dX + dW, 4096 x 2048 -> 8192
+        M, K, N = 4096, 2048, 8192
+        rng = F.RNG(2)
+        X = F.param(torch.from_numpy(rng.normals(M * K)).to(dev))
+        W = F.param(torch.from_numpy(rng.normals(N * K)).to(dev))
+        g = torch.from_numpy(rng.normals(M * N)).to(dev)
+
+        def step():
+            F.resetTape()
+            X.grad, W.grad = None, None
+            Y = F.matmulT(X, W, M, K, N)
+            Y.grad = g
+            Y._b(Y.grad)
+
+        ms = _time_ms(step, args.steps, args.warmup)
+        fl = 3 * 2.0 * M * N * K
+        tf = fl / (ms / 1e3) / 1e12
+        out.update(metric="matmulT fwd+bwd TFLOP/s", value=tf, unit="TFLOP/s", ms=ms,
+                   roofline={"bound": "tensor", "achieved": tf, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                             "frac": tf / pk["bf16_tflops"], "peak_kind": f"bf16 dense burst ({kind})",
+                             "note": "op-level path: fp32 operands converted to bf16 inside the timed call"})
+    elif args.config == "c3":                    # crossEntropyMean fwd + bwd, 8192 x 32000
+        T, V = 8192, 32000
+        rng = F.RNG(3)
+        logits = F.param(torch.from_numpy(rng.normals(T * V, 2.0)).to(dev))
+        targets = torch.from_numpy(rng.ints(T, V)).to(dev)
+
+        def step():
+            F.resetTape()
+            logits.grad = None
+            L = F.crossEntropyMean(logits, targets, T, V)
+            L.grad = torch.ones(1, device=dev)
+            L._b(L.grad)
+
+        ms = _time_ms(step, args.steps, args.warmup)
+        gb = (2.0 * T * V * 4 + T * 4) / 1e9
+        bw = gb / (ms / 1e3)
+        out.update(metric="crossEntropyMean fwd+bwd GB/s", value=bw, unit="GB/s", ms=ms,
+                   roofline={"bound": "hbm", "achieved": bw, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                             "frac": bw / pk["hbm_gbs"], "traffic_algorithmic_gb": gb, "peak_kind": kind})
+    elif args.config == "c4":                    # causal GQA attention with RoPE, fused-path kernels
+        B, T, nH, nKV, dH = 8, 2048, 32, 8, 64
+        W = (nH + 2 * nKV) * dH
+        rng = F.RNG(4)
+        qkv = torch.from_numpy(rng.normals(B * T * W)).to(dev).to(torch.bfloat16)
+        dO = torch.from_numpy(rng.normals(B * T * nH * dH)).to(dev).to(torch.bfloat16)
+        O = torch.empty(B * T * nH * dH, device=dev, dtype=torch.bfloat16)
+        lse = torch.empty(B * nH * T, device=dev)
+        dqkv = torch.empty_like(qkv)
+        h = AD.ctx().handle
+
+        def step():
+            call("fcu_attn_fwd_bf16", h, qkv.data_ptr(), W, B, T, nH, nKV, dH, O.data_ptr(), lse.data_ptr())
+            call("fcu_attn_bwd_bf16", h, dO.data_ptr(), qkv.data_ptr(), W, O.data_ptr(), lse.data_ptr(),
+                 B, T, nH, nKV, dH, 10000.0, dqkv.data_ptr())
+
+        ms = _time_ms(step, args.steps, args.warmup)
+        fl = 3 * 2 * 2.0 * B * nH * (T * T / 2) * dH
+        tf = fl / (ms / 1e3) / 1e12
+        out.update(metric="causalAttn fwd+bwd TFLOP/s", value=tf, unit="TFLOP/s", ms=ms,
+                   roofline={"bound": "tensor", "achieved": tf, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                             "frac": tf / pk["bf16_tflops"], "peak_kind": f"bf16 dense burst ({kind})",
+                             "note": "algorithmic FLOPs (fwd 4, bwd 8 x B*H*T^2/2*d), recompute not counted"})
+    else:                                        # c1: the tiny char-LM train step
+        cfg = F.Config(vocabSize=64, dim=64, nLayers=2, nHeads=4, nKvHeads=4, hidden=176)
+        m = F.TrainableTransformer(cfg, seed=1)
+        opt = F.Adam(m.paramList, lr=3e-3)
+        ids = F.RNG(1).ints(65, 64)
+        inp, tgt = ids[:64], ids[1:65]
+
+        def step():
+            F.resetTape()
+            m.zeroGrad()
+            m.backward(m.loss(inp, tgt))
+            opt.step()
+
+        ms = _time_ms(step, args.steps, args.warmup)
+        out.update(metric="tiny train step (launch-latency bound)", value=ms * 1e3, unit="us/step",
+                   higher_is_better=False, tokens_per_s=64 / (ms / 1e3), ms=ms)
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -207,9 +348,15 @@ def main():
     ap.add_argument("--eager", action="store_true",
                     help="launch the step op by op instead of replaying its CUDA graph")
     ap.add_argument("--micro", choices=["gemm"], help="time one kernel alone (profiling)")
+    ap.add_argument("--zero", action="store_true",
+                    help="N > 1: shard Adam's state and update over the ranks (ZeRO-1)")
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4"],
+                    help="time one of the operator configs instead of the C5 train step")
     ap.add_argument("--shape", default="8192,2048,768")
     ap.add_argument("--op", default="fwd", choices=["fwd", "dx", "dw"])
     args = ap.parse_args()
+    if args.config:
+        return run_config(args)
     if args.micro == "gemm":
         run_micro_gemm(args)
         return
@@ -238,8 +385,13 @@ def main():
 
     cfg = F.Config(**C5)
     model = F.TrainableTransformer(cfg, seed=SEED)
-    opt = F.Adam(model.paramList, lr=LR)
-    dp = DataParallel(model) if world > 1 else None
+    if args.zero and world > 1:                 # ZeRO-1: sharded Adam state and update
+        from forgellm.dist import ShardedAdam
+        dp = DataParallel(model, shard=True)
+        opt = ShardedAdam(model, dp, lr=LR)
+    else:
+        opt = F.Adam(model.paramList, lr=LR)
+        dp = DataParallel(model) if world > 1 else None
     toks = F.RNG(SEED).ints(args.batch * (SEQ + 1), C5["vocabSize"]).reshape(args.batch, SEQ + 1)
     local_rows = toks if world == 1 else shard_rows(torch.from_numpy(toks), rank, world).numpy()
     batch_dev = torch.from_numpy(np.ascontiguousarray(local_rows)).cuda()
@@ -290,6 +442,7 @@ def main():
     for _ in range(args.steps):
         step(batch_dev)
     ev1.record(stream)
+    sampler.mid()
     torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1)
     clocks = sampler.stop()
@@ -358,7 +511,8 @@ def main():
             "data": "synthetic (RNG(5) tokens, initWeights seed 5)",
             "config": {"workload": "c5-125m-train-step",
                        "model": "llama-125m (forge-llm TrainableTransformer: V32000 D768 L12 H12/4 F2048)",
-                       "global_batch": args.batch, "seq_len": SEQ, "parallelism": f"dp{world}",
+                       "global_batch": args.batch, "seq_len": SEQ,
+                       "parallelism": f"dp{world}" + ("+zero1" if args.zero and world > 1 else ""),
                        "precision": args.precision, "l2": "working set >> L2 (GBs of activations)"},
             "e2e": {"value": e2e_value, "unit": "tokens/s",
                     "h2d_bytes_per_step": int(args.batch * (SEQ + 1) * 4),

@@ -238,4 +238,29 @@ int fcu_adam_step_sched(fcu_ctx *ctx, float *p, const float *g, float *m, float 
   return update_impl(ctx, p, g, m, v, n, nullptr, ss, info_dev, (__nv_bfloat16 *)p_bf16, hdev);
 }
 
+// The two halves of fcu_adam_step_sched for an optimizer whose update is
+// split into pieces (a rank's shard of every bucket): advance the schedule
+// once, then update each piece with the step's device-resident constants and
+// a caller-supplied (e.g. all-reduced) gradient sum of squares.
+int fcu_adam_sched_advance(fcu_ctx *ctx, const fcu_adam_sched *s, int32_t *t_dev, fcu_adam_hyper *h_dev) {
+  FCU_CTX(ctx);
+  FCU_REQUIRE(s && t_dev && h_dev && (((uintptr_t)h_dev & 7) == 0), "fcu_adam_sched_advance: bad args");
+  FCU_REQUIRE(s->total_steps > 0, "fcu_adam_sched_advance: total_steps must be > 0");
+  static_assert(sizeof(Hyper) == sizeof(fcu_adam_hyper), "Hyper mirrors fcu_adam_hyper");
+  adam_sched_kernel<<<1, 32, 0, ctx->stream>>>(s->lr, s->b1, s->b2, s->eps, s->wd, s->clip,
+                                               s->total_steps, t_dev, (Hyper *)h_dev);
+  FCU_CHECK_LAUNCH();
+  return FCU_OK;
+}
+
+int fcu_adam_update_dev(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int64_t n,
+                        const fcu_adam_hyper *h_dev, const double *sumsq_dev, double *info_dev,
+                        void *p_bf16) {
+  FCU_CTX(ctx);
+  FCU_REQUIRE(n >= 0 && p && g && m && v && h_dev && sumsq_dev, "fcu_adam_update_dev: bad args");
+  if (n == 0) return FCU_OK;
+  return update_impl(ctx, p, g, m, v, n, nullptr, sumsq_dev, info_dev, (__nv_bfloat16 *)p_bf16,
+                     (const Hyper *)h_dev);
+}
+
 }  // extern "C"

@@ -11,6 +11,7 @@ from .autograd import (Adam, Node, backward, gradCheck, leaf, linear, noGrad, op
 from .tensor import (causalAttn, causalAttnBatch, crossEntropyMean, embedLookup, matmulT,
                      ropeRows, rmsNorm, sliceCols, swigluRows, weightedSum)
 from .train import RNG, Config, TrainableTransformer, initWeights, train
+from .checkpoint import load_checkpoint, save_checkpoint
 
 
 def set_precision(mode: str) -> None:

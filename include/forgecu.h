@@ -302,6 +302,18 @@ typedef struct {
 int fcu_adam_step_sched(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int64_t n,
                         const fcu_adam_sched *s, int32_t *t_dev, double *info_dev, void *p_bf16);
 
+/* The halves of fcu_adam_step_sched, for an update split into pieces (a
+ * data-parallel rank's shard of every gradient bucket; no counterpart in the
+ * reference, whose Adam is one loop): fcu_adam_sched_advance increments
+ * t_dev once and writes that step's constants to h_dev (device memory);
+ * fcu_adam_update_dev then updates one piece with them and the caller's
+ * gradient sum of squares (the global one, all-reduced over the ranks).
+ * info_dev (3 doubles, may be NULL) receives {gnorm, scale, lr}. */
+int fcu_adam_sched_advance(fcu_ctx *ctx, const fcu_adam_sched *s, int32_t *t_dev, fcu_adam_hyper *h_dev);
+int fcu_adam_update_dev(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int64_t n,
+                        const fcu_adam_hyper *h_dev, const double *sumsq_dev, double *info_dev,
+                        void *p_bf16);
+
 /* Adam (fcu_adam_step semantics) that also writes bf16(p) into p_bf16, the
  * weight copy the bf16 GEMMs read.  sumsq_dev may be NULL (computed here). */
 int fcu_adam_step_shadow(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, int64_t n,
