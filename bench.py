@@ -282,9 +282,7 @@ def run_config(args):
         def step():
             F.resetTape()
             logits.grad = None
-            L = F.crossEntropyMean(logits, targets, T, V)
-            L.grad = torch.ones(1, device=dev)
-            L._b(L.grad)
+            F.backward(F.crossEntropyMean(logits, targets, T, V))
 
         ms = _time_ms(step, args.steps, args.warmup)
         gb = (2.0 * T * V * 4 + T * 4) / 1e9
@@ -330,7 +328,16 @@ def run_config(args):
 
         ms = _time_ms(step, args.steps, args.warmup)
         out.update(metric="tiny train step (launch-latency bound)", value=ms * 1e3, unit="us/step",
-                   higher_is_better=False, tokens_per_s=64 / (ms / 1e3), ms=ms)
+                   higher_is_better=False, tokens_per_s=64 / (ms / 1e3), ms=ms, mode="eager")
+        if m._use_fused():                       # the same step replayed as one CUDA graph
+            from forgellm.graph import CapturedStep
+            mg = F.TrainableTransformer(cfg, seed=1)
+            cs = CapturedStep(mg, F.Adam(mg.paramList, lr=3e-3), 1, 64)
+            batch = torch.from_numpy(ids.reshape(1, 65)).to(dev)
+            gms = _time_ms(lambda: cs(batch), args.steps, args.warmup)
+            out.update(value=gms * 1e3, tokens_per_s=64 / (gms / 1e3), ms=gms, mode="cuda graph",
+                       eager_us_per_step=ms * 1e3, launches_per_step=cs.launches_per_step)
+            cs.graph.reset()
     print(json.dumps(out), flush=True)
 
 

@@ -466,7 +466,8 @@ __global__ void __launch_bounds__(kCeThreads) ce_fwd_kernel(const float *logits,
   if (threadIdx.x == 0) row_loss[row] = lse - lt;
 }
 
-// Fused-path CE: bf16 gradient, loss per row.  Online max / sum in the
+// CE with the gradient as bf16 (the fused path) or fp32 (the operator), loss
+// per row.  Online max / sum in the
 // log2 domain (one FMA + one ex2 per logit), one block reduction, then a
 // second pass that re-reads the row (from L2: two 512-thread CTAs per SM keep
 // ~300 rows, under 40 MB, in flight) and writes (softmax - onehot) / T.
@@ -484,9 +485,17 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 constexpr int kCe2Threads = 512;
 constexpr int kCe2Unroll = 4;
 
+__device__ __forceinline__ void ce2_store4(__nv_bfloat16 *du, int64_t i4, float a, float b, float c, float d) {
+  reinterpret_cast<uint2 *>(du)[i4] = make_uint2(pack_bf16(a, b), pack_bf16(c, d));
+}
+__device__ __forceinline__ void ce2_store4(float *du, int64_t i4, float a, float b, float c, float d) {
+  reinterpret_cast<float4 *>(du)[i4] = make_float4(a, b, c, d);
+}
+
+template <typename TO>
 __global__ void __launch_bounds__(kCe2Threads, 2)
-    ce_bf16_kernel(const float *__restrict__ logits, const int32_t *__restrict__ targets, int64_t T,
-                   int64_t V, float *__restrict__ row_loss, __nv_bfloat16 *__restrict__ du) {
+    ce2_kernel(const float *__restrict__ logits, const int32_t *__restrict__ targets, int64_t T,
+               int64_t V, float *__restrict__ row_loss, TO *__restrict__ du) {
   __shared__ float shm[32], shs[32];
   constexpr float kL2e = 1.4426950408889634f;
   const int64_t row = blockIdx.x;
@@ -535,7 +544,7 @@ __global__ void __launch_bounds__(kCe2Threads, 2)
   for (int w = 0; w < kCe2Threads / 32; w++) S += shm[w] == -INFINITY ? 0.f : shs[w] * ex2_approx(shm[w] - M);
   const float lse2 = M + __log2f(S);            // log2-domain log-sum-exp
   const float invT = (float)(1.0 / (double)T);
-  uint2 *d2 = reinterpret_cast<uint2 *>(du + row * V);
+  TO *drow = du + row * V;
   for (int64_t base = threadIdx.x; base < V4; base += (int64_t)kCe2Threads * kCe2Unroll) {
     float4 v[kCe2Unroll];
 #pragma unroll
@@ -552,7 +561,7 @@ __global__ void __launch_bounds__(kCe2Threads, 2)
       const float o1 = (ex2_approx(fmaf(v[u].y, kL2e, -lse2)) - (i + 1 == tgt ? 1.f : 0.f)) * invT;
       const float o2 = (ex2_approx(fmaf(v[u].z, kL2e, -lse2)) - (i + 2 == tgt ? 1.f : 0.f)) * invT;
       const float o3 = (ex2_approx(fmaf(v[u].w, kL2e, -lse2)) - (i + 3 == tgt ? 1.f : 0.f)) * invT;
-      d2[i4] = make_uint2(pack_bf16(o0, o1), pack_bf16(o2, o3));
+      ce2_store4(drow, i4, o0, o1, o2, o3);
     }
   }
   if (threadIdx.x == 0) row_loss[row] = lse2 * 0.6931471805599453f - lt;
@@ -823,7 +832,9 @@ int fcu_ce_fwd(fcu_ctx *ctx, const float *logits, const int32_t *targets, int64_
   if (rc) return rc;
   float *row_loss = (float *)scr;
   bool aligned = ((uintptr_t)logits % 16 == 0) && ((uintptr_t)dunit % 16 == 0);
-  if (aligned && V % 4 == 0 && V <= (int64_t)kCeThreads * kCeVec * 4)
+  if (aligned && V % 4 == 0)
+    ce2_kernel<float><<<(int)T, kCe2Threads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
+  else if (aligned && V % 4 == 0 && V <= (int64_t)kCeThreads * kCeVec * 4)
     ce_fwd_kernel<true><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
   else
     ce_fwd_kernel<false><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
@@ -845,7 +856,7 @@ int fcu_ce_fwd_bf16grad(fcu_ctx *ctx, const float *logits, const int32_t *target
   __nv_bfloat16 *du = (__nv_bfloat16 *)dlogits_bf16;
   bool aligned = ((uintptr_t)logits % 16 == 0) && ((uintptr_t)du % 8 == 0);
   if (aligned && V % 4 == 0)
-    ce_bf16_kernel<<<(int)T, kCe2Threads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, du);
+    ce2_kernel<__nv_bfloat16><<<(int)T, kCe2Threads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, du);
   else if (aligned && V % 4 == 0 && V <= (int64_t)kCeThreads * kCeVec * 4)
     ce_fwd_kernel<true, __nv_bfloat16><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V,
                                                                                row_loss, du);
@@ -915,7 +926,9 @@ int fcu_ce_fwd_static(fcu_ctx *ctx, const float *logits, const int32_t *targets,
   // Every row writes its own slot before mean_kernel reads it, so nothing
   // left over from an earlier call is ever read.
   bool aligned = ((uintptr_t)logits % 16 == 0) && ((uintptr_t)dunit % 16 == 0);
-  if (aligned && V % 4 == 0 && V <= (int64_t)kCeThreads * kCeVec * 4)
+  if (aligned && V % 4 == 0)
+    ce2_kernel<float><<<(int)T, kCe2Threads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
+  else if (aligned && V % 4 == 0 && V <= (int64_t)kCeThreads * kCeVec * 4)
     ce_fwd_kernel<true><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
   else
     ce_fwd_kernel<false><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);

@@ -206,11 +206,19 @@ def crossEntropyMean(logits: Node, targets, T: int, V: int) -> Node:
     call("fcu_ce_fwd", c.handle, ptr(logits.data), ptr(tg), T, V, ptr(loss), ptr(dunit))
 
     def bwd(g):
+        # The usual case: this loss is the one backward() seeded with the
+        # constant 1 and the logits have no gradient storage yet, so the
+        # stored (P - OneHot)/T already is dLogits: adopt it, no second pass.
+        if out._seeded_one and logits._grad is None and logits._gslot is None:
+            logits._grad = dunit
+            logits._gzero = False
+            return
         cc = ctx()
         gL, a = logits._gout()
         call("fcu_axpy_dev", cc.handle, ptr(g), ptr(dunit), T * V, ptr(gL), a)
 
-    return op(loss, bwd)
+    out = op(loss, bwd)
+    return out
 
 
 def addTensors(a: Node, b: Node, n: int) -> Node:
