@@ -16,7 +16,7 @@ from .checkpoint import load_checkpoint, save_checkpoint
 
 def set_precision(mode: str) -> None:
     """Arithmetic of the contractions on the current device: "fp32"
-    (CUDA cores, parity), "tf32x3" or "bf16" (tcgen05 tensor cores)."""
+    (CUDA cores, parity) or "bf16" (tcgen05 tensor cores)."""
     from .autograd import ctx
     ctx().set_precision(PRECISIONS[mode])
 

@@ -13,8 +13,8 @@ import threading
 _PKG_ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB_PATH = os.environ.get("FORGECU_LIB", os.path.join(_PKG_ROOT, "libforgecu.so"))
 
-FCU_PREC_FP32, FCU_PREC_TF32X3, FCU_PREC_BF16 = 0, 1, 2
-PRECISIONS = {"fp32": FCU_PREC_FP32, "tf32x3": FCU_PREC_TF32X3, "bf16": FCU_PREC_BF16}
+FCU_PREC_FP32, FCU_PREC_BF16 = 0, 2
+PRECISIONS = {"fp32": FCU_PREC_FP32, "bf16": FCU_PREC_BF16}
 
 
 class ForgeCUError(RuntimeError):

@@ -46,12 +46,10 @@ typedef enum {
 /* Arithmetic used by the contractions (matmulT, attention).
  *   FP32   : fp32 operands and accumulation on the CUDA cores.  Parity mode:
  *            relL2 <= 1e-5 against the JS operators.
- *   TF32X3 : tensor cores (tcgen05 kind::tf32), each operand split into a
- *            tf32 head and a tf32 tail, three products, fp32 accumulate.
- *            Same relL2 <= 1e-5 bound as FP32.
  *   BF16   : tensor cores (tcgen05 kind::f16) on bf16-rounded operands, fp32
- *            accumulate.  Looser bound, relL2 <= 1e-2 (stated per test). */
-typedef enum { FCU_PREC_FP32 = 0, FCU_PREC_TF32X3 = 1, FCU_PREC_BF16 = 2 } fcu_precision;
+ *            accumulate.  Looser bound, relL2 <= 1e-2 (stated per test).
+ * (Value 1 is reserved; fcu_ctx_set_precision rejects it.) */
+typedef enum { FCU_PREC_FP32 = 0, FCU_PREC_BF16 = 2 } fcu_precision;
 
 typedef struct fcu_ctx fcu_ctx;
 
