@@ -16,6 +16,7 @@ constexpr int kThreads = 256;
 
 __global__ void sumsq_partial_kernel(const float *__restrict__ g, int64_t n,
                                      double *__restrict__ part, int vec) {
+  fcu::pdl_trigger();
   __shared__ double sh[32];
   double s = 0;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -33,6 +34,7 @@ __global__ void sumsq_partial_kernel(const float *__restrict__ g, int64_t n,
 
 __global__ void sumsq_final_kernel(const double *__restrict__ part, int nblk,
                                    double *__restrict__ out, int acc) {
+  fcu::pdl_trigger();
   if (threadIdx.x == 0 && blockIdx.x == 0) {
     double s = 0;
     for (int b = 0; b < nblk; b++) s += part[b];
@@ -59,6 +61,7 @@ __global__ void adam_update_kernel(float *__restrict__ p, const float *__restric
                                    const double *__restrict__ sumsq, double *__restrict__ info,
                                    int vec, __nv_bfloat16 *__restrict__ shadow,
                                    const Hyper *__restrict__ hdev) {
+  fcu::pdl_trigger();
   if (hdev) h = *hdev;  // the on-device schedule of fcu_adam_step_sched
   const double gnorm = sqrt(sumsq[0]);
   const double scale = gnorm > h.clip ? h.clip / gnorm : 1.0;
@@ -124,6 +127,7 @@ int sumsq_impl(fcu_ctx *ctx, const float *g, int64_t n, double *out, int acc) {
 __global__ void adam_sched_kernel(double lr0, double b1, double b2, double eps, double wd,
                                   double clip, double total, int32_t *__restrict__ t_dev,
                                   Hyper *__restrict__ out) {
+  fcu::pdl_trigger();
   if (threadIdx.x == 0 && blockIdx.x == 0) {
     const int t = ++t_dev[0];
     double tt = (double)t / total;

@@ -24,6 +24,7 @@ __global__ void __launch_bounds__(kRows) attn_fwd_kernel(const float *__restrict
                                                          int nH, int nKV, int dH, float scale,
                                                          float *__restrict__ O,
                                                          float *__restrict__ lse) {
+  fcu::pdl_trigger();
   extern __shared__ float smem[];
   float *Ks = smem;                   // [kRows][MAXD]
   float *Vs = smem + kRows * MAXD;    // [kRows][MAXD]
@@ -104,6 +105,7 @@ __global__ void __launch_bounds__(kRows) attn_fwd_kernel(const float *__restrict
 // Delta[b,h,t] = sum_d dO[t,h,d] * O[t,h,d]  (the rowsum(P * dP) of the JS).
 __global__ void attn_delta_kernel(const float *__restrict__ dO, const float *__restrict__ O,
                                   int B, int T, int nH, int dH, float *__restrict__ delta) {
+  fcu::pdl_trigger();
   int64_t rows = (int64_t)B * T * nH;
   int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
@@ -127,6 +129,7 @@ __global__ void __launch_bounds__(kRows) attn_bwd_dkdv_kernel(
     const float *__restrict__ dO, const float *__restrict__ lse, const float *__restrict__ delta,
     int T, int nH, int nKV, int dH, float scale, float *__restrict__ dK, float *__restrict__ dV,
     int acc) {
+  fcu::pdl_trigger();
   extern __shared__ float smem[];
   constexpr int P = MAXD + 1;
   float *Kown = smem;                    // [kRows][P]
@@ -234,6 +237,7 @@ __global__ void __launch_bounds__(kRows) attn_bwd_dq_kernel(
     const float *__restrict__ Q, const float *__restrict__ K, const float *__restrict__ V,
     const float *__restrict__ dO, const float *__restrict__ lse, const float *__restrict__ delta,
     int T, int nH, int nKV, int dH, float scale, float *__restrict__ dQ, int acc) {
+  fcu::pdl_trigger();
   extern __shared__ float smem[];
   constexpr int P = MAXD + 1;
   float *Ks = smem;                  // [kRows][MAXD]

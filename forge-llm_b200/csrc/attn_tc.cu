@@ -247,6 +247,7 @@ __device__ __forceinline__ void store_rows(View<void> dst, const float (&a)[D / 
 // ------------------------------------------------------------------ forward
 template <int D, typename TI, typename TO>
 __global__ void __launch_bounds__(kThreads) attn_fwd_tc_kernel(Args A) {
+  fcu::pdl_trigger();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   constexpr bool kAsync = sizeof(TI) == 2;
   __nv_bfloat16 *sQ = reinterpret_cast<__nv_bfloat16 *>(smem_raw);
@@ -359,6 +360,7 @@ __global__ void __launch_bounds__(kThreads) attn_fwd_tc_kernel(Args A) {
 // ------------------------------------------------------------------ backward dK dV
 template <int D, typename TI, typename TO>
 __global__ void __launch_bounds__(kThreads) attn_bwd_dkdv_tc_kernel(Args A) {
+  fcu::pdl_trigger();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   constexpr bool kAsync = sizeof(TI) == 2;
   __nv_bfloat16 *sK = reinterpret_cast<__nv_bfloat16 *>(smem_raw);
@@ -462,6 +464,7 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_dkdv_tc_kernel(Args A) {
 // (row, kv head, element pair).
 template <int D>
 __global__ void attn_kv_reduce_kernel(Args A, int group) {
+  fcu::pdl_trigger();
   const int64_t kvD = (int64_t)A.nKV * D;
   const int64_t pairs = A.rows * (kvD / 2);
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < pairs;
@@ -494,6 +497,7 @@ __global__ void attn_kv_reduce_kernel(Args A, int group) {
 // ------------------------------------------------------------------ backward dQ
 template <int D, typename TI, typename TO>
 __global__ void __launch_bounds__(kThreads) attn_bwd_dq_tc_kernel(Args A) {
+  fcu::pdl_trigger();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   constexpr bool kAsync = sizeof(TI) == 2;
   __nv_bfloat16 *sQ = reinterpret_cast<__nv_bfloat16 *>(smem_raw);
@@ -570,6 +574,7 @@ __global__ void __launch_bounds__(kThreads) attn_bwd_dq_tc_kernel(Args A) {
 // delta[b,h,t] = sum_d dO[t,h,d] * O[t,h,d] (the rowsum(P * dP) of the JS), one warp per row.
 template <typename TI>
 __global__ void attn_delta_tc_kernel(Args A, int B, int D) {
+  fcu::pdl_trigger();
   const int64_t rows = (int64_t)B * A.T * A.nH;
   const int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;

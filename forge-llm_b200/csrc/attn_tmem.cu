@@ -58,6 +58,7 @@ struct FwdParams {
 
 __global__ void __launch_bounds__(kThreads, 2)
     attn_fwd_tmem_kernel(const __grid_constant__ CUtensorMap tm, FwdParams p) {
+  fcu::pdl_trigger();
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t *sQ = smem + kOffQ, *sK = smem + kOffK, *sV = smem + kOffV;
   uint64_t *bars = (uint64_t *)(smem + kOffBar);
@@ -105,6 +106,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tO = tmem + 128, tP = tmem + 192;
+  pdl_wait();   // the previous kernel's outputs are complete from here on
 
   if (!aligned) {
     // nothing issued; fall through to the dealloc
@@ -348,6 +350,7 @@ __device__ __forceinline__ void rope_back(float &x, float &y, float2 cs) {
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_dkdv_tmem_kernel(const __grid_constant__ CUtensorMap tm_qkv,
                               const __grid_constant__ CUtensorMap tm_do, BwdParams p) {
+  fcu::pdl_trigger();
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t *sK = smem + kKV_K, *sV = smem + kKV_V, *sQ = smem + kKV_Q, *sG = smem + kKV_G;
   float *sL = (float *)(smem + kKV_L), *sDl = (float *)(smem + kKV_D);
@@ -410,6 +413,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 320;
   const uint32_t tPt = tmem + 384, tDt = tmem + 448;   // P^T, dS^T as bf16 pairs
+  pdl_wait();   // the previous kernel's outputs are complete from here on
 
   if (!aligned) {
   } else if (warp == 0) {
@@ -656,6 +660,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_dq_tmem_kernel(const __grid_constant__ CUtensorMap tm_qkv,
                             const __grid_constant__ CUtensorMap tm_do, BwdParams p) {
+  fcu::pdl_trigger();
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t *sQ = smem + kQ_Q, *sG = smem + kQ_G, *sK = smem + kQ_K, *sV = smem + kQ_V;
   uint64_t *bars = (uint64_t *)(smem + kQ_Bar);
@@ -699,6 +704,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tdP = tmem + 128, tdS = tmem + 256, tdQ0 = tmem + 320;
+  pdl_wait();   // the previous kernel's outputs are complete from here on
 
   if (!aligned) {
   } else if (warp == 0) {
@@ -895,6 +901,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 __global__ void attn_delta64_kernel(const __nv_bfloat16 *__restrict__ dO,
                                     const __nv_bfloat16 *__restrict__ O, int64_t units, int nH, int T,
                                     float *__restrict__ delta) {
+  fcu::pdl_trigger();
   const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t unit = t >> 3;                  // token row * nH + head
   float s = 0.f;
@@ -926,6 +933,7 @@ __global__ void attn_delta64_kernel(const __nv_bfloat16 *__restrict__ dO,
 __global__ void attn_kv_reduce64_kernel(const float *__restrict__ pk, const float *__restrict__ pv,
                                         int group, int64_t rows, int nH, int nKV, int T,
                                         const float2 *__restrict__ rope, __nv_bfloat16 *dqkv, int64_t ld) {
+  fcu::pdl_trigger();
   const int64_t kvD = (int64_t)nKV * kD, q4 = kvD / 4, n = rows * q4;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
     const int64_t row = e / q4;
@@ -985,7 +993,8 @@ int attn_fwd_tmem(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, i
   }
   const int64_t grid = (int64_t)p.n_qt * nH * B;
   FCU_REQUIRE(grid <= INT32_MAX, "attention: grid too large");
-  attn_fwd_tmem_kernel<<<(unsigned)grid, kThreads, kSmemBytes, ctx->stream>>>(map, p);
+  FCU_CHECK_CUDA(launch_pdl(attn_fwd_tmem_kernel, dim3((unsigned)grid), dim3(kThreads), kSmemBytes,
+                            ctx->stream, map, p));
   FCU_CHECK_LAUNCH();
   return FCU_OK;
 }
@@ -1043,7 +1052,8 @@ int attn_bwd_tmem(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv,
   const int64_t items_q = (int64_t)p.n_t * nH * B;
   const int64_t grid_q = items_q < ctx->num_sms ? items_q : ctx->num_sms;   // persistent
   FCU_REQUIRE(items_q <= INT32_MAX, "attention backward: grid too large");
-  attn_bwd_dkdv_tmem_kernel<<<(unsigned)grid_kv, kBwdThreads, kKVSmem, ctx->stream>>>(map_qkv, map_do, p);
+  FCU_CHECK_CUDA(launch_pdl(attn_bwd_dkdv_tmem_kernel, dim3((unsigned)grid_kv), dim3(kBwdThreads), kKVSmem,
+                            ctx->stream, map_qkv, map_do, p));
   FCU_CHECK_LAUNCH();
   if (split) {
     const int64_t n = (int64_t)B * T * nKV * kD / 4;
@@ -1053,7 +1063,8 @@ int attn_bwd_tmem(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv,
                                                             rope, (__nv_bfloat16 *)dqkv, ld_qkv);
     FCU_CHECK_LAUNCH();
   }
-  attn_bwd_dq_tmem_kernel<<<(unsigned)grid_q, kBwdThreads, kQSmem, ctx->stream>>>(map_qkv, map_do, p);
+  FCU_CHECK_CUDA(launch_pdl(attn_bwd_dq_tmem_kernel, dim3((unsigned)grid_q), dim3(kBwdThreads), kQSmem,
+                            ctx->stream, map_qkv, map_do, p));
   FCU_CHECK_LAUNCH();
   return FCU_OK;
 }

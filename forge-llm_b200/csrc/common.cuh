@@ -53,6 +53,34 @@ int attn_bwd_tmem(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv,
                   const float *lse, float *delta, int B, int T, int nH, int nKV, const float2 *rope,
                   void *dqkv, int split, float *pk, float *pv);
 
+// Programmatic dependent launch.  A kernel launched with launch_pdl may
+// start while the previous kernel in the stream is finishing: it runs its
+// prologue (barrier init, TMEM allocation) and must call pdl_wait() before
+// it reads or writes any global memory.  Every kernel on the training step
+// calls pdl_trigger() at its start, which lets such a dependent launch once
+// all of its own CTAs are resident.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// FORGECU_NO_PDL=1 in the environment launches these kernels plainly.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 }  // namespace fcu
 
 #define FCU_CHECK_CUDA(expr)                                                  \

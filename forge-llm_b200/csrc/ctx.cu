@@ -1,5 +1,6 @@
 // Context, error reporting and device-memory entry points of libforgecu.so.
 #include <stdarg.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <atomic>
@@ -12,6 +13,14 @@ static thread_local char g_err[1024] = "";
 static std::atomic<unsigned long long> g_launches{0};
 
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *e = getenv("FORGECU_NO_PDL");
+    return !(e && e[0] == '1');
+  }();
+  return on;
+}
 
 void set_error(const char *fmt, ...) {
   va_list ap;

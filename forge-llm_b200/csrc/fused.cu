@@ -35,6 +35,7 @@ __global__ void rmsnorm_fwd_bf16_kernel(const float *__restrict__ X, const float
                                         int64_t T, int64_t D, float eps,
                                         __nv_bfloat16 *__restrict__ out, float *__restrict__ inv,
                                         const float *__restrict__ A, float *__restrict__ Xout) {
+  fcu::pdl_trigger();
   const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= T) return;
@@ -83,6 +84,7 @@ __global__ void rmsnorm_fwd_bf16_rc_kernel(const float *__restrict__ X, const fl
                                            const float *__restrict__ w, int64_t T, float eps,
                                            float *__restrict__ Xout, __nv_bfloat16 *__restrict__ out,
                                            float *__restrict__ inv) {
+  fcu::pdl_trigger();
   constexpr int D = 128 * NC;
   const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -152,6 +154,7 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_bwd_fused_kernel(
     const float *__restrict__ G, const float *__restrict__ X, const float *__restrict__ w,
     const float *__restrict__ inv, int64_t T, int64_t D, int64_t rows_per_block,
     float *__restrict__ dX, int acc_dx, __nv_bfloat16 *__restrict__ dXb, float *__restrict__ part) {
+  fcu::pdl_trigger();
   extern __shared__ float sm[];  // [nwarps][D]
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int64_t D4 = D >> 2;
@@ -234,6 +237,7 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_bwd_fused_kernel(
 // threads summing every 8th partial, then a fixed-order sum of the 8.
 __global__ void colsum_kernel(const float *__restrict__ part, int nblk, int64_t D,
                               float *__restrict__ out, int acc) {
+  fcu::pdl_trigger();
   __shared__ float sh[8][33];
   const int64_t c = (int64_t)blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
@@ -253,6 +257,7 @@ __global__ void colsum_kernel(const float *__restrict__ part, int nblk, int64_t 
 // act[t, j] = silu(gu[t, j]) * gu[t, H + j]; 8 units per thread.
 __global__ void swiglu_fwd_bf16_kernel(const __nv_bfloat16 *__restrict__ gu, int64_t N, int64_t H,
                                        __nv_bfloat16 *__restrict__ act) {
+  fcu::pdl_trigger();
   const int64_t H8 = H >> 3, total = N * H8;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
        e += (int64_t)gridDim.x * blockDim.x) {
@@ -276,6 +281,7 @@ __global__ void swiglu_fwd_bf16_kernel(const __nv_bfloat16 *__restrict__ gu, int
 __global__ void swiglu_bwd_bf16_kernel(const __nv_bfloat16 *__restrict__ dact,
                                        const __nv_bfloat16 *__restrict__ gu, int64_t N, int64_t H,
                                        __nv_bfloat16 *__restrict__ dgu) {
+  fcu::pdl_trigger();
   const int64_t H8 = H >> 3, total = N * H8;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
        e += (int64_t)gridDim.x * blockDim.x) {
@@ -299,6 +305,7 @@ __global__ void swiglu_bwd_bf16_kernel(const __nv_bfloat16 *__restrict__ dact,
 }
 
 __global__ void to_bf16_kernel(const float *__restrict__ x, int64_t n, __nv_bfloat16 *__restrict__ y) {
+  fcu::pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     y[i] = __float2bfloat16_rn(x[i]);
@@ -306,6 +313,7 @@ __global__ void to_bf16_kernel(const float *__restrict__ x, int64_t n, __nv_bflo
 
 __global__ void scale_bf16_dev_kernel(__nv_bfloat16 *__restrict__ y, int64_t n,
                                       const float *__restrict__ alpha) {
+  fcu::pdl_trigger();
   const float a = alpha[0];
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)

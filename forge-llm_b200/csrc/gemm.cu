@@ -21,6 +21,7 @@ __global__ void __launch_bounds__(NT) sgemm_kernel(const float *__restrict__ A, 
                                                    const float *__restrict__ B, int64_t ldb,
                                                    float *__restrict__ C, int64_t ldc, int64_t M,
                                                    int64_t N, int64_t K, int beta) {
+  fcu::pdl_trigger();
   __shared__ float As[2][BK][BM + 4];
   __shared__ float Bs[2][BK][BN + 4];
   const int tid = threadIdx.x;

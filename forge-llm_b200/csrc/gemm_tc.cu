@@ -167,6 +167,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, TcParams p) {
+  fcu::pdl_trigger();
   constexpr int BN = TileCfg<BN_>::BN;
   constexpr int STAGES = TileCfg<BN_>::STAGES;
   constexpr int B_BYTES = TileCfg<BN_>::B_BYTES;
@@ -206,6 +207,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();   // the previous kernel's outputs are complete from here on
 
   // Work units: (output tile, K slice).  With split-K (p.splits > 1) unit u
   // covers k-blocks [kb0, kb1) of tile u / splits; its partial tile goes to
@@ -420,6 +422,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 // ------------------------------------------------------------------ fp32 -> bf16
 __global__ void to_bf16_kernel(const float *__restrict__ x, int64_t n, __nv_bfloat16 *__restrict__ y) {
+  fcu::pdl_trigger();
   const int64_t n4 = n >> 2;
   const float4 *x4 = reinterpret_cast<const float4 *>(x);
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
@@ -543,6 +546,7 @@ int partials(fcu_ctx *ctx, size_t bytes, void **out) {
 // summed in slice order (deterministic), for every output mode of the GEMM
 // epilogue.  One thread per pair of adjacent columns (RoPE rotates pairs).
 __global__ void splitk_reduce_kernel(TcParams p) {
+  fcu::pdl_trigger();
   const int64_t hp = (p.N + 1) / 2;  // column pairs per row
   const int64_t pairs = (int64_t)p.M * hp, mn = (int64_t)p.ws_rows * p.ldc;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -580,6 +584,7 @@ __global__ void splitk_reduce_kernel(TcParams p) {
 // The same with four adjacent columns per thread (16-byte loads of every
 // slice, one 16- or 8-byte store), for N % 4 == 0 and 16-byte aligned outputs.
 __global__ void splitk_reduce4_kernel(TcParams p) {
+  fcu::pdl_trigger();
   const int64_t q4 = p.N / 4;                   // column quads per row
   const int64_t quads = (int64_t)p.M * q4, mn = (int64_t)p.ws_rows * p.ldc;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -763,9 +768,11 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
   const int units = p.tiles_m * p.tiles_n * p.splits;
   const int grid = units < ctx->num_sms ? units : ctx->num_sms;
   if (bn == 256)
-    gemm_bf16_tc_kernel<256><<<grid, NUM_THREADS, TileCfg<256>::SMEM_BYTES, ctx->stream>>>(ta, tb, tc, p);
+    FCU_CHECK_CUDA(launch_pdl(gemm_bf16_tc_kernel<256>, dim3(grid), dim3(NUM_THREADS),
+                              TileCfg<256>::SMEM_BYTES, ctx->stream, ta, tb, tc, p));
   else
-    gemm_bf16_tc_kernel<128><<<grid, NUM_THREADS, TileCfg<128>::SMEM_BYTES, ctx->stream>>>(ta, tb, tc, p);
+    FCU_CHECK_CUDA(launch_pdl(gemm_bf16_tc_kernel<128>, dim3(grid), dim3(NUM_THREADS),
+                              TileCfg<128>::SMEM_BYTES, ctx->stream, ta, tb, tc, p));
   FCU_CHECK_LAUNCH();
   if (p.splits > 1) {
     const bool vec = N % 4 == 0 && (((uintptr_t)p.C | (uintptr_t)p.R | (uintptr_t)p.ws) & 15) == 0 &&
@@ -813,6 +820,7 @@ int gemm_tc(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float *C, i
 // (cos, sin) table [T][head_dim/2] in fp32 for the RoPE epilogue, rounded
 // once from the double angles of ropeRows (src/L2/tensor.js:141-143).
 __global__ void rope_table_f32_kernel(float2 *tab, int T, int half, int head_dim, double theta) {
+  fcu::pdl_trigger();
   const int64_t n = (int64_t)T * half;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
        e += (int64_t)gridDim.x * blockDim.x) {

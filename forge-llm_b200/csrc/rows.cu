@@ -24,6 +24,7 @@ inline int grid_for(int64_t n, int per_block, int cap) {
 // of an out-of-range typed-array slot does (undefined -> NaN on store).
 __global__ void embed_fwd_kernel(const float *__restrict__ W, const int32_t *__restrict__ ids,
                                  int64_t T, int64_t V, int64_t D, float *__restrict__ out) {
+  fcu::pdl_trigger();
   int64_t total = T * D;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
        e += (int64_t)gridDim.x * blockDim.x) {
@@ -37,6 +38,7 @@ __global__ void embed_fwd_kernel(const float *__restrict__ W, const int32_t *__r
 // within an id, by ascending t -- the order the JS loop adds them in.
 __global__ void embed_keys_kernel(const int32_t *__restrict__ ids, int64_t T, int64_t P,
                                   unsigned long long *__restrict__ keys) {
+  fcu::pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < P;
        i += (int64_t)gridDim.x * blockDim.x) {
     if (i < T) {
@@ -53,6 +55,7 @@ constexpr int kSortSpan = 2048;  // elements sorted per CTA in shared memory
 // Bitonic stages k in [k_lo, k_hi] (powers of two) restricted to strides
 // j < kSortSpan, on chunks of kSortSpan elements.
 __global__ void bitonic_smem_kernel(unsigned long long *__restrict__ a, int64_t k_lo, int64_t k_hi) {
+  fcu::pdl_trigger();
   __shared__ unsigned long long s[kSortSpan];
   const int64_t base = (int64_t)blockIdx.x * kSortSpan;
   for (int i = threadIdx.x; i < kSortSpan; i += blockDim.x) s[i] = a[base + i];
@@ -79,6 +82,7 @@ __global__ void bitonic_smem_kernel(unsigned long long *__restrict__ a, int64_t 
 
 __global__ void bitonic_global_kernel(unsigned long long *__restrict__ a, int64_t P, int64_t j,
                                       int64_t k) {
+  fcu::pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < P;
        i += (int64_t)gridDim.x * blockDim.x) {
     int64_t ixj = i ^ j;
@@ -98,6 +102,7 @@ __global__ void bitonic_global_kernel(unsigned long long *__restrict__ a, int64_
 __global__ void embed_segsum_kernel(const unsigned long long *__restrict__ keys, int64_t T,
                                     int64_t V, int64_t D, const float *__restrict__ dX,
                                     float *__restrict__ dW) {
+  fcu::pdl_trigger();
   int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
   if (i >= T) return;
@@ -124,6 +129,7 @@ __global__ void embed_segsum_kernel(const unsigned long long *__restrict__ keys,
 template <int NC>
 __global__ void embed_segsum4_kernel(const unsigned long long *__restrict__ keys, int64_t T, int64_t V,
                                      const float *__restrict__ dX, float *__restrict__ dW) {
+  fcu::pdl_trigger();
   constexpr int D = 128 * NC;
   const int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -158,6 +164,7 @@ __global__ void embed_segsum4_kernel(const unsigned long long *__restrict__ keys
 __global__ void rmsnorm_fwd_kernel(const float *__restrict__ X, const float *__restrict__ w,
                                    int64_t T, int64_t D, double eps, float *__restrict__ out,
                                    float *__restrict__ inv) {
+  fcu::pdl_trigger();
   int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
   if (row >= T) return;
@@ -181,6 +188,7 @@ __global__ void rmsnorm_bwd_kernel(const float *__restrict__ G, const float *__r
                                    const float *__restrict__ w, const float *__restrict__ inv,
                                    int64_t T, int64_t D, int64_t rows_per_block,
                                    float *__restrict__ dX, int acc_dx, float *__restrict__ part) {
+  fcu::pdl_trigger();
   extern __shared__ float sm[];  // [nwarps][D]
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   float *mine = sm + (int64_t)wid * D;
@@ -217,6 +225,7 @@ __global__ void rmsnorm_bwd_kernel(const float *__restrict__ G, const float *__r
 // threads summing every 8th partial, then a fixed-order sum of the 8.
 __global__ void colsum_kernel(const float *__restrict__ part, int nblk, int64_t D,
                               float *__restrict__ out, int acc) {
+  fcu::pdl_trigger();
   __shared__ float sh[8][33];
   const int64_t c = (int64_t)blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
@@ -235,6 +244,7 @@ __global__ void colsum_kernel(const float *__restrict__ part, int nblk, int64_t 
 // ---------------------------------------------------------------- ropeRows
 // tab[pos][i] = (cos, sin)(pos / theta^(2i/dHead)), in double as the JS.
 __global__ void rope_table_kernel(double2 *tab, int npos, int half, int dHead, double theta) {
+  fcu::pdl_trigger();
   int64_t n = (int64_t)npos * half;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
        e += (int64_t)gridDim.x * blockDim.x) {
@@ -251,6 +261,7 @@ template <bool BWD>
 __global__ void rope_kernel(const float *__restrict__ X, int64_t T, int nHead, int dHead, int pos0,
                             int posStride, const double2 *__restrict__ tab,
                             float *__restrict__ out, int acc) {
+  fcu::pdl_trigger();
   const int half = dHead >> 1;
   const int64_t D = (int64_t)nHead * dHead;
   const int64_t npairs = T * nHead * half;
@@ -285,6 +296,7 @@ __global__ void rope_kernel(const float *__restrict__ X, int64_t T, int nHead, i
 template <bool BWD>
 __global__ void slicecols_kernel(const float *__restrict__ src, int64_t M, int64_t K, int64_t off,
                                  int64_t len, float *__restrict__ dst, int acc) {
+  fcu::pdl_trigger();
   int64_t n = M * len;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
        e += (int64_t)gridDim.x * blockDim.x) {
@@ -302,6 +314,7 @@ __global__ void slicecols_kernel(const float *__restrict__ src, int64_t M, int64
 // ---------------------------------------------------------------- swiglu
 __global__ void swiglu_fwd_kernel(const float *__restrict__ G, const float *__restrict__ U,
                                   int64_t n, float *__restrict__ out) {
+  fcu::pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     float g = G[i];
@@ -313,6 +326,7 @@ __global__ void swiglu_fwd_kernel(const float *__restrict__ G, const float *__re
 __global__ void swiglu_bwd_kernel(const float *__restrict__ dO, const float *__restrict__ G,
                                   const float *__restrict__ U, int64_t n, float *__restrict__ dG,
                                   float *__restrict__ dU, int acc) {
+  fcu::pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     float g = G[i], d = dO[i];
@@ -332,6 +346,7 @@ __global__ void swiglu_bwd_kernel(const float *__restrict__ dO, const float *__r
 // ---------------------------------------------------------------- add
 __global__ void add_kernel(const float *__restrict__ a, const float *__restrict__ b, int64_t n,
                            float *__restrict__ out) {
+  fcu::pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     out[i] = a[i] + b[i];
@@ -339,6 +354,7 @@ __global__ void add_kernel(const float *__restrict__ a, const float *__restrict_
 
 __global__ void add_bwd_kernel(const float *__restrict__ g, int64_t n, float *__restrict__ da,
                                int acc_a, float *__restrict__ db, int acc_b) {
+  fcu::pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     float v = g[i];
@@ -403,6 +419,7 @@ __global__ void __launch_bounds__(kCeThreads) ce_fwd_kernel(const float *logits,
                                                             const int32_t *__restrict__ targets,
                                                             int64_t T, int64_t V,
                                                             float *row_loss, TO *dunit) {
+  fcu::pdl_trigger();
   __shared__ float shm[32], shs[32];
   const int64_t row = blockIdx.x;
   const float *l = logits + row * V;
@@ -496,6 +513,7 @@ template <typename TO>
 __global__ void __launch_bounds__(kCe2Threads, 2)
     ce2_kernel(const float *__restrict__ logits, const int32_t *__restrict__ targets, int64_t T,
                int64_t V, float *__restrict__ row_loss, TO *__restrict__ du) {
+  fcu::pdl_trigger();
   __shared__ float shm[32], shs[32];
   constexpr float kL2e = 1.4426950408889634f;
   const int64_t row = blockIdx.x;
@@ -569,6 +587,7 @@ __global__ void __launch_bounds__(kCe2Threads, 2)
 
 // loss = sum(row_loss) / T, summed in double in row order by one CTA.
 __global__ void mean_kernel(const float *__restrict__ v, int64_t n, float *__restrict__ out) {
+  fcu::pdl_trigger();
   __shared__ double sh[32];
   double s = 0;
   // fixed assignment: thread i takes rows i, i+blockDim, ... then a fixed tree
@@ -579,6 +598,7 @@ __global__ void mean_kernel(const float *__restrict__ v, int64_t n, float *__res
 
 __global__ void wsum_kernel(const float *__restrict__ Y, const float *__restrict__ t, int64_t n,
                             float *__restrict__ out) {
+  fcu::pdl_trigger();
   __shared__ double sh[32];
   double s = 0;
   for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += (double)Y[i] * (double)t[i];
@@ -588,6 +608,7 @@ __global__ void wsum_kernel(const float *__restrict__ Y, const float *__restrict
 
 __global__ void axpy_dev_kernel(const float *__restrict__ alpha, const float *__restrict__ x,
                                 int64_t n, float *__restrict__ y, int acc) {
+  fcu::pdl_trigger();
   const float a = alpha[0];
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
@@ -595,6 +616,7 @@ __global__ void axpy_dev_kernel(const float *__restrict__ alpha, const float *__
 }
 
 __global__ void scale_kernel(float *__restrict__ y, int64_t n, float a) {
+  fcu::pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     y[i] *= a;
