@@ -934,9 +934,48 @@ int gemm_tc_error(fcu_ctx *ctx) {
   FCU_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
   if (h) {
     set_error("tensor-core kernel: a bounded wait ran out (code %d)", h);
+    FCU_CHECK_CUDA(cudaMemsetAsync(err, 0, sizeof(int), ctx->stream));   // reported once
     return FCU_ERR_TIMEOUT;
   }
   return FCU_OK;
 }
 
+namespace {
+
+// One mbarrier whose phase 0 nothing completes: the bounded wait of the
+// tensor-core kernels runs out after `cycles` and the error word records
+// code 99, exactly as a stalled pipeline would, without faulting the GPU.
+__global__ void selftest_wait_kernel(int *err, long long cycles) {
+  fcu::pdl_trigger();
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const long long t0 = clock64();
+    bool done = false;
+    while (!(done = mbar_try_wait(&bar, 0)))
+      if (clock64() - t0 > cycles) break;
+    if (!done) atomicExch(err, 99);
+  }
+}
+
+}  // namespace
+
 }  // namespace fcu
+
+extern "C" int fcu_selftest_bounded_wait(fcu_ctx *ctx, int64_t cycles) {
+  using namespace fcu;
+  FCU_CTX(ctx);
+  FCU_REQUIRE(cycles >= 1000 && cycles <= 4000000000ll, "fcu_selftest_bounded_wait: cycles %lld",
+              (long long)cycles);
+  void *ws = nullptr;
+  int *err = nullptr;
+  int rc = workspace(ctx, 0, &ws, &err);
+  if (rc) return rc;
+  selftest_wait_kernel<<<1, 32, 0, ctx->stream>>>(err, (long long)cycles);
+  FCU_CHECK_LAUNCH();
+  return FCU_OK;
+}

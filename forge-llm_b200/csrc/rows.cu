@@ -585,6 +585,21 @@ __global__ void __launch_bounds__(kCe2Threads, 2)
   if (threadIdx.x == 0) row_loss[row] = lse2 * 0.6931471805599453f - lt;
 }
 
+// Training windows (train.js:258-262): out[b][i] = data[s_b + i], or the last
+// token of the stream where the window runs past its end.
+__global__ void gather_windows_kernel(const int32_t *__restrict__ data, int64_t n,
+                                      const int32_t *__restrict__ starts, int B, int T1,
+                                      int32_t *__restrict__ out) {
+  fcu::pdl_trigger();
+  const int64_t total = (int64_t)B * T1;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int b = (int)(e / T1), i = (int)(e - (int64_t)b * T1);
+    const int64_t k = (int64_t)starts[b] + i;
+    out[e] = (k >= 0 && k < n) ? data[k] : data[n - 1];
+  }
+}
+
 // loss = sum(row_loss) / T, summed in double in row order by one CTA.
 __global__ void mean_kernel(const float *__restrict__ v, int64_t n, float *__restrict__ out) {
   fcu::pdl_trigger();
@@ -862,6 +877,19 @@ int fcu_ce_fwd(fcu_ctx *ctx, const float *logits, const int32_t *targets, int64_
     ce_fwd_kernel<false><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
   FCU_CHECK_LAUNCH();
   mean_kernel<<<1, 1024, 0, ctx->stream>>>(row_loss, T, loss_out);
+  FCU_CHECK_LAUNCH();
+  return FCU_OK;
+}
+
+int fcu_gather_windows(fcu_ctx *ctx, const int32_t *data, int64_t n, const int32_t *starts, int B,
+                       int T1, int32_t *out) {
+  FCU_CTX(ctx);
+  FCU_REQUIRE(n > 0 && B >= 0 && T1 > 0 && data && starts && out, "fcu_gather_windows: bad args");
+  if (B == 0) return FCU_OK;
+  const int64_t total = (int64_t)B * T1;
+  int blocks = (int)((total + 255) / 256);
+  if (blocks > 4 * ctx->num_sms) blocks = 4 * ctx->num_sms;
+  gather_windows_kernel<<<blocks, 256, 0, ctx->stream>>>(data, n, starts, B, T1, out);
   FCU_CHECK_LAUNCH();
   return FCU_OK;
 }

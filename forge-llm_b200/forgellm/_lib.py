@@ -112,6 +112,8 @@ _SIGS = {
     "fcu_attn_bwd_bf16": (_INT, [_P, _P, _P, _I64, _P, _P, _INT, _INT, _INT, _INT, _INT, _D, _P]),
     "fcu_adam_step_shadow": (_INT, [_P, _P, _P, _P, _P, _I64, C.POINTER(AdamHyper), _P, _P, _P]),
     "fcu_adam_step_sched": (_INT, [_P, _P, _P, _P, _P, _I64, C.POINTER(AdamSched), _P, _P, _P]),
+    "fcu_selftest_bounded_wait": (_INT, [_P, _I64]),
+    "fcu_gather_windows": (_INT, [_P, _P, _I64, _P, _INT, _INT, _P]),
     "fcu_adam_sched_advance": (_INT, [_P, C.POINTER(AdamSched), _P, _P]),
     "fcu_adam_update_dev": (_INT, [_P, _P, _P, _P, _P, _I64, _P, _P, _P, _P]),
     "fcu_to_bf16": (_INT, [_P, _P, _I64, _P]),

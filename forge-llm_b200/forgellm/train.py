@@ -342,7 +342,16 @@ class TrainableTransformer:
 
 def train(model: TrainableTransformer, data, opts=None, **kw) -> list:
     """Training loop (train.js:246-276): B random windows per step, block-
-    diagonal batch loss, Adam with clip 1 and wd 0.01."""
+    diagonal batch loss, Adam with clip 1 and wd 0.01.
+
+    The token stream is uploaded once; each step's window starts are drawn
+    from the forge-llm RNG exactly as the JS draws them and the windows are
+    gathered on the device (fcu_gather_windows), so the batches are the
+    reference's.  On the fused bf16 path the step is replayed as one CUDA
+    graph (`graph=False` in the options runs it op by op); the gather writes
+    straight into the graph's batch buffer."""
+    from . import autograd as AD
+    from ._lib import call
     opts = dict(opts or {}, **kw)
     steps = opts.get("steps", 100)
     B = opts.get("batchSize", 8)
@@ -351,20 +360,44 @@ def train(model: TrainableTransformer, data, opts=None, **kw) -> list:
     logEvery = opts.get("logEvery", 10)
     rng = RNG(opts.get("seed", 7))
     opt = Adam(model.paramList, lr=lr, totalSteps=steps, clip=1.0, wd=0.01)
+    dev = model.flat_params.device
+    tokens = torch.as_tensor(np.asarray(data, dtype=np.int32)).to(dev)
+    n = tokens.numel()
+    T1 = seqLen + 1
+    use_graph = opts.get("graph", True) and model._use_fused()
+    cs = None
+    if use_graph:
+        from .graph import CapturedStep
+        cs = CapturedStep(model, opt, B, seqLen)
+        batch = cs.batch
+    else:
+        batch = torch.empty((B, T1), dtype=torch.int32, device=dev)
+    starts_host = torch.empty(B, dtype=torch.int32).pin_memory()
+    starts = torch.empty(B, dtype=torch.int32, device=dev)
     history = []
-    data = list(data)
     for step in range(steps):
-        batch = []
-        for _ in range(B):
-            s = rng.int(max(1, len(data) - seqLen - 1))
-            row = [data[s + i] if s + i < len(data) else data[-1] for i in range(seqLen + 1)]
-            batch.append(row)
-        resetTape()
-        model.zeroGrad()
-        lossNode = model.lossBatch(batch)
-        l = model.backward(lossNode)
-        info = opt.step()
+        for b in range(B):
+            starts_host[b] = rng.int(max(1, n - seqLen - 1))
+        starts.copy_(starts_host, non_blocking=True)
+        call("fcu_gather_windows", AD.ctx().handle, tokens.data_ptr(), n, starts.data_ptr(), B, T1,
+             batch.data_ptr())
+        if cs is not None:
+            loss_dev = cs(None)
+            info_dev = cs.info
+        else:
+            resetTape()
+            model.zeroGrad()
+            lossNode = model.lossBatch(batch)
+            loss_dev = lossNode.data
+            model.backward(lossNode)
+            info = opt.step()
         if step % logEvery == 0 or step == steps - 1:
+            l = float(loss_dev.reshape(-1)[0].item())
+            if cs is not None:
+                g_, _, lr_ = (float(x) for x in info_dev.cpu().tolist())
+                info = {"gnorm": g_, "lr": lr_}
             history.append({"step": step, "loss": l, "lr": info["lr"], "gnorm": info["gnorm"]})
             print(f"  step {step:4d}  loss {l:.4f}  lr {info['lr']:.2e}  |g| {info['gnorm']:.3f}")
+    if cs is not None:
+        cs.graph.reset()
     return history

@@ -64,8 +64,15 @@ int fcu_ctx_get_precision(const fcu_ctx *ctx);
 int fcu_sync(fcu_ctx *ctx);
 /* FCU_ERR_TIMEOUT if a kernel on this context recorded a bounded wait that
  * ran out (the kernel then returned early; its outputs are invalid).
- * Synchronises the context's stream and clears nothing. */
+ * Synchronises the context's stream; a recorded timeout is reported once
+ * (the device word is cleared after it is read). */
 int fcu_check_device_error(fcu_ctx *ctx);
+/* Failure-detection self-test (no counterpart in the reference): one kernel
+ * whose bounded mbarrier wait can never complete runs out after `cycles`
+ * SM clocks (1e3..4e9) and records the timeout as the tensor-core kernels
+ * do, without faulting the GPU; fcu_check_device_error then reports it and
+ * the context stays usable. */
+int fcu_selftest_bounded_wait(fcu_ctx *ctx, int64_t cycles);
 /* Kernels launched by this library since it was loaded (all contexts). */
 unsigned long long fcu_launch_count(void);
 
@@ -258,6 +265,14 @@ int fcu_axpy_dev(fcu_ctx *ctx, const float *alpha_dev, const float *x, int64_t n
 /* ---------------------------------------------------------------- weightedSum */
 /* out[0] = sum_i Y[i] t[i] (src/L2/tensor.js:380-389), device scalar. */
 int fcu_wsum_fwd(fcu_ctx *ctx, const float *Y, const float *t, int64_t n, float *out);
+
+/* ---------------------------------------------------------------- training windows */
+/* The batch of train() (src/L6/train.js:256-262) gathered on the device from
+ * a device-resident token stream: out[b*T1 + i] = data[starts[b] + i], or
+ * data[n-1] past the end of the stream.  starts (device, B values) are drawn
+ * on the host from the forge-llm RNG exactly as the JS draws them. */
+int fcu_gather_windows(fcu_ctx *ctx, const int32_t *data, int64_t n, const int32_t *starts, int B,
+                       int T1, int32_t *out);
 
 /* ---------------------------------------------------------------- Adam */
 typedef struct {
