@@ -348,6 +348,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int nbox = min(BN, p.N - n0) > 0 ? (min(BN, p.N - n0) + cw - 1) / cw : 0;
 #pragma unroll 1
       for (int c = 0; c < nbox; c++) {
+        const int n = n0 + c * cw;
+        // RoPE (cos, sin) of this row's position for the box's head, loaded
+        // before the TMEM read so the two latencies overlap (the box's 64
+        // columns lie inside one head: head_dim % 64 == 0)
+        const bool rope_box = bf16_out && p.mode == kOutBF16Rope && n < p.rope_cols && gm < p.M;
+        float2 cs[32];
+        if (rope_box) {
+          const int half = p.head_dim >> 1;
+          const float4 *cs4 = reinterpret_cast<const float4 *>(p.rope + (gm % p.rope_T) * half + (n % p.head_dim) / 2);
+#pragma unroll
+          for (int i = 0; i < 16; i++) {
+            const float4 t = cs4[i];
+            cs[2 * i] = make_float2(t.x, t.y);
+            cs[2 * i + 1] = make_float2(t.z, t.w);
+          }
+        }
         uint32_t r0[32], r1[32];
         tmem_ld32(tbase + (uint32_t)(c * cw), r0);
         if (bf16_out) tmem_ld32(tbase + (uint32_t)(c * cw + 32), r1);
@@ -365,23 +381,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint8_t *box = stg + (seq & 1) * EPI_BOX;
         if (lane == 0) bulk_wait_read<1>();        // the store that last used this buffer has read it
         __syncwarp();
-        const int n = n0 + c * cw;
         if (!bf16_out) {
 #pragma unroll
           for (int j = 0; j < 8; j++)
             *reinterpret_cast<float4 *>(box + lane * 128 + ((j ^ (lane & 7)) << 4)) =
                 make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         } else {
-          if (p.mode == kOutBF16Rope && n < p.rope_cols && gm < p.M) {
-            // the box's 64 columns lie inside one head (head_dim % 64 == 0)
-            const int half = p.head_dim >> 1;
-            const float2 *cs_row = p.rope + (gm % p.rope_T) * half + (n % p.head_dim) / 2;
+          if (rope_box) {
 #pragma unroll
             for (int i = 0; i < 32; i++) {
-              const float2 cs = cs_row[i];
               const float a = v[2 * i], b = v[2 * i + 1];
-              v[2 * i] = a * cs.x - b * cs.y;
-              v[2 * i + 1] = a * cs.y + b * cs.x;
+              v[2 * i] = a * cs[i].x - b * cs[i].y;
+              v[2 * i + 1] = a * cs[i].y + b * cs[i].x;
             }
           }
 #pragma unroll
