@@ -136,31 +136,31 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_wait_drain(q_full, 0);
     for (int i = nk - S < 0 ? 0 : nk - S; i < nk; i++) mbar_wait_drain(&k_full[i % S], (uint32_t)(i / S) & 1u);
     for (int i = nv - S < 0 ? 0 : nv - S; i < nv; i++) mbar_wait_drain(&v_full[i % S], (uint32_t)(i / S) & 1u);
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (whole warp; elect.sync picks the issuing lane)
     const uint32_t id_s = instr_desc_bf16(0, 0, kBM, kBN);   // Q, K both K-major
     const uint32_t id_o = instr_desc_bf16(0, 1, kBM, kD);    // P K-major, V MN-major
-    bool ok = mbar_wait(q_full, 0, abort_flag);
+    bool ok = warp_wait(q_full, 0, abort_flag);
     const uint64_t dQ = desc_k(smem_u32(sQ));
     const uint64_t dK0 = desc_k(smem_u32(sK)), dV0 = desc_mn(smem_u32(sV), kBN);
     constexpr uint64_t kTileStep = kTile >> 4;
     for (int j = 0; j <= nkv && ok; j++) {
       if (j < nkv) {
         const int s = j % S;
-        if (!mbar_wait(&k_full[s], (uint32_t)(j / S) & 1u, abort_flag)) { ok = false; break; }
-        if (j > 0 && !mbar_wait(s_free, (uint32_t)(j - 1) & 1u, abort_flag)) { ok = false; break; }
+        if (!warp_wait(&k_full[s], (uint32_t)(j / S) & 1u, abort_flag)) { ok = false; break; }
+        if (j > 0 && !warp_wait(s_free, (uint32_t)(j - 1) & 1u, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint64_t dK = dK0 + (uint64_t)s * kTileStep;
 #pragma unroll
         for (int k = 0; k < kD / 16; k++)
-          umma_bf16(tS, dQ + k * kDescKStep, dK + k * kDescKStep, id_s, k > 0 ? 1u : 0u);
-        umma_commit(s_full);
-        umma_commit(&k_empty[s]);
+          umma_bf16_w(tS, dQ + k * kDescKStep, dK + k * kDescKStep, id_s, k > 0 ? 1u : 0u);
+        umma_commit_w(s_full);
+        umma_commit_w(&k_empty[s]);
       }
       if (j > 0) {
         const int i = j - 1, s = i % S;
-        if (!mbar_wait(&v_full[s], (uint32_t)(i / S) & 1u, abort_flag) ||
-            !mbar_wait(p_full, (uint32_t)i & 1u, abort_flag)) {
+        if (!warp_wait(&v_full[s], (uint32_t)(i / S) & 1u, abort_flag) ||
+            !warp_wait(p_full, (uint32_t)i & 1u, abort_flag)) {
           ok = false;
           break;
         }
@@ -168,16 +168,16 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint64_t dV = dV0 + (uint64_t)s * kTileStep;
 #pragma unroll
         for (int k = 0; k < kBN / 16; k++)
-          umma_bf16_ts(tO, tP + (uint32_t)(8 * k), dV + k * kDescMNStep, id_o, (i > 0 || k > 0) ? 1u : 0u);
-        umma_commit(o_done);
-        umma_commit(&v_empty[s]);
+          umma_bf16_ts_w(tO, tP + (uint32_t)(8 * k), dV + k * kDescMNStep, id_o, (i > 0 || k > 0) ? 1u : 0u);
+        umma_commit_w(o_done);
+        umma_commit_w(&v_empty[s]);
       }
     }
     if (!ok) {
       *abort_flag = 1;
       atomicExch(p.err, 12);
     }
-    umma_commit(mma_done);
+    umma_commit_w(mma_done);
     mbar_wait_drain(mma_done, 0);
   } else if (warp >= 2) {
     // ---------------- softmax
@@ -467,8 +467,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         mbar_wait_drain(&q_full[i % kKStages], (uint32_t)(i / kKStages) & 1u);
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer
-    if (lane == 0) {
+    // ---------------- MMA issuer (whole warp; elect.sync picks the issuing lane)
+    {
       const uint32_t id_n128 = instr_desc_bf16(0, 0, kBM, kBN);
       const uint32_t id_n64 = instr_desc_bf16(0, 1, kBM, kD);
       constexpr uint64_t kTileStep = kTile >> 4;
@@ -479,36 +479,36 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       int u = 0, ii = 0, prev_u = 0, prev_s = 0, prev_kb = 0, prev_ii = 0;
       // dV += P^T dO, dK += dS^T Q for the previous unit (one unit behind its S / dP MMAs)
       auto issue_dvdk = [&]() -> bool {
-        if (!mbar_wait(pds_full, (uint32_t)prev_u & 1u, abort_flag)) return false;
-        if (prev_first && !mbar_wait(acc_free, ((uint32_t)prev_ii & 1u) ^ 1u, abort_flag)) return false;
+        if (!warp_wait(pds_full, (uint32_t)prev_u & 1u, abort_flag)) return false;
+        if (prev_first && !warp_wait(acc_free, ((uint32_t)prev_ii & 1u) ^ 1u, abort_flag)) return false;
         tc_fence_after();
         const uint64_t bq = dQm0 + (uint64_t)prev_s * kTileStep, bg = dGm0 + (uint64_t)prev_s * kTileStep;
 #pragma unroll
         for (int k = 0; k < kBM / 16; k++)
-          umma_bf16_ts(tdV, tPt + (uint32_t)(8 * k), bg + k * kDescMNStep, id_n64, (!prev_first || k > 0) ? 1u : 0u);
+          umma_bf16_ts_w(tdV, tPt + (uint32_t)(8 * k), bg + k * kDescMNStep, id_n64, (!prev_first || k > 0) ? 1u : 0u);
 #pragma unroll
         for (int k = 0; k < kBM / 16; k++)
-          umma_bf16_ts(tdK, tDt + (uint32_t)(8 * k), bq + k * kDescMNStep, id_n64, (!prev_first || k > 0) ? 1u : 0u);
-        umma_commit(pds_free);
-        umma_commit(&q_empty[prev_s]);
+          umma_bf16_ts_w(tdK, tDt + (uint32_t)(8 * k), bq + k * kDescMNStep, id_n64, (!prev_first || k > 0) ? 1u : 0u);
+        umma_commit_w(pds_free);
+        umma_commit_w(&q_empty[prev_s]);
         if (prev_last) {
-          umma_commit(acc_full);
-          umma_commit(&kv_empty[prev_kb]);
+          umma_commit_w(acc_full);
+          umma_commit_w(&kv_empty[prev_kb]);
         }
         return true;
       };
       for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x, ii++) {
         const Item w = item(idx);
         const int kb = ii & 1;
-        if (!mbar_wait(&kv_full[kb], (uint32_t)(ii >> 1) & 1u, abort_flag)) {
+        if (!warp_wait(&kv_full[kb], (uint32_t)(ii >> 1) & 1u, abort_flag)) {
           ok = false;
           break;
         }
         const uint64_t ak = dK0 + (uint64_t)kb * kTileStep, av = dV0 + (uint64_t)kb * kTileStep;
         for (int it = 0; it < w.n_iter; it++, u++) {
           const int s = u % kKStages;
-          if (!mbar_wait(&q_full[s], (uint32_t)(u / kKStages) & 1u, abort_flag) ||
-              (u > 0 && !mbar_wait(st_free, (uint32_t)(u - 1) & 1u, abort_flag))) {
+          if (!warp_wait(&q_full[s], (uint32_t)(u / kKStages) & 1u, abort_flag) ||
+              (u > 0 && !warp_wait(st_free, (uint32_t)(u - 1) & 1u, abort_flag))) {
             ok = false;
             break;
           }
@@ -516,11 +516,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const uint64_t bq = dQk0 + (uint64_t)s * kTileStep, bg = dGk0 + (uint64_t)s * kTileStep;
 #pragma unroll
           for (int k = 0; k < kD / 16; k++)
-            umma_bf16(tS, ak + k * kDescKStep, bq + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
+            umma_bf16_w(tS, ak + k * kDescKStep, bq + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
 #pragma unroll
           for (int k = 0; k < kD / 16; k++)
-            umma_bf16(tdP, av + k * kDescKStep, bg + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
-          umma_commit(st_full);
+            umma_bf16_w(tdP, av + k * kDescKStep, bg + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
+          umma_commit_w(st_full);
           if (have_prev && !issue_dvdk()) {
             ok = false;
             break;
@@ -539,7 +539,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         *abort_flag = 1;
         atomicExch(p.err, 22);
       }
-      umma_commit(mma_done);
+      umma_commit_w(mma_done);
       mbar_wait_drain(mma_done, 0);
     }
   } else {
@@ -572,9 +572,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int qc = q0 + cb;                 // first query of these columns
         const bool mask = qc < key || qc + 64 > p.T;
         uint32_t pp[32], dd[32];
+        // lse / delta of the next four columns are loaded one step ahead; the
+        // compiler barrier at the end of each step keeps it from hoisting all
+        // 32 loads to the top (their 128 registers would spill)
+        float4 l4n = L4[0], d4n = D4[0];
 #pragma unroll
         for (int c4 = 0; c4 < 16; c4++) {
-          const float4 l4 = L4[c4], d4 = D4[c4];
+          const float4 l4 = l4n, d4 = d4n;
+          if (c4 < 15) {
+            l4n = L4[c4 + 1];
+            d4n = D4[c4 + 1];
+          }
           const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
           float pr[4];
 #pragma unroll
@@ -589,6 +597,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           pp[2 * c4 + 1] = pack2_bf16(pr[2], pr[3]);
           dd[2 * c4] = pack2_bf16(pr[0] * (dp[4 * c4] - dv[0]), pr[1] * (dp[4 * c4 + 1] - dv[1]));
           dd[2 * c4 + 1] = pack2_bf16(pr[2] * (dp[4 * c4 + 2] - dv[2]), pr[3] * (dp[4 * c4 + 3] - dv[3]));
+          asm volatile("" ::: "memory");
         }
         // dV/dK of the previous unit must be done reading P^T / dS^T.
         if (u > 0 && !warp_wait(pds_free, (uint32_t)(u - 1) & 1u, abort_flag)) {
@@ -744,8 +753,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         mbar_wait_drain(&kv_full[i % kQStages], (uint32_t)(i / kQStages) & 1u);
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer
-    if (lane == 0) {
+    // ---------------- MMA issuer (whole warp; elect.sync picks the issuing lane)
+    {
       const uint32_t id_n128 = instr_desc_bf16(0, 0, kBM, kBN);
       const uint32_t id_n64 = instr_desc_bf16(0, 1, kBM, kD);
       const uint64_t dQ0 = desc_k(smem_u32(sQ)), dG0 = desc_k(smem_u32(sG));
@@ -756,31 +765,31 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       int u = 0, ii = 0, prev_u = 0, prev_s = 0, prev_qb = 0;
       // dQ += dS K for the previous unit (one unit behind its S / dP MMAs)
       auto issue_dq = [&]() -> bool {
-        if (!mbar_wait(ds_full, (uint32_t)prev_u & 1u, abort_flag)) return false;
+        if (!warp_wait(ds_full, (uint32_t)prev_u & 1u, abort_flag)) return false;
         tc_fence_after();
         const uint64_t bk = dKm0 + (uint64_t)prev_s * kTileStep;
         const uint32_t acc = tdQ0 + (uint32_t)(prev_qb * kD);
 #pragma unroll
         for (int k = 0; k < kBN / 16; k++)
-          umma_bf16_ts(acc, tdS + (uint32_t)(8 * k), bk + k * kDescMNStep, id_n64, (!prev_first || k > 0) ? 1u : 0u);
-        umma_commit(ds_free);
-        umma_commit(&kv_empty[prev_s]);
-        if (prev_last) umma_commit(&acc_full[prev_qb]);
+          umma_bf16_ts_w(acc, tdS + (uint32_t)(8 * k), bk + k * kDescMNStep, id_n64, (!prev_first || k > 0) ? 1u : 0u);
+        umma_commit_w(ds_free);
+        umma_commit_w(&kv_empty[prev_s]);
+        if (prev_last) umma_commit_w(&acc_full[prev_qb]);
         return true;
       };
       for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x, ii++) {
         const int qt = p.n_t - 1 - idx / per;
         const int qb = ii & 1;
-        if (!mbar_wait(&qg_full[qb], (uint32_t)(ii >> 1) & 1u, abort_flag) ||
-            !mbar_wait(&acc_free[qb], ((uint32_t)(ii >> 1) & 1u) ^ 1u, abort_flag)) {
+        if (!warp_wait(&qg_full[qb], (uint32_t)(ii >> 1) & 1u, abort_flag) ||
+            !warp_wait(&acc_free[qb], ((uint32_t)(ii >> 1) & 1u) ^ 1u, abort_flag)) {
           ok = false;
           break;
         }
         const uint64_t aq = dQ0 + (uint64_t)qb * kTileStep, ag = dG0 + (uint64_t)qb * kTileStep;
         for (int j = 0; j <= qt; j++, u++) {
           const int s = u % kQStages;
-          if (!mbar_wait(&kv_full[s], (uint32_t)(u / kQStages) & 1u, abort_flag) ||
-              (u > 0 && !mbar_wait(sp_free, (uint32_t)(u - 1) & 1u, abort_flag))) {
+          if (!warp_wait(&kv_full[s], (uint32_t)(u / kQStages) & 1u, abort_flag) ||
+              (u > 0 && !warp_wait(sp_free, (uint32_t)(u - 1) & 1u, abort_flag))) {
             ok = false;
             break;
           }
@@ -788,12 +797,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const uint64_t bk = dKk0 + (uint64_t)s * kTileStep, bv = dVk0 + (uint64_t)s * kTileStep;
 #pragma unroll
           for (int k = 0; k < kD / 16; k++)
-            umma_bf16(tS, aq + k * kDescKStep, bk + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
+            umma_bf16_w(tS, aq + k * kDescKStep, bk + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
 #pragma unroll
           for (int k = 0; k < kD / 16; k++)
-            umma_bf16(tdP, ag + k * kDescKStep, bv + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
-          umma_commit(sp_full);
-          if (j == qt) umma_commit(&qg_empty[qb]);   // this item's Q / dO are read
+            umma_bf16_w(tdP, ag + k * kDescKStep, bv + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
+          umma_commit_w(sp_full);
+          if (j == qt) umma_commit_w(&qg_empty[qb]);   // this item's Q / dO are read
           if (have_prev && !issue_dq()) {
             ok = false;
             break;
@@ -811,7 +820,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         *abort_flag = 1;
         atomicExch(p.err, 32);
       }
-      umma_commit(mma_done);
+      umma_commit_w(mma_done);
       mbar_wait_drain(mma_done, 0);
     }
   } else {

@@ -7,6 +7,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "swiglu_math.cuh"
 
 namespace {
 
@@ -267,12 +268,7 @@ __global__ void swiglu_fwd_bf16_kernel(const __nv_bfloat16 *__restrict__ gu, int
     const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w}, uw[4] = {u4.x, u4.y, u4.z, u4.w};
     uint32_t ow[4];
 #pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const float2 g = unpack_bf16(gw[k]), u = unpack_bf16(uw[k]);
-      const float a = g.x / (1.f + __expf(-g.x)) * u.x;
-      const float b = g.y / (1.f + __expf(-g.y)) * u.y;
-      ow[k] = pack_bf16(a, b);
-    }
+    for (int k = 0; k < 4; k++) ow[k] = fcu::swiglu_fwd_pair(gw[k], uw[k]);
     *reinterpret_cast<uint4 *>(act + t * H + j) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
   }
 }
@@ -293,12 +289,7 @@ __global__ void swiglu_bwd_bf16_kernel(const __nv_bfloat16 *__restrict__ dact,
                    uw[4] = {u4.x, u4.y, u4.z, u4.w};
     uint32_t og[4], ou[4];
 #pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const float2 d = unpack_bf16(dw[k]), g = unpack_bf16(gw[k]), u = unpack_bf16(uw[k]);
-      const float sx = 1.f / (1.f + __expf(-g.x)), sy = 1.f / (1.f + __expf(-g.y));
-      og[k] = pack_bf16(d.x * u.x * (sx + g.x * sx * (1.f - sx)), d.y * u.y * (sy + g.y * sy * (1.f - sy)));
-      ou[k] = pack_bf16(d.x * g.x * sx, d.y * g.y * sy);
-    }
+    for (int k = 0; k < 4; k++) fcu::swiglu_bwd_pair(dw[k], gw[k], uw[k], og[k], ou[k]);
     *reinterpret_cast<uint4 *>(dgu + t * 2 * H + j) = make_uint4(og[0], og[1], og[2], og[3]);
     *reinterpret_cast<uint4 *>(dgu + t * 2 * H + H + j) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
   }

@@ -22,6 +22,7 @@
 #include <string.h>
 
 #include "gemm.cuh"
+#include "swiglu_math.cuh"
 #include "tc_ptx.cuh"
 
 namespace fcu {
@@ -58,7 +59,14 @@ struct TileCfg {
 //   kOutBF16Rope Cb[m,n] = bf16(rope(acc)) for n < rope_cols, bf16(acc) after:
 //                interleaved pairs (2i, 2i+1) of each head_dim-wide head are
 //                rotated by the (cos, sin) of position m % rope_T.
-enum : int { kOutF32 = 0, kOutF32Res = 1, kOutBF16 = 2, kOutBF16Rope = 3 };
+//   kOutSwiGLU   the gate|up projection: a 256-wide tile holds gate units
+//                j0..j0+127 in accumulator columns [0,128) and the up units
+//                of the same j in [128,256) (B is loaded as those two row
+//                blocks); writes g and u to Cb [M, 2H] and silu(g) * u of the
+//                bf16-rounded values to act [M, H] (through tmC2).
+//   kOutSwiGLUBwd the down projection's input gradient d = bf16(acc) [M, H]
+//                turned into dg | du [M, 2H] with the forward's g | u (aux).
+enum : int { kOutF32 = 0, kOutF32Res = 1, kOutBF16 = 2, kOutBF16Rope = 3, kOutSwiGLU = 4, kOutSwiGLUBwd = 5 };
 
 struct TcParams {
   int M, N, K;
@@ -77,6 +85,8 @@ struct TcParams {
   float *ws;               // split-K partial tiles [splits][ws_rows][ldc]
   int ws_rows;             // M rounded up to the 128-row tile
   int tma_out;             // 1: epilogue stores through shared memory + TMA (tmC)
+  int H;                   // kOutSwiGLU*: hidden units
+  const __nv_bfloat16 *aux;  // kOutSwiGLUBwd: g | u [M, 2H]
 };
 
 using namespace tc;
@@ -162,11 +172,15 @@ __device__ __forceinline__ void store_chunk(const TcParams &p, int64_t gm, int n
   }
 }
 
-template <int BN_>
+// SW selects the epilogue at compile time: 0 the generic modes, 1
+// kOutSwiGLU, 2 kOutSwiGLUBwd (each instantiation holds one epilogue, so the
+// register allocation of one does not constrain the others).
+template <int BN_, int SW>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmC, TcParams p) {
+                        const __grid_constant__ CUtensorMap tmC,
+                        const __grid_constant__ CUtensorMap tmC2, TcParams p) {
   fcu::pdl_trigger();
   constexpr int BN = TileCfg<BN_>::BN;
   constexpr int STAGES = TileCfg<BN_>::STAGES;
@@ -244,7 +258,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int j = 0; j < BM / 64; j++) tma_load_2d(a + j * BK * 128, &tmA, m0 + 64 * j, k0, &full[s]);
         }
-        if (!p.b_mn) {
+        if (SW == 1) {
+          // gate rows j0.. then up rows H + j0.. of the same 128 hidden units
+          tma_load_2d(b, &tmB, k0, tn * 128, &full[s]);
+          tma_load_2d(b + 128 * 128, &tmB, k0, p.H + tn * 128, &full[s]);
+        } else if (!p.b_mn) {
           tma_load_2d(b, &tmB, k0, n0, &full[s]);
         } else {
 #pragma unroll
@@ -259,8 +277,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // Drain: every copy this thread issued has landed before the CTA exits.
     for (int i = it - STAGES < 0 ? 0 : it - STAGES; i < it; i++)
       mbar_wait(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u, abort_flag);
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (whole warp; elect.sync picks the issuing lane)
     const uint32_t idesc = instr_desc_bf16(p.a_mn, p.b_mn, BM, BN);
     const uint64_t dA0 = p.a_mn ? desc_mn(smem_u32(sA), BK) : desc_k(smem_u32(sA));
     const uint64_t dB0 = p.b_mn ? desc_mn(smem_u32(sB), BK) : desc_k(smem_u32(sB));
@@ -273,7 +291,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int kb1 = (int)((int64_t)nk * (sp + 1) / p.splits);
       const int acc = ti & 1;
       const uint32_t aph = (uint32_t)(ti >> 1) & 1u;
-      if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag)) {
+      if (!warp_wait(&tempty[acc], aph ^ 1u, abort_flag)) {
         ok = false;
         break;
       }
@@ -282,7 +300,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int kb = kb0; kb < kb1; kb++, it++) {
         const int s = it % STAGES;
         const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-        if (!mbar_wait(&full[s], ph, abort_flag)) {
+        if (!warp_wait(&full[s], ph, abort_flag)) {
           ok = false;
           break;
         }
@@ -291,18 +309,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint64_t b = dB0 + (uint64_t)s * (B_BYTES >> 4);
 #pragma unroll
         for (int k = 0; k < BK / UMMA_K; k++)
-          umma_bf16(d_tmem, a + k * kA, b + k * kB, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
-        umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+          umma_bf16_w(d_tmem, a + k * kA, b + k * kB, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+        umma_commit_w(&empty[s]);  // frees the stage once these MMAs have read it
       }
       if (!ok) break;
-      umma_commit(&tfull[acc]);  // accumulator complete
+      umma_commit_w(&tfull[acc]);  // accumulator complete
     }
     if (!ok) {
       *abort_flag = 1;
       atomicExch(p.err, 2);
     }
-    umma_commit(mma_done);
-    mbar_wait(mma_done, 0, abort_flag);
+    umma_commit_w(mma_done);
+    warp_wait(mma_done, 0, abort_flag);
   } else if (warp >= 2) {
     // ---------------- epilogue
     const int q = warp & 3;             // TMEM lane quarter this warp may access
@@ -331,7 +349,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int64_t gm = (int64_t)tm * BM + row;
       const int n0 = tn * BN;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      if (!p.tma_out) {
+      if (SW == 0 && !p.tma_out) {
         if (p.splits > 1) part.C = p.ws + (int64_t)sp * p.ws_rows * p.ldc;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; c++) {
@@ -345,6 +363,119 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         continue;
       }
       const int m_box = tm * BM + q * 32;          // first output row of this warp's boxes
+      // One 32-row x 64-column bf16 box of packed words w through the
+      // staging buffer to `map` at column x.
+      auto emit_bf16 = [&](const uint32_t *w, const CUtensorMap *map, int x) {
+        uint8_t *box = stg + (seq & 1) * EPI_BOX;
+        if (lane == 0) bulk_wait_read<1>();        // the store that last used this buffer has read it
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+          *reinterpret_cast<uint4 *>(box + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+              make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && m_box < p.M) {
+          tma_store_2d(map, box, x, m_box);
+          bulk_commit();
+        }
+        seq++;
+      };
+      // 64 accumulator columns from col as 32 bf16 pairs.
+      auto load_bf16x64 = [&](int col, uint32_t *w) {
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          uint32_t r[32];
+          tmem_ld32(tbase + (uint32_t)(col + 32 * h), r);
+#pragma unroll
+          for (int i = 0; i < 16; i++)
+            w[16 * h + i] = pack2_bf16(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+        }
+      };
+      if (SW == 1) {
+        const int j0 = tn * 128;
+#pragma unroll 1
+        for (int c = 0; c < 2; c++) {
+          uint32_t gw[32], uw[32];
+          load_bf16x64(c * 64, gw);
+          load_bf16x64(128 + c * 64, uw);
+          if (c == 1) {                            // accumulator no longer needed
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+          }
+          emit_bf16(gw, &tmC, j0 + c * 64);
+          emit_bf16(uw, &tmC, p.H + j0 + c * 64);
+#pragma unroll
+          for (int i = 0; i < 32; i++) gw[i] = swiglu_fwd_pair(gw[i], uw[i]);
+          emit_bf16(gw, &tmC2, j0 + c * 64);
+        }
+        continue;
+      }
+      if (SW == 2) {
+        const int nb = (min(BN, p.N - n0) + 63) / 64;   // p.N = H, a multiple of 64
+#pragma unroll 1
+        for (int c = 0; c < nb; c++) {
+          const int j = n0 + c * 64;
+          // dg goes through staging buffer 0 and du through buffer 1, both
+          // written 32 columns at a time
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+          // this row's forward g and u for the whole box, loaded before the
+          // TMEM reads so the latencies overlap
+          uint4 g4[8], u4[8];
+          if (gm < p.M) {
+            const uint4 *gp = reinterpret_cast<const uint4 *>(p.aux + gm * 2 * p.H + j);
+            const uint4 *up = reinterpret_cast<const uint4 *>(p.aux + gm * 2 * p.H + p.H + j);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+              g4[i] = __ldg(gp + i);
+              u4[i] = __ldg(up + i);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) g4[i] = u4[i] = make_uint4(0u, 0u, 0u, 0u);
+          }
+#pragma unroll
+          for (int h = 0; h < 2; h++) {
+            uint32_t r[32];
+            tmem_ld32(tbase + (uint32_t)(c * 64 + 32 * h), r);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+              const uint4 ga = g4[4 * h + i], ua = u4[4 * h + i];
+              const uint32_t gw[4] = {ga.x, ga.y, ga.z, ga.w};
+              const uint32_t uw[4] = {ua.x, ua.y, ua.z, ua.w};
+              uint32_t og[4], ou[4];
+#pragma unroll
+              for (int k = 0; k < 4; k++) {
+                const uint32_t dw = pack2_bf16(__uint_as_float(r[8 * i + 2 * k]), __uint_as_float(r[8 * i + 2 * k + 1]));
+                swiglu_bwd_pair(dw, gw[k], uw[k], og[k], ou[k]);
+              }
+              const int off = lane * 128 + (((4 * h + i) ^ (lane & 7)) << 4);
+              *reinterpret_cast<uint4 *>(stg + off) = make_uint4(og[0], og[1], og[2], og[3]);
+              *reinterpret_cast<uint4 *>(stg + EPI_BOX + off) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
+            }
+          }
+          if (c == nb - 1) {                       // accumulator no longer needed
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && m_box < p.M) {
+            tma_store_2d(&tmC, stg, j, m_box);
+            tma_store_2d(&tmC, stg + EPI_BOX, p.H + j, m_box);
+            bulk_commit();
+          }
+        }
+        if (nb == 0) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+        continue;
+      }
       const int nbox = min(BN, p.N - n0) > 0 ? (min(BN, p.N - n0) + cw - 1) / cw : 0;
 #pragma unroll 1
       for (int c = 0; c < nbox; c++) {
@@ -670,7 +801,28 @@ struct TcOut {
   __nv_bfloat16 *Cb = nullptr;
   const float2 *rope = nullptr;
   int rope_T = 1, rope_cols = 0, head_dim = 2;
+  __nv_bfloat16 *Cb2 = nullptr;       // kOutSwiGLU: act [M, H]
+  const __nv_bfloat16 *aux = nullptr; // kOutSwiGLUBwd: g | u [M, 2H]
 };
+
+namespace {
+
+// Launches one instantiation (its shared-memory opt-in set on first use).
+template <int BN_, int SW>
+int launch_tc(fcu_ctx *ctx, int grid, const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
+              const CUtensorMap &tc2, const TcParams &p) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    FCU_CHECK_CUDA(cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN_, SW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)TileCfg<BN_>::SMEM_BYTES));
+    attr_set = true;
+  }
+  FCU_CHECK_CUDA(launch_pdl(gemm_bf16_tc_kernel<BN_, SW>, dim3(grid), dim3(NUM_THREADS), TileCfg<BN_>::SMEM_BYTES,
+                            ctx->stream, ta, tb, tc, tc2, p));
+  return FCU_OK;
+}
+
+}  // namespace
 
 // out[M,N] = A . B in the layouts of `op` (bf16 operands), written as `o` says.
 int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfloat16 *B,
@@ -685,20 +837,22 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
   // 128-wide tile (twice the tiles).
   const int nk = (int)((K + BK - 1) / BK);
   const int64_t tiles256 = ((M + BM - 1) / BM) * ((N + 255) / 256);
+  const bool swiglu = o.mode == kOutSwiGLU || o.mode == kOutSwiGLUBwd;
   int splits = 1;
-  if (tiles256 < 2 * ctx->num_sms && nk >= 32) {
+  if (!swiglu && tiles256 < 2 * ctx->num_sms && nk >= 32) {
     int s = (int)((2 * ctx->num_sms + tiles256 - 1) / tiles256);
     s = s > 16 ? 16 : s;
     s = s > nk / 16 ? nk / 16 : s;
     if (s >= 2) splits = s;
   }
-  const int bn = (splits == 1 && tiles256 < 2 * ctx->num_sms && N > 128) ? 128 : 256;
+  // (the SwiGLU forward pairs gate and up halves in one 256-wide tile)
+  const int bn = (o.mode != kOutSwiGLU && splits == 1 && tiles256 < 2 * ctx->num_sms && N > 128) ? 128 : 256;
   CUtensorMap ta, tb;
   int a_mn = 0, b_mn = 0;
   switch (op) {
     case GemmOp::kFwd:
       rc = tc_make_map(&ta, A, M, K, K, 64, BM);
-      if (!rc) rc = tc_make_map(&tb, B, N, K, K, 64, (uint32_t)bn);
+      if (!rc) rc = tc_make_map(&tb, B, N, K, K, 64, o.mode == kOutSwiGLU ? 128u : (uint32_t)bn);
       break;
     case GemmOp::kDx:
       b_mn = 1;
@@ -729,7 +883,9 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
   p.a_mn = a_mn;
   p.b_mn = b_mn;
   p.tiles_m = (int)((M + BM - 1) / BM);
-  p.tiles_n = (int)((N + bn - 1) / bn);
+  p.tiles_n = o.mode == kOutSwiGLU ? (int)(N / 256) : (int)((N + bn - 1) / bn);
+  p.H = o.mode == kOutSwiGLU ? (int)(N / 2) : (int)N;
+  p.aux = o.aux;
   p.err = err;
   p.splits = splits;
   p.ws = nullptr;
@@ -742,10 +898,18 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
   }
   // TMA epilogue: needs 16-byte aligned output rows; the fp32 + residual
   // epilogue keeps the direct stores.
-  CUtensorMap tc;
+  CUtensorMap tc, tc2;
   memset(&tc, 0, sizeof(tc));
+  memset(&tc2, 0, sizeof(tc2));
   p.tma_out = 0;
-  if (splits > 1) {
+  if (swiglu) {
+    // g | u (or dg | du) [M, 2H] and, forward, act [M, H]: 64-column boxes
+    const uint64_t H = (uint64_t)p.H;
+    rc = tc_make_map(&tc, o.Cb, M, 2 * H, 2 * H, 64, 32);
+    if (!rc && o.mode == kOutSwiGLU) rc = tc_make_map(&tc2, o.Cb2, M, H, H, 64, 32);
+    if (rc) return rc;
+    p.tma_out = 1;
+  } else if (splits > 1) {
     if (N % 4 == 0) {
       rc = tc_make_map_f32(&tc, p.ws, (uint64_t)splits * p.ws_rows, N, N, 32, 32);
       if (rc) return rc;
@@ -764,26 +928,18 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
       p.tma_out = 1;
     }
   }
-  static bool attr_set[2] = {false, false};
-  if (!attr_set[bn == 128]) {
-    if (bn == 256)
-      FCU_CHECK_CUDA(cudaFuncSetAttribute(gemm_bf16_tc_kernel<256>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)TileCfg<256>::SMEM_BYTES));
-    else
-      FCU_CHECK_CUDA(cudaFuncSetAttribute(gemm_bf16_tc_kernel<128>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)TileCfg<128>::SMEM_BYTES));
-    attr_set[bn == 128] = true;
-  }
   const int units = p.tiles_m * p.tiles_n * p.splits;
   const int grid = units < ctx->num_sms ? units : ctx->num_sms;
-  if (bn == 256)
-    FCU_CHECK_CUDA(launch_pdl(gemm_bf16_tc_kernel<256>, dim3(grid), dim3(NUM_THREADS),
-                              TileCfg<256>::SMEM_BYTES, ctx->stream, ta, tb, tc, p));
-  else
-    FCU_CHECK_CUDA(launch_pdl(gemm_bf16_tc_kernel<128>, dim3(grid), dim3(NUM_THREADS),
-                              TileCfg<128>::SMEM_BYTES, ctx->stream, ta, tb, tc, p));
+  const int sw = o.mode == kOutSwiGLU ? 1 : o.mode == kOutSwiGLUBwd ? 2 : 0;
+  if (bn == 256) {
+    rc = sw == 1 ? launch_tc<256, 1>(ctx, grid, ta, tb, tc, tc2, p)
+       : sw == 2 ? launch_tc<256, 2>(ctx, grid, ta, tb, tc, tc2, p)
+                 : launch_tc<256, 0>(ctx, grid, ta, tb, tc, tc2, p);
+  } else {
+    rc = sw == 2 ? launch_tc<128, 2>(ctx, grid, ta, tb, tc, tc2, p)
+                 : launch_tc<128, 0>(ctx, grid, ta, tb, tc, tc2, p);
+  }
+  if (rc) return rc;
   FCU_CHECK_LAUNCH();
   if (p.splits > 1) {
     const bool vec = N % 4 == 0 && (((uintptr_t)p.C | (uintptr_t)p.R | (uintptr_t)p.ws) & 15) == 0 &&
@@ -917,6 +1073,25 @@ extern "C" int fcu_gemm_bf16(fcu_ctx *ctx, int op, const void *A, const void *B,
       if (rc) return rc;
       break;
     }
+    case FCU_OUT_BF16_SWIGLU:
+      FCU_REQUIRE(gop == GemmOp::kFwd, "fcu_gemm_bf16: FCU_OUT_BF16_SWIGLU needs op FCU_GEMM_FWD");
+      FCU_REQUIRE(N % 256 == 0, "fcu_gemm_bf16: FCU_OUT_BF16_SWIGLU needs N = 2H with H %% 128 == 0 (N=%lld)",
+                  (long long)N);
+      FCU_REQUIRE(out->out2 != nullptr && ((((uintptr_t)out->out) | (uintptr_t)out->out2) & 15) == 0,
+                  "fcu_gemm_bf16: FCU_OUT_BF16_SWIGLU needs 16-byte aligned out and out2");
+      o.mode = kOutSwiGLU;
+      o.Cb = (__nv_bfloat16 *)out->out;
+      o.Cb2 = (__nv_bfloat16 *)out->out2;
+      break;
+    case FCU_OUT_BF16_SWIGLU_BWD:
+      FCU_REQUIRE(N % 64 == 0, "fcu_gemm_bf16: FCU_OUT_BF16_SWIGLU_BWD needs N = H with H %% 64 == 0 (N=%lld)",
+                  (long long)N);
+      FCU_REQUIRE(out->aux != nullptr && ((((uintptr_t)out->out) | (uintptr_t)out->aux) & 15) == 0,
+                  "fcu_gemm_bf16: FCU_OUT_BF16_SWIGLU_BWD needs 16-byte aligned out and aux");
+      o.mode = kOutSwiGLUBwd;
+      o.Cb = (__nv_bfloat16 *)out->out;
+      o.aux = (const __nv_bfloat16 *)out->aux;
+      break;
     default:
       set_error("fcu_gemm_bf16: unknown output mode %d", out->mode);
       return FCU_ERR_ARG;

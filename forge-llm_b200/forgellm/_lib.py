@@ -35,11 +35,13 @@ class GemmOut(C.Structure):
     """fcu_gemm_out."""
     _fields_ = [("mode", C.c_int), ("out", C.c_void_p), ("accumulate", C.c_int),
                 ("residual", C.c_void_p), ("rope_T", C.c_int), ("rope_cols", C.c_int),
-                ("head_dim", C.c_int), ("rope_theta", C.c_double)]
+                ("head_dim", C.c_int), ("rope_theta", C.c_double), ("out2", C.c_void_p),
+                ("aux", C.c_void_p)]
 
 
 GEMM_FWD, GEMM_DX, GEMM_DW = 0, 1, 2
 OUT_F32, OUT_F32_RESIDUAL, OUT_BF16, OUT_BF16_ROPE = 0, 1, 2, 3
+OUT_BF16_SWIGLU, OUT_BF16_SWIGLU_BWD = 4, 5
 
 
 class AdamHyper(C.Structure):

@@ -14,7 +14,9 @@ into neighbours:
   epilogues; in the backward the residual gradient is updated in place by
   the fused RMSNorm backward, which also emits its bf16 copy;
 * gate and up are one GEMM against the contiguous [ffn_gate; ffn_up] block of
-  the flat parameters (paramList order puts them back to back);
+  the flat parameters (paramList order puts them back to back); SwiGLU and
+  its backward run as separate HBM-bound kernels (a GEMM-epilogue variant of
+  both exists, bit-identical, behind `fuse_swiglu`, and is slower on B200);
 * cross-entropy writes (P - onehot)/T directly in bf16 for the LM-head
   backward.
 
@@ -29,8 +31,8 @@ import ctypes as C
 import torch
 
 from . import autograd as AD
-from ._lib import (GEMM_DW, GEMM_DX, GEMM_FWD, OUT_BF16, OUT_BF16_ROPE, OUT_F32,
-                   OUT_F32_RESIDUAL, GemmOut, call)
+from ._lib import (GEMM_DW, GEMM_DX, GEMM_FWD, OUT_BF16, OUT_BF16_ROPE, OUT_BF16_SWIGLU,
+                   OUT_BF16_SWIGLU_BWD, OUT_F32, OUT_F32_RESIDUAL, GemmOut, call)
 from .tensor import _timed
 
 BF16 = torch.bfloat16
@@ -91,14 +93,25 @@ class FusedStep:
         self.dO = e(N * qD, dt=BF16)
         self.dqkv = e(N * c.qkvOut, dt=BF16)
         self.ids = None
+        # SwiGLU in the gate|up and down-gradient GEMM epilogues: the same
+        # bits as the standalone kernels, but off by default -- on B200 the
+        # GEMM epilogue's stores already limit those short-K products, and
+        # the extra g/u/act traffic there (measured at the config-5 shapes:
+        # 644 us vs 360 + 150 us forward, 842 us vs 207 + 210 us backward)
+        # costs more than the separate HBM passes it saves.
+        self.fuse_swiglu = False
+        self.can_fuse_swiglu = H % 128 == 0
 
     # ------------------------------------------------------------ helpers
-    def _gemm(self, h, op, A, B, M, N, K, mode, out, accumulate=0, residual=None, rope=False):
+    def _gemm(self, h, op, A, B, M, N, K, mode, out, accumulate=0, residual=None, rope=False,
+              out2=None, aux=None):
         c = self.m.cfg
         o = GemmOut(mode, out.data_ptr(), accumulate,
                     residual.data_ptr() if residual is not None else None,
                     self.T if rope else 0, (c.nHeads + c.nKvHeads) * c.dHead if rope else 0,
-                    c.dHead if rope else 0, float(c.ropeTheta) if rope else 0.0)
+                    c.dHead if rope else 0, float(c.ropeTheta) if rope else 0.0,
+                    out2.data_ptr() if out2 is not None else None,
+                    aux.data_ptr() if aux is not None else None)
         _timed(2 * M * N * K,
                lambda: call("fcu_gemm_bf16", h, op, A.data_ptr(), B.data_ptr(), M, N, K, C.byref(o)))
 
@@ -132,8 +145,12 @@ class FusedStep:
             call("fcu_rmsnorm_fwd_bf16_add", h, L.x.data_ptr(), self.br.data_ptr(),
                  Lp["ln2"].data.data_ptr(), N, D, eps, L.x1.data_ptr(), L.xn2.data_ptr(),
                  L.inv2.data_ptr())
-            self._gemm(h, GEMM_FWD, L.xn2, Lw["ffn_gu"], N, 2 * H, D, OUT_BF16, L.gu)
-            call("fcu_swiglu_fwd_bf16", h, L.gu.data_ptr(), N, H, L.act.data_ptr())
+            if self.fuse_swiglu and self.can_fuse_swiglu:
+                self._gemm(h, GEMM_FWD, L.xn2, Lw["ffn_gu"], N, 2 * H, D, OUT_BF16_SWIGLU, L.gu,
+                           out2=L.act)
+            else:
+                self._gemm(h, GEMM_FWD, L.xn2, Lw["ffn_gu"], N, 2 * H, D, OUT_BF16, L.gu)
+                call("fcu_swiglu_fwd_bf16", h, L.gu.data_ptr(), N, H, L.act.data_ptr())
             # x_next = x1 + act.down^T, added inside the next ln1 (or ln_f)
             self._gemm(h, GEMM_FWD, L.act, Lw["ffn_down"], N, D, H, OUT_F32, self.br)
             if l + 1 < c.nLayers:
@@ -173,12 +190,16 @@ class FusedStep:
              self.gx_b.data_ptr(), gl.data_ptr(), al)
         for l in range(c.nLayers - 1, -1, -1):
             L, Lp, Lw = self.layers[l], P["layers"][l], W["layers"][l]
-            # ff = act . Wdown^T  (dY = g_x2, in gx / gx_b)
-            self._gemm(h, GEMM_DX, self.gx_b, Lw["ffn_down"], N, H, D, OUT_BF16, self.dact)
+            # ff = act . Wdown^T  (dY = g_x2, in gx / gx_b); d act -> d[g | u]
+            if self.fuse_swiglu and self.can_fuse_swiglu:
+                self._gemm(h, GEMM_DX, self.gx_b, Lw["ffn_down"], N, H, D, OUT_BF16_SWIGLU_BWD,
+                           self.dgu, aux=L.gu)
+            else:
+                self._gemm(h, GEMM_DX, self.gx_b, Lw["ffn_down"], N, H, D, OUT_BF16, self.dact)
+                call("fcu_swiglu_bwd_bf16", h, self.dact.data_ptr(), L.gu.data_ptr(), N, H,
+                     self.dgu.data_ptr())
             gd, ad = Lp["ffn_down"]._gout()
             self._gemm(h, GEMM_DW, self.gx_b, L.act, D, H, N, OUT_F32, gd, accumulate=ad)
-            call("fcu_swiglu_bwd_bf16", h, self.dact.data_ptr(), L.gu.data_ptr(), N, H,
-                 self.dgu.data_ptr())
             # [g | u] = xn2 . [Wgate; Wup]^T
             self._gemm(h, GEMM_DX, self.dgu, Lw["ffn_gu"], N, D, 2 * H, OUT_F32, self.dxn)
             gg, ag = Lp["ffn_gate"]._gout()

@@ -104,7 +104,23 @@ int fcu_matmulT_bwd(fcu_ctx *ctx, const float *dY, const float *X, const float *
  * does as separate ops (residual add, RoPE, bf16 copies of gradients), so no
  * fp32 -> bf16 conversion pass or column slice is ever run. */
 enum { FCU_GEMM_FWD = 0, FCU_GEMM_DX = 1, FCU_GEMM_DW = 2 };
-enum { FCU_OUT_F32 = 0, FCU_OUT_F32_RESIDUAL = 1, FCU_OUT_BF16 = 2, FCU_OUT_BF16_ROPE = 3 };
+enum {
+  FCU_OUT_F32 = 0,
+  FCU_OUT_F32_RESIDUAL = 1,
+  FCU_OUT_BF16 = 2,
+  FCU_OUT_BF16_ROPE = 3,
+  /* gate|up projection with swigluRows (tensor.js:272-290) in the epilogue:
+   * op FCU_GEMM_FWD, B = [Wgate; Wup] with N = 2H rows, H % 128 == 0;
+   * out = g | u bf16 [M, 2H] as BF16 would write it, out2 = silu(g) * u bf16
+   * [M, H] from the bf16-rounded g and u (bit-identical to
+   * fcu_swiglu_fwd_bf16 applied to out) */
+  FCU_OUT_BF16_SWIGLU = 4,
+  /* down-projection input gradient with the swigluRows backward in the
+   * epilogue: N = H (H % 64 == 0), aux = the forward's g | u bf16 [M, 2H];
+   * out = dg | du bf16 [M, 2H], computed from bf16(A.B) (bit-identical to
+   * BF16 output followed by fcu_swiglu_bwd_bf16) */
+  FCU_OUT_BF16_SWIGLU_BWD = 5
+};
 
 typedef struct {
   int mode;               /* FCU_OUT_* */
@@ -115,6 +131,8 @@ typedef struct {
   int rope_cols;          /* columns [0, rope_cols) are rotated (q and k of a fused qkv) */
   int head_dim;
   double rope_theta;
+  void *out2;             /* FCU_OUT_BF16_SWIGLU: the activation output */
+  const void *aux;        /* FCU_OUT_BF16_SWIGLU_BWD: the forward's gate|up values */
 } fcu_gemm_out;
 
 /* One tcgen05 contraction on bf16 operands (fp32 accumulate) in the layouts

@@ -85,6 +85,33 @@ def test_fused_step_is_deterministic_and_accumulates():
     assert np.array_equal(host(m.flat_grads), g1)
 
 
+@pytest.mark.parametrize("kw,B,T", [
+    (dict(dim=64, hidden=128, nLayers=2, nHeads=4, nKvHeads=2, vocabSize=96), 2, 70),
+    (dict(dim=256, hidden=768, nLayers=1, nHeads=4, nKvHeads=2, vocabSize=256), 1, 200),
+])
+def test_swiglu_epilogue_fusion_changes_no_bit(kw, B, T):
+    """The step with SwiGLU in the GEMM epilogues gives bit-identical loss and
+    gradients to the step with the standalone SwiGLU kernels."""
+    import forgellm as F
+    rows = O.RNG(11).ints(B * (T + 1), kw["vocabSize"]).reshape(B, T + 1)
+    m = F.TrainableTransformer(F.Config(**kw), seed=4)
+    out = []
+    for fuse in (True, False):
+        m.zeroGrad()
+        F.resetTape()
+        loss = m.lossBatch(rows)
+        fs = m._fused_steps[(B, T)]
+        assert fs.can_fuse_swiglu
+        if fs.fuse_swiglu != fuse:          # rerun the forward on the other path
+            fs.fuse_swiglu = fuse
+            F.resetTape()
+            loss = m.lossBatch(rows)
+        lv = m.backward(loss)
+        out.append((float(lv), host(m.flat_grads).copy()))
+    assert out[0][0] == out[1][0]
+    assert np.array_equal(out[0][1], out[1][1])
+
+
 def test_bf16_weight_copy_follows_adam_and_host_writes():
     import forgellm as F
     kw = dict(dim=64, hidden=128, nLayers=1, nHeads=4, nKvHeads=4, vocabSize=64)

@@ -174,6 +174,92 @@ def test_gemm_bf16_output_modes(op, M, N, K, mode):
     assert relf(want.numpy(), got.numpy()) <= tol
 
 
+def _gemm_out(mode, out, out2=None, aux=None):
+    from forgellm import _lib
+    return _lib.GemmOut(mode, out.data_ptr(), 0, None, 0, 0, 0, 0.0,
+                        out2.data_ptr() if out2 is not None else None,
+                        aux.data_ptr() if aux is not None else None)
+
+
+@pytest.mark.parametrize("M,H,K", [(256, 128, 64), (333, 384, 96), (1000, 2048, 768)])
+def test_gemm_swiglu_epilogue_is_bit_identical(M, H, K):
+    """FCU_OUT_BF16_SWIGLU (gate|up GEMM with swigluRows in the epilogue)
+    writes exactly what the bf16 GEMM followed by fcu_swiglu_fwd_bf16 writes,
+    ragged row counts included."""
+    import ctypes
+    from forgellm import _lib
+    from forgellm.autograd import ctx
+    h = ctx().handle
+    g = torch.Generator(device="cuda").manual_seed(M + H + K)
+    A = torch.randn(M * K, device="cuda", generator=g).to(torch.bfloat16)
+    B = (0.3 * torch.randn(2 * H * K, device="cuda", generator=g)).to(torch.bfloat16)
+    gu = torch.zeros(M * 2 * H, device="cuda", dtype=torch.bfloat16)
+    act = torch.zeros(M * H, device="cuda", dtype=torch.bfloat16)
+    _lib.call("fcu_gemm_bf16", h, 0, A.data_ptr(), B.data_ptr(), M, 2 * H, K,
+              ctypes.byref(_gemm_out(_lib.OUT_BF16, gu)))
+    _lib.call("fcu_swiglu_fwd_bf16", h, gu.data_ptr(), M, H, act.data_ptr())
+    gu2 = torch.full_like(gu, 7.0)
+    act2 = torch.full_like(act, 7.0)
+    _lib.call("fcu_gemm_bf16", h, 0, A.data_ptr(), B.data_ptr(), M, 2 * H, K,
+              ctypes.byref(_gemm_out(_lib.OUT_BF16_SWIGLU, gu2, out2=act2)))
+    torch.cuda.synchronize()
+    device_ok()
+    assert torch.equal(gu, gu2)
+    assert torch.equal(act, act2)
+    # and the product itself is right
+    ref = A.double().view(M, K) @ B.double().view(2 * H, K).T
+    assert relf(ref.cpu().numpy(), gu.double().cpu().view(M, 2 * H).numpy()) <= 5e-3
+
+
+@pytest.mark.parametrize("M,H,K", [(256, 128, 64), (333, 192, 96), (1000, 2048, 768)])
+def test_gemm_swiglu_bwd_epilogue_is_bit_identical(M, H, K):
+    """FCU_OUT_BF16_SWIGLU_BWD (down-projection input gradient with the
+    swigluRows backward in the epilogue) writes exactly what the bf16 dX GEMM
+    followed by fcu_swiglu_bwd_bf16 writes."""
+    import ctypes
+    from forgellm import _lib
+    from forgellm.autograd import ctx
+    h = ctx().handle
+    g = torch.Generator(device="cuda").manual_seed(7 * M + H + K)
+    dY = torch.randn(M * K, device="cuda", generator=g).to(torch.bfloat16)
+    W = (0.3 * torch.randn(K * H, device="cuda", generator=g)).to(torch.bfloat16)
+    gu = (2 * torch.randn(M * 2 * H, device="cuda", generator=g)).to(torch.bfloat16)
+    dact = torch.zeros(M * H, device="cuda", dtype=torch.bfloat16)
+    dgu = torch.zeros(M * 2 * H, device="cuda", dtype=torch.bfloat16)
+    _lib.call("fcu_gemm_bf16", h, 1, dY.data_ptr(), W.data_ptr(), M, H, K,
+              ctypes.byref(_gemm_out(_lib.OUT_BF16, dact)))
+    _lib.call("fcu_swiglu_bwd_bf16", h, dact.data_ptr(), gu.data_ptr(), M, H, dgu.data_ptr())
+    dgu2 = torch.full_like(dgu, 7.0)
+    _lib.call("fcu_gemm_bf16", h, 1, dY.data_ptr(), W.data_ptr(), M, H, K,
+              ctypes.byref(_gemm_out(_lib.OUT_BF16_SWIGLU_BWD, dgu2, aux=gu)))
+    torch.cuda.synchronize()
+    device_ok()
+    assert torch.equal(dgu, dgu2)
+    assert bool(torch.isfinite(dgu2.float()).all())
+
+
+def test_gemm_swiglu_modes_reject_bad_shapes():
+    import ctypes
+    from forgellm import _lib
+    from forgellm.autograd import ctx
+    h = ctx().handle
+    A = torch.zeros(128 * 64, device="cuda", dtype=torch.bfloat16)
+    B = torch.zeros(192 * 64, device="cuda", dtype=torch.bfloat16)
+    out = torch.zeros(128 * 192, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(F_error()):   # N = 2H = 192: H is not a multiple of 128
+        _lib.call("fcu_gemm_bf16", h, 0, A.data_ptr(), B.data_ptr(), 128, 192, 64,
+                  ctypes.byref(_gemm_out(_lib.OUT_BF16_SWIGLU, out, out2=out)))
+    with pytest.raises(F_error()):   # no forward values
+        _lib.call("fcu_gemm_bf16", h, 1, A.data_ptr(), B.data_ptr(), 128, 192, 64,
+                  ctypes.byref(_gemm_out(_lib.OUT_BF16_SWIGLU_BWD, out)))
+    device_ok()
+
+
+def F_error():
+    from forgellm import ForgeCUError
+    return ForgeCUError
+
+
 # ------------------------------------------------------------------ attention (bf16 mode)
 ATTN_BF16_BOUND = 2e-2   # bf16 Q/K/V/P/dS operands, fp32 softmax and accumulation
 
