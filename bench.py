@@ -36,6 +36,37 @@ sys.path.insert(0, os.path.join(ROOT, "forge-llm_b200"))
 C5 = dict(vocabSize=32000, dim=768, nLayers=12, nHeads=12, nKvHeads=4, hidden=2048,
           normEps=1e-5, ropeTheta=10000)
 GLOBAL_BATCH, SEQ, LR, SEED = 64, 1024, 3e-4, 5
+# DRAM bytes per tcgen05 GEMM launch of the batch-64 step: dram__bytes_read.sum
+# + dram__bytes_write.sum from one single-pass ncu capture of the 147 GEMM
+# launches of one step (66.31 GB read + 27.78 GB written), averaged per launch.
+GEMM_DRAM_BYTES_PER_LAUNCH_B64 = 640.07e6
+
+
+def gemm_algorithmic_bytes(tokens: int):
+    """(bytes, launches) of the fused bf16 step's GEMMs: every operand read
+    once and every output written once (bf16 activations, fp32 branch
+    outputs / input gradients / weight gradients, fp32 logits)."""
+    D, H, V, L = C5["dim"], C5["hidden"], C5["vocabSize"], C5["nLayers"]
+    qkv, qD, N = (C5["nHeads"] + 2 * C5["nKvHeads"]) * 64, C5["nHeads"] * 64, tokens
+    b, f = 2, 4
+    per_layer = [
+        N * D * b + qkv * D * b + N * qkv * b,            # qkv (RoPE epilogue)
+        N * qD * b + D * qD * b + N * D * f,              # wo -> fp32 branch
+        N * D * b + 2 * H * D * b + N * 2 * H * b,        # gate | up
+        N * H * b + D * H * b + N * D * f,                # down -> fp32 branch
+        N * D * b + D * H * b + N * H * b,                # down dX
+        N * D * b + N * H * b + D * H * f,                # down dW
+        N * 2 * H * b + 2 * H * D * b + N * D * f,        # gate|up dX
+        N * 2 * H * b + N * D * b + 2 * H * D * f,        # gate|up dW
+        N * D * b + D * qD * b + N * qD * b,              # wo dX
+        N * D * b + N * qD * b + D * qD * f,              # wo dW
+        N * qkv * b + qkv * D * b + N * D * f,            # qkv dX
+        N * qkv * b + N * D * b + qkv * D * f,            # qkv dW
+    ]
+    head = [N * D * b + V * D * b + N * V * f,            # logits (fp32)
+            N * V * b + V * D * b + N * D * f,            # LM-head dX
+            N * V * b + N * D * b + V * D * f]            # LM-head dW
+    return L * sum(per_layer) + sum(head), 12 * L + 3
 MATMUL_PARAMS = 100_073_472
 FLOP_PER_TOKEN = 6 * MATMUL_PARAMS + 12 * 3 * 2 * 768 * 1024   # 657.06 MFLOP (fwd + bwd)
 METRIC = "train tokens/s fwd+bwd+Adam (125M Llama-style, ctx 1024, global batch 64)"
@@ -508,6 +539,10 @@ def main():
     if rank == 0:
         pk, pk_kind = peaks()
         achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
+        gb, gl = gemm_algorithmic_bytes(args.batch * SEQ)
+        alg_bytes = gb / gl if args.precision == "bf16" else None
+        traffic = (GEMM_DRAM_BYTES_PER_LAUNCH_B64
+                   if args.precision == "bf16" and args.batch == GLOBAL_BATCH and world == 1 else None)
         peak = pk["bf16_tflops_sustained"]
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -524,10 +559,14 @@ def main():
                     "h2d_bytes_per_step": int(args.batch * (SEQ + 1) * 4),
                     "d2h_bytes_per_step": 4 * world},
             "gpu_launches": int(launches),
-            "roofline": {"kernel": "matmulT contractions (fcu_matmulT_fwd/bwd)", "bound": "tensor",
+            "roofline": {"kernel": "gemm_bf16_tc_kernel: every matmulT fwd / dX / dW contraction of the step",
+                         "bound": "tensor",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak if peak else None,
-                         "peak_kind": f"bf16 dense sustained ({pk_kind})", "traffic": None,
+                         "peak_kind": f"bf16 dense sustained ({pk_kind})",
+                         "traffic": traffic,
+                         "traffic_unit": "DRAM bytes per GEMM launch (ncu, mean over one step's launches)",
+                         "algorithmic_bytes_per_launch": alg_bytes,
                          "gemm_share_of_step": (gemm_ms / gemm_steps) / (ms / args.steps) if ms else None,
                          "measured": gemm_where,
                          "model_tflops": FLOP_PER_TOKEN * value / 1e12},
