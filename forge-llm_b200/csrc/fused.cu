@@ -18,11 +18,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t *>(&v);
 }
 
-__device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
-  __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162 *>(&u);
-  return __bfloat1622float2(v);
-}
-
 inline int grid_for(int64_t n, int per_block, int cap) {
   int64_t g = (n + per_block - 1) / per_block;
   return (int)(g < 1 ? 1 : (g > cap ? cap : g));
@@ -150,8 +145,19 @@ int rmsnorm_fwd_rc_launch(cudaStream_t st, const float *X, const float *A, const
 // dX) (the next GEMM's operand); per-block dw partials sum g*x*inv over the
 // block's rows, accumulated in registers per warp and combined across warps
 // in a fixed order (deterministic).  NC = float4 chunks each lane owns.
+//
+// A float4 of w through the read-only path at each use (an L1 hit): the asm
+// keeps the compiler from holding all NC of them in registers for the row.
+__device__ __forceinline__ float4 ld_w(const float4 *p) {
+  float4 v;
+  asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p));
+  return v;
+}
+
 template <int NC>
-__global__ void __launch_bounds__(kThreads) rmsnorm_bwd_fused_kernel(
+__global__ void __launch_bounds__(kThreads, NC <= 6 ? 2 : 1) rmsnorm_bwd_fused_kernel(
     const float *__restrict__ G, const float *__restrict__ X, const float *__restrict__ w,
     const float *__restrict__ inv, int64_t T, int64_t D, int64_t rows_per_block,
     float *__restrict__ dX, int acc_dx, __nv_bfloat16 *__restrict__ dXb, float *__restrict__ part) {
@@ -159,21 +165,22 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_bwd_fused_kernel(
   extern __shared__ float sm[];  // [nwarps][D]
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int64_t D4 = D >> 2;
+  // w is re-read from L1 per row instead of being held in registers, which
+  // leaves room for the prefetched dX at two blocks per SM
   const float4 *w4 = reinterpret_cast<const float4 *>(w);
-  float4 wv[NC], dw[NC];
+  float4 dw[NC];
 #pragma unroll
-  for (int k = 0; k < NC; k++) {
-    const int64_t c = lane + 32 * k;
-    wv[k] = c < D4 ? w4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
-    dw[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
+  for (int k = 0; k < NC; k++) dw[k] = make_float4(0.f, 0.f, 0.f, 0.f);
   const float invD = 1.f / (float)D;
   const int64_t r0 = blockIdx.x * rows_per_block;
   const int64_t r1 = min(T, r0 + rows_per_block);
   for (int64_t row = r0 + wid; row < r1; row += nw) {
     const float4 *g4 = reinterpret_cast<const float4 *>(G + row * D);
     const float4 *x4 = reinterpret_cast<const float4 *>(X + row * D);
-    float4 gv[NC], xv[NC];
+    float4 *d4 = reinterpret_cast<float4 *>(dX + row * D);
+    // G, X and (accumulating) the old dX of the row are all requested before
+    // the row reduction, so their latencies overlap
+    float4 gv[NC], xv[NC], pv[NC];
     float dot = 0.f;
 #pragma unroll
     for (int k = 0; k < NC; k++) {
@@ -181,30 +188,37 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_bwd_fused_kernel(
       if (c < D4) {
         gv[k] = g4[c];
         xv[k] = x4[c];
-        dot += gv[k].x * wv[k].x * xv[k].x + gv[k].y * wv[k].y * xv[k].y +
-               gv[k].z * wv[k].z * xv[k].z + gv[k].w * wv[k].w * xv[k].w;
+        pv[k] = acc_dx ? d4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < NC; k++) {
+      const int64_t c = lane + 32 * k;
+      if (c < D4) {
+        const float4 wv = ld_w(w4 + c);
+        dot += gv[k].x * wv.x * xv[k].x + gv[k].y * wv.y * xv[k].y +
+               gv[k].z * wv.z * xv[k].z + gv[k].w * wv.w * xv[k].w;
       }
     }
     dot = warp_sum(dot);
     const float iv = inv[row];
     const float cc = dot * iv * iv * iv * invD;
-    float4 *d4 = reinterpret_cast<float4 *>(dX + row * D);
     uint2 *b2 = dXb ? reinterpret_cast<uint2 *>(dXb + row * D) : nullptr;
 #pragma unroll
     for (int k = 0; k < NC; k++) {
       const int64_t c = lane + 32 * k;
       if (c < D4) {
+        const float4 wv = ld_w(w4 + c);
         float4 o;
-        o.x = gv[k].x * wv[k].x * iv - cc * xv[k].x;
-        o.y = gv[k].y * wv[k].y * iv - cc * xv[k].y;
-        o.z = gv[k].z * wv[k].z * iv - cc * xv[k].z;
-        o.w = gv[k].w * wv[k].w * iv - cc * xv[k].w;
+        o.x = gv[k].x * wv.x * iv - cc * xv[k].x;
+        o.y = gv[k].y * wv.y * iv - cc * xv[k].y;
+        o.z = gv[k].z * wv.z * iv - cc * xv[k].z;
+        o.w = gv[k].w * wv.w * iv - cc * xv[k].w;
         if (acc_dx) {
-          const float4 p = d4[c];
-          o.x += p.x;
-          o.y += p.y;
-          o.z += p.z;
-          o.w += p.w;
+          o.x += pv[k].x;
+          o.y += pv[k].y;
+          o.z += pv[k].z;
+          o.w += pv[k].w;
         }
         d4[c] = o;
         if (b2) {
