@@ -22,10 +22,21 @@ __global__ void sumsq_partial_kernel(const float *__restrict__ g, int64_t n,
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t n4 = vec ? (n >> 2) : 0;
   const float4 *g4 = reinterpret_cast<const float4 *>(g);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
-    float4 v = g4[i];
-    s += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+  // four float4 loads in flight per thread, four independent fp64 sums
+  // (combined in a fixed order, so the result is deterministic)
+  double s1 = 0, s2 = 0, s3 = 0;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += 4 * stride) {
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 a = g4[i];
+    const float4 b = i + stride < n4 ? g4[i + stride] : z;
+    const float4 c = i + 2 * stride < n4 ? g4[i + 2 * stride] : z;
+    const float4 d = i + 3 * stride < n4 ? g4[i + 3 * stride] : z;
+    s += (double)a.x * a.x + (double)a.y * a.y + (double)a.z * a.z + (double)a.w * a.w;
+    s1 += (double)b.x * b.x + (double)b.y * b.y + (double)b.z * b.z + (double)b.w * b.w;
+    s2 += (double)c.x * c.x + (double)c.y * c.y + (double)c.z * c.z + (double)c.w * c.w;
+    s3 += (double)d.x * d.x + (double)d.y * d.y + (double)d.z * d.z + (double)d.w * d.w;
   }
+  s = (s + s1) + (s2 + s3);
   for (int64_t i = (n4 << 2) + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride)
     s += (double)g[i] * g[i];
   s = block_sum(s, sh);
@@ -56,7 +67,7 @@ __device__ __forceinline__ void adam_elem(float &p, float g, float &m, float &v,
   p = (float)((double)p - h.lr * mh / (sqrt(vh) + h.eps));
 }
 
-__global__ void adam_update_kernel(float *__restrict__ p, const float *__restrict__ g,
+__global__ void __launch_bounds__(kThreads, 3) adam_update_kernel(float *__restrict__ p, const float *__restrict__ g,
                                    float *__restrict__ m, float *__restrict__ v, int64_t n, Hyper h,
                                    const double *__restrict__ sumsq, double *__restrict__ info,
                                    int vec, __nv_bfloat16 *__restrict__ shadow,
@@ -78,8 +89,10 @@ __global__ void adam_update_kernel(float *__restrict__ p, const float *__restric
     float4 *m4 = reinterpret_cast<float4 *>(m);
     float4 *v4 = reinterpret_cast<float4 *>(v);
     const float4 *g4 = reinterpret_cast<const float4 *>(g);
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
-      float4 pp = p4[i], gg = g4[i], mm = m4[i], vv = v4[i];
+    // Two float4 groups per thread and iteration, all eight loads issued
+    // before the fp64 arithmetic, so twice the bytes are in flight (the
+    // update is otherwise bound by memory-level parallelism).
+    auto update4 = [&](int64_t i, float4 pp, float4 gg, float4 mm, float4 vv) {
       adam_elem(pp.x, gg.x, mm.x, vv.x, scale, h);
       adam_elem(pp.y, gg.y, mm.y, vv.y, scale, h);
       adam_elem(pp.z, gg.z, mm.z, vv.z, scale, h);
@@ -94,6 +107,19 @@ __global__ void adam_update_kernel(float *__restrict__ p, const float *__restric
         u.y = *reinterpret_cast<uint32_t *>(&b);
         reinterpret_cast<uint2 *>(shadow)[i] = u;
       }
+    };
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += 2 * stride) {
+      const int64_t j = i + stride;
+      const float4 pa = p4[i], ga = g4[i], ma = m4[i], va = v4[i];
+      float4 pb = pa, gb = ga, mb = ma, vb = va;
+      if (j < n4) {
+        pb = p4[j];
+        gb = g4[j];
+        mb = m4[j];
+        vb = v4[j];
+      }
+      update4(i, pa, ga, ma, va);
+      if (j < n4) update4(j, pb, gb, mb, vb);
     }
     start = n4 << 2;
   }
@@ -109,8 +135,12 @@ __global__ void adam_update_kernel(float *__restrict__ p, const float *__restric
 
 inline bool aligned16(const void *a) { return ((uintptr_t)a & 15) == 0; }
 
+// Blocks of the sum-of-squares pass; its per-block partials sit at the head
+// of the context scratch (callers place their own values after them).
+inline int sumsq_nblk(const fcu_ctx *ctx) { return 4 * ctx->num_sms; }
+
 int sumsq_impl(fcu_ctx *ctx, const float *g, int64_t n, double *out, int acc) {
-  const int nblk = 2 * ctx->num_sms;
+  const int nblk = sumsq_nblk(ctx);
   void *scr = nullptr;
   int rc = fcu::ctx_scratch(ctx, sizeof(double) * nblk, &scr);
   if (rc) return rc;
@@ -190,7 +220,7 @@ int fcu_adam_step(fcu_ctx *ctx, float *p, const float *g, float *m, float *v, in
   if (n == 0) return FCU_OK;
   // The sum of squares lands in the tail of the context scratch, after the
   // per-block partials that sumsq_impl keeps at its head.
-  const int nblk = 2 * ctx->num_sms;
+  const int nblk = sumsq_nblk(ctx);
   void *scr = nullptr;
   int rc = fcu::ctx_scratch(ctx, sizeof(double) * (nblk + 1), &scr);
   if (rc) return rc;
@@ -209,7 +239,7 @@ int fcu_adam_step_shadow(fcu_ctx *ctx, float *p, const float *g, float *m, float
   if (n == 0) return FCU_OK;
   const double *ss = sumsq_dev;
   if (!ss) {
-    const int nblk = 2 * ctx->num_sms;
+    const int nblk = sumsq_nblk(ctx);
     void *scr = nullptr;
     int rc = fcu::ctx_scratch(ctx, sizeof(double) * (nblk + 1), &scr);
     if (rc) return rc;
@@ -228,7 +258,7 @@ int fcu_adam_step_sched(fcu_ctx *ctx, float *p, const float *g, float *m, float 
   FCU_REQUIRE(s->total_steps > 0, "fcu_adam_step_sched: total_steps must be > 0");
   if (n == 0) return FCU_OK;
   // scratch: [nblk partial sums][sum of squares][Hyper]
-  const int nblk = 2 * ctx->num_sms;
+  const int nblk = sumsq_nblk(ctx);
   void *scr = nullptr;
   int rc = fcu::ctx_scratch(ctx, sizeof(double) * (nblk + 1) + sizeof(Hyper) + 64, &scr);
   if (rc) return rc;
