@@ -319,6 +319,26 @@ struct BwdParams {
   int *err;
 };
 
+// The dQ element loop: dS = exp2(S c - L) (dP - delta) for this warp's 64 key
+// columns as bf16 pairs, instantiated with and without the diagonal mask
+// (column valid iff column <= lim).  Only the last key tile of a query tile
+// needs the mask, and the loop is issue-bound, so the other tiles skip its
+// compares and selects.
+template <bool kMasked>
+__device__ __forceinline__ void dq_elements(const BwdParams &p, const float (&sv)[64], const float (&dp)[64],
+                                            float L, float Dq, int lim, uint32_t (&dd)[32]) {
+#pragma unroll
+  for (int c = 0; c < 32; c++) {
+    float p0 = ex2_ftz(fmaf(sv[2 * c], p.scale_log2, -L));
+    float p1 = ex2_ftz(fmaf(sv[2 * c + 1], p.scale_log2, -L));
+    if (kMasked) {
+      if (2 * c > lim) p0 = 0.f;
+      if (2 * c + 1 > lim) p1 = 0.f;
+    }
+    dd[c] = pack2_bf16(p0 * (dp[2 * c] - Dq), p1 * (dp[2 * c + 1] - Dq));
+  }
+}
+
 // dK/dV kernel shared memory: K / V double-buffered per item, a (Q, dO, lse,
 // delta) ring across items
 constexpr int kKStages = 4;
@@ -849,16 +869,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sp_free);
-        const int lim = j == qt ? r - cb : 1 << 30;   // diagonal tile: key column c valid if c <= lim
+        const int lim = r - cb;                 // diagonal tile: key column c valid if c <= lim
         uint32_t dd[32];
-#pragma unroll
-        for (int c = 0; c < 32; c++) {
-          float p0 = ex2_ftz(fmaf(sv[2 * c], p.scale_log2, -L));
-          float p1 = ex2_ftz(fmaf(sv[2 * c + 1], p.scale_log2, -L));
-          if (2 * c > lim) p0 = 0.f;
-          if (2 * c + 1 > lim) p1 = 0.f;
-          dd[c] = pack2_bf16(p0 * (dp[2 * c] - Dq), p1 * (dp[2 * c + 1] - Dq));
-        }
+        if (j == qt)                            // only the diagonal key tile needs the mask
+          dq_elements<true>(p, sv, dp, L, Dq, lim, dd);
+        else
+          dq_elements<false>(p, sv, dp, L, Dq, lim, dd);
         if (u > 0 && !warp_wait(ds_free, (uint32_t)(u - 1) & 1u, abort_flag)) {
           ok = false;
           break;
