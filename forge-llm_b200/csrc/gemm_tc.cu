@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       atomicExch(p.err, 2);
     }
     umma_commit_w(mma_done);
-    warp_wait(mma_done, 0, abort_flag);
+    mbar_wait_drain(mma_done, 0);   // every MMA issued has completed before TMEM is freed
   } else if (warp >= 2) {
     // ---------------- epilogue
     const int q = warp & 3;             // TMEM lane quarter this warp may access
