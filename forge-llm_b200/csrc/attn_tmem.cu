@@ -327,15 +327,18 @@ struct BwdParams {
 template <bool kMasked>
 __device__ __forceinline__ void dq_elements(const BwdParams &p, const float (&sv)[64], const float (&dp)[64],
                                             float L, float Dq, int lim, uint32_t (&dd)[32]) {
+  const float2 sc = make_float2(p.scale_log2, p.scale_log2), nl = make_float2(-L, -L);
+  const float2 nd = make_float2(-Dq, -Dq);
 #pragma unroll
   for (int c = 0; c < 32; c++) {
-    float p0 = ex2_ftz(fmaf(sv[2 * c], p.scale_log2, -L));
-    float p1 = ex2_ftz(fmaf(sv[2 * c + 1], p.scale_log2, -L));
+    const float2 t = fma2(make_float2(sv[2 * c], sv[2 * c + 1]), sc, nl);   // s c - L
+    float p0 = ex2_ftz(t.x), p1 = ex2_ftz(t.y);
     if (kMasked) {
       if (2 * c > lim) p0 = 0.f;
       if (2 * c + 1 > lim) p1 = 0.f;
     }
-    dd[c] = pack2_bf16(p0 * (dp[2 * c] - Dq), p1 * (dp[2 * c + 1] - Dq));
+    const float2 g = mul2(make_float2(p0, p1), add2(make_float2(dp[2 * c], dp[2 * c + 1]), nd));
+    dd[c] = pack2_bf16(g.x, g.y);
   }
 }
 
