@@ -5,7 +5,7 @@
 // Forward, per CTA: one 128-row query tile of one head, looping over the
 // 128-key blocks at or before its diagonal.
 //   warp 0      TMA: Q once, then a 3-deep ring of (K, V) blocks
-//   warp 1      TMEM owner + MMA issuer (one thread):
+//   warp 1      TMEM owner + MMA issuer (warp-wide, elect.sync picks the lane):
 //                 S_j = Q K_j^T        128x128x64  -> TMEM cols [0, 128)
 //                 O  += P_j V_j        128x64x128  -> TMEM cols [128, 192)
 //               issued in the order S_0, S_1, PV_0, S_2, PV_1, ... so the next
@@ -290,9 +290,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 // dK/dV, per CTA one 128-key tile of one kv head (or, head-split, of one q
 // head), looping over the query tiles at or after it of every q head of the
 // GQA group:
-//   warp 0      TMA: K, V once; a 5-deep ring of (Q, dO) tiles plus the
+//   warp 0      TMA: K, V once; a 4-deep ring of (Q, dO) tiles plus the
 //               tile's log-sum-exp and delta = rowsum(dO * O) rows
-//   warp 1      MMA (one thread):  S^T = K Q^T, dP^T = V dO^T (128x128x64,
+//   warp 1      MMA (warp-wide, elect.sync):  S^T = K Q^T, dP^T = V dO^T (128x128x64,
 //               TMEM cols [0,128), [128,256)), then for the previous tile
 //               dV += P^T dO, dK += dS^T Q (128x64x128, cols [256,320),
 //               [320,384))

@@ -10,7 +10,8 @@
 //
 // CTA = 6 warps, one CTA per SM, looping over output tiles:
 //   warp 0      TMA producer: STAGES-deep ring of (A,B) k-blocks
-//   warp 1      TMEM owner + MMA issuer (one thread): 4 x (128x256x16) per k-block
+//   warp 1      TMEM owner + MMA issuer (warp-wide, elect.sync picks the
+//               lane): 4 x (128x256x16) per k-block
 //   warps 2..5  epilogue: TMEM -> registers -> global, double-buffered
 //               accumulators so the epilogue of tile i overlaps the
 //               mainloop of tile i+1 (2 x 256 TMEM columns = all 512).
