@@ -133,6 +133,8 @@ typedef struct {
   double rope_theta;
   void *out2;             /* FCU_OUT_BF16_SWIGLU: the activation output */
   const void *aux;        /* FCU_OUT_BF16_SWIGLU_BWD: the forward's gate|up values */
+  /* (out2 and aux are read only in those two modes, so a caller that fills
+   * just the fields above them keeps working for the other modes) */
 } fcu_gemm_out;
 
 /* One tcgen05 contraction on bf16 operands (fp32 accumulate) in the layouts
