@@ -92,6 +92,12 @@ int fcu_ctx_destroy(fcu_ctx *ctx) {
   return FCU_OK;
 }
 
+int fcu_ctx_scratch_bytes(const fcu_ctx *ctx, size_t *out) {
+  FCU_REQUIRE(ctx && out, "fcu_ctx_scratch_bytes: null argument");
+  *out = ctx->scratch_bytes;
+  return FCU_OK;
+}
+
 int fcu_ctx_set_stream(fcu_ctx *ctx, void *stream) {
   FCU_CTX(ctx);
   ctx->stream = (cudaStream_t)stream;

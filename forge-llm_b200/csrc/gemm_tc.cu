@@ -276,8 +276,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       atomicExch(p.err, 1);
     }
     // Drain: every copy this thread issued has landed before the CTA exits.
+    // The wait ignores the abort flag (another role may have set it): the
+    // copies always complete, and none may still write this CTA's shared
+    // memory once it has exited.
     for (int i = it - STAGES < 0 ? 0 : it - STAGES; i < it; i++)
-      mbar_wait(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u, abort_flag);
+      mbar_wait_drain(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u);
   } else if (warp == 1) {
     // ---------------- MMA issuer (whole warp; elect.sync picks the issuing lane)
     const uint32_t idesc = instr_desc_bf16(p.a_mn, p.b_mn, BM, BN);

@@ -365,10 +365,8 @@ __global__ void add_bwd_kernel(const float *__restrict__ g, int64_t n, float *__
 
 // ---------------------------------------------------------------- cross entropy
 // One CTA per row.  Pass 1: online (max, sum exp) over the row; pass 2 writes
-// (exp(l - lse) - onehot)/T.  When the row fits the register cache (V <= 32
-// floats per thread, vectorisable) the row is read from HBM once.
+// (exp(l - lse) - onehot)/T.
 constexpr int kCeThreads = 1024;
-constexpr int kCeVec = 8;  // float4 per thread in the cached path -> V <= 32768
 
 __device__ __forceinline__ void ce_merge(float &m, float &s, float m2, float s2) {
   float mn = fmaxf(m, m2);
@@ -401,20 +399,14 @@ __device__ __forceinline__ void ce_block_reduce(float &m, float &s, float *shm, 
   }
 }
 
-__device__ __forceinline__ void ce_store4(float *p, float4 o) { *reinterpret_cast<float4 *>(p) = o; }
-__device__ __forceinline__ void ce_store4(__nv_bfloat16 *p, float4 o) {
-  __nv_bfloat162 a = __floats2bfloat162_rn(o.x, o.y), b = __floats2bfloat162_rn(o.z, o.w);
-  uint2 u;
-  u.x = *reinterpret_cast<uint32_t *>(&a);
-  u.y = *reinterpret_cast<uint32_t *>(&b);
-  *reinterpret_cast<uint2 *>(p) = u;
-}
 __device__ __forceinline__ void ce_store1(float *p, float v) { *p = v; }
 __device__ __forceinline__ void ce_store1(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
 
-// TO = float: the op-level gradient; TO = bf16: the fused path, where the
-// gradient is the next tensor-core GEMM's operand.
-template <bool CACHED, typename TO = float>
+// CE for rows that the vectorised ce2_kernel cannot read (a logits or
+// gradient pointer not 16-byte aligned, or V not a multiple of 4): scalar
+// loads, two passes over the row.  TO = float: the op-level gradient; TO =
+// bf16: the fused path, where the gradient is the next GEMM's operand.
+template <typename TO = float>
 __global__ void __launch_bounds__(kCeThreads) ce_fwd_kernel(const float *logits,
                                                             const int32_t *__restrict__ targets,
                                                             int64_t T, int64_t V,
@@ -427,58 +419,21 @@ __global__ void __launch_bounds__(kCeThreads) ce_fwd_kernel(const float *logits,
   const float invT = (float)(1.0 / (double)T);
   const int32_t tgt = targets[row];
   float m = -INFINITY, s = 0.f;
-  float4 cache[CACHED ? kCeVec : 1];
-  if (CACHED) {
-    const float4 *l4 = reinterpret_cast<const float4 *>(l);
-    const int64_t V4 = V >> 2;
-#pragma unroll
-    for (int k = 0; k < kCeVec; k++) {
-      int64_t i4 = threadIdx.x + (int64_t)k * kCeThreads;
-      float4 v = i4 < V4 ? l4[i4] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-      cache[k] = v;
-      float mx = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
-      if (mx > m) {
-        s = (m == -INFINITY) ? 0.f : s * expf(m - mx);
-        m = mx;
-      }
-      if (m != -INFINITY)
-        s += expf(v.x - m) + expf(v.y - m) + expf(v.z - m) + expf(v.w - m);
+  for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
+    float v = l[i];
+    if (v > m) {
+      s = (m == -INFINITY) ? 0.f : s * expf(m - v);
+      m = v;
     }
-  } else {
-    for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
-      float v = l[i];
-      if (v > m) {
-        s = (m == -INFINITY) ? 0.f : s * expf(m - v);
-        m = v;
-      }
-      s += expf(v - m);
-    }
+    s += expf(v - m);
   }
   ce_block_reduce(m, s, shm, shs);
   const float lse = m + logf(s);
   const float lt = (tgt >= 0 && tgt < V) ? l[tgt] : __int_as_float(0x7fc00000);
   __syncthreads();  // every thread has read l[tgt] before any in-place write
-  if (CACHED) {
-    const int64_t V4 = V >> 2;
-#pragma unroll
-    for (int k = 0; k < kCeVec; k++) {
-      int64_t i4 = threadIdx.x + (int64_t)k * kCeThreads;
-      if (i4 < V4) {
-        float4 v = cache[k];
-        int64_t i = i4 * 4;
-        float4 o;
-        o.x = (expf(v.x - lse) - (i + 0 == tgt ? 1.f : 0.f)) * invT;
-        o.y = (expf(v.y - lse) - (i + 1 == tgt ? 1.f : 0.f)) * invT;
-        o.z = (expf(v.z - lse) - (i + 2 == tgt ? 1.f : 0.f)) * invT;
-        o.w = (expf(v.w - lse) - (i + 3 == tgt ? 1.f : 0.f)) * invT;
-        ce_store4(du + i, o);
-      }
-    }
-  } else {
-    for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
-      float v = l[i];
-      ce_store1(du + i, (expf(v - lse) - (i == tgt ? 1.f : 0.f)) * invT);
-    }
+  for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
+    float v = l[i];
+    ce_store1(du + i, (expf(v - lse) - (i == tgt ? 1.f : 0.f)) * invT);
   }
   if (threadIdx.x == 0) row_loss[row] = lse - lt;
 }
@@ -871,10 +826,8 @@ int fcu_ce_fwd(fcu_ctx *ctx, const float *logits, const int32_t *targets, int64_
   bool aligned = ((uintptr_t)logits % 16 == 0) && ((uintptr_t)dunit % 16 == 0);
   if (aligned && V % 4 == 0)
     ce2_kernel<float><<<(int)T, kCe2Threads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
-  else if (aligned && V % 4 == 0 && V <= (int64_t)kCeThreads * kCeVec * 4)
-    ce_fwd_kernel<true><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
   else
-    ce_fwd_kernel<false><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
+    ce_fwd_kernel<float><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
   FCU_CHECK_LAUNCH();
   mean_kernel<<<1, 1024, 0, ctx->stream>>>(row_loss, T, loss_out);
   FCU_CHECK_LAUNCH();
@@ -907,11 +860,8 @@ int fcu_ce_fwd_bf16grad(fcu_ctx *ctx, const float *logits, const int32_t *target
   bool aligned = ((uintptr_t)logits % 16 == 0) && ((uintptr_t)du % 8 == 0);
   if (aligned && V % 4 == 0)
     ce2_kernel<__nv_bfloat16><<<(int)T, kCe2Threads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, du);
-  else if (aligned && V % 4 == 0 && V <= (int64_t)kCeThreads * kCeVec * 4)
-    ce_fwd_kernel<true, __nv_bfloat16><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V,
-                                                                               row_loss, du);
   else
-    ce_fwd_kernel<false, __nv_bfloat16><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V,
+    ce_fwd_kernel<__nv_bfloat16><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V,
                                                                                 row_loss, du);
   FCU_CHECK_LAUNCH();
   mean_kernel<<<1, 1024, 0, ctx->stream>>>(row_loss, T, loss_out);
@@ -978,10 +928,8 @@ int fcu_ce_fwd_static(fcu_ctx *ctx, const float *logits, const int32_t *targets,
   bool aligned = ((uintptr_t)logits % 16 == 0) && ((uintptr_t)dunit % 16 == 0);
   if (aligned && V % 4 == 0)
     ce2_kernel<float><<<(int)T, kCe2Threads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
-  else if (aligned && V % 4 == 0 && V <= (int64_t)kCeThreads * kCeVec * 4)
-    ce_fwd_kernel<true><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
   else
-    ce_fwd_kernel<false><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
+    ce_fwd_kernel<float><<<(int)T, kCeThreads, 0, ctx->stream>>>(logits, targets, T, V, row_loss, dunit);
   FCU_CHECK_LAUNCH();
   mean_kernel<<<1, 1024, 0, ctx->stream>>>(row_loss, T, loss_out);
   FCU_CHECK_LAUNCH();

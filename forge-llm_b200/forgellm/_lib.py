@@ -72,6 +72,7 @@ _SIGS = {
     "fcu_ctx_get_precision": (_INT, [_P]),
     "fcu_sync": (_INT, [_P]),
     "fcu_launch_count": (C.c_ulonglong, []),
+    "fcu_ctx_scratch_bytes": (_INT, [_P, C.POINTER(C.c_size_t)]),
     "fcu_check_device_error": (_INT, [_P]),
     "fcu_malloc": (_INT, [_P, C.c_size_t, C.POINTER(_P)]),
     "fcu_free": (_INT, [_P, _P]),

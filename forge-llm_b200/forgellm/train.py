@@ -344,12 +344,17 @@ def train(model: TrainableTransformer, data, opts=None, **kw) -> list:
     """Training loop (train.js:246-276): B random windows per step, block-
     diagonal batch loss, Adam with clip 1 and wd 0.01.
 
-    The token stream is uploaded once; each step's window starts are drawn
-    from the forge-llm RNG exactly as the JS draws them and the windows are
-    gathered on the device (fcu_gather_windows), so the batches are the
-    reference's.  On the fused bf16 path the step is replayed as one CUDA
-    graph (`graph=False` in the options runs it op by op); the gather writes
-    straight into the graph's batch buffer."""
+    The token stream is uploaded once.  Every step's window starts are drawn
+    before the loop, from the forge-llm RNG in the JS's order (B draws per
+    step, step by step; the RNG serves nothing else), and uploaded in one
+    copy; step k gathers its windows on the device (fcu_gather_windows) from
+    starts[k*B:(k+1)*B].  So the batches are the reference's, and no host
+    buffer is rewritten while the GPU may still read it: the loop only syncs
+    to log.  On the fused bf16 path the step is replayed as one CUDA graph
+    (`graph=False` in the options runs it op by op); the gather writes
+    straight into the graph's batch buffer.  `onBatch(step, batch)`, if
+    given, is called after each step's gather with the device batch tensor
+    (stream-ordered: clone it to keep it)."""
     from . import autograd as AD
     from ._lib import call
     opts = dict(opts or {}, **kw)
@@ -372,15 +377,16 @@ def train(model: TrainableTransformer, data, opts=None, **kw) -> list:
         batch = cs.batch
     else:
         batch = torch.empty((B, T1), dtype=torch.int32, device=dev)
-    starts_host = torch.empty(B, dtype=torch.int32).pin_memory()
-    starts = torch.empty(B, dtype=torch.int32, device=dev)
+    span = max(1, n - seqLen - 1)
+    starts_host = np.array([rng.int(span) for _ in range(steps * B)], dtype=np.int32)
+    starts = torch.as_tensor(starts_host).to(dev)   # one synchronous upload
+    on_batch = opts.get("onBatch")
     history = []
     for step in range(steps):
-        for b in range(B):
-            starts_host[b] = rng.int(max(1, n - seqLen - 1))
-        starts.copy_(starts_host, non_blocking=True)
-        call("fcu_gather_windows", AD.ctx().handle, tokens.data_ptr(), n, starts.data_ptr(), B, T1,
-             batch.data_ptr())
+        call("fcu_gather_windows", AD.ctx().handle, tokens.data_ptr(), n,
+             starts.data_ptr() + 4 * step * B, B, T1, batch.data_ptr())
+        if on_batch is not None:
+            on_batch(step, batch)
         if cs is not None:
             loss_dev = cs(None)
             info_dev = cs.info

@@ -75,6 +75,10 @@ int fcu_check_device_error(fcu_ctx *ctx);
 int fcu_selftest_bounded_wait(fcu_ctx *ctx, int64_t cycles);
 /* Kernels launched by this library since it was loaded (all contexts). */
 unsigned long long fcu_launch_count(void);
+/* Bytes of per-row scratch the context currently holds (0 until an entry
+ * point that needs scratch first runs; it only grows).  No counterpart in
+ * the reference: hosts with a fixed memory budget read it to plan for it. */
+int fcu_ctx_scratch_bytes(const fcu_ctx *ctx, size_t *out);
 
 /* Device memory for hosts without an allocator of their own (the N-API
  * addon).  The Python host allocates through PyTorch instead. */
@@ -272,9 +276,12 @@ int fcu_ce_fwd(fcu_ctx *ctx, const float *logits, const int32_t *targets, int64_
  * exits).  Larger T is rejected with FCU_ERR_ARG.  The first call on a device
  * looks up the array's device address (cudaGetSymbolAddress, with that device
  * current) and caches it; make that first call before any stream capture.
- * All calls share the one array, so calls whose kernels overlap on the GPU
- * (other streams, other threads) race; calls on one stream are ordered and
- * safe.  Results equal fcu_ce_fwd's. */
+ * The cached address belongs to the device's current primary context: after
+ * cudaDeviceReset (or anything else that destroys that context) it is stale,
+ * so a process that resets a device must not call this entry point on it
+ * again.  All calls share the one array, so calls whose kernels overlap on
+ * the GPU (other streams, other threads) race; calls on one stream are
+ * ordered and safe.  Results equal fcu_ce_fwd's. */
 int fcu_ce_fwd_static(fcu_ctx *ctx, const float *logits, const int32_t *targets, int64_t T,
                       int64_t V, float *loss_out, float *dunit);
 

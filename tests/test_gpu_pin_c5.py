@@ -1,0 +1,193 @@
+"""The benchmarked step, pinned at the benchmarked configuration.
+
+bench.py times the bf16 fused step of the Llama-style ~125M model (vocab
+32000, d_model 768, 12 layers, 12 q / 4 kv heads x 64, SwiGLU 2048, context
+1024; src/L6/train.js:120-185).  These tests run that model at full depth and
+full context length:
+
+- the bf16 fused step (tcgen05 GEMMs and attention, bf16 activations) against
+  the fp32 CUDA-core path on the same weights and tokens, B = 2 sequences of
+  T = 1024: the loss, every parameter tensor's gradient, the global gradient
+  norm and one Adam update.  The fp32 path is itself held to relL2 <= 1e-5
+  against the CPU oracle (next test and tests/test_gpu_model.py), so the
+  comparison is pinned to the reference's arithmetic;
+- one sequence of the same model through both GPU paths against the oracle's
+  model_step directly;
+- the tcgen05 attention entries at BASELINE config 4 (B 8, 32/8 heads,
+  T 2048, d 64, RoPE) against oracle slices.
+
+Stated bounds for the bf16 step (bf16 operands for every contraction, fp32
+accumulation, fp32 master weights, gradients and residual stream):
+  loss                       relative  <= C5_LOSS_TOL
+  flat gradient              relL2     <= C5_FLAT_TOL
+  each parameter tensor      relL2     <= C5_TENSOR_TOL (embedding/LM head,
+                                          norms, every layer's projections)
+  global gradient norm       relative  <= C5_GNORM_TOL
+  first Adam update          relL2     <= C5_ADAM_TOL of the update itself
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+C5 = dict(vocabSize=32000, dim=768, nLayers=12, nHeads=12, nKvHeads=4, hidden=2048)
+
+C5_LOSS_TOL = 2e-3
+C5_FLAT_TOL = 3e-2
+C5_TENSOR_TOL = 5e-2
+C5_GNORM_TOL = 2e-2
+C5_ADAM_TOL = 0.5
+FP32_TOL = 1e-5
+
+
+def _rows(B, T):
+    """The bench's token draw: 1025-id windows from RNG(5)."""
+    ids = O.RNG(5).ints(64 * 1025, 32000).reshape(64, 1025)
+    return np.ascontiguousarray(ids[:B, :T + 1])
+
+
+def _step(precision, rows, adam=False):
+    import forgellm as F
+    F.set_precision(precision)
+    try:
+        m = F.TrainableTransformer(F.Config(**C5), seed=5)
+        if precision == "bf16":
+            assert m._use_fused()
+        F.resetTape()
+        m.zeroGrad()
+        loss = m.backward(m.lossBatch(rows))
+        g = m.flat_grads.cpu().numpy().copy()
+        out = dict(loss=float(loss), g=g)
+        if adam:
+            p0 = m.flat_params.cpu().numpy().copy()
+            info = F.Adam(m.paramList, lr=3e-4).step()
+            out["gnorm"] = float(info["gnorm"])
+            out["dp"] = m.flat_params.cpu().numpy() - p0
+        del m
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        return out
+    finally:
+        F.set_precision("fp32")
+
+
+def _per_tensor(ref, got):
+    from forgellm.train import Config, param_shapes
+    off, out = 0, {}
+    for name, n in param_shapes(Config(**C5)):
+        out[name] = O.rel_l2(ref[off:off + n], got[off:off + n])
+        off += n
+    assert off == ref.size
+    return out
+
+
+def c5_bf16_vs_fp32(B=2, T=1024):
+    """Measured agreement of the two GPU paths at config 5 (also used to
+    report the figures the bounds above were set from)."""
+    rows = _rows(B, T)
+    a = _step("fp32", rows, adam=True)
+    b = _step("bf16", rows, adam=True)
+    return dict(loss=abs(b["loss"] - a["loss"]) / abs(a["loss"]),
+                flat=O.rel_l2(a["g"], b["g"]),
+                tensors=_per_tensor(a["g"], b["g"]),
+                gnorm=abs(b["gnorm"] - a["gnorm"]) / a["gnorm"],
+                adam=O.rel_l2(a["dp"], b["dp"]),
+                loss_fp32=a["loss"], loss_bf16=b["loss"])
+
+
+def test_c5_bf16_step_matches_fp32_path_at_full_size():
+    r = c5_bf16_vs_fp32()
+    assert r["loss"] <= C5_LOSS_TOL, r["loss"]
+    assert r["flat"] <= C5_FLAT_TOL, r["flat"]
+    bad = {k: v for k, v in r["tensors"].items() if not v <= C5_TENSOR_TOL}
+    assert not bad, bad
+    assert r["gnorm"] <= C5_GNORM_TOL, r["gnorm"]
+    assert r["adam"] <= C5_ADAM_TOL, r["adam"]
+
+
+def test_c5_one_sequence_against_oracle():
+    """Config-5 model, one sequence (T = 128): the fp32 path to 1e-5 and the
+    bf16 fused path to the bounds above, both against the oracle's
+    model_step (src/L6/train.js:120-185 restated)."""
+    B, T = 1, 128
+    rows = _rows(B, T)
+    ocfg = O.Config(**C5)
+    P = O.init_weights(ocfg, 5)
+    G = np.zeros_like(P)
+    O.set_threads(16)
+    try:
+        lo = float(O.model_step(ocfg, P, rows[:, :-1].ravel(), rows[:, 1:].ravel(), B, T, G))
+    finally:
+        O.set_threads(1)
+    a = _step("fp32", rows)
+    assert abs(a["loss"] - lo) <= FP32_TOL * abs(lo), (a["loss"], lo)
+    assert O.rel_l2(G, a["g"]) <= FP32_TOL, O.rel_l2(G, a["g"])
+    bad = {k: v for k, v in _per_tensor(G, a["g"]).items() if not v <= 10 * FP32_TOL}
+    assert not bad, bad
+    b = _step("bf16", rows)
+    assert abs(b["loss"] - lo) <= C5_LOSS_TOL * abs(lo), (b["loss"], lo)
+    assert O.rel_l2(G, b["g"]) <= C5_FLAT_TOL, O.rel_l2(G, b["g"])
+    bad = {k: v for k, v in _per_tensor(G, b["g"]).items() if not v <= C5_TENSOR_TOL}
+    assert not bad, bad
+
+
+def test_c4_tcgen05_attention_against_oracle_slices():
+    """BASELINE config 4 through the fused path's tcgen05 attention entries:
+    Q/K/V/dO ~N(0,1) from RNG(4), RoPE (theta 10000) on q and k before the
+    forward (the fused path rotates in the qkv GEMM epilogue), the backward
+    rotating dq and dk back.  Two (sequence, kv-group) slices are checked
+    against the oracle's fp32 causalAttnBatch + ropeRows: O to 1e-2 and
+    dQ / dK / dV to 2e-2 (bf16 q/k/v, P and dS)."""
+    from forgellm import _lib
+    from forgellm.autograd import ctx
+    B, T, nH, nKV, dH = 8, 2048, 32, 8, 64
+    rng = O.RNG(4)
+    Q = rng.normals(B * T * nH * dH)
+    K = rng.normals(B * T * nKV * dH)
+    V = rng.normals(B * T * nKV * dH)
+    dO = rng.normals(B * T * nH * dH)
+    h = ctx().handle
+    dev = torch.device("cuda")
+    Qd, Kd, Vd = (torch.from_numpy(x).to(dev) for x in (Q, K, V))
+    qr = torch.empty(B * T, nH * dH, device=dev)
+    kr = torch.empty(B * T, nKV * dH, device=dev)
+    _lib.call("fcu_rope_fwd", h, Qd.data_ptr(), B * T, nH, dH, 0, 10000.0, T, qr.data_ptr())
+    _lib.call("fcu_rope_fwd", h, Kd.data_ptr(), B * T, nKV, dH, 0, 10000.0, T, kr.data_ptr())
+    qkv = torch.cat((qr, kr, Vd.view(B * T, nKV * dH)), 1).to(torch.bfloat16)
+    width = qkv.shape[1]
+    Og = torch.empty(B * T, nH * dH, device=dev, dtype=torch.bfloat16)
+    lse = torch.empty(B * nH * T, device=dev)
+    _lib.call("fcu_attn_fwd_bf16", h, qkv.data_ptr(), width, B, T, nH, nKV, dH, Og.data_ptr(),
+              lse.data_ptr())
+    dOb = torch.from_numpy(dO).to(dev).to(torch.bfloat16)
+    dqkv = torch.empty_like(qkv)
+    _lib.call("fcu_attn_bwd_bf16", h, dOb.data_ptr(), qkv.data_ptr(), width, Og.data_ptr(),
+              lse.data_ptr(), B, T, nH, nKV, dH, 10000.0, dqkv.data_ptr())
+    torch.cuda.synchronize()
+    assert _lib.lib().fcu_check_device_error(h) == 0
+    Oh = Og.float().cpu().numpy().reshape(B, T, nH, dH)
+    dq = dqkv[:, :nH * dH].float().cpu().numpy().reshape(B, T, nH, dH)
+    dk = dqkv[:, nH * dH:(nH + nKV) * dH].float().cpu().numpy().reshape(B, T, nKV, dH)
+    dv = dqkv[:, (nH + nKV) * dH:].float().cpu().numpy().reshape(B, T, nKV, dH)
+    group = nH // nKV
+    O.set_threads(16)
+    try:
+        for b, kvh in [(0, 0), (6, 5)]:
+            hs = slice(kvh * group, (kvh + 1) * group)
+            q = Q.reshape(B, T, nH, dH)[b, :, hs].ravel()
+            k = K.reshape(B, T, nKV, dH)[b, :, kvh].ravel()
+            v = V.reshape(B, T, nKV, dH)[b, :, kvh].ravel()
+            go = dO.reshape(B, T, nH, dH)[b, :, hs].ravel()
+            oq = O.rope_fwd(q, T, group, dH, 0, 10000.0, T)
+            ok = O.rope_fwd(k, T, 1, dH, 0, 10000.0, T)
+            o, P = O.attn_fwd(oq, ok, v, 1, T, group, 1, dH)
+            assert O.rel_l2(o, Oh[b, :, hs].ravel()) <= 1e-2
+            gq, gk, gv = O.attn_bwd(go, oq, ok, v, P, 1, T, group, 1, dH)
+            assert O.rel_l2(O.rope_bwd(gq, T, group, dH, 0, 10000.0, T), dq[b, :, hs].ravel()) <= 2e-2
+            assert O.rel_l2(O.rope_bwd(gk, T, 1, dH, 0, 10000.0, T), dk[b, :, kvh].ravel()) <= 2e-2
+            assert O.rel_l2(gv, dv[b, :, kvh].ravel()) <= 2e-2
+    finally:
+        O.set_threads(1)

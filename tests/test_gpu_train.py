@@ -45,3 +45,35 @@ def test_train_graph_follows_op_by_op(precision):
         assert np.abs(pe - pg).max() <= 1e-4 * max(1.0, float(np.abs(pe).max()))
     finally:
         F.set_precision("fp32")
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_train_batches_are_the_js_windows_without_per_step_sync(graph):
+    """train() at its default logEvery (10) over 13 steps: the host never
+    waits between steps 1-9, so a host buffer rewritten per step would be
+    read late.  The batches the device used (cloned in stream order) must be
+    the windows train.js:256-264 draws from RNG(seed)."""
+    import forgellm as F
+    F.set_precision("bf16")
+    try:
+        n, B, seqLen, steps, seed = 3000, 3, 64, 13, 7
+        data = F.RNG(9).ints(n, KW["vocabSize"])
+        rng = F.RNG(seed)
+        want = []
+        for _ in range(steps):
+            rows = []
+            for _ in range(B):
+                s = rng.int(max(1, n - seqLen - 1))
+                rows.append([data[s + i] if s + i < n else data[-1] for i in range(seqLen + 1)])
+            want.append(np.array(rows, np.int32))
+        got = []
+        m = F.TrainableTransformer(F.Config(**KW), seed=2)
+        hist = F.train(m, data, steps=steps, batchSize=B, seqLen=seqLen, lr=3e-3, seed=seed,
+                       graph=graph, onBatch=lambda k, b: got.append(b.clone()))
+        torch.cuda.synchronize()
+        assert [h["step"] for h in hist] == [0, 10, 12]
+        assert len(got) == steps
+        for k in range(steps):
+            assert np.array_equal(got[k].cpu().numpy(), want[k]), k
+    finally:
+        F.set_precision("fp32")
