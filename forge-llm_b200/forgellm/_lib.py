@@ -14,11 +14,17 @@ _PKG_ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB_PATH = os.environ.get("FORGECU_LIB", os.path.join(_PKG_ROOT, "libforgecu.so"))
 
 FCU_PREC_FP32, FCU_PREC_BF16 = 0, 2
+FCU_ERR_ARG, FCU_ERR_CUDA, FCU_ERR_NCCL, FCU_ERR_TIMEOUT, FCU_ERR_UNSUPPORTED = -1, -2, -3, -4, -5
+FCU_COMM_ID_BYTES = 128
 PRECISIONS = {"fp32": FCU_PREC_FP32, "bf16": FCU_PREC_BF16}
 
 
 class ForgeCUError(RuntimeError):
-    """A libforgecu entry point returned a non-zero fcu_status."""
+    """A libforgecu entry point returned a non-zero fcu_status (`.status`)."""
+
+    def __init__(self, msg, status=None):
+        super().__init__(msg)
+        self.status = status
 
 
 class RngState(C.Structure):
@@ -121,6 +127,17 @@ _SIGS = {
     "fcu_adam_update_dev": (_INT, [_P, _P, _P, _P, _P, _I64, _P, _P, _P, _P]),
     "fcu_to_bf16": (_INT, [_P, _P, _I64, _P]),
     "fcu_scale_bf16_dev": (_INT, [_P, _P, _I64, _P]),
+    "fcu_comm_unique_id": (_INT, [_P]),
+    "fcu_comm_init": (_INT, [_INT, _P, _INT, _INT, _D, C.POINTER(_P)]),
+    "fcu_comm_destroy": (_INT, [_P]),
+    "fcu_comm_abort": (_INT, [_P]),
+    "fcu_comm_info": (_INT, [_P, C.POINTER(_INT), C.POINTER(_INT), C.POINTER(_INT)]),
+    "fcu_allreduce_grads": (_INT, [_P, _P, _P, _I64]),
+    "fcu_reduce_scatter_grads": (_INT, [_P, _P, _P, _I64]),
+    "fcu_allgather_params": (_INT, [_P, _P, _P, _I64, _INT]),
+    "fcu_allreduce_sum_f64": (_INT, [_P, _P, _P, _I64]),
+    "fcu_comm_join": (_INT, [_P, _P]),
+    "fcu_comm_poll": (_INT, [_P, _D]),
     "fcu_rng_init": (None, [C.POINTER(RngState), C.c_uint32]),
     "fcu_rng_next": (_D, [C.POINTER(RngState)]),
     "fcu_rng_normal": (_D, [C.POINTER(RngState)]),
@@ -165,7 +182,7 @@ def exported_symbols():
 def check(rc: int, what: str = "") -> None:
     if rc != 0:
         msg = lib().fcu_last_error().decode(errors="replace")
-        raise ForgeCUError(f"{what} failed (status {rc}): {msg}")
+        raise ForgeCUError(f"{what} failed (status {rc}): {msg}", rc)
 
 
 def call(name: str, *args) -> None:

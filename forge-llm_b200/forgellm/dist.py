@@ -8,11 +8,87 @@ gradient buffer; that block's all-reduce (NCCL AVG) is launched as soon as the
 tape replay has run the layer's last gradient-writing closure, so it overlaps
 the backward of the layers below.  Every rank then takes the identical Adam
 step on identical averaged gradients, keeping the replicas equal.
+
+On GPUs the collectives go through libforgecu's C-ABI (`NcclComm`, the
+fcu_comm_* / fcu_allreduce_grads entry points: a non-blocking NCCL
+communicator with bounded waits and abort on deadline).  torch.distributed
+only bootstraps it (the 128-byte NCCL id is broadcast from rank 0) and runs
+the gloo collectives of the CPU tests.
 """
 from __future__ import annotations
 
+import ctypes as C
+
 import torch
 import torch.distributed as dist
+
+
+class NcclComm:
+    """This rank's NCCL communicator, created and driven through libforgecu's
+    C-ABI (include/forgecu.h, "data-parallel exchange").  Every collective is
+    enqueued after the work already queued on the context's stream and runs on
+    the communicator's own stream; `join()` makes the context's stream wait
+    for all of them.  `poll()` is the host-side check between steps: it
+    raises ForgeCUError (status FCU_ERR_TIMEOUT or FCU_ERR_NCCL) and aborts
+    the communicator if the collectives do not finish in time or a peer
+    failed."""
+
+    def __init__(self, group=None, timeout_s: float = 120.0, device: int | None = None):
+        from . import autograd as AD
+        from ._lib import FCU_COMM_ID_BYTES, call
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.timeout_s = float(timeout_s)
+        uid = C.create_string_buffer(FCU_COMM_ID_BYTES)
+        if self.rank == 0:
+            call("fcu_comm_unique_id", uid)
+        obj = [uid.raw if self.rank == 0 else None]
+        src = dist.get_global_rank(group, 0) if group is not None else 0
+        dist.broadcast_object_list(obj, src=src, group=group)
+        uid = C.create_string_buffer(obj[0], FCU_COMM_ID_BYTES)
+        dev = torch.cuda.current_device() if device is None else device
+        h = C.c_void_p()
+        call("fcu_comm_init", dev, uid, self.world, self.rank, self.timeout_s, C.byref(h))
+        self.handle = h
+        self._AD = AD
+
+    def _ctx(self):
+        return self._AD.ctx().handle
+
+    def allreduce_avg(self, t: torch.Tensor) -> None:
+        from ._lib import call
+        call("fcu_allreduce_grads", self._ctx(), self.handle, t.data_ptr(), t.numel())
+
+    def reduce_scatter_avg(self, t: torch.Tensor) -> None:
+        from ._lib import call
+        call("fcu_reduce_scatter_grads", self._ctx(), self.handle, t.data_ptr(), t.numel())
+
+    def allgather(self, t: torch.Tensor) -> None:
+        from ._lib import call
+        call("fcu_allgather_params", self._ctx(), self.handle, t.data_ptr(), t.numel(), t.element_size())
+
+    def allreduce_sum_f64(self, t: torch.Tensor) -> None:
+        from ._lib import call
+        call("fcu_allreduce_sum_f64", self._ctx(), self.handle, t.data_ptr(), t.numel())
+
+    def join(self) -> None:
+        from ._lib import call
+        call("fcu_comm_join", self._ctx(), self.handle)
+
+    def poll(self, timeout_s: float | None = None) -> None:
+        from ._lib import call
+        call("fcu_comm_poll", self.handle, self.timeout_s if timeout_s is None else float(timeout_s))
+
+    def abort(self) -> None:
+        from ._lib import call
+        if self.handle is not None:
+            call("fcu_comm_abort", self.handle)
+
+    def close(self) -> None:
+        from ._lib import lib
+        if self.handle is not None:
+            lib().fcu_comm_destroy(self.handle)
+            self.handle = None
 
 
 class DataParallel:
@@ -23,12 +99,18 @@ class DataParallel:
     with AVG; backends without AVG (gloo, used by the CPU tests) reduce with
     SUM and divide after the wait."""
 
-    def __init__(self, model, group=None, shard: bool = False):
+    def __init__(self, model, group=None, shard: bool = False, comm: NcclComm | None = None,
+                 timeout_s: float = 120.0):
         self.model = model
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.native_avg = dist.get_backend(group) == "nccl"
+        # GPU ranks exchange through the C-ABI communicator; gloo (the CPU
+        # tests) through torch.distributed
+        self.comm = comm
+        if self.comm is None and self.native_avg and self.world > 1 and model.flat_grads.is_cuda:
+            self.comm = NcclComm(group, timeout_s=timeout_s)
         # shard=True (ZeRO-1, with ShardedAdam): each bucket is reduce-
         # scattered, rank r receiving the average of slice r of the bucket
         self.shard = shard
@@ -58,6 +140,13 @@ class DataParallel:
             return
         a, b = self.blocks[key]
         buf = self.model.flat_grads[a:b]
+        if self.comm is not None:
+            if self.shard:
+                self.comm.reduce_scatter_avg(buf)   # rank r receives slice r, in place
+            else:
+                self.comm.allreduce_avg(buf)
+            self.launched.add(key)
+            return
         op = dist.ReduceOp.AVG if self.native_avg else dist.ReduceOp.SUM
         if self.shard and self.native_avg:
             n = (b - a) // self.world
@@ -75,6 +164,8 @@ class DataParallel:
             for key in self.blocks:
                 if key not in self.launched:
                     self._ready(key)
+            if self.comm is not None:
+                self.comm.join()
             for buf, h in self.handles:
                 h.wait()
                 if not self.native_avg:
@@ -82,8 +173,23 @@ class DataParallel:
         self.handles.clear()
         self.launched.clear()
 
+    def check(self, timeout_s: float | None = None) -> None:
+        """Between steps: wait (bounded) until this rank's collectives have
+        finished; raises ForgeCUError and aborts the communicator on a
+        deadline miss or a failed peer."""
+        if self.comm is not None:
+            self.comm.poll(timeout_s)
+
     def detach(self) -> None:
         self.model.grad_ready_hook = None
+
+    def close(self) -> None:
+        """Detach and destroy the communicator (release any CUDA graph that
+        replays its collectives first)."""
+        self.detach()
+        if self.comm is not None:
+            self.comm.close()
+            self.comm = None
 
 
 class ShardedAdam:
@@ -137,10 +243,22 @@ class ShardedAdam:
         pf, gf = self._flat
         for i, (a, b) in enumerate(self.own):
             call("fcu_sumsq", h, gf.data_ptr() + 4 * a, b - a, self._ss.data_ptr(), 1 if i else 0)
-        dist.all_reduce(self._ss, op=dist.ReduceOp.SUM, group=self.dp.group)
+        if self.dp.comm is not None:
+            self.dp.comm.allreduce_sum_f64(self._ss)
+            self.dp.comm.join()
+        else:
+            dist.all_reduce(self._ss, op=dist.ReduceOp.SUM, group=self.dp.group)
 
     def _gather(self, shadow):
         pf = self.model.flat_params
+        comm = self.dp.comm
+        if comm is not None:
+            for a, b in self.dp.blocks.values():
+                comm.allgather(pf[a:b])
+                if shadow is not None:
+                    comm.allgather(shadow[a:b])
+            comm.join()
+            return
         for a, b in self.dp.blocks.values():
             n = (b - a) // self.dp.world
             r = self.dp.rank

@@ -388,6 +388,61 @@ int64_t fcu_model_num_params(const fcu_model_cfg *cfg);
  * ffn_down[D*H]. */
 int fcu_init_weights(const fcu_model_cfg *cfg, uint32_t seed, float *host_out);
 
+/* ---------------------------------------------------------------- data-parallel exchange */
+/* NCCL over NVLink / NVSwitch, one communicator per GPU.  The reference has no
+ * counterpart (it trains on one CPU thread); this is the exchange a
+ * data-parallel host wraps around Adam.step (src/L2/autograd.js:214-244) when
+ * TrainableTransformer's batch (src/L6/train.js:175-185) is split by sequence
+ * over the GPUs: every rank averages the flat gradient buffer, bucket by
+ * bucket while its backward continues, then takes the identical Adam step.
+ *
+ * NCCL is loaded at run time (libnccl.so.2, or the path in FORGECU_NCCL_LIB);
+ * FCU_ERR_UNSUPPORTED if it cannot be.  Communicators are non-blocking
+ * (ncclConfig_t.blocking = 0): every wait for NCCL is bounded, and a
+ * communicator that misses a deadline or reports an asynchronous error is
+ * aborted (ncclCommAbort, which also ends its kernels in flight) and the call
+ * returns FCU_ERR_TIMEOUT / FCU_ERR_NCCL.  An aborted communicator only
+ * accepts fcu_comm_destroy.
+ *
+ * Collectives are stream-ordered: each one starts on the communicator's own
+ * stream once the work already queued on ctx's stream is done (an event), so
+ * it overlaps what ctx launches next; fcu_comm_join makes ctx's stream wait
+ * for all of them.  The fork and join are legal inside CUDA stream capture. */
+typedef struct fcu_comm fcu_comm;
+#define FCU_COMM_ID_BYTES 128
+/* A fresh NCCL unique id: rank 0 makes it and the host hands the bytes to
+ * every rank (a store, MPI, a file ...). */
+int fcu_comm_unique_id(void *id_out);
+/* Joins the nranks-rank communicator named by id as `rank`, on CUDA device
+ * `device` (-1: the calling thread's current device, which must then be the
+ * device of the contexts later passed with it).  Waits at most timeout_s for
+ * every rank to join. */
+int fcu_comm_init(int device, const void *id, int nranks, int rank, double timeout_s, fcu_comm **out);
+/* Finalizes (bounded) and frees the communicator; after an abort it only frees. */
+int fcu_comm_destroy(fcu_comm *comm);
+int fcu_comm_abort(fcu_comm *comm);
+/* nranks / rank / device (any output may be NULL); FCU_ERR_NCCL once aborted. */
+int fcu_comm_info(const fcu_comm *comm, int *nranks, int *rank, int *device);
+/* buf[0..n) = average over the ranks of buf (in place): one gradient bucket,
+ * e.g. one layer's contiguous block of the flat gradient buffer. */
+int fcu_allreduce_grads(fcu_ctx *ctx, fcu_comm *comm, float *buf, int64_t n);
+/* ZeRO-1: rank r's slice buf[r*n/R, (r+1)*n/R) = average over the ranks of
+ * that slice of buf (in place; n % nranks == 0). */
+int fcu_reduce_scatter_grads(fcu_ctx *ctx, fcu_comm *comm, float *buf, int64_t n);
+/* ZeRO-1: every rank's slice buf[r*n/R, (r+1)*n/R) gathered into all of buf
+ * (in place); elem_bytes 4 (fp32 parameters) or 2 (their bf16 copy). */
+int fcu_allgather_params(fcu_ctx *ctx, fcu_comm *comm, void *buf, int64_t n, int elem_bytes);
+/* buf[0..n) = sum over the ranks (fp64, in place): the global gradient sum
+ * of squares for Adam's norm clipping. */
+int fcu_allreduce_sum_f64(fcu_ctx *ctx, fcu_comm *comm, double *buf, int64_t n);
+/* ctx's stream waits for every collective launched on comm so far. */
+int fcu_comm_join(fcu_ctx *ctx, fcu_comm *comm);
+/* Host check between steps (not during stream capture): FCU_OK once every
+ * collective launched since the last poll has finished; FCU_ERR_TIMEOUT if
+ * they have not within timeout_s, FCU_ERR_NCCL on an asynchronous error (both
+ * abort the communicator). */
+int fcu_comm_poll(fcu_comm *comm, double timeout_s);
+
 /* ---------------------------------------------------------------- misc */
 /* y[i] *= alpha (data-parallel gradient averaging). */
 int fcu_scale(fcu_ctx *ctx, float *y, int64_t n, float alpha);

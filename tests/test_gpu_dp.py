@@ -1,7 +1,9 @@
-"""Data parallelism on 2 GPUs (skipped with fewer): the averaged gradients of
-a batch split over two NCCL ranks equal the full-batch gradients of one
-process (fp32 parity mode, relL2 <= 1e-5), and after one Adam step the two
-replicas hold bit-identical parameters."""
+"""Data parallelism on 2 GPUs (skipped with fewer), through the C-ABI NCCL
+communicator (fcu_comm_init / fcu_allreduce_grads / fcu_reduce_scatter_grads /
+fcu_allgather_params): the averaged gradients of a batch split over two ranks
+equal the full-batch gradients of one process (fp32 parity mode, relL2 <=
+1e-5), and after one Adam step the two replicas hold bit-identical
+parameters; ZeRO-1 matches replicated Adam, eager and graph-captured."""
 import os
 import socket
 
@@ -48,8 +50,9 @@ def _rank(rank, world, port, q):
         opt.step()
         p = m.flat_params.cpu().numpy()
         torch.cuda.synchronize()
+        dp.check(60.0)             # the C-ABI communicator saw no failure
         q.put((rank, g, p))
-        dp.detach()
+        dp.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -128,7 +131,8 @@ def _rank_zero(rank, world, port, q, graph):
             if graph:
                 cs.graph.reset()
                 del cs
-            dp.detach()
+            dp.check(60.0)
+            dp.close()
         q.put((rank, out))
         dist.barrier()
     finally:
