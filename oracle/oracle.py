@@ -21,9 +21,10 @@ _LIB_PATH = os.path.join(_HERE, "liboracle.so")
 
 
 def build() -> str:
-    """Compile liboracle.so from forge_oracle.c (make, in this directory)."""
-    src = os.path.join(_HERE, "forge_oracle.c")
-    if (not os.path.exists(_LIB_PATH)) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+    """Compile liboracle.so from forge_oracle.c and forge_oracle_infer.c (make,
+    in this directory)."""
+    srcs = [os.path.join(_HERE, f) for f in ("forge_oracle.c", "forge_oracle_infer.c")]
+    if (not os.path.exists(_LIB_PATH)) or os.path.getmtime(_LIB_PATH) < max(map(os.path.getmtime, srcs)):
         subprocess.run(["make", "-s", "-C", _HERE, "CC=gcc"], check=True)
     return _LIB_PATH
 
@@ -98,6 +99,27 @@ def _declare(L):
         "or_init_weights": (None, [C.POINTER(OrCfg), C.c_uint32, _f]),
         "or_model_step": (C.c_float, [C.POINTER(OrCfg), _f, _f, _i, _i, C.c_int, C.c_int, _f]),
     }
+    _u8 = C.POINTER(C.c_uint8)
+    sig.update({
+        "or_fp16_to_fp32": (C.c_float, [C.c_int]),
+        "or_fp32_to_fp16": (C.c_int, [C.c_double]),
+        "or_block_size": (C.c_int, [C.c_int]),
+        "or_block_bytes": (C.c_int, [C.c_int]),
+        "or_row_bytes": (C.c_int64, [C.c_int, _i64]),
+        "or_dot": (C.c_double, [_f, _f, _i64]),
+        "or_matvec": (None, [_f, _f, _f, _i64, _i64]),
+        "or_dequantize": (C.c_int, [C.c_int, _u8, _i64, _f, _i64]),
+        "or_dotq": (C.c_double, [C.c_int, _u8, _f, _i64, _i64, _i64]),
+        "or_quantlinear_fwd": (None, [C.c_int, _u8, _f, _i64, _i64, _f, _i64]),
+        "or_quantize_row": (C.c_int64, [C.c_int, _f, _i64, _u8]),
+        "or_attention_decode": (None, [_f, _f, _f, _f, _i64, _i64, C.c_double, C.c_int, _i64, _i64]),
+        "or_attention_naive": (None, [_f, _f, _f, _f, _i64, _i64, C.c_double, C.c_int, _i64, _i64]),
+        "or_flash_attention": (None, [_f, _f, _f, _f, _i64, _i64, C.c_double, C.c_int, _i64, _i64,
+                                      C.c_int]),
+        "or_rmsnorm_vec": (None, [_f, _f, _f, _i64, C.c_double]),
+        "or_rope_table": (None, [_i64, C.c_int, C.c_double, _f, _f]),
+        "or_transformer_forward": (None, [C.c_void_p, C.c_int, _i64, _f, _f, _f]),
+    })
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
         fn.restype = res
@@ -373,3 +395,198 @@ def model_step(cfg: Config, P, ids, targets, B, T, G=None, want_logits=False):
     logits = np.empty(B * T * cfg.vocabSize, np.float32) if want_logits else None
     loss = lib().or_model_step(C.byref(c), _fp(P), _fp(G), _ip(ids), _ip(tg), B, T, _fp(logits))
     return (np.float32(loss), logits) if want_logits else np.float32(loss)
+
+
+# ---------------------------------------------------------------- inference side
+# GGML type numbers (quant.js:34-38) of the formats the decode kernels read.
+F32, F16, Q4_0, Q5_0, Q8_0, Q4_K, Q5_K, Q6_K = 0, 1, 2, 6, 8, 12, 13, 14
+
+
+def _u8p(a):
+    assert a.dtype == np.uint8 and a.flags.c_contiguous
+    return a.ctypes.data_as(C.POINTER(C.c_uint8))
+
+
+def _bytes(data) -> np.ndarray:
+    """A weight byte stream: uint8 as is, float32 / float16 arrays by their bytes."""
+    a = np.ascontiguousarray(data)
+    return a if a.dtype == np.uint8 else a.view(np.uint8)
+
+
+def fp32_to_fp16(x: float) -> int:
+    return int(lib().or_fp32_to_fp16(float(x)))
+
+
+def fp16_to_fp32(h: int) -> float:
+    return float(lib().or_fp16_to_fp32(int(h)))
+
+
+def block_size(t: int) -> int:
+    return int(lib().or_block_size(t))
+
+
+def block_bytes(t: int) -> int:
+    return int(lib().or_block_bytes(t))
+
+
+def row_bytes(t: int, n: int) -> int:
+    return int(lib().or_row_bytes(t, n))
+
+
+def dot(a, b) -> float:
+    a, b = f32(a).ravel(), f32(b).ravel()
+    return float(lib().or_dot(_fp(a), _fp(b), a.size))
+
+
+def matvec(W, x, N, K):
+    out = np.empty(N, np.float32)
+    lib().or_matvec(_fp(out), _fp(f32(W)), _fp(f32(x)), N, K)
+    return out
+
+
+def quantize_row(t: int, x) -> np.ndarray:
+    """quantizeRow (quant.js:594-604) of a flat float32 array (types 0, 1, 8,
+    12, 13, 14)."""
+    x = f32(x).ravel()
+    out = np.zeros(max(1, row_bytes(t, x.size)), np.uint8)
+    n = lib().or_quantize_row(t, _fp(x), x.size, _u8p(out))
+    if n < 0:
+        raise ValueError(f"quantizeRow: type {t} not supported")
+    return out[:n]
+
+
+def dequantize(t: int, data, n: int, byte_off: int = 0) -> np.ndarray:
+    data = _bytes(data)
+    out = np.zeros(n, np.float32)
+    if lib().or_dequantize(t, _u8p(data), n, _fp(out), byte_off):
+        raise ValueError(f"dequantize: type {t} not supported")
+    return out
+
+
+def dotq(t: int, data, x, n: int, x_off: int = 0, byte_off: int = 0) -> float:
+    data = _bytes(data)
+    return float(lib().or_dotq(t, _u8p(data), _fp(f32(x)), n, x_off, byte_off))
+
+
+def quantlinear_fwd(t: int, data, x, N: int, K: int) -> np.ndarray:
+    """QuantLinear.forward (nn.js:27-32): out[N] = W . x."""
+    data = _bytes(data)
+    out = np.empty(N, np.float32)
+    lib().or_quantlinear_fwd(t, _u8p(data), _fp(f32(x)), N, K, _fp(out), 0)
+    return out
+
+
+def _attn(fn, q, K, V, n, d, scale, causal, q_off, k_off, *extra):
+    out = np.empty(d, np.float32)
+    getattr(lib(), fn)(_fp(out), _fp(f32(q)), _fp(f32(K)), _fp(f32(V)), n, d, float(scale),
+                       1 if causal else 0, q_off, k_off, *extra)
+    return out
+
+
+def attention_decode(q, K, V, n, d, scale, causal=True, q_off=0, k_off=0):
+    return _attn("or_attention_decode", q, K, V, n, d, scale, causal, q_off, k_off)
+
+
+def attention_naive(q, K, V, n, d, scale, causal=True, q_off=0, k_off=0):
+    return _attn("or_attention_naive", q, K, V, n, d, scale, causal, q_off, k_off)
+
+
+def flash_attention(q, K, V, n, d, scale, causal=True, q_off=0, k_off=0, block=64):
+    return _attn("or_flash_attention", q, K, V, n, d, scale, causal, q_off, k_off, block)
+
+
+def rmsnorm_vec(x, w, eps):
+    x = f32(x).ravel()
+    out = np.empty_like(x)
+    lib().or_rmsnorm_vec(_fp(out), _fp(x), _fp(f32(w)), x.size, float(eps))
+    return out
+
+
+def rope_table(max_pos, dim, theta=10000.0):
+    cos = np.empty(max_pos * dim // 2, np.float32)
+    sin = np.empty_like(cos)
+    lib().or_rope_table(max_pos, dim, float(theta), _fp(cos), _fp(sin))
+    return cos, sin
+
+
+class _InferModel(C.Structure):
+    _fields_ = [("vocab", C.c_int), ("dim", C.c_int), ("n_layers", C.c_int), ("n_heads", C.c_int),
+                ("n_kv_heads", C.c_int), ("hidden", C.c_int), ("max_seq", C.c_int),
+                ("norm_eps", C.c_double), ("rope_theta", C.c_double), ("tok_type", C.c_int),
+                ("w_type", C.c_int), ("tok_emb", C.c_void_p), ("ln_f", C.c_void_p),
+                ("ln1", C.c_void_p), ("ln2", C.c_void_p), ("wqkv", C.c_void_p), ("wo", C.c_void_p),
+                ("gate", C.c_void_p), ("up", C.c_void_p), ("down", C.c_void_p)]
+
+
+class InferModel:
+    """Transformer (transformer.js:67-185) for the oracle's inference forward:
+    weights as QuantLinear byte streams.  `w` maps the export names
+    (tok_emb, ln_f, layer.{l}.{ln1, ln2, wqkv, wo, ffn_gate, ffn_up,
+    ffn_down}) to float32 arrays; matrices are quantized to `w_type`, the
+    embedding / LM head to `tok_type`."""
+
+    def __init__(self, cfg: "Config", w: dict, max_seq: int, w_type: int = 0, tok_type: int = 0):
+        self.cfg, self.max_seq = cfg, max_seq
+        D, H = cfg.dim, cfg.hidden
+        dH = D // cfg.nHeads
+        qkv = (cfg.nHeads + 2 * cfg.nKvHeads) * dH
+        self._keep = []
+
+        def q(arr, t):
+            b = quantize_row(t, arr)
+            self._keep.append(b)
+            return b
+
+        self.tok = q(w["tok_emb"], tok_type)
+        self.ln_f = f32(w["ln_f"])
+        L = cfg.nLayers
+        names = ("wqkv", "wo", "ffn_gate", "ffn_up", "ffn_down")
+        self.mats = {k: [q(w[f"layer.{l}"][k], w_type) for l in range(L)] for k in names}
+        self.norms = {k: [f32(w[f"layer.{l}"][k]) for l in range(L)] for k in ("ln1", "ln2")}
+        self._keep += [self.ln_f] + self.norms["ln1"] + self.norms["ln2"]
+
+        def ptrs(arrs):
+            a = (C.c_void_p * len(arrs))(*[x.ctypes.data for x in arrs])
+            self._keep.append(a)
+            return C.cast(a, C.c_void_p)
+
+        self.s = _InferModel(cfg.vocabSize, D, L, cfg.nHeads, cfg.nKvHeads, H, max_seq,
+                             float(cfg.normEps), float(cfg.ropeTheta), tok_type, w_type,
+                             self.tok.ctypes.data, self.ln_f.ctypes.data,
+                             ptrs(self.norms["ln1"]), ptrs(self.norms["ln2"]),
+                             ptrs(self.mats["wqkv"]), ptrs(self.mats["wo"]), ptrs(self.mats["ffn_gate"]),
+                             ptrs(self.mats["ffn_up"]), ptrs(self.mats["ffn_down"]))
+        kv = cfg.nKvHeads * dH
+        self.cache_k = np.zeros(L * max_seq * kv, np.float32)
+        self.cache_v = np.zeros_like(self.cache_k)
+        del qkv
+
+    def forward(self, token: int, pos: int) -> np.ndarray:
+        logits = np.empty(self.cfg.vocabSize, np.float32)
+        lib().or_transformer_forward(C.byref(self.s), int(token), int(pos), _fp(self.cache_k),
+                                     _fp(self.cache_v), _fp(logits))
+        return logits
+
+
+def unflatten_weights(cfg: "Config", P) -> dict:
+    """The flat paramList-order buffer of init_weights as the export dict
+    (toParams / exportWeights order, train.js:60-78)."""
+    P = f32(P).ravel()
+    V, D, H, L = cfg.vocabSize, cfg.dim, cfg.hidden, cfg.nLayers
+    dH = D // cfg.nHeads
+    qkv = (cfg.nHeads + 2 * cfg.nKvHeads) * dH
+    w, off = {}, 0
+
+    def take(n):
+        nonlocal off
+        a = P[off:off + n]
+        off += n
+        return a
+
+    w["tok_emb"] = take(V * D)
+    w["ln_f"] = take(D)
+    for l in range(L):
+        w[f"layer.{l}"] = {"ln1": take(D), "ln2": take(D), "wqkv": take(qkv * D), "wo": take(D * D),
+                           "ffn_gate": take(H * D), "ffn_up": take(H * D), "ffn_down": take(D * H)}
+    assert off == P.size
+    return w

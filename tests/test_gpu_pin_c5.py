@@ -17,13 +17,14 @@ full context length:
   T 2048, d 64, RoPE) against oracle slices.
 
 Stated bounds for the bf16 step (bf16 operands for every contraction, fp32
-accumulation, fp32 master weights, gradients and residual stream):
-  loss                       relative  <= C5_LOSS_TOL
-  flat gradient              relL2     <= C5_FLAT_TOL
-  each parameter tensor      relL2     <= C5_TENSOR_TOL (embedding/LM head,
-                                          norms, every layer's projections)
-  global gradient norm       relative  <= C5_GNORM_TOL
-  first Adam update          relL2     <= C5_ADAM_TOL of the update itself
+accumulation, fp32 master weights, gradients and residual stream), B 2 x
+T 1024 against the fp32 path:
+  loss                       relative  <= 1e-4
+  flat gradient              relL2     <= 2e-2
+  each parameter tensor      relL2     <= 2.5e-2 (embedding/LM head, norms,
+                                          every layer's projections)
+  global gradient norm       relative  <= 2e-3
+  first Adam update          relL2     <= 0.2 of the update itself
 """
 import numpy as np
 import pytest
@@ -35,11 +36,20 @@ pytestmark = pytest.mark.gpu
 
 C5 = dict(vocabSize=32000, dim=768, nLayers=12, nHeads=12, nKvHeads=4, hidden=2048)
 
-C5_LOSS_TOL = 2e-3
-C5_FLAT_TOL = 3e-2
-C5_TENSOR_TOL = 5e-2
-C5_GNORM_TOL = 2e-2
-C5_ADAM_TOL = 0.5
+# Measured on B200 at B 2, T 1024 (bf16 against the fp32 path): loss 8.3e-6,
+# flat gradient 1.08e-2, worst tensor 1.39e-2 (layer norms and ffn_gate),
+# gradient norm 4.7e-4, first Adam update 0.100 (its step is about
+# lr * sign(g), so elements whose tiny gradients change sign dominate it).
+# The bounds are about twice those.
+C5_LOSS_TOL = 1e-4
+C5_FLAT_TOL = 2e-2
+C5_TENSOR_TOL = 2.5e-2
+C5_GNORM_TOL = 2e-3
+C5_ADAM_TOL = 0.2
+# One sequence of T = 128 against the oracle (fewer tokens average less)
+SEQ_LOSS_TOL = 2e-3
+SEQ_FLAT_TOL = 3e-2
+SEQ_TENSOR_TOL = 5e-2
 FP32_TOL = 1e-5
 
 
@@ -109,9 +119,9 @@ def test_c5_bf16_step_matches_fp32_path_at_full_size():
 
 
 def test_c5_one_sequence_against_oracle():
-    """Config-5 model, one sequence (T = 128): the fp32 path to 1e-5 and the
-    bf16 fused path to the bounds above, both against the oracle's
-    model_step (src/L6/train.js:120-185 restated)."""
+    """Config-5 model, one sequence (T = 128): the fp32 path to 1e-5 (each
+    tensor to 1e-4) and the bf16 fused path to the SEQ_* bounds, both against
+    the oracle's model_step (src/L6/train.js:120-185 restated)."""
     B, T = 1, 128
     rows = _rows(B, T)
     ocfg = O.Config(**C5)
@@ -128,9 +138,9 @@ def test_c5_one_sequence_against_oracle():
     bad = {k: v for k, v in _per_tensor(G, a["g"]).items() if not v <= 10 * FP32_TOL}
     assert not bad, bad
     b = _step("bf16", rows)
-    assert abs(b["loss"] - lo) <= C5_LOSS_TOL * abs(lo), (b["loss"], lo)
-    assert O.rel_l2(G, b["g"]) <= C5_FLAT_TOL, O.rel_l2(G, b["g"])
-    bad = {k: v for k, v in _per_tensor(G, b["g"]).items() if not v <= C5_TENSOR_TOL}
+    assert abs(b["loss"] - lo) <= SEQ_LOSS_TOL * abs(lo), (b["loss"], lo)
+    assert O.rel_l2(G, b["g"]) <= SEQ_FLAT_TOL, O.rel_l2(G, b["g"])
+    bad = {k: v for k, v in _per_tensor(G, b["g"]).items() if not v <= SEQ_TENSOR_TOL}
     assert not bad, bad
 
 
