@@ -84,6 +84,17 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
       : "memory");
 }
 
+// Untiled bulk copy of `bytes` contiguous bytes global -> shared memory,
+// completing on an mbarrier.  Both addresses 16-byte aligned, bytes a
+// multiple of 16.
+__device__ __forceinline__ void bulk_load_1d(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"((uint64_t)src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 2-D TMA store / reduce-add of a shared-memory box to global memory, as a
 // bulk async-group (commit with bulk_commit, reuse the source after
 // bulk_wait_read).  The start coordinates must not be negative.

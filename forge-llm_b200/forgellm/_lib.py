@@ -127,6 +127,11 @@ _SIGS = {
     "fcu_adam_update_dev": (_INT, [_P, _P, _P, _P, _P, _I64, _P, _P, _P, _P]),
     "fcu_to_bf16": (_INT, [_P, _P, _I64, _P]),
     "fcu_scale_bf16_dev": (_INT, [_P, _P, _I64, _P]),
+    "fcu_ggml_row_bytes": (_I64, [_INT, _I64]),
+    "fcu_quant_matvec": (_INT, [_P, _INT, _P, _I64, _I64, _P, _I64, _P]),
+    "fcu_dequantize_rows": (_INT, [_P, _INT, _P, _I64, _I64, _P, _I64, _P]),
+    "fcu_decode_rope_kv": (_INT, [_P, _P, _I64, _INT, _INT, _INT, _INT, _D, _P, _P, _P, _I64, _P, _INT, _INT]),
+    "fcu_attn_decode": (_INT, [_P, _P, _I64, _P, _P, _I64, _P, _INT, _INT, _P, _INT, _INT, _INT, _INT, _D, _P]),
     "fcu_comm_unique_id": (_INT, [_P]),
     "fcu_comm_init": (_INT, [_INT, _P, _INT, _INT, _D, C.POINTER(_P)]),
     "fcu_comm_destroy": (_INT, [_P]),

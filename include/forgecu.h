@@ -388,6 +388,63 @@ int64_t fcu_model_num_params(const fcu_model_cfg *cfg);
  * ffn_down[D*H]. */
 int fcu_init_weights(const fcu_model_cfg *cfg, uint32_t seed, float *host_out);
 
+/* ---------------------------------------------------------------- inference side (decode) */
+/* GGML tensor types these kernels read (GGMLType, src/L3/quant.js:34-38).
+ * FCU_GGML_Q4_0 / FCU_GGML_Q5_0 are decoded as the reference decodes them
+ * (src/L3/quant.js:191-205: f16 d, then nibble j&1 of byte 2 + j/2, Q5_0
+ * without its high bits), which is not ggml's own Q4_0 / Q5_0 layout. */
+enum {
+  FCU_GGML_F32 = 0,
+  FCU_GGML_F16 = 1,
+  FCU_GGML_Q4_0 = 2,
+  FCU_GGML_Q5_0 = 6,
+  FCU_GGML_Q8_0 = 8,
+  FCU_GGML_Q4_K = 12,
+  FCU_GGML_Q5_K = 13,
+  FCU_GGML_Q6_K = 14
+};
+/* Bytes of one row of n elements (rowBytes, src/L3/quant.js:62); -1 for an
+ * unsupported type.  Host function. */
+int64_t fcu_ggml_row_bytes(int type, int64_t n);
+/* Y[m, n] = sum_k W[n, k] X[m, k] for m < M: QuantLinear.forward
+ * (src/L4/nn.js:27-32; dotQ src/L3/quant.js:215-310, matvec
+ * src/L0/numeric.js:85-100 for F32) applied to M vectors in one pass over W.
+ * W: N rows of K elements in GGML blocks (row n at n * fcu_ggml_row_bytes),
+ * 16-byte aligned; X [M, K] fp32 16-byte aligned; Y [M, N] fp32.  K a
+ * multiple of the type's block (32 or 256; any K for F32 / F16), one row at
+ * most 24 KiB, K <= 24576.  fp32 accumulation (the JS accumulates in double). */
+int fcu_quant_matvec(fcu_ctx *ctx, int type, const void *W, int64_t N, int64_t K, const float *X, int64_t M,
+                     float *Y);
+/* out[r, :] = dequantize(row rows[r] of W) (src/L3/quant.js:109-209),
+ * bit-identical to the JS; rows NULL: rows 0..nrows-1.  An id outside [0, N)
+ * gives a NaN row.  The quantized embedding lookup of
+ * src/L6/transformer.js:122-132 is rows = the token ids. */
+int fcu_dequantize_rows(fcu_ctx *ctx, int type, const void *W, int64_t N, int64_t K, const int32_t *rows,
+                        int64_t nrows, float *out);
+/* For each of B sequences, qkv row b ([q heads | k heads | v heads], dH each,
+ * row stride ld_qkv floats): RoPE at position positions[b] (device) on the
+ * q and k heads in place (applyRopeHead, src/L6/transformer.js:56-64, with
+ * the fp32 table of ropeTable, src/L1/special.js:116-127), then k and v
+ * written to that position's cache row (KVCache.put / PagedKVCache.put,
+ * src/L5/attention.js:135-139, 166-171).  Cache row of position p of
+ * sequence b: block_table[b * max_blocks + p / block_size] * block_size +
+ * p % block_size (block_table NULL: block b * max_blocks + p / block_size);
+ * rows are row_stride floats apart, kv head h at column h * dH.  A position
+ * outside [0, max_blocks * block_size) leaves that sequence untouched. */
+int fcu_decode_rope_kv(fcu_ctx *ctx, float *qkv, int64_t ld_qkv, int B, int nH, int nKV, int dH, double theta,
+                       const int32_t *positions, float *k_cache, float *v_cache, int64_t row_stride,
+                       const int32_t *block_table, int max_blocks, int block_size);
+/* out[b, h*dH:(h+1)*dH] = attention of q head h of sequence b (q rows ld_q
+ * floats apart) over cache positions [0, seq_lens[b]) (device; clamped to
+ * max_blocks * block_size) with kv head h / (nH / nKV) and the given scale:
+ * the decode loop of src/L6/transformer.js:157-172 with attentionDecode
+ * (src/L5/attention.js:31-57).  A length of 0 gives zeros.  dH <= 256,
+ * nH / nKV <= 16.  Sequences longer than 256 positions are split across CTAs
+ * and merged; the partials use the context's scratch. */
+int fcu_attn_decode(fcu_ctx *ctx, const float *q, int64_t ld_q, const float *k_cache, const float *v_cache,
+                    int64_t row_stride, const int32_t *block_table, int max_blocks, int block_size,
+                    const int32_t *seq_lens, int B, int nH, int nKV, int dH, double scale, float *out);
+
 /* ---------------------------------------------------------------- data-parallel exchange */
 /* NCCL over NVLink / NVSwitch, one communicator per GPU.  The reference has no
  * counterpart (it trains on one CPU thread); this is the exchange a
