@@ -372,6 +372,120 @@ def run_config(args):
     print(json.dumps(out), flush=True)
 
 
+def run_decode(args):
+    """The inference-side kernels (`--config decode`), one JSON line each:
+    QuantLinear matvec (fcu_quant_matvec) per GGML format on a weight larger
+    than L2, decode attention (fcu_attn_decode) over a batch of long KV
+    caches, and one decode step of the config-5 model with Q4_K matrices for
+    1 and 32 sequences.  Weight bytes are random GGML blocks with finite f16
+    scales (their values do not change the work); the cache and vectors are
+    N(0, 1)."""
+    import math
+
+    import torch
+    import forgellm as F
+    from forgellm import autograd as AD
+    from forgellm import infer as I
+    from forgellm._lib import call
+    pk, kind = peaks()
+    h = AD.ctx().handle
+    dev = "cuda"
+    gen = torch.Generator(device=dev).manual_seed(7)
+
+    def ggml_bytes(t, N, K):
+        rb = I.row_bytes(t, K)
+        if t == I.F32:
+            return torch.randn(N * K, device=dev, generator=gen).view(torch.uint8)
+        if t == I.F16:
+            return torch.randn(N * K, device=dev, generator=gen).half().view(torch.uint8)
+        b = torch.randint(0, 256, (N * rb,), dtype=torch.uint8, device=dev, generator=gen)
+        bb = {I.Q4_0: 18, I.Q5_0: 22, I.Q8_0: 34, I.Q4_K: 144, I.Q5_K: 176, I.Q6_K: 210}[t]
+        blk = b.view(-1, bb)
+        d = torch.full((blk.shape[0],), 0.01, device=dev).half().view(torch.uint8).view(-1, 2)
+        if t == I.Q6_K:
+            blk[:, 208:210] = d
+        else:
+            blk[:, 0:2] = d
+            if t in (I.Q4_K, I.Q5_K):
+                blk[:, 2:4] = d
+        return b
+
+    K = 4096
+    for t, name in ((I.Q4_K, "Q4_K"), (I.Q5_K, "Q5_K"), (I.Q6_K, "Q6_K"), (I.Q8_0, "Q8_0"), (I.F16, "F16"),
+                    (I.F32, "F32")):
+        rb = I.row_bytes(t, K)
+        N = max(4096, (512 << 20) // rb)       # ~512 MiB of weights: well beyond the 126 MB L2
+        W = ggml_bytes(t, N, K)
+        for M in (1, 8):
+            X = torch.randn(M, K, device=dev, generator=gen)
+            Y = torch.empty(M, N, device=dev)
+            ms = _time_ms(lambda: call("fcu_quant_matvec", h, t, W.data_ptr(), N, K, X.data_ptr(), M, Y.data_ptr()),
+                          args.steps, args.warmup)
+            gb = (N * rb + M * K * 4 + M * N * 4) / 1e9
+            bw = gb / (ms / 1e3)
+            print(json.dumps({"config": "decode", "kernel": "fcu_quant_matvec", "type": name, "N": N, "K": K, "M": M,
+                              "metric": "QuantLinear.forward GB/s", "value": bw, "unit": "GB/s", "ms": ms,
+                              "roofline": {"bound": "hbm", "achieved": bw, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                           "frac": bw / pk["hbm_gbs"], "peak_kind": kind,
+                                           "algorithmic_gb": gb},
+                              "data": "synthetic GGML blocks"}), flush=True)
+        del W
+        torch.cuda.empty_cache()
+    # decode attention: B sequences of n cached positions each
+    for B, n, nH, nKV, dH in ((64, 4096, 32, 8, 128), (32, 1024, 12, 4, 64), (1, 1024, 12, 4, 64)):
+        kvDim = nKV * dH
+        kc = torch.randn(B * n, kvDim, device=dev, generator=gen)
+        vc = torch.randn(B * n, kvDim, device=dev, generator=gen)
+        ld = (nH + 2 * nKV) * dH
+        q = torch.randn(B, ld, device=dev, generator=gen)
+        out = torch.empty(B, nH * dH, device=dev)
+        lens = torch.full((B,), n, dtype=torch.int32, device=dev)
+        ms = _time_ms(lambda: call("fcu_attn_decode", h, q.data_ptr(), ld, kc.data_ptr(), vc.data_ptr(), kvDim, None,
+                                   1, n, lens.data_ptr(), B, nH, nKV, dH, 1 / math.sqrt(dH), out.data_ptr()),
+                      args.steps, args.warmup)
+        gb = (2.0 * B * n * kvDim * 4 + B * ld * 4 + B * nH * dH * 4) / 1e9
+        bw = gb / (ms / 1e3)
+        print(json.dumps({"config": "decode", "kernel": "fcu_attn_decode", "B": B, "n": n, "nH": nH, "nKV": nKV,
+                          "dH": dH, "metric": "decode attention GB/s", "value": bw, "unit": "GB/s", "ms": ms,
+                          "roofline": {"bound": "hbm", "achieved": bw, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                       "frac": bw / pk["hbm_gbs"], "peak_kind": kind, "algorithmic_gb": gb},
+                          "l2": "cache > L2" if gb > 0.126 else "cache fits L2 (latency-bound size)"}),
+              flush=True)
+        del kc, vc
+        torch.cuda.empty_cache()
+    # one decode step of the config-5 model (Q4_K matrices, Q8_0 embedding / LM head)
+    cfg = F.Config(**C5, maxSeq=1024)
+    w = {"tok_emb": I.QuantLinear(I.Q8_0, ggml_bytes(I.Q8_0, cfg.vocabSize, cfg.dim), cfg.vocabSize, cfg.dim),
+         "ln_f": torch.ones(cfg.dim)}
+    for l in range(cfg.nLayers):
+        shapes = {"wqkv": (cfg.qkvOut, cfg.dim), "wo": (cfg.dim, cfg.dim), "ffn_gate": (cfg.hidden, cfg.dim),
+                  "ffn_up": (cfg.hidden, cfg.dim), "ffn_down": (cfg.dim, cfg.hidden)}
+        L = {k: I.QuantLinear(I.Q4_K, ggml_bytes(I.Q4_K, n_, k_), n_, k_) for k, (n_, k_) in shapes.items()}
+        L.update(ln1=torch.ones(cfg.dim), ln2=torch.ones(cfg.dim))
+        w[f"layer.{l}"] = L
+    tr = F.Transformer(cfg).loadWeights(w)
+    wbytes = tr.tokEmb.bytesSize() + sum(q.bytesSize() for L in tr.layers for k, q in L.items()
+                                         if isinstance(q, I.QuantLinear))
+    for B in (1, 32):
+        cache = F.KVCache(cfg.nLayers, cfg.maxSeq, cfg.kvDim, batch=B)
+        toks = [int(x) for x in F.RNG(5).ints(B, cfg.vocabSize)]
+        state = {"pos": 0}
+
+        def step():
+            p = state["pos"] % 512 + 256          # positions 256..767: a half-filled cache
+            tr.forwardBatch(toks, [p] * B, cache)
+            state["pos"] += 1
+
+        for p in range(256):                      # fill the first 256 positions
+            tr.forwardBatch(toks, [p] * B, cache)
+        ms = _time_ms(step, args.steps, args.warmup)
+        print(json.dumps({"config": "decode", "kernel": "Transformer.forwardBatch (config-5 model, Q4_K)",
+                          "B": B, "metric": "decode tokens/s", "value": B / (ms / 1e3), "unit": "tokens/s",
+                          "ms_per_step": ms, "weight_bytes": wbytes,
+                          "weights_gb_per_s": wbytes / 1e9 / (ms / 1e3),
+                          "note": "eager host loop: 12 layers x 11 launches + embed / head per step"}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -388,11 +502,13 @@ def main():
     ap.add_argument("--micro", choices=["gemm"], help="time one kernel alone (profiling)")
     ap.add_argument("--zero", action="store_true",
                     help="N > 1: shard Adam's state and update over the ranks (ZeRO-1)")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4"],
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "decode"],
                     help="time one of the operator configs instead of the C5 train step")
     ap.add_argument("--shape", default="8192,2048,768")
     ap.add_argument("--op", default="fwd", choices=["fwd", "dx", "dw"])
     args = ap.parse_args()
+    if args.config == "decode":
+        return run_decode(args)
     if args.config:
         return run_config(args)
     if args.micro == "gemm":

@@ -189,14 +189,15 @@ def test_decode_rope_kv_rotates_and_writes_the_cache(paged):
     qkv = O.RNG(2).normals(B * ld).reshape(B, ld)
     kc = torch.zeros(phys * block, kvDim, device="cuda")
     vc = torch.zeros_like(kc)
-    xd = _dev(qkv)
-    _lib.call("fcu_decode_rope_kv", _ctx(), xd.data_ptr(), ld, B, nH, nKV, dH, theta, _dev(pos).data_ptr(),
-              kc.data_ptr(), vc.data_ptr(), kvDim, _dev(table).data_ptr() if paged else None, max_blocks, block)
+    xd, posd, td = _dev(qkv), _dev(pos), _dev(table)   # held: the kernels read them later
+    tptr = td.data_ptr() if paged else None
+    _lib.call("fcu_decode_rope_kv", _ctx(), xd.data_ptr(), ld, B, nH, nKV, dH, theta, posd.data_ptr(),
+              kc.data_ptr(), vc.data_ptr(), kvDim, tptr, max_blocks, block)
     # a position outside the cache changes nothing
     bad = _dev(np.array([128, -1, 500], np.int32))
     before = xd.clone()
     _lib.call("fcu_decode_rope_kv", _ctx(), xd.data_ptr(), ld, B, nH, nKV, dH, theta, bad.data_ptr(),
-              kc.data_ptr(), vc.data_ptr(), kvDim, _dev(table).data_ptr() if paged else None, max_blocks, block)
+              kc.data_ptr(), vc.data_ptr(), kvDim, tptr, max_blocks, block)
     torch.cuda.synchronize()
     assert torch.equal(before, xd)
     cosT, sinT = O.rope_table(128, dH, theta)

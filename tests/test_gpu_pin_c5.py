@@ -46,10 +46,12 @@ C5_FLAT_TOL = 2e-2
 C5_TENSOR_TOL = 2.5e-2
 C5_GNORM_TOL = 2e-3
 C5_ADAM_TOL = 0.2
-# One sequence of T = 128 against the oracle (fewer tokens average less)
-SEQ_LOSS_TOL = 2e-3
-SEQ_FLAT_TOL = 3e-2
-SEQ_TENSOR_TOL = 5e-2
+# One sequence of T = 128 against the oracle.  Measured: bf16 loss 1.9e-5,
+# flat 1.08e-2, worst tensor 1.52e-2; the fp32 path flat 2.0e-6, worst
+# tensor 2.9e-6, loss exact.
+SEQ_LOSS_TOL = 1e-4
+SEQ_FLAT_TOL = 2e-2
+SEQ_TENSOR_TOL = 3e-2
 FP32_TOL = 1e-5
 
 
@@ -119,9 +121,10 @@ def test_c5_bf16_step_matches_fp32_path_at_full_size():
 
 
 def test_c5_one_sequence_against_oracle():
-    """Config-5 model, one sequence (T = 128): the fp32 path to 1e-5 (each
-    tensor to 1e-4) and the bf16 fused path to the SEQ_* bounds, both against
-    the oracle's model_step (src/L6/train.js:120-185 restated)."""
+    """Config-5 model, one sequence (T = 128): the fp32 path to 1e-5 (the
+    loss, the flat gradient and each tensor) and the bf16 fused path to the
+    SEQ_* bounds, both against the oracle's model_step
+    (src/L6/train.js:120-185 restated)."""
     B, T = 1, 128
     rows = _rows(B, T)
     ocfg = O.Config(**C5)
@@ -135,7 +138,7 @@ def test_c5_one_sequence_against_oracle():
     a = _step("fp32", rows)
     assert abs(a["loss"] - lo) <= FP32_TOL * abs(lo), (a["loss"], lo)
     assert O.rel_l2(G, a["g"]) <= FP32_TOL, O.rel_l2(G, a["g"])
-    bad = {k: v for k, v in _per_tensor(G, a["g"]).items() if not v <= 10 * FP32_TOL}
+    bad = {k: v for k, v in _per_tensor(G, a["g"]).items() if not v <= FP32_TOL}
     assert not bad, bad
     b = _step("bf16", rows)
     assert abs(b["loss"] - lo) <= SEQ_LOSS_TOL * abs(lo), (b["loss"], lo)
