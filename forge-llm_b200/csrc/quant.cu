@@ -125,9 +125,9 @@ __global__ void __launch_bounds__(256) dequant_rows_kernel(const uint8_t *__rest
 constexpr int kQmvThreads = 256;
 constexpr int kQmvWarps = kQmvThreads / 32;
 constexpr int kQmvStages = 3;
-constexpr int kQmvChunk = 24576;               // bytes of rows per stage
+constexpr int kQmvChunk = 16384;               // bytes of rows per stage (3 CTAs per SM fit)
 constexpr int kQmvBuf = kQmvChunk + 32;        // + room for the 16-byte widening
-constexpr int kQmvHeader = 128;                // mbarriers + abort flag
+constexpr int kQmvHeader = 512;                // mbarriers, abort flag, row partial sums
 
 struct QmvArgs {
   const uint8_t *W;
@@ -160,43 +160,116 @@ __device__ __forceinline__ void fma_x4(float (&acc)[MB], const float (&w)[4], co
     }
 }
 
-// One row (in shared memory) against the MB vectors: this lane's share.
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xFFu; }
+
+// Where x[k] sits in shared memory.  For Q4_K / Q5_K the float4 index bits
+// (2-3) are XORed with the 64-element group bits (6-7), for Q8_0 bit 2 with
+// the block parity (bit 5): the 8 lanes of a quarter-warp then read 8
+// different bank quads.  Linear for the others.
+template <int T>
+__device__ __forceinline__ int64_t xs_swz(int64_t k) {
+  if (T == kQ4K || T == kQ5K) return k ^ (((k >> 6) & 3) << 2);
+  if (T == kQ8_0) return k ^ (((k >> 5) & 1) << 2);   // odd blocks' halves swapped
+  return k;
+}
+template <int T>
+__host__ __device__ constexpr bool uses_xsum() { return T == kQ4K || T == kQ5K; }
+
+// 6-bit scale / min of K-quant sub-block j from the block header words
+// hy = scales[0..3], hz = scales[4..7], hw = scales[8..11] (getScaleMinK4Into).
+__device__ __forceinline__ void scale_min_hdr(int j, uint32_t hy, uint32_t hz, uint32_t hw, float &sc, float &mn) {
+  uint32_t s, m;
+  if (j < 4) {
+    s = byte_of(hy, j) & 63;
+    m = byte_of(hz, j) & 63;
+  } else {
+    s = (byte_of(hw, j - 4) & 0xF) | ((byte_of(hy, j - 4) >> 6) << 4);
+    m = (byte_of(hw, j - 4) >> 4) | ((byte_of(hz, j - 4) >> 6) << 4);
+  }
+  sc = small_u2f(s);
+  mn = small_u2f(m);
+}
+
+// One row (in shared memory) against the MB vectors: this lane's share of
+// the row's 256-element units u0, u0 + ustep, ... (a K-quant super-block, 8
+// blocks of 32, or 256 F32 / F16 elements; lane l takes 8 of the 256).
 template <int T, int MB>
 __device__ __forceinline__ void row_dot(const uint8_t *row, const float *xs, int64_t K, int M, int lane,
-                                        float (&acc)[MB]) {
+                                        float (&acc)[MB], int u0, int ustep) {
   if (T == kQ4K || T == kQ5K) {
-    const int j = lane >> 3, p = (lane & 7) * 4;
-    const int64_t nsb = K >> 8;
-    for (int64_t sb = 0; sb < nsb; sb++) {
-      const uint8_t *b = row + sb * fmt_bb(T);
-      const float d = h2f(ld16(b)), dmin = h2f(ld16(b + 2));
+    // lane = (super-block sbl of 4, 64-element group j, half h): 16 quant
+    // bytes = the 16 low-nibble elements j*64 + 16h + i (sub-block 2j) and
+    // the 16 high-nibble ones 32 further on (sub-block 2j + 1).  Each
+    // sub-block's scale is factored out: d*sc*sum(q x) - dmin*m*sum(x), with
+    // the sums of x over 16 elements precomputed (xsum); x is read through
+    // the swizzle of xs_index.
+    const int sbl = lane >> 3, j = (lane >> 1) & 3, h = lane & 1;
+    const int nsb = (int)(K >> 8);
+    const float *xsum = xs + (int64_t)M * K;     // [M][K / 16]
+#pragma unroll 1
+    for (int sb = u0 * 4 + sbl; sb < nsb; sb += ustep * 4) {
+      const uint8_t *b = row + (int64_t)sb * fmt_bb(T);
+      const uint4 hd = *reinterpret_cast<const uint4 *>(b);   // d, dmin, scales[12]
+      const uint4 qv = *reinterpret_cast<const uint4 *>(b + (T == kQ4K ? 16 : 48) + j * 32 + 16 * h);
+      uint4 qhv = make_uint4(0, 0, 0, 0);
+      if (T == kQ5K) qhv = *reinterpret_cast<const uint4 *>(b + 16 + 16 * h);
+      const float d = h2f(hd.x & 0xFFFFu), dmin = h2f(hd.x >> 16);
       float sc0, mn0, sc1, mn1;
-      scale_min_k4(2 * j, b + 4, sc0, mn0);
-      scale_min_k4(2 * j + 1, b + 4, sc1, mn1);
-      const float d1 = d * sc0, n1 = dmin * mn0, d2 = d * sc1, n2 = dmin * mn1;
-      const uint32_t q = ld32(b + (T == kQ4K ? 16 : 48) + j * 32 + p);
-      uint32_t qh = 0;
-      if (T == kQ5K) qh = ld32(b + 16 + p);
-      float wl[4], wh[4];
+      scale_min_hdr(2 * j, hd.y, hd.z, hd.w, sc0, mn0);
+      scale_min_hdr(2 * j + 1, hd.y, hd.z, hd.w, sc1, mn1);
+      const int64_t klo = (int64_t)sb * 256 + j * 64 + 16 * h;
+      // two partial sums per half (even / odd float4) keep the FMA chains short
+      float slo[MB][2], shi[MB][2];
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        uint32_t lo = (q >> (8 * e)) & 0xF, hi = (q >> (8 * e + 4)) & 0xF;
-        if (T == kQ5K) {
-          lo |= ((qh >> (8 * e + 2 * j)) & 1) << 4;
-          hi |= ((qh >> (8 * e + 2 * j + 1)) & 1) << 4;
+      for (int m = 0; m < MB; m++) slo[m][0] = slo[m][1] = shi[m][0] = shi[m][1] = 0.f;
+      const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+      const uint32_t hw[4] = {qhv.x, qhv.y, qhv.z, qhv.w};
+#pragma unroll
+      for (int f = 0; f < 4; f++) {
+        uint32_t lo = qw[f] & 0x0F0F0F0Fu, hi = (qw[f] >> 4) & 0x0F0F0F0Fu;
+        if (T == kQ5K) {   // bit 2j (low) / 2j+1 (high) of each qh byte is the 5th bit
+          lo |= ((hw[f] >> (2 * j)) & 0x01010101u) << 4;
+          hi |= ((hw[f] >> (2 * j + 1)) & 0x01010101u) << 4;
         }
-        wl[e] = fmaf(d1, small_u2f(lo), -n1);
-        wh[e] = fmaf(d2, small_u2f(hi), -n2);
+        float ql[4], qh[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          ql[e] = __int_as_float((int)__byte_perm(lo, 0x4B000000u, 0x7650u | e)) - 8388608.0f;
+          qh[e] = __int_as_float((int)__byte_perm(hi, 0x4B000000u, 0x7650u | e)) - 8388608.0f;
+        }
+#pragma unroll
+        for (int m = 0; m < MB; m++)
+          if (m < M) {
+            const float4 xl = *reinterpret_cast<const float4 *>(xs + m * K + xs_swz<T>(klo + 4 * f));
+            const float4 xh = *reinterpret_cast<const float4 *>(xs + m * K + xs_swz<T>(klo + 32 + 4 * f));
+            float &sl = slo[m][f & 1], &sh = shi[m][f & 1];
+            sl = fmaf(ql[0], xl.x, sl);
+            sl = fmaf(ql[1], xl.y, sl);
+            sl = fmaf(ql[2], xl.z, sl);
+            sl = fmaf(ql[3], xl.w, sl);
+            sh = fmaf(qh[0], xh.x, sh);
+            sh = fmaf(qh[1], xh.y, sh);
+            sh = fmaf(qh[2], xh.z, sh);
+            sh = fmaf(qh[3], xh.w, sh);
+          }
       }
-      const int64_t kb = sb * 256 + j * 64 + p;
-      fma_x4<MB>(acc, wl, xs, K, M, kb);
-      fma_x4<MB>(acc, wh, xs, K, M, kb + 32);
+      const float d1 = d * sc0, n1 = dmin * mn0, d2 = d * sc1, n2 = dmin * mn1;
+#pragma unroll
+      for (int m = 0; m < MB; m++)
+        if (m < M) {
+          const float xl = xsum[m * (K >> 4) + (klo >> 4)], xh = xsum[m * (K >> 4) + (klo >> 4) + 2];
+          acc[m] = fmaf(d1, slo[m][0] + slo[m][1], acc[m]);
+          acc[m] = fmaf(-n1, xl, acc[m]);
+          acc[m] = fmaf(d2, shi[m][0] + shi[m][1], acc[m]);
+          acc[m] = fmaf(-n2, xh, acc[m]);
+        }
     }
   } else if (T == kQ6K) {
     const int half = lane >> 4, l0 = (lane & 15) * 2, is = l0 >> 4;
-    const int64_t nsb = K >> 8;
-    for (int64_t sb = 0; sb < nsb; sb++) {
-      const uint8_t *b = row + sb * 210;
+    const int nsb = (int)(K >> 8);
+#pragma unroll 2
+    for (int sb = u0; sb < nsb; sb += ustep) {
+      const uint8_t *b = row + (int64_t)sb * 210;
       const float d = h2f(ld16(b + 208));
       const uint32_t qa = ld16(b + half * 64 + l0), qb = ld16(b + half * 64 + 32 + l0);
       const uint32_t qh = ld16(b + 128 + half * 32 + l0);
@@ -212,7 +285,7 @@ __device__ __forceinline__ void row_dot(const uint8_t *row, const float *xs, int
           const uint32_t hb = (qh >> (8 * e + 2 * qd)) & 3;
           w[e] = dq * (small_u2f(nib | (hb << 4)) - 32.0f);
         }
-        const int64_t k = sb * 256 + half * 128 + qd * 32 + l0;
+        const int64_t k = (int64_t)sb * 256 + half * 128 + qd * 32 + l0;
 #pragma unroll
         for (int m = 0; m < MB; m++)
           if (m < M) {
@@ -224,20 +297,42 @@ __device__ __forceinline__ void row_dot(const uint8_t *row, const float *xs, int
     }
   } else if (T == kQ8_0 || T == kQ4_0 || T == kQ5_0) {
     const int64_t nblk = K >> 5;
+    const int nunit = (int)((nblk + 7) >> 3);
     const int o = (lane & 3) * 8;
-    for (int64_t blk = lane >> 2; blk < nblk; blk += 8) {
+#pragma unroll 2
+    for (int u = u0; u < nunit; u += ustep) {
+      const int64_t blk = (int64_t)u * 8 + (lane >> 2);
+      if (blk >= nblk) continue;
       const uint8_t *b = row + blk * fmt_bb(T);
       const float d = h2f(ld16(b));
-      float w[8];
-      if (T == kQ8_0) {
+      if constexpr (T == kQ8_0) {
+        // d * sum(q x): int8 q as a float by one byte permute into 2^23's
+        // exponent (q + 128 after the sign flip), then the bias removed
+        float q[8];
 #pragma unroll
         for (int e = 0; e < 8; e += 2) {
           const uint32_t v = ld16(b + 2 + o + e);
-          w[e] = d * (small_u2f((v & 0xFF) ^ 0x80) - 128.0f);
-          w[e + 1] = d * (small_u2f(((v >> 8) & 0xFF) ^ 0x80) - 128.0f);
+          q[e] = __int_as_float((int)(__byte_perm(v, 0x4B000000u, 0x7650u) ^ 0x80u)) - 8388736.0f;
+          q[e + 1] = __int_as_float((int)(__byte_perm(v, 0x4B000000u, 0x7651u) ^ 0x80u)) - 8388736.0f;
         }
+        const int64_t k = blk * 32 + o;
+#pragma unroll
+        for (int m = 0; m < MB; m++)
+          if (m < M) {
+            const float4 x0 = *reinterpret_cast<const float4 *>(xs + m * K + xs_swz<T>(k));
+            const float4 x1 = *reinterpret_cast<const float4 *>(xs + m * K + xs_swz<T>(k + 4));
+            float sa = q[0] * x0.x, sb = q[4] * x1.x;
+            sa = fmaf(q[1], x0.y, sa);
+            sb = fmaf(q[5], x1.y, sb);
+            sa = fmaf(q[2], x0.z, sa);
+            sb = fmaf(q[6], x1.z, sb);
+            sa = fmaf(q[3], x0.w, sa);
+            sb = fmaf(q[7], x1.w, sb);
+            acc[m] = fmaf(d, sa + sb, acc[m]);
+          }
       } else {
         // byte 2 + j/2, nibble j&1 (the reference's reading of these blocks)
+        float w[8];
 #pragma unroll
         for (int e = 0; e < 8; e += 4) {
           const uint32_t v = ld16(b + 2 + (o >> 1) + (e >> 1));
@@ -247,26 +342,34 @@ __device__ __forceinline__ void row_dot(const uint8_t *row, const float *xs, int
             w[e + t] = (small_u2f(q) - (T == kQ4_0 ? 8.0f : 0.0f)) * d;
           }
         }
+        const int64_t k = blk * 32 + o;
+        const float w0[4] = {w[0], w[1], w[2], w[3]}, w1[4] = {w[4], w[5], w[6], w[7]};
+        fma_x4<MB>(acc, w0, xs, K, M, k);
+        fma_x4<MB>(acc, w1, xs, K, M, k + 4);
       }
-      const int64_t k = blk * 32 + o;
-      const float w0[4] = {w[0], w[1], w[2], w[3]}, w1[4] = {w[4], w[5], w[6], w[7]};
-      fma_x4<MB>(acc, w0, xs, K, M, k);
-      fma_x4<MB>(acc, w1, xs, K, M, k + 4);
     }
   } else {   // F32 / F16: element k of the row at byte k * (4 | 2)
-    for (int64_t k = lane; k < K; k += 32) {
-      const float w = T == kF32 ? __int_as_float((int)ld32(row + 4 * k)) : h2f(ld16(row + 2 * k));
-      fma_x<MB>(acc, w, xs, K, M, k);
+    const int nunit = (int)((K + 255) >> 8);
+    for (int u = u0; u < nunit; u += ustep) {
+#pragma unroll
+      for (int t = 0; t < 8; t++) {
+        const int64_t k = (int64_t)u * 256 + t * 32 + lane;
+        if (k < K) {
+          const float w = T == kF32 ? __int_as_float((int)ld32(row + 4 * k)) : h2f(ld16(row + 2 * k));
+          fma_x<MB>(acc, w, xs, K, M, k);
+        }
+      }
     }
   }
 }
 
 template <int T, int MB>
-__global__ void __launch_bounds__(kQmvThreads) quant_matvec_kernel(QmvArgs a) {
+__global__ void __launch_bounds__(kQmvThreads, 3) quant_matvec_kernel(QmvArgs a) {
   pdl_trigger();
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + 64);
+  float *part = reinterpret_cast<float *>(smem + 128);   // [8 warps][MB]: split rows' partials
   uint8_t *bufs = smem + kQmvHeader;
   float *xs = reinterpret_cast<float *>(bufs + kQmvStages * kQmvBuf);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -302,8 +405,22 @@ __global__ void __launch_bounds__(kQmvThreads) quant_matvec_kernel(QmvArgs a) {
 
   if (tid == 0)
     for (int64_t i = 0; i < my_chunks && i < kQmvStages; i++) issue(i);
-  // the input vectors, for the whole kernel
-  for (int64_t i = tid; i < (int64_t)a.M * a.K; i += kQmvThreads) xs[i] = a.X[i];
+  // the input vectors, for the whole kernel (and, for the K-quants, their
+  // sums over each 16 elements, in element order)
+  for (int64_t i = tid; i < (int64_t)a.M * a.K; i += kQmvThreads) {
+    const int64_t m = i / a.K, k = i - m * a.K;
+    xs[m * a.K + xs_swz<T>(k)] = a.X[i];
+  }
+  if (uses_xsum<T>()) {
+    float *xsum = xs + (int64_t)a.M * a.K;
+    for (int64_t g = tid; g < (int64_t)a.M * (a.K >> 4); g += kQmvThreads) {
+      const float *src = a.X + g * 16;
+      float v = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; i++) v += src[i];
+      xsum[g] = v;
+    }
+  }
   __syncthreads();
 
   for (int64_t i = 0; i < my_chunks; i++) {
@@ -332,18 +449,35 @@ __global__ void __launch_bounds__(kQmvThreads) quant_matvec_kernel(QmvArgs a) {
       __syncthreads();
     }
     const uint8_t *rows = buf + (s0 - a0);
-    for (int64_t lr = warp; lr < r1 - r0; lr += kQmvWarps) {
+    // rows of the chunk over the warps; a chunk of fewer than 8 rows gives
+    // each row wpr warps, which take its units in turn and leave partial sums
+    // that are added in warp order below (deterministic)
+    const int rc = (int)(r1 - r0);
+    int wpr = 1;
+    while (wpr * 2 * rc <= kQmvWarps) wpr *= 2;
+    const int groups = kQmvWarps / wpr, gi = warp / wpr, wi = warp - gi * wpr;
+    for (int lr = gi; lr < rc; lr += groups) {
       float acc[MB];
 #pragma unroll
       for (int m = 0; m < MB; m++) acc[m] = 0.f;
-      row_dot<T, MB>(rows + lr * a.row_bytes, xs, a.K, a.M, lane, acc);
+      row_dot<T, MB>(rows + (int64_t)lr * a.row_bytes, xs, a.K, a.M, lane, acc, wi, wpr);
 #pragma unroll
       for (int m = 0; m < MB; m++) {
         const float v = warp_sum(acc[m]);
-        if (lane == 0 && m < a.M) a.Y[m * a.N + r0 + lr] = v;
+        if (lane == 0 && m < a.M) {
+          if (wpr == 1) a.Y[m * a.N + r0 + lr] = v;
+          else part[(lr * wpr + wi) * MB + m] = v;
+        }
       }
     }
     __syncthreads();   // every warp is done with this stage before it is refilled
+    if (wpr > 1)
+      for (int t = tid; t < rc * a.M; t += kQmvThreads) {
+        const int r = t / a.M, m = t - r * a.M;
+        float v = 0.f;
+        for (int w = 0; w < wpr; w++) v += part[(r * wpr + w) * MB + m];
+        a.Y[m * a.N + r0 + r] = v;
+      }
     if (tid == 0 && i + kQmvStages < my_chunks) issue(i + kQmvStages);
   }
 }
@@ -430,11 +564,15 @@ int fcu_quant_matvec(fcu_ctx *ctx, int type, const void *W, int64_t N, int64_t K
   // vectors per launch: as many as fit beside the stages (<= 8)
   const int64_t x_budget = 227 * 1024 - kQmvHeader - kQmvStages * kQmvBuf;
   int MB = 8;
-  while (MB > 1 && (int64_t)MB * K * 4 > x_budget) MB >>= 1;
+  while (MB > 1 && (int64_t)MB * (K + K / 16) * 4 > x_budget) MB >>= 1;
+  // rows per chunk: whole warps' worth (a multiple of 8) where rows are
+  // narrow, fewer (each split over several warps) where they are wide or the
+  // tensor is small, so that every SM gets chunks
   const int64_t rows_max = kQmvChunk / rb;
   int64_t R = (N + 4 * ctx->num_sms - 1) / (4 * ctx->num_sms);
   if (R < 1) R = 1;
   if (R > rows_max) R = rows_max;
+  if (R > kQmvWarps) R -= R % kQmvWarps;
   QmvArgs a{};
   a.W = (const uint8_t *)W;
   a.N = N;
@@ -451,8 +589,8 @@ int fcu_quant_matvec(fcu_ctx *ctx, int type, const void *W, int64_t N, int64_t K
     a.X = X + m0 * K;
     a.Y = Y + m0 * N;
     a.M = mg;
-    const size_t smem = kQmvHeader + kQmvStages * kQmvBuf + (size_t)mb * K * 4;
-    const int per_sm = smem <= 113 * 1024 ? 2 : 1;
+    const size_t smem = kQmvHeader + kQmvStages * kQmvBuf + (size_t)mb * K * 4 + (size_t)mb * (K / 16) * 4;
+    const int per_sm = smem <= 75 * 1024 ? 3 : smem <= 113 * 1024 ? 2 : 1;
     int64_t grid = a.n_chunks < (int64_t)per_sm * ctx->num_sms ? a.n_chunks : (int64_t)per_sm * ctx->num_sms;
     rc = launch_matvec(ctx, type, a, mb, (int)grid, smem);
     if (rc) return rc;
