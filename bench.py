@@ -36,10 +36,39 @@ sys.path.insert(0, os.path.join(ROOT, "forge-llm_b200"))
 C5 = dict(vocabSize=32000, dim=768, nLayers=12, nHeads=12, nKvHeads=4, hidden=2048,
           normEps=1e-5, ropeTheta=10000)
 GLOBAL_BATCH, SEQ, LR, SEED = 64, 1024, 3e-4, 5
-# DRAM bytes per tcgen05 GEMM launch of the batch-64 step: dram__bytes_read.sum
-# + dram__bytes_write.sum from one single-pass ncu capture of the 147 GEMM
-# launches of one step (66.31 GB read + 27.78 GB written), averaged per launch.
-GEMM_DRAM_BYTES_PER_LAUNCH_B64 = 640.07e6
+# DRAM bytes (read, written) of one launch of each distinct GEMM of the
+# config-5 step, from single-launch ncu captures (`bench.py --micro gemm` at
+# that shape, dram__bytes_read.sum / dram__bytes_write.sum, one pass; the
+# commands are in profiles/gemm_dram_c5_shapes.md).  The twelve per-layer
+# shapes run 12 times a step at 65,536 tokens; the three LM-head shapes were
+# captured at 16,384 tokens (a 2 GB case instead of 8 GB) and count 4 times.
+GEMM_DRAM_BY_SHAPE = {
+    "qkv_fwd": (102702336, 119859968),
+    "wo_fwd": (101916672, 143022080),
+    "gateup_fwd": (110621952, 480962304),
+    "down_fwd": (272200192, 161538048),
+    "down_dx": (103938560, 214766336),
+    "down_dw": (608569088, 42380800),
+    "gateup_dx": (693938944, 177318400),
+    "gateup_dw": (1263725312, 42735616),
+    "wo_dx": (101913600, 59498240),
+    "wo_dw": (335384832, 23501824),
+    "qkv_dx": (169878528, 154056704),
+    "qkv_dw": (485890560, 22544896),
+    "logits_fwd": (418706432, 2039416576),
+    "lm_dx": (1302358784, 41938176),
+    "lm_dw": (1562301952, 86944768),
+}
+GEMM_LAUNCHES_B64 = 12 * 12 + 3
+
+
+def gemm_dram_bytes_per_launch_b64() -> float:
+    """Mean DRAM bytes per GEMM launch of the batch-64 step (the roofline's
+    `traffic`), from the per-shape captures above."""
+    total = 0
+    for k, (r, w) in GEMM_DRAM_BY_SHAPE.items():
+        total += (4 if k in ("logits_fwd", "lm_dx", "lm_dw") else 12) * (r + w)
+    return total / GEMM_LAUNCHES_B64
 
 
 def gemm_algorithmic_bytes(tokens: int):
@@ -224,7 +253,7 @@ def run_micro_gemm(args):
     import ctypes
     import forgellm as F
     from forgellm import autograd as AD
-    from forgellm._lib import GemmOut, OUT_F32, call
+    from forgellm._lib import GemmOut, OUT_BF16, OUT_F32, call
     F.set_precision("bf16")
     M, N, K = (int(x) for x in args.shape.split(","))
     op = {"fwd": 0, "dx": 1, "dw": 2}[args.op]
@@ -233,8 +262,9 @@ def run_micro_gemm(args):
     nb = N * K if op == 0 else K * N
     A = torch.randn(na, device="cuda", generator=g).to(torch.bfloat16)
     Bm = torch.randn(nb, device="cuda", generator=g).to(torch.bfloat16)
-    C = torch.empty(M * N, device="cuda")
-    o = GemmOut(OUT_F32, C.data_ptr(), 0, None, 0, 0, 0, 0.0)
+    bf16_out = args.out == "bf16"
+    C = torch.empty(M * N, device="cuda", dtype=torch.bfloat16 if bf16_out else torch.float32)
+    o = GemmOut(OUT_BF16 if bf16_out else OUT_F32, C.data_ptr(), 0, None, 0, 0, 0, 0.0)
     h = AD.ctx().handle
 
     def run():
@@ -252,7 +282,7 @@ def run_micro_gemm(args):
     ms = e0.elapsed_time(e1) / args.steps
     tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
     pk, kind = peaks()
-    print(json.dumps({"micro": "gemm_bf16_tc", "op": args.op, "M": M, "N": N, "K": K,
+    print(json.dumps({"micro": "gemm_bf16_tc", "op": args.op, "M": M, "N": N, "K": K, "out": args.out,
                       "ms": ms, "tflops": tf, "frac_of_burst_peak": tf / pk["bf16_tflops"],
                       "peak_kind": kind}), flush=True)
 
@@ -506,6 +536,7 @@ def main():
                     help="time one of the operator configs instead of the C5 train step")
     ap.add_argument("--shape", default="8192,2048,768")
     ap.add_argument("--op", default="fwd", choices=["fwd", "dx", "dw"])
+    ap.add_argument("--out", default="f32", choices=["f32", "bf16"], help="--micro gemm output type")
     args = ap.parse_args()
     if args.config == "decode":
         return run_decode(args)
@@ -657,7 +688,7 @@ def main():
         achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
         gb, gl = gemm_algorithmic_bytes(args.batch * SEQ)
         alg_bytes = gb / gl if args.precision == "bf16" else None
-        traffic = (GEMM_DRAM_BYTES_PER_LAUNCH_B64
+        traffic = (gemm_dram_bytes_per_launch_b64()
                    if args.precision == "bf16" and args.batch == GLOBAL_BATCH and world == 1 else None)
         peak = pk["bf16_tflops_sustained"]
         line = {
@@ -681,7 +712,7 @@ def main():
                          "frac": achieved / peak if peak else None,
                          "peak_kind": f"bf16 dense sustained ({pk_kind})",
                          "traffic": traffic,
-                         "traffic_unit": "DRAM bytes per GEMM launch (ncu, mean over one step's launches)",
+                         "traffic_unit": "DRAM bytes per GEMM launch (ncu single-launch captures per shape, mean over the step's launches)",
                          "algorithmic_bytes_per_launch": alg_bytes,
                          "gemm_share_of_step": (gemm_ms / gemm_steps) / (ms / args.steps) if ms else None,
                          "measured": gemm_where,

@@ -1097,4 +1097,150 @@ int attn_bwd_tmem(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv,
   return FCU_OK;
 }
 
+// ------------------------------------------------------------------ operator entries
+// causalAttn / causalAttnBatch on fp32 operands (fcu_attn_fwd / fcu_attn_bwd
+// in FCU_PREC_BF16 mode, head dim 64) on the same tcgen05 kernels: the fp32
+// Q / K / V (and dO, O) are packed into the bf16 qkv layout the kernels read,
+// and the bf16 outputs are widened back to fp32 (adding into the gradients
+// when accumulating, the JS `grad +=`).  The packed copies live in a buffer
+// of their own (grown on demand, one per device), so the kernels' scratch
+// (delta, head-split partials) is untouched.
+namespace {
+
+int op_buffer(fcu_ctx *ctx, size_t bytes, void **out) {
+  struct Buf {
+    void *p = nullptr;
+    size_t n = 0;
+  };
+  static thread_local Buf bufs[64];
+  Buf &b = bufs[ctx->device & 63];
+  if (bytes > b.n) {
+    if (b.p) {
+      FCU_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
+      FCU_CHECK_CUDA(cudaFree(b.p));
+      b.p = nullptr;
+      b.n = 0;
+    }
+    FCU_CHECK_CUDA(cudaMalloc(&b.p, bytes));
+    b.n = bytes;
+  }
+  *out = b.p;
+  return FCU_OK;
+}
+
+// dst[r, col0 + c] = bf16(src[r, c]) for c < cols (4 at a time; cols % 4 == 0)
+__global__ void pack_bf16_kernel(const float *__restrict__ src, int64_t rows, int cols, __nv_bfloat16 *dst,
+                                 int64_t ld, int col0) {
+  const int c4 = cols / 4;
+  const int64_t n = rows * c4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / c4;
+    const int c = (int)(i - r * c4) * 4;
+    const float4 v = *reinterpret_cast<const float4 *>(src + r * cols + c);
+    __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t *>(&a);
+    u.y = *reinterpret_cast<uint32_t *>(&b);
+    *reinterpret_cast<uint2 *>(dst + r * ld + col0 + c) = u;
+  }
+}
+
+// dst[r, c] (+)= float(src[r, col0 + c])
+__global__ void unpack_bf16_kernel(const __nv_bfloat16 *__restrict__ src, int64_t ld, int col0, int64_t rows,
+                                   int cols, float *dst, int accumulate) {
+  const int c4 = cols / 4;
+  const int64_t n = rows * c4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / c4;
+    const int c = (int)(i - r * c4) * 4;
+    const uint2 u = *reinterpret_cast<const uint2 *>(src + r * ld + col0 + c);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.y));
+    float4 v = make_float4(a.x, a.y, b.x, b.y);
+    float4 *d = reinterpret_cast<float4 *>(dst + r * cols + c);
+    if (accumulate) {
+      const float4 o = *d;
+      v.x += o.x;
+      v.y += o.y;
+      v.z += o.z;
+      v.w += o.w;
+    }
+    *d = v;
+  }
+}
+
+int pack(fcu_ctx *ctx, const float *src, int64_t rows, int cols, __nv_bfloat16 *dst, int64_t ld, int col0) {
+  const int64_t n = rows * (cols / 4);
+  const int blocks = (int)((n + 255) / 256 < 16 * ctx->num_sms ? (n + 255) / 256 : 16 * ctx->num_sms);
+  pack_bf16_kernel<<<blocks, 256, 0, ctx->stream>>>(src, rows, cols, dst, ld, col0);
+  FCU_CHECK_LAUNCH();
+  return FCU_OK;
+}
+
+int unpack(fcu_ctx *ctx, const __nv_bfloat16 *src, int64_t ld, int col0, int64_t rows, int cols, float *dst,
+           int accumulate) {
+  const int64_t n = rows * (cols / 4);
+  const int blocks = (int)((n + 255) / 256 < 16 * ctx->num_sms ? (n + 255) / 256 : 16 * ctx->num_sms);
+  unpack_bf16_kernel<<<blocks, 256, 0, ctx->stream>>>(src, ld, col0, rows, cols, dst, accumulate);
+  FCU_CHECK_LAUNCH();
+  return FCU_OK;
+}
+
+bool op_aligned(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
+}  // namespace
+
+bool attn_tmem_op_supported(int dH, const void *a, const void *b, const void *c, const void *d) {
+  return dH == kD && op_aligned(a) && op_aligned(b) && op_aligned(c) && op_aligned(d);
+}
+
+int attn_fwd_op_tmem(fcu_ctx *ctx, const float *Q, const float *K, const float *V, int B, int T, int nH,
+                     int nKV, float *O, float *lse) {
+  const int64_t rows = (int64_t)B * T, W = (int64_t)(nH + 2 * nKV) * kD, qD = (int64_t)nH * kD,
+                kvD = (int64_t)nKV * kD;
+  void *buf = nullptr;
+  int rc = op_buffer(ctx, (size_t)rows * (W + qD) * sizeof(__nv_bfloat16), &buf);
+  if (rc) return rc;
+  __nv_bfloat16 *qkv = (__nv_bfloat16 *)buf, *Ob = qkv + rows * W;
+  if ((rc = pack(ctx, Q, rows, (int)qD, qkv, W, 0)) || (rc = pack(ctx, K, rows, (int)kvD, qkv, W, (int)qD)) ||
+      (rc = pack(ctx, V, rows, (int)kvD, qkv, W, (int)(qD + kvD))))
+    return rc;
+  rc = attn_fwd_tmem(ctx, qkv, W, B, T, nH, nKV, Ob, lse);
+  if (rc) return rc;
+  return unpack(ctx, Ob, qD, 0, rows, (int)qD, O, 0);
+}
+
+int attn_bwd_op_tmem(fcu_ctx *ctx, const float *dO, const float *Q, const float *K, const float *V,
+                     const float *O, const float *lse, int B, int T, int nH, int nKV, float *dQ, float *dK,
+                     float *dV, int accumulate) {
+  const int64_t rows = (int64_t)B * T, W = (int64_t)(nH + 2 * nKV) * kD, qD = (int64_t)nH * kD,
+                kvD = (int64_t)nKV * kD;
+  void *buf = nullptr;
+  // qkv and dqkv [rows, W], dO and O [rows, qD], all bf16
+  int rc = op_buffer(ctx, (size_t)rows * (2 * W + 2 * qD) * sizeof(__nv_bfloat16), &buf);
+  if (rc) return rc;
+  __nv_bfloat16 *qkv = (__nv_bfloat16 *)buf, *dqkv = qkv + rows * W, *dOb = dqkv + rows * W,
+                *Ob = dOb + rows * qD;
+  if ((rc = pack(ctx, Q, rows, (int)qD, qkv, W, 0)) || (rc = pack(ctx, K, rows, (int)kvD, qkv, W, (int)qD)) ||
+      (rc = pack(ctx, V, rows, (int)kvD, qkv, W, (int)(qD + kvD))) ||
+      (rc = pack(ctx, dO, rows, (int)qD, dOb, qD, 0)) || (rc = pack(ctx, O, rows, (int)qD, Ob, qD, 0)))
+    return rc;
+  // the kernels' own scratch: delta, and the head-split partials on small grids
+  const int64_t ctas = (int64_t)div_up(T, kBM) * nKV * B;
+  const int split = (nH > nKV && ctas < 4 * (int64_t)ctx->num_sms) ? 1 : 0;
+  const size_t delta_bytes = (sizeof(float) * (size_t)B * nH * T + 255) & ~(size_t)255;
+  const size_t part_bytes = split ? sizeof(float) * (size_t)(nH / nKV) * B * T * kvD : 0;
+  void *scr = nullptr;
+  rc = ctx_scratch(ctx, delta_bytes + 2 * part_bytes, &scr);
+  if (rc) return rc;
+  float *pk = split ? (float *)((uint8_t *)scr + delta_bytes) : nullptr;
+  float *pv = split ? (float *)((uint8_t *)scr + delta_bytes + part_bytes) : nullptr;
+  rc = attn_bwd_tmem(ctx, dOb, qkv, W, Ob, lse, (float *)scr, B, T, nH, nKV, nullptr, dqkv, split, pk, pv);
+  if (rc) return rc;
+  if ((rc = unpack(ctx, dqkv, W, 0, rows, (int)qD, dQ, accumulate)) ||
+      (rc = unpack(ctx, dqkv, W, (int)qD, rows, (int)kvD, dK, accumulate)))
+    return rc;
+  return unpack(ctx, dqkv, W, (int)(qD + kvD), rows, (int)kvD, dV, accumulate);
+}
+
 }  // namespace fcu

@@ -45,6 +45,16 @@ int attn_bwd_tc(cudaStream_t st, const float *dO, const float *Q, const float *K
                 const float *lse, const float *delta, int B, int T, int nH, int nKV, int dH,
                 float *dQ, float *dK, float *dV, int acc);
 
+// The operator entries (fcu_attn_fwd / _bwd, bf16 mode) on the tcgen05
+// kernels: fp32 operands packed to bf16 (attn_tmem.cu); head dim 64 and
+// 16-byte aligned operands.
+bool attn_tmem_op_supported(int dH, const void *a, const void *b, const void *c, const void *d);
+int attn_fwd_op_tmem(fcu_ctx *ctx, const float *Q, const float *K, const float *V, int B, int T, int nH,
+                     int nKV, float *O, float *lse);
+int attn_bwd_op_tmem(fcu_ctx *ctx, const float *dO, const float *Q, const float *K, const float *V,
+                     const float *O, const float *lse, int B, int T, int nH, int nKV, float *dQ, float *dK,
+                     float *dV, int accumulate);
+
 // tcgen05 attention (attn_tmem.cu): head dim 64, bf16 qkv buffer.
 bool attn_tmem_supported(int dH);
 int attn_fwd_tmem(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, int nH, int nKV,

@@ -106,7 +106,7 @@ int fcu_ctx_set_stream(fcu_ctx *ctx, void *stream) {
 
 int fcu_ctx_set_precision(fcu_ctx *ctx, int precision) {
   FCU_CTX(ctx);
-  FCU_REQUIRE(precision == FCU_PREC_FP32 || precision == FCU_PREC_BF16,
+  FCU_REQUIRE(precision == FCU_PREC_FP32 || precision == FCU_PREC_FP32_TC || precision == FCU_PREC_BF16,
               "fcu_ctx_set_precision: unknown mode %d", precision);
   ctx->precision = precision;
   return FCU_OK;

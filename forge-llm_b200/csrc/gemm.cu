@@ -148,6 +148,7 @@ int gemm_simt(cudaStream_t st, GemmOp op, const float *A, const float *B, float 
 int gemm_dispatch(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float *C, int64_t M,
                   int64_t N, int64_t K, int beta) {
   if (ctx->precision == FCU_PREC_FP32) return gemm_simt(ctx->stream, op, A, B, C, M, N, K, beta);
+  if (ctx->precision == FCU_PREC_FP32_TC) return gemm_split6(ctx, op, A, B, C, M, N, K, beta);
   return gemm_tc(ctx, op, A, B, C, M, N, K, beta);
 }
 

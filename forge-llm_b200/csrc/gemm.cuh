@@ -17,6 +17,10 @@ int gemm_tc(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float *C, i
             int64_t N, int64_t K, int beta);
 int gemm_dispatch(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float *C, int64_t M,
                   int64_t N, int64_t K, int beta);
+// FCU_PREC_FP32_TC: fp32 operands on the tensor cores (three-way bf16 split,
+// six products; gemm_tc.cu).
+int gemm_split6(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float *C, int64_t M, int64_t N,
+                int64_t K, int beta);
 
 }  // namespace fcu
 

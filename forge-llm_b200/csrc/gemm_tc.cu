@@ -988,6 +988,109 @@ int gemm_tc(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float *C, i
   return rc;
 }
 
+// ---------------------------------------------------------------- fp32 on the tensor cores
+// FCU_PREC_FP32_TC: every fp32 operand x is split into three bf16 parts,
+// x0 = bf16(x), x1 = bf16(x - x0), x2 = bf16(x - x0 - x1) (each difference is
+// exact in fp32), and the product is the sum of the six part products
+// a_i b_j with i + j <= 2, laid out as one bf16 contraction six times as
+// long: A' = [a0 a0 a0 a1 a1 a2], B' = [b0 b1 b2 b0 b1 b0] along K.  The
+// dropped terms are about 2^-24 of |a b|, so the result carries fp32-level
+// error (the products are exact and accumulate in fp32, as the tcgen05 GEMM
+// does for bf16).  Every matmulT contraction runs as the forward form
+// C[M,N] = A'[M,6K'] . B'[N,6K']^T: the split kernel reads its operand
+// transposed where the op needs it and pads K to a multiple of 8 with zeros,
+// so any shape runs on the tensor cores.  Long contractions are processed in
+// chunks (C accumulates) to bound the bf16 copies.
+namespace {
+
+constexpr int kSplitTile = 32;
+constexpr uint32_t kPatA = 0u | 0u << 2 | 0u << 4 | 1u << 6 | 1u << 8 | 2u << 10;   // a0 a0 a0 a1 a1 a2
+constexpr uint32_t kPatB = 0u | 1u << 2 | 2u << 4 | 0u << 6 | 1u << 8 | 0u << 10;   // b0 b1 b2 b0 b1 b0
+
+// S[r, c] = src[r * rs + c * cs], r < R, c < L.  dst [R, 6 * Lp] bf16 with
+// dst[r, j * Lp + c] = part pat_j of S[r, c] (zero for L <= c < Lp).
+__global__ void __launch_bounds__(256) split6_kernel(const float *__restrict__ src, int64_t R, int64_t L,
+                                                     int64_t rs, int64_t cs, int64_t Lp, uint32_t pat,
+                                                     __nv_bfloat16 *__restrict__ dst) {
+  fcu::pdl_trigger();
+  __shared__ float tile[kSplitTile][kSplitTile + 1];
+  const int tx = threadIdx.x, ty = threadIdx.y;   // 32 x 8
+  const int64_t r0 = (int64_t)blockIdx.y * kSplitTile, c0 = (int64_t)blockIdx.x * kSplitTile;
+  if (cs == 1) {   // rows contiguous: read along c
+    for (int i = ty; i < kSplitTile; i += 8) {
+      const int64_t r = r0 + i, c = c0 + tx;
+      tile[i][tx] = (r < R && c < L) ? src[r * rs + c] : 0.f;
+    }
+  } else {         // transposed read: consecutive threads walk r
+    for (int i = ty; i < kSplitTile; i += 8) {
+      const int64_t r = r0 + tx, c = c0 + i;
+      tile[tx][i] = (r < R && c < L) ? src[r * rs + c * cs] : 0.f;
+    }
+  }
+  __syncthreads();
+  for (int i = ty; i < kSplitTile; i += 8) {
+    const int64_t r = r0 + i, c = c0 + tx;
+    if (r >= R || c >= Lp) continue;
+    const float x = tile[i][tx];
+    const __nv_bfloat16 p0 = __float2bfloat16_rn(x);
+    const float e1 = x - __bfloat162float(p0);
+    const __nv_bfloat16 p1 = __float2bfloat16_rn(e1);
+    const __nv_bfloat16 p2 = __float2bfloat16_rn(e1 - __bfloat162float(p1));
+    const __nv_bfloat16 parts[3] = {p0, p1, p2};
+    __nv_bfloat16 *row = dst + r * 6 * Lp + c;
+#pragma unroll
+    for (int j = 0; j < 6; j++) row[j * Lp] = parts[(pat >> (2 * j)) & 3];
+  }
+}
+
+int split6(fcu_ctx *ctx, const float *src, int64_t R, int64_t L, int64_t rs, int64_t cs, int64_t Lp, uint32_t pat,
+           __nv_bfloat16 *dst) {
+  dim3 grid((unsigned)((Lp + kSplitTile - 1) / kSplitTile), (unsigned)((R + kSplitTile - 1) / kSplitTile));
+  FCU_REQUIRE(grid.y <= 65535, "fp32 tensor-core split: %lld rows", (long long)R);
+  split6_kernel<<<grid, dim3(32, 8), 0, ctx->stream>>>(src, R, L, rs, cs, Lp, pat, dst);
+  FCU_CHECK_LAUNCH();
+  return FCU_OK;
+}
+
+}  // namespace
+
+int gemm_split6(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float *C, int64_t M, int64_t N,
+                int64_t K, int beta) {
+  // Strides of the two operands as S_a[m, k] and S_b[n, k] (contraction k).
+  int64_t ars, acs, brs, bcs;
+  switch (op) {
+    case GemmOp::kFwd: ars = K, acs = 1, brs = K, bcs = 1; break;   // A[M,K], B[N,K]
+    case GemmOp::kDx: ars = K, acs = 1, brs = 1, bcs = N; break;    // A[M,K], B[K,N]
+    default: ars = 1, acs = M, brs = 1, bcs = N; break;             // A[K,M], B[K,N]
+  }
+  // contraction chunk: the two bf16 copies (12 bytes per element of each
+  // operand's chunk) within about 1 GiB
+  const int64_t budget = (int64_t)1 << 30;
+  int64_t chunk = budget / (12 * (M + N));
+  chunk -= chunk % 64;
+  if (chunk < 64) chunk = 64;
+  if (chunk > K) chunk = K;
+  const int64_t Lp_max = (chunk + 7) / 8 * 8;
+  const size_t bytes_a = round_up((size_t)M * 6 * Lp_max * 2, 1024);
+  void *ws = nullptr;
+  int *err = nullptr;
+  int rc = workspace(ctx, bytes_a + round_up((size_t)N * 6 * Lp_max * 2, 1024), &ws, &err);
+  if (rc) return rc;
+  __nv_bfloat16 *Ab = (__nv_bfloat16 *)ws, *Bb = (__nv_bfloat16 *)((uint8_t *)ws + bytes_a);
+  for (int64_t k0 = 0; k0 < K; k0 += chunk) {
+    const int64_t L = K - k0 < chunk ? K - k0 : chunk, Lp = (L + 7) / 8 * 8;
+    rc = split6(ctx, A + k0 * acs, M, L, ars, acs, Lp, kPatA, Ab);
+    if (!rc) rc = split6(ctx, B + k0 * bcs, N, L, brs, bcs, Lp, kPatB, Bb);
+    if (rc) return rc;
+    TcOut o;
+    o.C = C;
+    o.beta = (beta || k0 > 0) ? 1 : 0;
+    rc = gemm_bf16_tc(ctx, GemmOp::kFwd, Ab, Bb, M, N, 6 * Lp, o, err);
+    if (rc) return rc;
+  }
+  return FCU_OK;
+}
+
 // (cos, sin) table [T][head_dim/2] in fp32 for the RoPE epilogue, rounded
 // once from the double angles of ropeRows (src/L2/tensor.js:141-143).
 __global__ void rope_table_f32_kernel(float2 *tab, int T, int half, int head_dim, double theta) {

@@ -13,10 +13,10 @@ import threading
 _PKG_ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB_PATH = os.environ.get("FORGECU_LIB", os.path.join(_PKG_ROOT, "libforgecu.so"))
 
-FCU_PREC_FP32, FCU_PREC_BF16 = 0, 2
+FCU_PREC_FP32, FCU_PREC_FP32_TC, FCU_PREC_BF16 = 0, 1, 2
 FCU_ERR_ARG, FCU_ERR_CUDA, FCU_ERR_NCCL, FCU_ERR_TIMEOUT, FCU_ERR_UNSUPPORTED = -1, -2, -3, -4, -5
 FCU_COMM_ID_BYTES = 128
-PRECISIONS = {"fp32": FCU_PREC_FP32, "bf16": FCU_PREC_BF16}
+PRECISIONS = {"fp32": FCU_PREC_FP32, "fp32tc": FCU_PREC_FP32_TC, "bf16": FCU_PREC_BF16}
 
 
 class ForgeCUError(RuntimeError):

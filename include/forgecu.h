@@ -44,12 +44,18 @@ typedef enum {
 } fcu_status;
 
 /* Arithmetic used by the contractions (matmulT, attention).
- *   FP32   : fp32 operands and accumulation on the CUDA cores.  Parity mode:
- *            relL2 <= 1e-5 against the JS operators.
- *   BF16   : tensor cores (tcgen05 kind::f16) on bf16-rounded operands, fp32
- *            accumulate.  Looser bound, relL2 <= 1e-2 (stated per test).
- * (Value 1 is reserved; fcu_ctx_set_precision rejects it.) */
-typedef enum { FCU_PREC_FP32 = 0, FCU_PREC_BF16 = 2 } fcu_precision;
+ *   FP32    : fp32 operands and accumulation on the CUDA cores.  Parity mode:
+ *             relL2 <= 1e-5 against the JS operators.
+ *   FP32_TC : the matmulT contractions (matmulT fwd / dX / dW, linear) on the
+ *             tensor cores at fp32-level accuracy: each fp32 operand is split
+ *             into three bf16 parts, x = x0 + x1 + x2, and the six part
+ *             products a_i b_j with i + j <= 2 run as one tcgen05 contraction
+ *             six times as long (the dropped terms are ~2^-24 of |a b|).  Any
+ *             shape (K padded with zeros).  Same parity bound as FP32;
+ *             attention and the other operators as in FP32.
+ *   BF16    : tensor cores (tcgen05 kind::f16) on bf16-rounded operands, fp32
+ *             accumulate.  Looser bound, relL2 <= 1e-2 (stated per test). */
+typedef enum { FCU_PREC_FP32 = 0, FCU_PREC_FP32_TC = 1, FCU_PREC_BF16 = 2 } fcu_precision;
 
 typedef struct fcu_ctx fcu_ctx;
 

@@ -24,8 +24,12 @@ def test_config5_algorithmic_work():
     gb, launches = b.gemm_algorithmic_bytes(64 * 1024)
     assert launches == 147
     assert gb == 75_962_515_456
-    # the per-launch traffic ncu measured is above the algorithmic bytes (re-reads, split-K partials)
-    assert b.GEMM_DRAM_BYTES_PER_LAUNCH_B64 > gb / launches
+    # the per-launch traffic of the per-shape ncu captures is above the
+    # algorithmic bytes (operand re-reads and split-K partials of the weight
+    # gradients) and covers every distinct GEMM of the step
+    assert b.GEMM_LAUNCHES_B64 == launches
+    assert len(b.GEMM_DRAM_BY_SHAPE) == 15
+    assert b.gemm_dram_bytes_per_launch_b64() > gb / launches
 
 
 def test_reference_arm_prints_one_contract_line():

@@ -1,4 +1,6 @@
-"""GPU-path invariants and full training steps against the oracle.
+"""GPU-path invariants and full training steps against the oracle, in the
+fp32 mode (CUDA cores) and the fp32 tensor-core mode (every matmulT / linear
+contraction on tcgen05 through the three-way bf16 split).
 
 * verify.js I-30, I-33a, I-33b, I-33c, I-33d, I-34, I-35, I-36 with every
   forward and backward on the GPU, at the reference's thresholds.
@@ -17,11 +19,15 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-5
 
 
-@pytest.fixture(scope="module", autouse=True)
-def fp32_mode():
+@pytest.fixture(scope="module", autouse=True, params=["fp32", "fp32tc"])
+def fp32_mode(request):
+    """Every test of this module runs in both fp32-parity modes: the CUDA
+    cores, and the tensor cores (matmulT as a three-way bf16 split with six
+    products), at the same thresholds."""
     import forgellm as F
+    F.set_precision(request.param)
+    yield request.param
     F.set_precision("fp32")
-    yield
 
 
 def F():

@@ -395,3 +395,31 @@ def test_attn_bwd_bf16_entry(B, T, nH, nKV, theta):
     for name, sl in (("dq", slice(0, qD)), ("dk", slice(qD, qD + kD)), ("dv", slice(qD + kD, width))):
         err = relf(ref[:, sl].cpu().numpy(), got[:, sl].cpu().numpy())
         assert err <= 2e-2, (name, err)
+
+
+def test_tc_attention_operator_accumulates_on_tcgen05():
+    """causalAttnBatch in bf16 mode at head dim 64 runs the tcgen05 kernels on
+    packed bf16 copies of its fp32 operands; its backward follows the JS
+    `grad +=`: a second backward without zeroing doubles every gradient
+    exactly (the packed gradient is deterministic)."""
+    from forgellm import _lib
+    from forgellm.autograd import ctx
+    B, T, nH, nKV, dH = 2, 200, 6, 2, 64
+    rng = O.RNG(77)
+    q, k, v, g = (torch.from_numpy(rng.normals(B * T * h * dH)).cuda() for h in (nH, nKV, nKV, nH))
+    o = torch.empty(B * T * nH * dH, device="cuda")
+    lse = torch.empty(B * nH * T, device="cuda")
+    grads = [torch.zeros(B * T * h * dH, device="cuda") for h in (nH, nKV, nKV)]
+    h = ctx().handle
+    _lib.call("fcu_attn_fwd", h, q.data_ptr(), k.data_ptr(), v.data_ptr(), B, T, nH, nKV, dH, o.data_ptr(),
+              lse.data_ptr())
+    snaps = []
+    for acc in (0, 1):
+        _lib.call("fcu_attn_bwd", h, g.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                  lse.data_ptr(), B, T, nH, nKV, dH, *(t.data_ptr() for t in grads), acc)
+        torch.cuda.synchronize()
+        snaps.append([t.clone() for t in grads])
+    device_ok()
+    for one, two in zip(*snaps):
+        assert torch.isfinite(one).all()
+        assert torch.equal(two, 2 * one)
