@@ -523,8 +523,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--precision", default=os.environ.get("FORGECU_PRECISION", "bf16"),
-                    choices=["fp32", "bf16"],
-                    help="bf16: tensor-core fused step (default); fp32: CUDA-core parity mode")
+                    choices=["fp32", "fp32tc", "bf16"],
+                    help="bf16: tensor-core fused step (default); fp32: CUDA-core parity mode; "
+                         "fp32tc: parity mode with matmulT on the tensor cores")
     ap.add_argument("--batch", type=int, default=GLOBAL_BATCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true",
@@ -695,7 +696,8 @@ def main():
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": {"fp32": "f32", "bf16": "bf16 operands, f32 accumulate/master"}[args.precision],
+            "dtype": {"fp32": "f32", "fp32tc": "f32 (matmulT as 3-way bf16 split on tcgen05)",
+                      "bf16": "bf16 operands, f32 accumulate/master"}[args.precision],
             "data": "synthetic (RNG(5) tokens, initWeights seed 5)",
             "config": {"workload": "c5-125m-train-step",
                        "model": "llama-125m (forge-llm TrainableTransformer: V32000 D768 L12 H12/4 F2048)",

@@ -999,8 +999,8 @@ int gemm_tc(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float *C, i
 // does for bf16).  Every matmulT contraction runs as the forward form
 // C[M,N] = A'[M,6K'] . B'[N,6K']^T: the split kernel reads its operand
 // transposed where the op needs it and pads K to a multiple of 8 with zeros,
-// so any shape runs on the tensor cores.  Long contractions are processed in
-// chunks (C accumulates) to bound the bf16 copies.
+// so any shape runs on the tensor cores.  The contraction runs in chunks of
+// 128 (C accumulates in fp32 between them).
 namespace {
 
 constexpr int kSplitTile = 32;
@@ -1063,13 +1063,13 @@ int gemm_split6(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float *
     case GemmOp::kDx: ars = K, acs = 1, brs = 1, bcs = N; break;    // A[M,K], B[K,N]
     default: ars = 1, acs = M, brs = 1, bcs = N; break;             // A[K,M], B[K,N]
   }
-  // contraction chunk: the two bf16 copies (12 bytes per element of each
-  // operand's chunk) within about 1 GiB
-  const int64_t budget = (int64_t)1 << 30;
-  int64_t chunk = budget / (12 * (M + N));
-  chunk -= chunk % 64;
-  if (chunk < 64) chunk = 64;
-  if (chunk > K) chunk = K;
+  // Contraction chunks of kTcChunk: the tensor cores accumulate at most
+  // 6 x kTcChunk products per output (their fp32 accumulation does not round
+  // each addition to nearest, so its error grows with the number of terms:
+  // relL2 2e-5 against double over a 12,288-term contraction), and the chunks
+  // are added into C by the GEMM epilogue in IEEE fp32.
+  constexpr int64_t kTcChunk = 128;
+  const int64_t chunk = K < kTcChunk ? K : kTcChunk;
   const int64_t Lp_max = (chunk + 7) / 8 * 8;
   const size_t bytes_a = round_up((size_t)M * 6 * Lp_max * 2, 1024);
   void *ws = nullptr;
