@@ -20,7 +20,8 @@ from .infer import (KVCache, PagedKVCache, QuantLinear, Transformer, attentionDe
 
 def set_precision(mode: str) -> None:
     """Arithmetic of the contractions on the current device: "fp32"
-    (CUDA cores, parity) or "bf16" (tcgen05 tensor cores)."""
+    (CUDA cores, parity), "fp32tc" (parity, matmulT on the tcgen05 tensor
+    cores through a three-way bf16 split) or "bf16" (tcgen05 tensor cores)."""
     from .autograd import ctx
     ctx().set_precision(PRECISIONS[mode])
 
