@@ -376,7 +376,7 @@ int fcu_attn_fwd(fcu_ctx *ctx, const float *Q, const float *K, const float *V, i
   FCU_REQUIRE(Q && K && V && O && lse, "fcu_attn_fwd: null pointer");
   cudaStream_t st = ctx->stream;
   if (ctx->precision == FCU_PREC_BF16 && fcu::attn_tmem_op_supported(dH, Q, K, V, O))
-    return fcu::attn_fwd_op_tmem(ctx, Q, K, V, B, T, nH, nKV, O, lse);
+    return fcu::attn_fwd_op_tmem(ctx, Q, K, V, B, T, nH, nKV, dH, O, lse);
   if (ctx->precision == FCU_PREC_BF16 && fcu::attn_tc_supported(dH, Q, K, V))
     return fcu::attn_fwd_tc(st, Q, K, V, B, T, nH, nKV, dH, O, lse);
   if (dH <= 16) return attn_fwd_launch<16>(st, Q, K, V, B, T, nH, nKV, dH, O, lse);
@@ -394,7 +394,7 @@ int fcu_attn_bwd(fcu_ctx *ctx, const float *dO, const float *Q, const float *K, 
   FCU_REQUIRE(dO && Q && K && V && O && lse && dQ && dK && dV, "fcu_attn_bwd: null pointer");
   if (ctx->precision == FCU_PREC_BF16 && fcu::attn_tmem_op_supported(dH, Q, K, V, O) &&
       fcu::attn_tmem_op_supported(dH, dO, dQ, dK, dV))
-    return fcu::attn_bwd_op_tmem(ctx, dO, Q, K, V, O, lse, B, T, nH, nKV, dQ, dK, dV, accumulate);
+    return fcu::attn_bwd_op_tmem(ctx, dO, Q, K, V, O, lse, B, T, nH, nKV, dH, dQ, dK, dV, accumulate);
   void *scr = nullptr;
   rc = fcu::ctx_scratch(ctx, sizeof(float) * (size_t)B * nH * T, &scr);
   if (rc) return rc;

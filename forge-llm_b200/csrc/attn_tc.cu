@@ -697,7 +697,6 @@ int attn_bwd_tc(cudaStream_t st, const float *dO, const float *Q, const float *K
   return bwd_dispatch<float, float>(st, a, B, dH);
 }
 
-int rope_table_f32(fcu_ctx *ctx, int T, int head_dim, double theta, const float2 **out);
 
 }  // namespace fcu
 
@@ -714,7 +713,8 @@ int fcu_attn_fwd_bf16(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int 
               "fcu_attn_fwd_bf16: qkv row stride %lld", (long long)ld_qkv);
   FCU_REQUIRE(qkv && O && lse && (((uintptr_t)qkv | (uintptr_t)O) & 15) == 0,
               "fcu_attn_fwd_bf16: null or unaligned pointer");
-  if (attn_tmem_supported(dH)) return attn_fwd_tmem(ctx, qkv, ld_qkv, B, T, nH, nKV, O, lse);
+  if (attn_tmem_supported(dH)) return attn_fwd_tmem(ctx, qkv, ld_qkv, B, T, nH, nKV, O, lse, dH);
+  if (attn_tmem_padded(dH)) return attn_fwd_tmem_padded(ctx, qkv, ld_qkv, B, T, nH, nKV, dH, O, lse);
   const int64_t qD = (int64_t)nH * dH, kvD = (int64_t)nKV * dH;
   Args a{};
   a.q = {qkv, ld_qkv, 0};
@@ -761,8 +761,10 @@ int fcu_attn_bwd_bf16(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_
     float *pk = split ? (float *)((uint8_t *)scr + delta_bytes) : nullptr;
     float *pv = split ? (float *)((uint8_t *)scr + delta_bytes + part_bytes) : nullptr;
     return attn_bwd_tmem(ctx, dO, qkv, ld_qkv, O, lse, (float *)scr, B, T, nH, nKV, rope, dqkv, split,
-                         pk, pv);
+                         pk, pv, dH);
   }
+  if (attn_tmem_padded(dH))
+    return attn_bwd_tmem_padded(ctx, dO, qkv, ld_qkv, O, lse, B, T, nH, nKV, dH, rope_theta, dqkv);
   // Small grids (few sequences per GPU) balance the causal work better with
   // one dK/dV CTA per q head and a reduction over each GQA group.
   const int64_t kv_ctas = (int64_t)div_up(T, kTile) * nKV * B;

@@ -993,7 +993,7 @@ bool attn_tmem_supported(int dH) { return dH == kD; }
 // O [B*T, nH*64] bf16 and lse [B][nH][T] from the bf16 qkv buffer (row stride
 // ld_qkv elements: q heads, then k heads, then v heads, 64 columns each).
 int attn_fwd_tmem(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, int nH, int nKV,
-                  void *O, float *lse) {
+                  void *O, float *lse, int dh) {
   int rc = tc_get_encode();
   if (rc) return rc;
   int *err = nullptr;
@@ -1009,7 +1009,7 @@ int attn_fwd_tmem(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, i
   p.nH = nH;
   p.nKV = nKV;
   p.n_qt = div_up(T, kBM);
-  p.scale_log2 = (float)(1.0 / sqrt((double)kD)) * kLog2e;
+  p.scale_log2 = (float)(1.0 / sqrt((double)dh)) * kLog2e;
   p.O = (__nv_bfloat16 *)O;
   p.lse = lse;
   p.err = err;
@@ -1034,7 +1034,7 @@ int attn_fwd_tmem(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, i
 // (group * B*T * nKV*64 floats each), used when `split` is set.
 int attn_bwd_tmem(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv, const void *O,
                   const float *lse, float *delta, int B, int T, int nH, int nKV, const float2 *rope,
-                  void *dqkv, int split, float *pk, float *pv) {
+                  void *dqkv, int split, float *pk, float *pv, int dh) {
   int rc = tc_get_encode();
   if (rc) return rc;
   int *err = nullptr;
@@ -1057,7 +1057,7 @@ int attn_bwd_tmem(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv,
   p.n_t = div_up(T, kBM);
   p.group = nH / nKV;
   p.split = split;
-  p.scale = (float)(1.0 / sqrt((double)kD));
+  p.scale = (float)(1.0 / sqrt((double)dh));
   p.scale_log2 = p.scale * kLog2e;
   p.lse = lse;
   p.delta = delta;
@@ -1128,36 +1128,47 @@ int op_buffer(fcu_ctx *ctx, size_t bytes, void **out) {
   return FCU_OK;
 }
 
-// dst[r, col0 + c] = bf16(src[r, c]) for c < cols (4 at a time; cols % 4 == 0)
-__global__ void pack_bf16_kernel(const float *__restrict__ src, int64_t rows, int cols, __nv_bfloat16 *dst,
-                                 int64_t ld, int col0) {
-  const int c4 = cols / 4;
-  const int64_t n = rows * c4;
+// Head-padded layouts.  The kernels read 64 columns per head; a head of dh
+// < 64 columns (dh % 4 == 0) is carried as its dh values followed by 64 - dh
+// zeros.  Zero columns add nothing to q.k, and the O / dq / dk / dv columns
+// they produce are zero and dropped, so the padded problem is the original
+// one (the softmax scale stays 1/sqrt(dh)).
+
+// dst[r, col0 + h*64 + c] = bf16(src[r, h*dh + c]) for c < dh, 0 for dh <= c < 64
+__global__ void pack_bf16_kernel(const float *__restrict__ src, int64_t rows, int heads, int dh,
+                                 __nv_bfloat16 *dst, int64_t ld, int col0) {
+  const int64_t n = rows * heads * (kD / 4);
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / c4;
-    const int c = (int)(i - r * c4) * 4;
-    const float4 v = *reinterpret_cast<const float4 *>(src + r * cols + c);
-    __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
-    uint2 u;
-    u.x = *reinterpret_cast<uint32_t *>(&a);
-    u.y = *reinterpret_cast<uint32_t *>(&b);
-    *reinterpret_cast<uint2 *>(dst + r * ld + col0 + c) = u;
+    const int64_t rh = i / (kD / 4);
+    const int c = (int)(i - rh * (kD / 4)) * 4;
+    const int64_t r = rh / heads;
+    const int h = (int)(rh - r * heads);
+    uint2 u = make_uint2(0u, 0u);
+    if (c < dh) {
+      const float4 v = *reinterpret_cast<const float4 *>(src + (r * heads + h) * dh + c);
+      __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+      u.x = *reinterpret_cast<uint32_t *>(&a);
+      u.y = *reinterpret_cast<uint32_t *>(&b);
+    }
+    *reinterpret_cast<uint2 *>(dst + r * ld + col0 + h * kD + c) = u;
   }
 }
 
-// dst[r, c] (+)= float(src[r, col0 + c])
+// dst[r, h*dh + c] (+)= float(src[r, col0 + h*64 + c]) for c < dh
 __global__ void unpack_bf16_kernel(const __nv_bfloat16 *__restrict__ src, int64_t ld, int col0, int64_t rows,
-                                   int cols, float *dst, int accumulate) {
-  const int c4 = cols / 4;
-  const int64_t n = rows * c4;
+                                   int heads, int dh, float *dst, int accumulate) {
+  const int c4 = dh / 4;
+  const int64_t n = rows * heads * c4;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / c4;
-    const int c = (int)(i - r * c4) * 4;
-    const uint2 u = *reinterpret_cast<const uint2 *>(src + r * ld + col0 + c);
+    const int64_t rh = i / c4;
+    const int c = (int)(i - rh * c4) * 4;
+    const int64_t r = rh / heads;
+    const int h = (int)(rh - r * heads);
+    const uint2 u = *reinterpret_cast<const uint2 *>(src + r * ld + col0 + h * kD + c);
     const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.x));
     const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.y));
     float4 v = make_float4(a.x, a.y, b.x, b.y);
-    float4 *d = reinterpret_cast<float4 *>(dst + r * cols + c);
+    float4 *d = reinterpret_cast<float4 *>(dst + rh * dh + c);
     if (accumulate) {
       const float4 o = *d;
       v.x += o.x;
@@ -1169,19 +1180,52 @@ __global__ void unpack_bf16_kernel(const __nv_bfloat16 *__restrict__ src, int64_
   }
 }
 
-int pack(fcu_ctx *ctx, const float *src, int64_t rows, int cols, __nv_bfloat16 *dst, int64_t ld, int col0) {
-  const int64_t n = rows * (cols / 4);
-  const int blocks = (int)((n + 255) / 256 < 16 * ctx->num_sms ? (n + 255) / 256 : 16 * ctx->num_sms);
-  pack_bf16_kernel<<<blocks, 256, 0, ctx->stream>>>(src, rows, cols, dst, ld, col0);
+// bf16 rows of dh-column heads <-> rows of 64-column heads (to_pad: zero
+// fill of columns [dh, 64); otherwise those columns are dropped).
+__global__ void repad_bf16_kernel(const __nv_bfloat16 *__restrict__ src, int64_t lds, __nv_bfloat16 *dst,
+                                  int64_t ldd, int64_t rows, int heads, int dh, int to_pad) {
+  const int c4 = (to_pad ? kD : dh) / 4;
+  const int64_t n = rows * heads * c4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t rh = i / c4;
+    const int c = (int)(i - rh * c4) * 4;
+    const int64_t r = rh / heads;
+    const int h = (int)(rh - r * heads);
+    if (to_pad) {
+      uint2 u = make_uint2(0u, 0u);
+      if (c < dh) u = *reinterpret_cast<const uint2 *>(src + r * lds + h * dh + c);
+      *reinterpret_cast<uint2 *>(dst + r * ldd + h * kD + c) = u;
+    } else {
+      *reinterpret_cast<uint2 *>(dst + r * ldd + h * dh + c) =
+          *reinterpret_cast<const uint2 *>(src + r * lds + h * kD + c);
+    }
+  }
+}
+
+int grid_for(fcu_ctx *ctx, int64_t n) {
+  return (int)((n + 255) / 256 < 16 * ctx->num_sms ? (n + 255) / 256 : 16 * ctx->num_sms);
+}
+
+int pack(fcu_ctx *ctx, const float *src, int64_t rows, int heads, int dh, __nv_bfloat16 *dst, int64_t ld,
+         int col0) {
+  pack_bf16_kernel<<<grid_for(ctx, rows * heads * (kD / 4)), 256, 0, ctx->stream>>>(src, rows, heads, dh, dst,
+                                                                                     ld, col0);
   FCU_CHECK_LAUNCH();
   return FCU_OK;
 }
 
-int unpack(fcu_ctx *ctx, const __nv_bfloat16 *src, int64_t ld, int col0, int64_t rows, int cols, float *dst,
-           int accumulate) {
-  const int64_t n = rows * (cols / 4);
-  const int blocks = (int)((n + 255) / 256 < 16 * ctx->num_sms ? (n + 255) / 256 : 16 * ctx->num_sms);
-  unpack_bf16_kernel<<<blocks, 256, 0, ctx->stream>>>(src, ld, col0, rows, cols, dst, accumulate);
+int unpack(fcu_ctx *ctx, const __nv_bfloat16 *src, int64_t ld, int col0, int64_t rows, int heads, int dh,
+           float *dst, int accumulate) {
+  unpack_bf16_kernel<<<grid_for(ctx, rows * heads * (dh / 4)), 256, 0, ctx->stream>>>(src, ld, col0, rows,
+                                                                                       heads, dh, dst, accumulate);
+  FCU_CHECK_LAUNCH();
+  return FCU_OK;
+}
+
+int repad(fcu_ctx *ctx, const void *src, int64_t lds, void *dst, int64_t ldd, int64_t rows, int heads, int dh,
+          int to_pad) {
+  repad_bf16_kernel<<<grid_for(ctx, rows * heads * ((to_pad ? kD : dh) / 4)), 256, 0, ctx->stream>>>(
+      (const __nv_bfloat16 *)src, lds, (__nv_bfloat16 *)dst, ldd, rows, heads, dh, to_pad);
   FCU_CHECK_LAUNCH();
   return FCU_OK;
 }
@@ -1190,29 +1234,52 @@ bool op_aligned(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
 }  // namespace
 
+bool attn_tmem_padded(int dH) { return dH > 0 && dH <= kD && dH % 4 == 0; }
+
 bool attn_tmem_op_supported(int dH, const void *a, const void *b, const void *c, const void *d) {
-  return dH == kD && op_aligned(a) && op_aligned(b) && op_aligned(c) && op_aligned(d);
+  return attn_tmem_padded(dH) && op_aligned(a) && op_aligned(b) && op_aligned(c) && op_aligned(d);
 }
 
 int attn_fwd_op_tmem(fcu_ctx *ctx, const float *Q, const float *K, const float *V, int B, int T, int nH,
-                     int nKV, float *O, float *lse) {
+                     int nKV, int dH, float *O, float *lse) {
   const int64_t rows = (int64_t)B * T, W = (int64_t)(nH + 2 * nKV) * kD, qD = (int64_t)nH * kD,
                 kvD = (int64_t)nKV * kD;
   void *buf = nullptr;
   int rc = op_buffer(ctx, (size_t)rows * (W + qD) * sizeof(__nv_bfloat16), &buf);
   if (rc) return rc;
   __nv_bfloat16 *qkv = (__nv_bfloat16 *)buf, *Ob = qkv + rows * W;
-  if ((rc = pack(ctx, Q, rows, (int)qD, qkv, W, 0)) || (rc = pack(ctx, K, rows, (int)kvD, qkv, W, (int)qD)) ||
-      (rc = pack(ctx, V, rows, (int)kvD, qkv, W, (int)(qD + kvD))))
+  if ((rc = pack(ctx, Q, rows, nH, dH, qkv, W, 0)) || (rc = pack(ctx, K, rows, nKV, dH, qkv, W, (int)qD)) ||
+      (rc = pack(ctx, V, rows, nKV, dH, qkv, W, (int)(qD + kvD))))
     return rc;
-  rc = attn_fwd_tmem(ctx, qkv, W, B, T, nH, nKV, Ob, lse);
+  rc = attn_fwd_tmem(ctx, qkv, W, B, T, nH, nKV, Ob, lse, dH);
   if (rc) return rc;
-  return unpack(ctx, Ob, qD, 0, rows, (int)qD, O, 0);
+  return unpack(ctx, Ob, qD, 0, rows, nH, dH, O, 0);
 }
 
+namespace {
+
+// delta, and the head-split dK / dV partials (kv columns padded to 64 per
+// head) on small grids, from the context scratch.
+int bwd_scratch(fcu_ctx *ctx, int B, int T, int nH, int nKV, int *split, float **delta, float **pk,
+                float **pv) {
+  const int64_t ctas = (int64_t)div_up(T, kBM) * nKV * B;
+  *split = (nH > nKV && ctas < 4 * (int64_t)ctx->num_sms) ? 1 : 0;
+  const size_t delta_bytes = (sizeof(float) * (size_t)B * nH * T + 255) & ~(size_t)255;
+  const size_t part_bytes = *split ? sizeof(float) * (size_t)(nH / nKV) * B * T * nKV * kD : 0;
+  void *scr = nullptr;
+  int rc = ctx_scratch(ctx, delta_bytes + 2 * part_bytes, &scr);
+  if (rc) return rc;
+  *delta = (float *)scr;
+  *pk = *split ? (float *)((uint8_t *)scr + delta_bytes) : nullptr;
+  *pv = *split ? (float *)((uint8_t *)scr + delta_bytes + part_bytes) : nullptr;
+  return FCU_OK;
+}
+
+}  // namespace
+
 int attn_bwd_op_tmem(fcu_ctx *ctx, const float *dO, const float *Q, const float *K, const float *V,
-                     const float *O, const float *lse, int B, int T, int nH, int nKV, float *dQ, float *dK,
-                     float *dV, int accumulate) {
+                     const float *O, const float *lse, int B, int T, int nH, int nKV, int dH, float *dQ,
+                     float *dK, float *dV, int accumulate) {
   const int64_t rows = (int64_t)B * T, W = (int64_t)(nH + 2 * nKV) * kD, qD = (int64_t)nH * kD,
                 kvD = (int64_t)nKV * kD;
   void *buf = nullptr;
@@ -1221,26 +1288,57 @@ int attn_bwd_op_tmem(fcu_ctx *ctx, const float *dO, const float *Q, const float 
   if (rc) return rc;
   __nv_bfloat16 *qkv = (__nv_bfloat16 *)buf, *dqkv = qkv + rows * W, *dOb = dqkv + rows * W,
                 *Ob = dOb + rows * qD;
-  if ((rc = pack(ctx, Q, rows, (int)qD, qkv, W, 0)) || (rc = pack(ctx, K, rows, (int)kvD, qkv, W, (int)qD)) ||
-      (rc = pack(ctx, V, rows, (int)kvD, qkv, W, (int)(qD + kvD))) ||
-      (rc = pack(ctx, dO, rows, (int)qD, dOb, qD, 0)) || (rc = pack(ctx, O, rows, (int)qD, Ob, qD, 0)))
+  if ((rc = pack(ctx, Q, rows, nH, dH, qkv, W, 0)) || (rc = pack(ctx, K, rows, nKV, dH, qkv, W, (int)qD)) ||
+      (rc = pack(ctx, V, rows, nKV, dH, qkv, W, (int)(qD + kvD))) ||
+      (rc = pack(ctx, dO, rows, nH, dH, dOb, qD, 0)) || (rc = pack(ctx, O, rows, nH, dH, Ob, qD, 0)))
     return rc;
-  // the kernels' own scratch: delta, and the head-split partials on small grids
-  const int64_t ctas = (int64_t)div_up(T, kBM) * nKV * B;
-  const int split = (nH > nKV && ctas < 4 * (int64_t)ctx->num_sms) ? 1 : 0;
-  const size_t delta_bytes = (sizeof(float) * (size_t)B * nH * T + 255) & ~(size_t)255;
-  const size_t part_bytes = split ? sizeof(float) * (size_t)(nH / nKV) * B * T * kvD : 0;
-  void *scr = nullptr;
-  rc = ctx_scratch(ctx, delta_bytes + 2 * part_bytes, &scr);
+  int split = 0;
+  float *delta = nullptr, *pk = nullptr, *pv = nullptr;
+  if ((rc = bwd_scratch(ctx, B, T, nH, nKV, &split, &delta, &pk, &pv))) return rc;
+  rc = attn_bwd_tmem(ctx, dOb, qkv, W, Ob, lse, delta, B, T, nH, nKV, nullptr, dqkv, split, pk, pv, dH);
   if (rc) return rc;
-  float *pk = split ? (float *)((uint8_t *)scr + delta_bytes) : nullptr;
-  float *pv = split ? (float *)((uint8_t *)scr + delta_bytes + part_bytes) : nullptr;
-  rc = attn_bwd_tmem(ctx, dOb, qkv, W, Ob, lse, (float *)scr, B, T, nH, nKV, nullptr, dqkv, split, pk, pv);
-  if (rc) return rc;
-  if ((rc = unpack(ctx, dqkv, W, 0, rows, (int)qD, dQ, accumulate)) ||
-      (rc = unpack(ctx, dqkv, W, (int)qD, rows, (int)kvD, dK, accumulate)))
+  if ((rc = unpack(ctx, dqkv, W, 0, rows, nH, dH, dQ, accumulate)) ||
+      (rc = unpack(ctx, dqkv, W, (int)qD, rows, nKV, dH, dK, accumulate)))
     return rc;
-  return unpack(ctx, dqkv, W, (int)(qD + kvD), rows, (int)kvD, dV, accumulate);
+  return unpack(ctx, dqkv, W, (int)(qD + kvD), rows, nKV, dH, dV, accumulate);
+}
+
+// The fused path's bf16 entries at head dims below 64: qkv (and dO, O) are
+// re-laid out with 64-column heads in the operator buffer, and the results
+// copied back to dh-column heads.  RoPE's backward runs inside the kernels
+// on a [T][32] table whose pairs past dh/2 are the identity.
+int attn_fwd_tmem_padded(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, int nH, int nKV, int dH,
+                         void *O, float *lse) {
+  const int64_t rows = (int64_t)B * T, W = (int64_t)(nH + 2 * nKV) * kD, qD = (int64_t)nH * kD;
+  void *buf = nullptr;
+  int rc = op_buffer(ctx, (size_t)rows * (W + qD) * sizeof(__nv_bfloat16), &buf);
+  if (rc) return rc;
+  __nv_bfloat16 *qkvp = (__nv_bfloat16 *)buf, *Op = qkvp + rows * W;
+  if ((rc = repad(ctx, qkv, ld_qkv, qkvp, W, rows, nH + 2 * nKV, dH, 1))) return rc;
+  if ((rc = attn_fwd_tmem(ctx, qkvp, W, B, T, nH, nKV, Op, lse, dH))) return rc;
+  return repad(ctx, Op, qD, O, (int64_t)nH * dH, rows, nH, dH, 0);
+}
+
+int attn_bwd_tmem_padded(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv, const void *O,
+                         const float *lse, int B, int T, int nH, int nKV, int dH, double rope_theta, void *dqkv) {
+  const int64_t rows = (int64_t)B * T, W = (int64_t)(nH + 2 * nKV) * kD, qD = (int64_t)nH * kD;
+  void *buf = nullptr;
+  int rc = op_buffer(ctx, (size_t)rows * (2 * W + 2 * qD) * sizeof(__nv_bfloat16), &buf);
+  if (rc) return rc;
+  __nv_bfloat16 *qkvp = (__nv_bfloat16 *)buf, *dqkvp = qkvp + rows * W, *dOp = dqkvp + rows * W,
+                *Op = dOp + rows * qD;
+  const int64_t ldo = (int64_t)nH * dH;
+  if ((rc = repad(ctx, qkv, ld_qkv, qkvp, W, rows, nH + 2 * nKV, dH, 1)) ||
+      (rc = repad(ctx, dO, ldo, dOp, qD, rows, nH, dH, 1)) || (rc = repad(ctx, O, ldo, Op, qD, rows, nH, dH, 1)))
+    return rc;
+  const float2 *rope = nullptr;
+  if (rope_theta > 0 && (rc = rope_table_f32(ctx, T, dH, rope_theta, &rope, kD / 2))) return rc;
+  int split = 0;
+  float *delta = nullptr, *pk = nullptr, *pv = nullptr;
+  if ((rc = bwd_scratch(ctx, B, T, nH, nKV, &split, &delta, &pk, &pv))) return rc;
+  rc = attn_bwd_tmem(ctx, dOp, qkvp, W, Op, lse, delta, B, T, nH, nKV, rope, dqkvp, split, pk, pv, dH);
+  if (rc) return rc;
+  return repad(ctx, dqkvp, W, dqkv, ld_qkv, rows, nH + 2 * nKV, dH, 0);
 }
 
 }  // namespace fcu

@@ -46,22 +46,36 @@ int attn_bwd_tc(cudaStream_t st, const float *dO, const float *Q, const float *K
                 float *dQ, float *dK, float *dV, int acc);
 
 // The operator entries (fcu_attn_fwd / _bwd, bf16 mode) on the tcgen05
-// kernels: fp32 operands packed to bf16 (attn_tmem.cu); head dim 64 and
-// 16-byte aligned operands.
+// kernels: fp32 operands packed to bf16 (attn_tmem.cu), heads of dH <= 64
+// columns (dH % 4 == 0) carried 64 wide with zero padding; 16-byte aligned
+// operands.
 bool attn_tmem_op_supported(int dH, const void *a, const void *b, const void *c, const void *d);
 int attn_fwd_op_tmem(fcu_ctx *ctx, const float *Q, const float *K, const float *V, int B, int T, int nH,
-                     int nKV, float *O, float *lse);
+                     int nKV, int dH, float *O, float *lse);
 int attn_bwd_op_tmem(fcu_ctx *ctx, const float *dO, const float *Q, const float *K, const float *V,
-                     const float *O, const float *lse, int B, int T, int nH, int nKV, float *dQ, float *dK,
-                     float *dV, int accumulate);
+                     const float *O, const float *lse, int B, int T, int nH, int nKV, int dH, float *dQ,
+                     float *dK, float *dV, int accumulate);
 
-// tcgen05 attention (attn_tmem.cu): head dim 64, bf16 qkv buffer.
+// tcgen05 attention (attn_tmem.cu) on a bf16 qkv buffer of 64-column heads;
+// dh is the heads' true width (the softmax scale is 1/sqrt(dh); columns past
+// dh must be zero).
 bool attn_tmem_supported(int dH);
 int attn_fwd_tmem(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, int nH, int nKV,
-                  void *O, float *lse);
+                  void *O, float *lse, int dh);
 int attn_bwd_tmem(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv, const void *O,
                   const float *lse, float *delta, int B, int T, int nH, int nKV, const float2 *rope,
-                  void *dqkv, int split, float *pk, float *pv);
+                  void *dqkv, int split, float *pk, float *pv, int dh);
+// The same kernels for heads narrower than 64 (dH % 4 == 0): the bf16
+// buffers are re-laid out with zero-padded 64-column heads around the call.
+bool attn_tmem_padded(int dH);
+int attn_fwd_tmem_padded(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, int nH, int nKV, int dH,
+                         void *O, float *lse);
+int attn_bwd_tmem_padded(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv, const void *O,
+                         const float *lse, int B, int T, int nH, int nKV, int dH, double rope_theta, void *dqkv);
+
+// (cos, sin) RoPE table [T][width] (width 0: head_dim/2; entries past
+// head_dim/2 are the identity), cached per device (gemm_tc.cu).
+int rope_table_f32(fcu_ctx *ctx, int T, int head_dim, double theta, const float2 **out, int width = 0);
 
 // Programmatic dependent launch.  A kernel launched with launch_pdl may
 // start while the previous kernel in the stream is finishing: it runs its

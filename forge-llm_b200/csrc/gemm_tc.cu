@@ -1091,14 +1091,20 @@ int gemm_split6(fcu_ctx *ctx, GemmOp op, const float *A, const float *B, float *
   return FCU_OK;
 }
 
-// (cos, sin) table [T][head_dim/2] in fp32 for the RoPE epilogue, rounded
-// once from the double angles of ropeRows (src/L2/tensor.js:141-143).
-__global__ void rope_table_f32_kernel(float2 *tab, int T, int half, int head_dim, double theta) {
+// (cos, sin) table [T][width] in fp32 for the RoPE epilogues, rounded once
+// from the double angles of ropeRows (src/L2/tensor.js:141-143); entries past
+// head_dim/2 (a table for heads carried 64 columns wide) are the identity.
+__global__ void rope_table_f32_kernel(float2 *tab, int T, int width, int head_dim, double theta) {
   fcu::pdl_trigger();
-  const int64_t n = (int64_t)T * half;
+  const int half = head_dim / 2;
+  const int64_t n = (int64_t)T * width;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
        e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t pos = e / half, i = e % half;
+    const int64_t pos = e / width, i = e % width;
+    if (i >= half) {
+      tab[e] = make_float2(1.f, 0.f);
+      continue;
+    }
     const double ang = (double)pos / pow(theta, (double)(2 * i) / (double)head_dim);
     double s, c;
     sincos(ang, &s, &c);
@@ -1106,23 +1112,25 @@ __global__ void rope_table_f32_kernel(float2 *tab, int T, int half, int head_dim
   }
 }
 
-int rope_table_f32(fcu_ctx *ctx, int T, int head_dim, double theta, const float2 **out) {
+int rope_table_f32(fcu_ctx *ctx, int T, int head_dim, double theta, const float2 **out, int width) {
   struct Tab {
     float2 *p = nullptr;
     int T = 0, head_dim = 0;
     double theta = 0;
   };
-  static thread_local Tab tabs[64];
-  Tab &t = tabs[ctx->device & 63];
+  // one cached table per device for each kind: [T][head_dim/2] and the
+  // 64-column padded [T][32]
+  static thread_local Tab tabs[2][64];
+  if (width <= 0) width = head_dim / 2;
+  Tab &t = tabs[width != head_dim / 2][ctx->device & 63];
   if (!t.p || t.T < T || t.head_dim != head_dim || t.theta != theta) {
     if (t.p) {
       FCU_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
       FCU_CHECK_CUDA(cudaFree(t.p));
       t.p = nullptr;
     }
-    const int half = head_dim / 2;
-    FCU_CHECK_CUDA(cudaMalloc(&t.p, sizeof(float2) * (size_t)T * half));
-    rope_table_f32_kernel<<<256, 256, 0, ctx->stream>>>(t.p, T, half, head_dim, theta);
+    FCU_CHECK_CUDA(cudaMalloc(&t.p, sizeof(float2) * (size_t)T * width));
+    rope_table_f32_kernel<<<256, 256, 0, ctx->stream>>>(t.p, T, width, head_dim, theta);
     FCU_CHECK_LAUNCH();
     t.T = T;
     t.head_dim = head_dim;

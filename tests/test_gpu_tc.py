@@ -314,15 +314,17 @@ def _attn_ref64(qkv, B, T, nH, nKV, dH):
     return o.permute(0, 2, 1, 3).reshape(B * T, nH * dH), lse
 
 
-@pytest.mark.parametrize("B,T,nH,nKV,extra", [(1, 64, 2, 2, 0), (2, 130, 4, 1, 0), (3, 300, 6, 2, 64),
-                                              (2, 1024, 12, 4, 0), (1, 2048, 32, 8, 0)])
-def test_attn_fwd_bf16_entry(B, T, nH, nKV, extra):
+@pytest.mark.parametrize("B,T,nH,nKV,extra,dH", [(1, 64, 2, 2, 0, 64), (2, 130, 4, 1, 0, 64), (3, 300, 6, 2, 64, 64),
+                                                 (2, 1024, 12, 4, 0, 64), (1, 2048, 32, 8, 0, 64),
+                                                 (1, 64, 4, 4, 0, 16), (2, 130, 4, 1, 8, 16),
+                                                 (3, 300, 6, 2, 64, 32), (2, 1024, 12, 4, 0, 32)])
+def test_attn_fwd_bf16_entry(B, T, nH, nKV, extra, dH):
     """The fused path's attention forward (bf16 qkv in, bf16 O + fp32 lse out)
     against float64 attention of the same bf16 inputs: only P's and O's bf16
-    rounding differ (relL2 <= 1e-2), the log-sum-exp to 1e-5."""
+    rounding differ (relL2 <= 1e-2), the log-sum-exp to 1e-5.  Head dims 16
+    and 32 run the same tcgen05 kernels on zero-padded 64-column heads."""
     from forgellm import _lib
     from forgellm.autograd import ctx
-    dH = 64
     width = (nH + 2 * nKV) * dH
     ld = width + extra
     g = torch.Generator(device="cuda").manual_seed(B * 1000 + T)
@@ -354,17 +356,19 @@ def _rope_back64(d, B, T, heads, dH, theta):
     return torch.stack((a * c + b * s, -a * s + b * c), -1).reshape(B * T, heads * dH)
 
 
-@pytest.mark.parametrize("B,T,nH,nKV,theta", [(1, 64, 2, 2, 0.0), (2, 130, 4, 1, 10000.0),
-                                              (3, 300, 6, 2, 10000.0), (2, 1024, 12, 4, 10000.0),
-                                              (16, 1024, 12, 4, 10000.0), (40, 512, 12, 4, 10000.0),
-                                              (1, 2048, 32, 8, 10000.0)])
-def test_attn_bwd_bf16_entry(B, T, nH, nKV, theta):
+@pytest.mark.parametrize("B,T,nH,nKV,theta,dH", [(1, 64, 2, 2, 0.0, 64), (2, 130, 4, 1, 10000.0, 64),
+                                                 (3, 300, 6, 2, 10000.0, 64), (2, 1024, 12, 4, 10000.0, 64),
+                                                 (16, 1024, 12, 4, 10000.0, 64), (40, 512, 12, 4, 10000.0, 64),
+                                                 (1, 2048, 32, 8, 10000.0, 64),
+                                                 (1, 64, 4, 4, 10000.0, 16), (2, 130, 4, 1, 0.0, 16),
+                                                 (3, 300, 6, 2, 10000.0, 32), (16, 256, 12, 4, 10000.0, 32)])
+def test_attn_bwd_bf16_entry(B, T, nH, nKV, theta, dH):
     """The fused path's attention backward (dq | dk | dv into the bf16 dqkv
     buffer, RoPE rotated back) against float64 autograd of the same bf16
-    inputs: relL2 <= 2e-2 (P and dS are bf16 operands), every gradient finite."""
+    inputs: relL2 <= 2e-2 (P and dS are bf16 operands), every gradient finite.
+    Head dims 16 and 32 run on zero-padded 64-column heads."""
     from forgellm import _lib
     from forgellm.autograd import ctx
-    dH = 64
     width = (nH + 2 * nKV) * dH
     g = torch.Generator(device="cuda").manual_seed(B * 77 + T)
     qkv = torch.randn(B * T, width, device="cuda", generator=g).to(torch.bfloat16)
@@ -397,14 +401,15 @@ def test_attn_bwd_bf16_entry(B, T, nH, nKV, theta):
         assert err <= 2e-2, (name, err)
 
 
-def test_tc_attention_operator_accumulates_on_tcgen05():
-    """causalAttnBatch in bf16 mode at head dim 64 runs the tcgen05 kernels on
-    packed bf16 copies of its fp32 operands; its backward follows the JS
-    `grad +=`: a second backward without zeroing doubles every gradient
-    exactly (the packed gradient is deterministic)."""
+@pytest.mark.parametrize("dH", [64, 32, 16])
+def test_tc_attention_operator_accumulates_on_tcgen05(dH):
+    """causalAttnBatch in bf16 mode runs the tcgen05 kernels on packed bf16
+    copies of its fp32 operands (heads below 64 columns zero-padded); its
+    backward follows the JS `grad +=`: a second backward without zeroing
+    doubles every gradient exactly (the packed gradient is deterministic)."""
     from forgellm import _lib
     from forgellm.autograd import ctx
-    B, T, nH, nKV, dH = 2, 200, 6, 2, 64
+    B, T, nH, nKV = 2, 200, 6, 2
     rng = O.RNG(77)
     q, k, v, g = (torch.from_numpy(rng.normals(B * T * h * dH)).cuda() for h in (nH, nKV, nKV, nH))
     o = torch.empty(B * T * nH * dH, device="cuda")
