@@ -39,6 +39,21 @@ constexpr int kThreads = 192;
 constexpr uint32_t kTmemCols = 256;            // S [0,128), O [128,192), P [192,256) (bf16 pairs)
 constexpr int kFwdStages = 3;                  // K/V ring depth
 constexpr float kRescaleLog2 = 8.f;
+#ifndef FCU_POLY_BWD
+#define FCU_POLY_BWD 4
+#endif
+// In the backward element loops one exponential pair in kPolyEvery is
+// computed on the FMA pipe (exp2_poly2) instead of the MUFU unit (0: MUFU
+// only).  Measured at config 4: dK/dV 461 -> 440 us and dQ 385 -> 377 us with
+// one pair in 4; one in 2 is slower.  The forward keeps MUFU only (its
+// softmax slowed from 246 to 260 us with one pair in 4).
+constexpr int kPolyEvery = FCU_POLY_BWD;
+template <int kEvery>
+__device__ __forceinline__ float2 exp2_pair(float2 x, int pair) {
+  if constexpr (kEvery > 0)
+    if (pair % kEvery == kEvery - 1) return exp2_poly2(x);
+  return make_float2(ex2_ftz(x.x), ex2_ftz(x.y));
+}
 constexpr float kLog2e = 1.4426950408889634f;
 
 // Shared memory map (byte offsets; tiles 1024-byte aligned for the swizzle).
@@ -222,10 +237,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       uint32_t pk[kBN / 2];                     // P as bf16 pairs
 #pragma unroll
       for (int c = 0; c < kBN; c += 2) {
-        const float e0 = ex2_ftz(fmaf(s[c], p.scale_log2, neg_m));
-        const float e1 = ex2_ftz(fmaf(s[c + 1], p.scale_log2, neg_m));
-        rs4[(c >> 1) & 3] += e0 + e1;
-        pk[c / 2] = pack2_bf16(e0, e1);
+        const float2 e = exp2_pair<0>(fma2(make_float2(s[c], s[c + 1]), make_float2(p.scale_log2, p.scale_log2),
+                                        make_float2(neg_m, neg_m)), c / 2);
+        rs4[(c >> 1) & 3] += e.x + e.y;
+        pk[c / 2] = pack2_bf16(e.x, e.y);
       }
       const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       l = l * alpha + rs;
@@ -332,13 +347,52 @@ __device__ __forceinline__ void dq_elements(const BwdParams &p, const float (&sv
 #pragma unroll
   for (int c = 0; c < 32; c++) {
     const float2 t = fma2(make_float2(sv[2 * c], sv[2 * c + 1]), sc, nl);   // s c - L
-    float p0 = ex2_ftz(t.x), p1 = ex2_ftz(t.y);
+    const float2 e = exp2_pair<kPolyEvery>(t, c);
+    float p0 = e.x, p1 = e.y;
     if (kMasked) {
       if (2 * c > lim) p0 = 0.f;
       if (2 * c + 1 > lim) p1 = 0.f;
     }
     const float2 g = mul2(make_float2(p0, p1), add2(make_float2(dp[2 * c], dp[2 * c + 1]), nd));
     dd[c] = pack2_bf16(g.x, g.y);
+  }
+}
+
+// The dK/dV element loop for this warp's 64 query columns: P^T = exp2(S^T c
+// - L) and dS^T = P^T (dP^T - delta) as bf16 pairs (packed f32x2 FMA / add /
+// mul), with -L and -delta of the columns read from shared memory four at a
+// time.  The compiler barrier at the end of each step keeps the loads from
+// being hoisted to the top, where their 128 registers would spill.
+__device__ __forceinline__ void dkdv_elements(float scale_log2, const float (&sv)[64], const float (&dp)[64],
+                                              const float4 *nL4, const float4 *nD4, uint32_t (&pp)[32],
+                                              uint32_t (&dd)[32]) {
+#pragma unroll
+  for (int c4 = 0; c4 < 16; c4++) {
+    const float4 l4 = nL4[c4], d4 = nD4[c4];
+    const int c = 4 * c4;
+    const float2 sc = make_float2(scale_log2, scale_log2);
+    const float2 e0 = exp2_pair<kPolyEvery>(fma2(make_float2(sv[c], sv[c + 1]), sc, make_float2(l4.x, l4.y)), 2 * c4);
+    const float2 e1 = exp2_pair<kPolyEvery>(fma2(make_float2(sv[c + 2], sv[c + 3]), sc, make_float2(l4.z, l4.w)), 2 * c4 + 1);
+    const float p0 = e0.x, p1 = e0.y, p2 = e1.x, p3 = e1.y;
+    pp[2 * c4] = pack2_bf16(p0, p1);
+    pp[2 * c4 + 1] = pack2_bf16(p2, p3);
+    dd[2 * c4] = pack2_bf16(p0 * (dp[c] + d4.x), p1 * (dp[c + 1] + d4.y));
+    dd[2 * c4 + 1] = pack2_bf16(p2 * (dp[c + 2] + d4.z), p3 * (dp[c + 3] + d4.w));
+    asm volatile("" ::: "memory");
+  }
+}
+
+// Masked columns (column c valid iff lo <= c < hi: queries before the key on
+// the diagonal tile, past the sequence end on a ragged one) get P = dS = +0
+// by clearing their bf16 halves; run only on the tiles that need it, after
+// the element loop, when its inputs are no longer live.
+__device__ __forceinline__ void dkdv_mask(int lo, int hi, uint32_t (&pp)[32], uint32_t (&dd)[32]) {
+#pragma unroll
+  for (int w = 0; w < 32; w++) {
+    const int c = 2 * w;
+    const uint32_t k = (c >= lo && c < hi ? 0x0000ffffu : 0u) | (c + 1 >= lo && c + 1 < hi ? 0xffff0000u : 0u);
+    pp[w] &= k;
+    dd[w] &= k;
   }
 }
 
@@ -473,8 +527,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int e = lane; e < kBM; e += 32) {
           const int q = q0 + e;
-          sL[s * kBM + e] = q < p.T ? p.lse[lrow + q] * kLog2e : 0.f;
-          sDl[s * kBM + e] = q < p.T ? p.delta[lrow + q] : 0.f;
+          sL[s * kBM + e] = q < p.T ? -(p.lse[lrow + q] * kLog2e) : 0.f;   // negated: the FMA adds them
+          sDl[s * kBM + e] = q < p.T ? -p.delta[lrow + q] : 0.f;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&q_full[s]);
@@ -593,35 +647,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const float4 *L4 = reinterpret_cast<const float4 *>(sL + s * kBM + cb);
         const float4 *D4 = reinterpret_cast<const float4 *>(sDl + s * kBM + cb);
         const int qc = q0 + cb;                 // first query of these columns
-        const bool mask = qc < key || qc + 64 > p.T;
         uint32_t pp[32], dd[32];
-        // lse / delta of the next four columns are loaded one step ahead; the
-        // compiler barrier at the end of each step keeps it from hoisting all
-        // 32 loads to the top (their 128 registers would spill)
-        float4 l4n = L4[0], d4n = D4[0];
-#pragma unroll
-        for (int c4 = 0; c4 < 16; c4++) {
-          const float4 l4 = l4n, d4 = d4n;
-          if (c4 < 15) {
-            l4n = L4[c4 + 1];
-            d4n = D4[c4 + 1];
-          }
-          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
-          float pr[4];
-#pragma unroll
-          for (int e = 0; e < 4; e++) {
-            pr[e] = ex2_ftz(fmaf(sv[4 * c4 + e], p.scale_log2, -lv[e]));
-            if (mask) {
-              const int q = qc + 4 * c4 + e;
-              if (q < key || q >= p.T) pr[e] = 0.f;
-            }
-          }
-          pp[2 * c4] = pack2_bf16(pr[0], pr[1]);
-          pp[2 * c4 + 1] = pack2_bf16(pr[2], pr[3]);
-          dd[2 * c4] = pack2_bf16(pr[0] * (dp[4 * c4] - dv[0]), pr[1] * (dp[4 * c4 + 1] - dv[1]));
-          dd[2 * c4 + 1] = pack2_bf16(pr[2] * (dp[4 * c4 + 2] - dv[2]), pr[3] * (dp[4 * c4 + 3] - dv[3]));
-          asm volatile("" ::: "memory");
-        }
+        // queries before the key (diagonal tile) or past the sequence end are masked
+        dkdv_elements(p.scale_log2, sv, dp, L4, D4, pp, dd);
+        if (qc < key || qc + 64 > p.T) dkdv_mask(key - qc, p.T - qc, pp, dd);
         // dV/dK of the previous unit must be done reading P^T / dS^T.
         if (u > 0 && !warp_wait(pds_free, (uint32_t)(u - 1) & 1u, abort_flag)) {
           ok = false;

@@ -319,6 +319,31 @@ __device__ __forceinline__ float2 mul2(float2 a, float2 b) {
   return d;
 }
 
+// 2^x for a pair on the FMA pipe instead of the MUFU unit (the softmax loops
+// are bound by MUFU throughput, 16 ex2 per clock per SM, so a share of their
+// exponentials is computed here).  Cody-Waite range reduction x = j + f with
+// j = rint(x) (adding 1.5 * 2^23 rounds to an integer in the low mantissa
+// bits) and |f| <= 1/2, then a degree-3 polynomial for 2^f whose coefficients
+// were fitted for minimal maximum relative error on [-1/2, 1/2] (7.5e-5, far
+// below the bf16 rounding of P), and j added to the exponent field.  x is
+// clamped below at -126, so scores that should vanish give 2^-126 rather than
+// 0; inputs are at most a few units above 0 here.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.f;         // 1.5 * 2^23
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 t = add2(x, make_float2(kRound, kRound));
+  const float2 j = add2(t, make_float2(-kRound, -kRound));
+  const float2 f = fma2(j, make_float2(-1.f, -1.f), x);
+  float2 q = fma2(f, make_float2(0.05517232418060303f, 0.05517232418060303f),
+                  make_float2(0.24261125922203064f, 0.24261125922203064f));
+  q = fma2(q, f, make_float2(0.6932607293128967f, 0.6932607293128967f));
+  q = fma2(q, f, make_float2(0.9999279975891113f, 0.9999279975891113f));
+  // t's bits are 0x4B400000 + j; shifted left by 23 only j << 23 remains
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t *r) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0],"
