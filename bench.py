@@ -516,6 +516,48 @@ def run_decode(args):
                           "note": "eager host loop: 12 layers x 11 launches + embed / head per step"}), flush=True)
 
 
+def profile_collectives(F, AD, model, opt, dp, batch):
+    """Every collective and join of one op-by-op step (`--comm-profile`),
+    timed with CUDA events on the communicator's and the context's streams:
+    per bucket its size, how long it queued behind earlier collectives after
+    its gradients were ready, and its duration; for each join how long the
+    compute stream waited (the exposed communication).  This rank's view."""
+    import torch
+
+    def eager_step():
+        F.resetTape()
+        model.zeroGrad()
+        loss = model.lossBatch(batch)
+        AD.backward(loss)
+        dp.finish()
+        opt.step()
+
+    eager_step()
+    torch.cuda.synchronize()
+    dp.comm.profile(256)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    eager_step()
+    s1.record()
+    torch.cuda.synchronize()
+    recs = dp.comm.profile_read()
+    dp.comm.profile(0)
+    colls = [r for r in recs if r["kind"] != "join"]
+    joins = [r for r in recs if r["kind"] == "join"]
+    return {
+        "step_ms": s0.elapsed_time(s1),
+        "collectives": [{"kind": r["kind"], "mbytes": round(r["bytes"] / 1e6, 3),
+                         "ready_ms": round(r["ready"], 3), "queued_ms": round(r["start"] - r["ready"], 3),
+                         "ms": round(r["end"] - r["start"], 3),
+                         "gbps": round(r["bytes"] / max(r["end"] - r["start"], 1e-6) / 1e6, 1)}
+                        for r in colls],
+        "joins_waited_ms": [round(r["end"] - r["ready"], 3) for r in joins],
+        "exposed_ms": round(sum(r["end"] - r["ready"] for r in joins), 3),
+        "measured": "CUDA events around each NCCL call (communicator stream) and join (compute stream), "
+                    "one op-by-op step after one untimed one; times from the first collective's ready time",
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -533,6 +575,9 @@ def main():
     ap.add_argument("--micro", choices=["gemm"], help="time one kernel alone (profiling)")
     ap.add_argument("--zero", action="store_true",
                     help="N > 1: shard Adam's state and update over the ranks (ZeRO-1)")
+    ap.add_argument("--comm-profile", action="store_true",
+                    help="N > 1: after the timed regions, time every collective of one op-by-op "
+                         "step with CUDA events and add them to the line (comm_profile)")
     ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "decode"],
                     help="time one of the operator configs instead of the C5 train step")
     ap.add_argument("--shape", default="8192,2048,768")
@@ -662,6 +707,10 @@ def main():
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = tokens_per_step * args.steps / (float(te[0]) / 1e3)
 
+    comm_profile = None
+    if args.comm_profile and dp is not None and dp.comm is not None:
+        comm_profile = profile_collectives(F, AD, model, opt, dp, batch_dev)
+
     gemm_where = "CUDA events around every matmulT in the timed region"
     gemm_steps = args.steps
     if use_graph:
@@ -721,6 +770,8 @@ def main():
                          "model_tflops": FLOP_PER_TOKEN * value / 1e12},
             "clocks": clocks,
         }
+        if comm_profile is not None:
+            line["comm_profile"] = comm_profile
         if world == 1 and not args.no_cpu_baseline:
             tps, sec = cpu_baseline(1)
             line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": 1, "kind": "port",

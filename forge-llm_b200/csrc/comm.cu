@@ -32,6 +32,7 @@
 #include <time.h>
 
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 
@@ -107,6 +108,14 @@ void pause_briefly() {
 
 }  // namespace
 
+// One profiled collective (or join): when its inputs were ready on the
+// context's stream, when it started and ended on the communicator's stream.
+struct CommProf {
+  cudaEvent_t ready = nullptr, start = nullptr, end = nullptr;
+  int kind = 0;
+  int64_t bytes = 0;
+};
+
 struct fcu_comm {
   const NcclApi *api = nullptr;
   ncclComm_t nc = nullptr;
@@ -116,6 +125,8 @@ struct fcu_comm {
   int pending = 0;   // collectives launched since the last fcu_comm_poll
   cudaStream_t stream = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr, done = nullptr;
+  std::vector<CommProf> prof;   // fcu_comm_profile: timing events, prof_used of them recorded
+  int prof_used = 0;
 };
 
 namespace {
@@ -205,6 +216,34 @@ int fork_from(fcu_ctx *ctx, fcu_comm *c, const char *what) {
   return FCU_OK;
 }
 
+// Profiling (fcu_comm_profile): timing events around a collective, outside
+// stream capture only.  prof_begin runs after fork_from, prof_end after the
+// NCCL call; a record is kept only if both were placed.
+bool prof_on(fcu_comm *c, fcu_ctx *ctx) {
+  if (c->prof_used >= (int)c->prof.size()) return false;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(ctx->stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return false;
+  return true;
+}
+
+int prof_begin(fcu_comm *c, fcu_ctx *ctx, int kind, int64_t bytes, bool *on) {
+  *on = prof_on(c, ctx);
+  if (!*on) return FCU_OK;
+  CommProf &r = c->prof[c->prof_used];
+  r.kind = kind;
+  r.bytes = bytes;
+  FCU_CHECK_CUDA(cudaEventRecord(r.ready, ctx->stream));
+  FCU_CHECK_CUDA(cudaEventRecord(r.start, c->stream));
+  return FCU_OK;
+}
+
+int prof_end(fcu_comm *c, bool on) {
+  if (!on) return FCU_OK;
+  FCU_CHECK_CUDA(cudaEventRecord(c->prof[c->prof_used].end, c->stream));
+  c->prof_used++;
+  return FCU_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -283,6 +322,11 @@ int fcu_comm_destroy(fcu_comm *comm) {
   }
   if (comm->stream) {
     cudaSetDevice(comm->device);
+    for (CommProf &r : comm->prof) {
+      cudaEventDestroy(r.ready);
+      cudaEventDestroy(r.start);
+      cudaEventDestroy(r.end);
+    }
     cudaEventDestroy(comm->fork);
     cudaEventDestroy(comm->join);
     cudaEventDestroy(comm->done);
@@ -304,9 +348,12 @@ int fcu_allreduce_grads(fcu_ctx *ctx, fcu_comm *comm, float *buf, int64_t n) {
   FCU_REQUIRE(n >= 0 && (n == 0 || buf), "fcu_allreduce_grads: bad buffer");
   int rc = fork_from(ctx, comm, "fcu_allreduce_grads");
   if (rc || n == 0) return rc;
+  bool on = false;
+  if ((rc = prof_begin(comm, ctx, 0, 4 * n, &on))) return rc;
   rc = nccl_result(comm, comm->api->AllReduce(buf, buf, (size_t)n, ncclFloat32, ncclAvg, comm->nc,
                                               comm->stream),
                    "fcu_allreduce_grads");
+  if (rc == FCU_OK) rc = prof_end(comm, on);
   if (rc == FCU_OK) comm->pending++;
   return rc;
 }
@@ -317,10 +364,13 @@ int fcu_reduce_scatter_grads(fcu_ctx *ctx, fcu_comm *comm, float *buf, int64_t n
   if (rc || n == 0) return rc;
   FCU_REQUIRE(n % comm->nranks == 0, "fcu_reduce_scatter_grads: %lld values do not split over %d ranks",
               (long long)n, comm->nranks);
+  bool on = false;
+  if ((rc = prof_begin(comm, ctx, 1, 4 * n, &on))) return rc;
   const int64_t per = n / comm->nranks;
   rc = nccl_result(comm, comm->api->ReduceScatter(buf, buf + (int64_t)comm->rank * per, (size_t)per,
                                                   ncclFloat32, ncclAvg, comm->nc, comm->stream),
                    "fcu_reduce_scatter_grads");
+  if (rc == FCU_OK) rc = prof_end(comm, on);
   if (rc == FCU_OK) comm->pending++;
   return rc;
 }
@@ -333,12 +383,15 @@ int fcu_allgather_params(fcu_ctx *ctx, fcu_comm *comm, void *buf, int64_t n, int
   if (rc || n == 0) return rc;
   FCU_REQUIRE(n % comm->nranks == 0, "fcu_allgather_params: %lld values do not split over %d ranks",
               (long long)n, comm->nranks);
+  bool on = false;
+  if ((rc = prof_begin(comm, ctx, 2, (int64_t)elem_bytes * n, &on))) return rc;
   const int64_t per = n / comm->nranks;
   char *base = (char *)buf;
   rc = nccl_result(comm, comm->api->AllGather(base + (int64_t)comm->rank * per * elem_bytes, buf,
                                               (size_t)per, elem_bytes == 4 ? ncclFloat32 : ncclBfloat16,
                                               comm->nc, comm->stream),
                    "fcu_allgather_params");
+  if (rc == FCU_OK) rc = prof_end(comm, on);
   if (rc == FCU_OK) comm->pending++;
   return rc;
 }
@@ -347,9 +400,12 @@ int fcu_allreduce_sum_f64(fcu_ctx *ctx, fcu_comm *comm, double *buf, int64_t n) 
   FCU_REQUIRE(n >= 0 && (n == 0 || buf), "fcu_allreduce_sum_f64: bad buffer");
   int rc = fork_from(ctx, comm, "fcu_allreduce_sum_f64");
   if (rc || n == 0) return rc;
+  bool on = false;
+  if ((rc = prof_begin(comm, ctx, 3, 8 * n, &on))) return rc;
   rc = nccl_result(comm, comm->api->AllReduce(buf, buf, (size_t)n, ncclFloat64, ncclSum, comm->nc,
                                               comm->stream),
                    "fcu_allreduce_sum_f64");
+  if (rc == FCU_OK) rc = prof_end(comm, on);
   if (rc == FCU_OK) comm->pending++;
   return rc;
 }
@@ -361,8 +417,72 @@ int fcu_comm_join(fcu_ctx *ctx, fcu_comm *comm) {
   if (!comm->stream) return FCU_OK;   // nothing launched yet
   FCU_REQUIRE(ctx->device == comm->device, "fcu_comm_join: context on device %d, communicator on %d",
               ctx->device, comm->device);
+  const bool on = prof_on(comm, ctx);
+  if (on) {
+    CommProf &r = comm->prof[comm->prof_used];
+    r.kind = 4;
+    r.bytes = 0;
+    FCU_CHECK_CUDA(cudaEventRecord(r.ready, ctx->stream));
+  }
   FCU_CHECK_CUDA(cudaEventRecord(comm->join, comm->stream));
   FCU_CHECK_CUDA(cudaStreamWaitEvent(ctx->stream, comm->join, 0));
+  if (on) {
+    CommProf &r = comm->prof[comm->prof_used++];
+    FCU_CHECK_CUDA(cudaEventRecord(r.start, ctx->stream));
+    FCU_CHECK_CUDA(cudaEventRecord(r.end, ctx->stream));
+  }
+  return FCU_OK;
+}
+
+int fcu_comm_profile(fcu_comm *comm, int max_records) {
+  int rc = comm_usable(comm, "fcu_comm_profile");
+  if (rc) return rc;
+  FCU_REQUIRE(max_records >= 0 && max_records <= 65536, "fcu_comm_profile: %d records", max_records);
+  FCU_REQUIRE(comm->device >= 0, "fcu_comm_profile: the communicator's device is not known yet");
+  if ((rc = comm_streams(comm))) return rc;
+  FCU_CHECK_CUDA(cudaSetDevice(comm->device));
+  FCU_CHECK_CUDA(cudaStreamSynchronize(comm->stream));   // no recorded event is still pending
+  while ((int)comm->prof.size() < max_records) {
+    CommProf r;
+    FCU_CHECK_CUDA(cudaEventCreate(&r.ready));
+    FCU_CHECK_CUDA(cudaEventCreate(&r.start));
+    FCU_CHECK_CUDA(cudaEventCreate(&r.end));
+    comm->prof.push_back(r);
+  }
+  while ((int)comm->prof.size() > max_records) {
+    CommProf &r = comm->prof.back();
+    cudaEventDestroy(r.ready);
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.end);
+    comm->prof.pop_back();
+  }
+  comm->prof_used = 0;
+  return FCU_OK;
+}
+
+int fcu_comm_profile_read(fcu_comm *comm, double *out, int max_records, int *n_out) {
+  FCU_REQUIRE(comm != nullptr && n_out != nullptr && (out != nullptr || max_records == 0),
+              "fcu_comm_profile_read: null argument");
+  *n_out = 0;
+  if (comm->prof_used == 0) return FCU_OK;
+  FCU_CHECK_CUDA(cudaSetDevice(comm->device));
+  for (int i = 0; i < comm->prof_used; i++) FCU_CHECK_CUDA(cudaEventSynchronize(comm->prof[i].end));
+  const int n = comm->prof_used < max_records ? comm->prof_used : max_records;
+  const cudaEvent_t t0 = comm->prof[0].ready;
+  for (int i = 0; i < n; i++) {
+    const CommProf &r = comm->prof[i];
+    float a = 0, b = 0, e = 0;
+    FCU_CHECK_CUDA(cudaEventElapsedTime(&a, t0, r.ready));
+    FCU_CHECK_CUDA(cudaEventElapsedTime(&b, t0, r.start));
+    FCU_CHECK_CUDA(cudaEventElapsedTime(&e, t0, r.end));
+    double *o = out + 5 * (int64_t)i;
+    o[0] = r.kind;
+    o[1] = (double)r.bytes;
+    o[2] = a;
+    o[3] = b;
+    o[4] = e;
+  }
+  *n_out = n;
   return FCU_OK;
 }
 

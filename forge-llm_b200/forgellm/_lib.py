@@ -143,6 +143,8 @@ _SIGS = {
     "fcu_allreduce_sum_f64": (_INT, [_P, _P, _P, _I64]),
     "fcu_comm_join": (_INT, [_P, _P]),
     "fcu_comm_poll": (_INT, [_P, _D]),
+    "fcu_comm_profile": (_INT, [_P, _INT]),
+    "fcu_comm_profile_read": (_INT, [_P, _P, _INT, _P]),
     "fcu_rng_init": (None, [C.POINTER(RngState), C.c_uint32]),
     "fcu_rng_next": (_D, [C.POINTER(RngState)]),
     "fcu_rng_normal": (_D, [C.POINTER(RngState)]),

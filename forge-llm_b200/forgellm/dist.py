@@ -79,6 +79,29 @@ class NcclComm:
         from ._lib import call
         call("fcu_comm_poll", self.handle, self.timeout_s if timeout_s is None else float(timeout_s))
 
+    PROFILE_KINDS = ("allreduce", "reduce_scatter", "allgather", "sum_f64", "join")
+
+    def profile(self, max_records: int) -> None:
+        """Time the next `max_records` collectives and joins (outside stream
+        capture) with CUDA events; 0 stops."""
+        from ._lib import call
+        call("fcu_comm_profile", self.handle, int(max_records))
+
+    def profile_read(self, max_records: int = 4096) -> list:
+        """The recorded collectives: [{kind, bytes, ready, start, end}] with
+        times in ms from the first record's ready time (ready: the context's
+        stream reached the call; start / end on the communicator's stream; a
+        join's end is when the context's stream could continue)."""
+        from ._lib import call
+        out = (C.c_double * (5 * max_records))()
+        n = C.c_int(0)
+        call("fcu_comm_profile_read", self.handle, out, max_records, C.byref(n))
+        recs = []
+        for i in range(n.value):
+            k, b, r, s, e = out[5 * i:5 * i + 5]
+            recs.append({"kind": self.PROFILE_KINDS[int(k)], "bytes": int(b), "ready": r, "start": s, "end": e})
+        return recs
+
     def abort(self) -> None:
         from ._lib import call
         if self.handle is not None:

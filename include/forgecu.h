@@ -505,6 +505,16 @@ int fcu_comm_join(fcu_ctx *ctx, fcu_comm *comm);
  * they have not within timeout_s, FCU_ERR_NCCL on an asynchronous error (both
  * abort the communicator). */
 int fcu_comm_poll(fcu_comm *comm, double timeout_s);
+/* Measurement (no counterpart in the reference): time the next max_records
+ * collectives and joins issued outside stream capture with CUDA events (0
+ * stops; restarting discards earlier records). */
+int fcu_comm_profile(fcu_comm *comm, int max_records);
+/* Waits for the recorded events and writes 5 doubles per record: kind (0
+ * all-reduce of fp32 gradients, 1 reduce-scatter, 2 all-gather, 3 fp64 sum,
+ * 4 join), bytes, then in ms from the first record's ready time: ready (the
+ * context's stream reached the call), start and end on the communicator's
+ * stream (for a join: when ctx's stream could continue). */
+int fcu_comm_profile_read(fcu_comm *comm, double *out, int max_records, int *n_out);
 
 /* ---------------------------------------------------------------- misc */
 /* y[i] *= alpha (data-parallel gradient averaging). */

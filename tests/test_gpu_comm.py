@@ -198,3 +198,39 @@ def test_zero1_two_ranks_sharing_one_gpu_match_replicated_adam():
         assert np.abs(rep - zero).max() <= 1e-5 * max(1.0, float(np.abs(rep).max()))
     assert np.array_equal(res[0][1], res[1][1])        # the gathers leave identical replicas
     assert np.array_equal(res[0][0], res[1][0])
+
+
+def test_one_rank_collective_profile():
+    """fcu_comm_profile / fcu_comm_profile_read: each collective and join
+    issued after profiling starts is recorded with its kind and byte count,
+    ready <= start <= end, the collectives run in issue order on the
+    communicator's stream, and a record limit drops the calls beyond it."""
+    from forgellm import _lib
+    from forgellm.autograd import ctx
+    from forgellm.dist import NcclComm
+    h = ctx().handle
+    comm = _comm1()
+    try:
+        x = torch.randn(1 << 22, device="cuda")
+        xb = x.to(torch.bfloat16)
+        _lib.call("fcu_allreduce_grads", h, comm, x.data_ptr(), x.numel())   # binds the device
+        torch.cuda.synchronize()
+        _lib.call("fcu_comm_profile", comm, 4)
+        _lib.call("fcu_allreduce_grads", h, comm, x.data_ptr(), x.numel())
+        _lib.call("fcu_reduce_scatter_grads", h, comm, x.data_ptr(), x.numel())
+        _lib.call("fcu_allgather_params", h, comm, xb.data_ptr(), xb.numel(), 2)
+        _lib.call("fcu_comm_join", h, comm)
+        _lib.call("fcu_allreduce_grads", h, comm, x.data_ptr(), x.numel())   # beyond the limit
+        torch.cuda.synchronize()
+        nc = NcclComm.__new__(NcclComm)
+        nc.handle = comm
+        recs = nc.profile_read(16)
+        assert [r["kind"] for r in recs] == ["allreduce", "reduce_scatter", "allgather", "join"]
+        assert [r["bytes"] for r in recs] == [4 * x.numel(), 4 * x.numel(), 2 * xb.numel(), 0]
+        for r in recs:
+            assert 0.0 <= r["ready"] <= r["start"] + 1e-3 and r["start"] <= r["end"] + 1e-3
+        for a, b in zip(recs[:2], recs[1:3]):
+            assert b["start"] >= a["end"] - 1e-3
+        _lib.call("fcu_comm_profile", comm, 0)
+    finally:
+        _lib.lib().fcu_comm_destroy(comm)

@@ -174,6 +174,45 @@ def test_gemm_bf16_output_modes(op, M, N, K, mode):
     assert relf(want.numpy(), got.numpy()) <= tol
 
 
+@pytest.mark.parametrize("op,M,N,K", [(2, 768, 768, 8192), (2, 4096, 768, 8192), (1, 8192, 768, 32000)])
+def test_gemm_split_k_repeats_bit_exactly(op, M, N, K):
+    """Split-K products (the weight-gradient and LM-head input-gradient shapes
+    of a batch-8 step): five launches in a row give the same bits, the output
+    matches float64 of the same bf16 operands, and an accumulating launch
+    adds exactly the product once more."""
+    import ctypes
+    from forgellm import _lib
+    from forgellm.autograd import ctx
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    A = (torch.randn(M * K, device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    B = (torch.randn(N * K, device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    out = torch.empty(M * N, device="cuda")
+    h = ctx().handle
+    outs = []
+    for _ in range(5):
+        out.fill_(float("nan"))
+        o = _lib.GemmOut(0, out.data_ptr(), 0, None, 0, 0, 0, 0.0)
+        _lib.call("fcu_gemm_bf16", h, op, A.data_ptr(), B.data_ptr(), M, N, K, ctypes.byref(o))
+        torch.cuda.synchronize()
+        outs.append(out.clone())
+    device_ok()
+    for x in outs[1:]:
+        assert torch.equal(x, outs[0])
+    Ad, Bd = A.double(), B.double()
+    if op == 1:
+        ref = Ad.view(M, K) @ Bd.view(K, N)
+    else:
+        ref = Ad.view(K, M).T @ Bd.view(K, N)
+    # the tensor cores' fp32 accumulation is not round-to-nearest: 1.8e-5
+    # relL2 measured over the 32,000-term contraction, within 1e-5 at 8,192
+    tol = EXACT if K <= 8192 else 4e-5
+    assert relf(ref.cpu().numpy(), out.double().view(M, N).cpu().numpy()) <= tol
+    o = _lib.GemmOut(0, out.data_ptr(), 1, None, 0, 0, 0, 0.0)
+    _lib.call("fcu_gemm_bf16", h, op, A.data_ptr(), B.data_ptr(), M, N, K, ctypes.byref(o))
+    torch.cuda.synchronize()
+    assert torch.equal(out, outs[0] + outs[0])
+
+
 def _gemm_out(mode, out, out2=None, aux=None):
     from forgellm import _lib
     return _lib.GemmOut(mode, out.data_ptr(), 0, None, 0, 0, 0, 0.0,
