@@ -78,6 +78,10 @@ def test_one_rank_collectives_replay_from_a_cuda_graph():
     try:
         x = torch.ones(4096, device="cuda")
         s = torch.zeros(1, dtype=torch.float64, device="cuda")
+        # one eager call first: the context's scratch (fcu_sumsq's partials) is
+        # allocated on first use, which stream capture does not allow
+        _lib.call("fcu_sumsq", ctx().handle, x.data_ptr(), x.numel(), s.data_ptr(), 0)
+        torch.cuda.synchronize()
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         graph = torch.cuda.CUDAGraph()
