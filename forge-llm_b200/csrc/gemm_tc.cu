@@ -225,8 +225,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   pdl_wait();   // the previous kernel's outputs are complete from here on
 
   // Work units: (output tile, K slice).  With split-K (p.splits > 1) unit u
-  // covers k-blocks [kb0, kb1) of tile u / splits; its partial tile goes to
-  // the workspace and a reduction kernel adds the slices in order.
+  // covers k-blocks [kb0, kb1) of slice u / num_tiles of tile u % num_tiles;
+  // its partial tile goes to the workspace and a reduction kernel adds the
+  // slices in order.  Slice-major order keeps the units in flight on the
+  // same K range, so each k-block of both operands is fetched from DRAM
+  // about once and reused from L2 by every tile that needs it.
   const int num_tiles = p.tiles_m * p.tiles_n;
   const int nk = (p.K + BK - 1) / BK;
   const int units = num_tiles * p.splits;
@@ -236,7 +239,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int it = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-      const int t = u / p.splits, sp = u - t * p.splits;
+      const int sp = u / num_tiles, t = u - sp * num_tiles;
       const int kb0 = (int)((int64_t)nk * sp / p.splits);
       const int kb1 = (int)((int64_t)nk * (sp + 1) / p.splits);
       int tm, tn;
@@ -290,7 +293,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int it = 0, ti = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ti++) {
-      const int sp = u % p.splits;
+      const int sp = u / num_tiles;
       const int kb0 = (int)((int64_t)nk * sp / p.splits);
       const int kb1 = (int)((int64_t)nk * (sp + 1) / p.splits);
       const int acc = ti & 1;
@@ -340,7 +343,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint8_t *stg = sEpi + q * 2 * EPI_BOX;
     int seq = 0;                        // boxes this warp has stored (staging buffer = seq & 1)
     for (int u = blockIdx.x; u < units; u += gridDim.x, ti++) {
-      const int t = u / p.splits, sp = u - t * p.splits;
+      const int sp = u / num_tiles, t = u - sp * num_tiles;
       int tm, tn;
       tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
       const int acc = ti & 1;
