@@ -134,7 +134,8 @@ def _cache_rows(table, b, n, block):
     return [int(table[b, p // block]) * block + p % block for p in range(n)]
 
 
-@pytest.mark.parametrize("nH,nKV,dH", [(12, 4, 64), (4, 4, 16), (16, 2, 128), (4, 2, 256)])
+@pytest.mark.parametrize("nH,nKV,dH", [(12, 4, 64), (4, 4, 16), (16, 2, 128), (4, 2, 256), (32, 8, 128),
+                                       (8, 8, 32), (6, 2, 96)])
 @pytest.mark.parametrize("paged", [False, True])
 def test_attn_decode_matches_oracle(nH, nKV, dH, paged):
     from forgellm import _lib
