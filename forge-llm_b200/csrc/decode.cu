@@ -183,6 +183,172 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(DecArgs a) {
   }
 }
 
+// The same for head dims that are a multiple of 32 (dH = 32 * E4) on 16-byte
+// aligned caches, with more rows in flight and fewer shuffles: 8 lanes share
+// a cache row (lane li holds the float4 chunks at elements c * 32 + 4 * li,
+// so each load instruction reads 128 contiguous bytes of a row), a warp
+// covers 4 rows per step and loads two steps (8 rows) before using them.  A
+// score is the lane's 4 * E4 products summed, then over its 8 lanes.  In the
+// weighted V sum each lane accumulates its chunks for its rows; the 4 row
+// groups of a warp are summed at the end.  Scores, softmax and the merge are
+// those of attn_decode_kernel.
+template <int E4, int GMAX>   // E4 = dH / 32; g <= GMAX, GMAX * E4 <= 16
+__global__ void __launch_bounds__(kDecThreads) attn_decode8_kernel(DecArgs a) {
+  pdl_trigger();
+  extern __shared__ __align__(16) float dsm[];
+  constexpr int dH = 32 * E4;
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sub = lane >> 3, li = lane & 7;
+  const int g = a.nH / a.nKV;
+  float *q_s = dsm;                                  // [g][dH]
+  float *s_s = q_s + g * dH;                         // [g][kChunk]
+  float *o_s = s_s + g * kChunk;                     // [kDecWarps][g][dH]
+  float *m_s = o_s + kDecWarps * g * dH;             // [g]
+  float *l_s = m_s + g;                              // [g]
+  pdl_wait();
+  int64_t n = a.seq_lens[b];
+  if (n < 0) n = 0;
+  if (n > a.cap) n = a.cap;                          // never past the sequence's own rows
+  const int64_t p0 = (int64_t)split * kChunk;
+  if (p0 >= n && !(split == 0 && n == 0)) return;
+  const int64_t p1 = p0 + kChunk < n ? p0 + kChunk : n;
+  const int np = (int)(p1 > p0 ? p1 - p0 : 0);
+  const int nsplit = (int)((n + kChunk - 1) / kChunk);
+  for (int i = threadIdx.x; i < g * dH; i += kDecThreads) {
+    const int hg = i / dH, e = i - hg * dH;
+    q_s[i] = a.q[(int64_t)b * a.ld_q + (int64_t)(kvh * g + hg) * dH + e];
+  }
+  __syncthreads();
+  // rows j0 + sub (r = 0) and j0 + 4 + sub (r = 1) of this warp's step
+  auto load_rows = [&](const float *cache, int j0, float4 (&v)[2][E4]) {
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+      const int j = j0 + 4 * r + sub;
+      if (j < np) {
+        const float4 *row = reinterpret_cast<const float4 *>(
+            cache + cache_row(a.table, a.max_blocks, a.block_size, b, p0 + j) * a.row_stride + (int64_t)kvh * dH);
+#pragma unroll
+        for (int c = 0; c < E4; c++) v[r][c] = row[c * 8 + li];
+      } else {
+#pragma unroll
+        for (int c = 0; c < E4; c++) v[r][c] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  };
+  for (int j0 = warp * 8; j0 < np; j0 += kDecWarps * 8) {
+    float4 kv[2][E4];
+    load_rows(a.kc, j0, kv);
+#pragma unroll
+    for (int hg = 0; hg < GMAX; hg++) {
+      if (hg < g) {
+        const float4 *qv = reinterpret_cast<const float4 *>(q_s + hg * dH);
+        float s[2] = {0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < E4; c++) {
+          const float4 qq = qv[c * 8 + li];
+#pragma unroll
+          for (int r = 0; r < 2; r++) {
+            s[r] = fmaf(qq.x, kv[r][c].x, s[r]);
+            s[r] = fmaf(qq.y, kv[r][c].y, s[r]);
+            s[r] = fmaf(qq.z, kv[r][c].z, s[r]);
+            s[r] = fmaf(qq.w, kv[r][c].w, s[r]);
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+          s[r] += __shfl_xor_sync(0xffffffffu, s[r], 1);
+          s[r] += __shfl_xor_sync(0xffffffffu, s[r], 2);
+          s[r] += __shfl_xor_sync(0xffffffffu, s[r], 4);
+          const int j = j0 + 4 * r + sub;
+          if (li == 0 && j < np) s_s[hg * kChunk + j] = s[r] * a.scale;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  // per head: the chunk's maximum, then p = exp(s - max) in place and its sum
+  for (int hg = warp; hg < g; hg += kDecWarps) {
+    float m = -INFINITY;
+    for (int j = lane; j < np; j += 32) m = fmaxf(m, s_s[hg * kChunk + j]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int j = lane; j < np; j += 32) {
+      const float p = expf(s_s[hg * kChunk + j] - m);
+      s_s[hg * kChunk + j] = p;
+      l += p;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      m_s[hg] = m;
+      l_s[hg] = l;
+    }
+  }
+  __syncthreads();
+  float4 acc[GMAX][E4];
+#pragma unroll
+  for (int hg = 0; hg < GMAX; hg++)
+#pragma unroll
+    for (int c = 0; c < E4; c++) acc[hg][c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j0 = warp * 8; j0 < np; j0 += kDecWarps * 8) {
+    float4 vv[2][E4];
+    load_rows(a.vc, j0, vv);
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+      const int j = j0 + 4 * r + sub;
+#pragma unroll
+      for (int hg = 0; hg < GMAX; hg++) {
+        if (hg < g) {
+          const float p = j < np ? s_s[hg * kChunk + j] : 0.f;
+#pragma unroll
+          for (int c = 0; c < E4; c++) {
+            acc[hg][c].x = fmaf(p, vv[r][c].x, acc[hg][c].x);
+            acc[hg][c].y = fmaf(p, vv[r][c].y, acc[hg][c].y);
+            acc[hg][c].z = fmaf(p, vv[r][c].z, acc[hg][c].z);
+            acc[hg][c].w = fmaf(p, vv[r][c].w, acc[hg][c].w);
+          }
+        }
+      }
+    }
+  }
+  // the warp's 4 row groups summed (lanes li, li + 8, li + 16, li + 24)
+#pragma unroll
+  for (int hg = 0; hg < GMAX; hg++) {
+    if (hg < g) {
+#pragma unroll
+      for (int c = 0; c < E4; c++) {
+        float4 v = acc[hg][c];
+#pragma unroll
+        for (int x = 8; x <= 16; x <<= 1) {
+          v.x += __shfl_xor_sync(0xffffffffu, v.x, x);
+          v.y += __shfl_xor_sync(0xffffffffu, v.y, x);
+          v.z += __shfl_xor_sync(0xffffffffu, v.z, x);
+          v.w += __shfl_xor_sync(0xffffffffu, v.w, x);
+        }
+        if (sub == 0) *reinterpret_cast<float4 *>(o_s + (warp * g + hg) * dH + c * 32 + 4 * li) = v;
+      }
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < g * dH; i += kDecThreads) {
+    const int hg = i / dH, e = i - hg * dH;
+    float o = 0.f;
+#pragma unroll
+    for (int w = 0; w < kDecWarps; w++) o += o_s[(w * g + hg) * dH + e];
+    const int h = kvh * g + hg;
+    if (nsplit <= 1) {
+      a.out[(int64_t)b * a.nH * dH + (int64_t)h * dH + e] = np > 0 ? o * (1.0f / l_s[hg]) : 0.f;
+    } else {
+      a.part_o[(((int64_t)b * a.nH + h) * a.splits + split) * dH + e] = o;
+      if (e == 0) {
+        float *ml = a.part_ml + (((int64_t)b * a.nH + h) * a.splits + split) * 2;
+        ml[0] = m_s[hg];
+        ml[1] = l_s[hg];
+      }
+    }
+  }
+}
+
 // Merges the chunks of every sequence longer than one chunk:
 // out = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M).
 __global__ void __launch_bounds__(128) attn_decode_combine(DecArgs a) {
@@ -314,6 +480,39 @@ int fcu_attn_decode(fcu_ctx *ctx, const float *q, int64_t ld_q, const float *k_c
   }
   dim3 grid(splits, nKV, B);
   const int g = nH / nKV, epl = (dH + 31) / 32;
+  cudaError_t e = cudaErrorInvalidValue;
+  // head dims 32 / 64 / 128 / 256 on 16-byte aligned caches: 8 lanes per row
+  int g2 = 1;
+  while (g2 < g) g2 <<= 1;
+  const int e4 = dH / 32;
+  const bool rows8 = dH % 32 == 0 && (e4 == 1 || e4 == 2 || e4 == 4 || e4 == 8) && g2 * e4 <= 16 &&
+                     row_stride % 4 == 0 && (((uintptr_t)k_cache | (uintptr_t)v_cache) & 15) == 0;
+  if (rows8) {
+    const size_t smem8 = decode_smem_bytes(g, dH, e4);
+#define FCU_DEC8_CASE(E, G)                                                                         \
+  if (e4 == E && g2 == G) {                                                                         \
+    static bool set[64] = {false};                                                                  \
+    if (!set[ctx->device & 63]) {                                                                   \
+      FCU_CHECK_CUDA(cudaFuncSetAttribute(attn_decode8_kernel<E, G>,                                \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); \
+      set[ctx->device & 63] = true;                                                                 \
+    }                                                                                               \
+    e = launch_pdl(attn_decode8_kernel<E, G>, grid, dim3(kDecThreads), smem8, ctx->stream, a);      \
+  }
+    FCU_DEC8_CASE(1, 1) FCU_DEC8_CASE(1, 2) FCU_DEC8_CASE(1, 4) FCU_DEC8_CASE(1, 8) FCU_DEC8_CASE(1, 16)
+    FCU_DEC8_CASE(2, 1) FCU_DEC8_CASE(2, 2) FCU_DEC8_CASE(2, 4) FCU_DEC8_CASE(2, 8)
+    FCU_DEC8_CASE(4, 1) FCU_DEC8_CASE(4, 2) FCU_DEC8_CASE(4, 4)
+    FCU_DEC8_CASE(8, 1) FCU_DEC8_CASE(8, 2)
+#undef FCU_DEC8_CASE
+    FCU_CHECK_CUDA(e);
+    note_launch();
+    if (splits > 1) {
+      e = launch_pdl(attn_decode_combine, dim3(nH, B), dim3(128), 0, ctx->stream, a);
+      FCU_CHECK_CUDA(e);
+      note_launch();
+    }
+    return FCU_OK;
+  }
   int gmax = 1;
   while (gmax < g) gmax <<= 1;
   int eplp = 1;
@@ -321,7 +520,6 @@ int fcu_attn_decode(fcu_ctx *ctx, const float *q, int64_t ld_q, const float *k_c
   FCU_REQUIRE(gmax * eplp <= kMaxAcc, "fcu_attn_decode: %d q heads per kv head at head dim %d is too wide",
               g, dH);
   const size_t smem = decode_smem_bytes(g, dH, eplp);
-  cudaError_t e = cudaErrorInvalidValue;
 #define FCU_DEC_CASE(E, G)                                                                          \
   if (eplp == E && gmax == G) {                                                                     \
     static bool set[64] = {false};                                                                  \
