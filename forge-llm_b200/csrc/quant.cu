@@ -126,8 +126,11 @@ constexpr int kQmvThreads = 256;
 constexpr int kQmvWarps = kQmvThreads / 32;
 constexpr int kQmvStages = 3;
 constexpr int kQmvChunk = 16384;               // bytes of rows per stage (3 CTAs per SM fit)
-constexpr int kQmvBuf = kQmvChunk + 32;        // + room for the 16-byte widening
-constexpr int kQmvHeader = 512;                // mbarriers, abort flag, row partial sums
+constexpr int kQmvChunkMax = 24576;            // a stage grown to hold 8 rows
+constexpr int kQmvPad = 32;                    // room for the 16-byte widening
+// Shared-memory header: mbarriers, abort flag, counters, the barrier path's
+// row partials at 128, the free-run partials [stages][8][MB] at 512.
+__host__ __device__ constexpr int qmv_header(int mb) { return (512 + kQmvStages * 8 * mb * 4 + 127) & ~127; }
 
 struct QmvArgs {
   const uint8_t *W;
@@ -137,6 +140,9 @@ struct QmvArgs {
   int M, rows_per_chunk;
   int64_t n_chunks;
   int *err;
+  int stage_bytes;  // bytes of rows per stage (a multiple of 16); stages are stage_bytes + 32 apart
+  int free_run;     // 1: every chunk holds whole warps' rows (or is the last) and no tail bytes:
+                    // warps run through the chunks independently (no CTA barrier per chunk)
 };
 
 // acc[m] += w * x[m][k] for the MB vectors (m < M).
@@ -370,11 +376,21 @@ __global__ void __launch_bounds__(kQmvThreads, 3) quant_matvec_kernel(QmvArgs a)
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + 64);
   float *part = reinterpret_cast<float *>(smem + 128);   // [8 warps][MB]: split rows' partials
-  uint8_t *bufs = smem + kQmvHeader;
-  float *xs = reinterpret_cast<float *>(bufs + kQmvStages * kQmvBuf);
+  unsigned *done_cnt = reinterpret_cast<unsigned *>(smem + 384);   // [stages]: warps done with the stage
+  unsigned *n_iss = reinterpret_cast<unsigned *>(smem + 400);      // [stages]: copies issued into it
+  unsigned *row_cnt = reinterpret_cast<unsigned *>(smem + 448);    // [stages][8]: warps done with a row
+  float *fpart = reinterpret_cast<float *>(smem + 512);            // [stages][8][MB]: free-run partials
+  const int buf_stride = a.stage_bytes + kQmvPad;
+  uint8_t *bufs = smem + qmv_header(MB);
+  float *xs = reinterpret_cast<float *>(bufs + kQmvStages * buf_stride);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid == 0) {
-    for (int s = 0; s < kQmvStages; s++) mbar_init(&full[s], 1);
+    for (int s = 0; s < kQmvStages; s++) {
+      mbar_init(&full[s], 1);
+      done_cnt[s] = 0;
+      n_iss[s] = 0;
+      for (int r = 0; r < kQmvWarps; r++) row_cnt[s * kQmvWarps + r] = 0;
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -399,8 +415,9 @@ __global__ void __launch_bounds__(kQmvThreads, 3) quant_matvec_kernel(QmvArgs a)
     if (a1 > tma_limit) a1 = tma_limit;
     const int st = (int)(i % kQmvStages);
     const uint32_t bytes = a1 > a0 ? (uint32_t)(a1 - a0) : 0u;
+    n_iss[st]++;
     mbar_expect_tx(&full[st], bytes);
-    if (bytes) bulk_load_1d(bufs + st * kQmvBuf, a.W + a0, bytes, &full[st]);
+    if (bytes) bulk_load_1d(bufs + st * buf_stride, a.W + a0, bytes, &full[st]);
   };
 
   if (tid == 0)
@@ -423,6 +440,86 @@ __global__ void __launch_bounds__(kQmvThreads, 3) quant_matvec_kernel(QmvArgs a)
   }
   __syncthreads();
 
+  if (a.free_run) {
+    // Each warp takes its rows of every chunk as soon as the chunk has
+    // landed (rows warp, warp + 8, ... of a chunk of 8k rows; a chunk of 1, 2
+    // or 4 rows gives each row 8, 4 or 2 warps, whose partial sums the warp
+    // that finishes the row last adds in warp order).  The warp that finishes
+    // a stage last (a shared-memory counter) refills it with the chunk
+    // kQmvStages further on.
+    bool ok = true;
+    for (int64_t i = 0; i < my_chunks; i++) {
+      const int st = (int)(i % kQmvStages);
+      if (!warp_wait(&full[st], (uint32_t)((i / kQmvStages) & 1), abort_flag)) {
+        ok = false;
+        break;
+      }
+      int64_t r0, r1;
+      chunk_rows(i, r0, r1);
+      const int64_t s0 = r0 * a.row_bytes;
+      const uint8_t *rows = bufs + st * buf_stride + (s0 & 15);
+      const int rc = (int)(r1 - r0);
+      int wpr = 1;
+      while (wpr * 2 * rc <= kQmvWarps) wpr *= 2;
+      const int groups = kQmvWarps / wpr, gi = warp / wpr, wi = warp - gi * wpr;
+      for (int lr = gi; lr < rc; lr += groups) {
+        float acc[MB];
+#pragma unroll
+        for (int m = 0; m < MB; m++) acc[m] = 0.f;
+        if (wpr == 1)   // the common case, with the unit loop's start and step known
+          row_dot<T, MB>(rows + (int64_t)lr * a.row_bytes, xs, a.K, a.M, lane, acc, 0, 1);
+        else
+          row_dot<T, MB>(rows + (int64_t)lr * a.row_bytes, xs, a.K, a.M, lane, acc, wi, wpr);
+        float v[MB];
+#pragma unroll
+        for (int m = 0; m < MB; m++) v[m] = warp_sum(acc[m]);
+        if (lane == 0) {
+          if (wpr == 1) {
+#pragma unroll
+            for (int m = 0; m < MB; m++)
+              if (m < a.M) a.Y[m * a.N + r0 + lr] = v[m];
+          } else {
+            float *pr = fpart + (st * kQmvWarps + lr * wpr) * MB;   // this row's wpr slots
+#pragma unroll
+            for (int m = 0; m < MB; m++) pr[wi * MB + m] = v[m];
+            __threadfence_block();
+            if (atomicAdd(&row_cnt[st * kQmvWarps + lr], 1u) == (unsigned)(wpr - 1)) {
+              row_cnt[st * kQmvWarps + lr] = 0;
+              __threadfence_block();
+              for (int m = 0; m < a.M && m < MB; m++) {
+                float t = 0.f;
+                for (int w = 0; w < wpr; w++) t += ((volatile float *)pr)[w * MB + m];
+                a.Y[m * a.N + r0 + lr] = t;
+              }
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();   // this warp's reads of the stage come before its count
+        if (atomicAdd(&done_cnt[st], 1u) == (unsigned)(kQmvWarps - 1)) {
+          done_cnt[st] = 0;
+          __threadfence_block();
+          if (i + kQmvStages < my_chunks) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // before the copy rewrites it
+            issue(i + kQmvStages);
+          }
+        }
+      }
+    }
+    if (!ok && lane == 0) {
+      *abort_flag = 1;
+      atomicExch(a.err, 40);
+    }
+    __syncthreads();
+    // every copy issued has landed before the CTA exits (at once on the normal path)
+    if (tid == 0)
+      for (int s = 0; s < kQmvStages; s++)
+        if (n_iss[s]) mbar_wait_drain(&full[s], (n_iss[s] - 1) & 1u);
+    return;
+  }
+
   for (int64_t i = 0; i < my_chunks; i++) {
     const int st = (int)(i % kQmvStages);
     const uint32_t ph = (uint32_t)((i / kQmvStages) & 1);
@@ -441,7 +538,7 @@ __global__ void __launch_bounds__(kQmvThreads, 3) quant_matvec_kernel(QmvArgs a)
     chunk_rows(i, r0, r1);
     const int64_t s0 = r0 * a.row_bytes, e0 = r1 * a.row_bytes;
     const int64_t a0 = s0 & ~(int64_t)15;
-    uint8_t *buf = bufs + st * kQmvBuf;
+    uint8_t *buf = bufs + st * buf_stride;
     // the tensor's last < 16 bytes, which no bulk copy covers
     const int64_t tail0 = tma_limit > a0 ? tma_limit : a0;
     if (e0 > tail0) {
@@ -525,6 +622,60 @@ int launch_matvec(fcu_ctx *ctx, int type, const QmvArgs &a, int MB, int grid, si
 }
 
 template <int T>
+int matvec_occupancy_t(int mb, size_t smem, int *out) {
+  auto query = [&](auto kernel) -> int {
+    FCU_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    FCU_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(out, kernel, kQmvThreads, smem));
+    return FCU_OK;
+  };
+  switch (mb) {
+    case 1: return query(quant_matvec_kernel<T, 1>);
+    case 2: return query(quant_matvec_kernel<T, 2>);
+    case 4: return query(quant_matvec_kernel<T, 4>);
+    case 8: return query(quant_matvec_kernel<T, 8>);
+  }
+  return FCU_ERR_ARG;
+}
+
+int matvec_occupancy_uncached(int type, int mb, size_t smem, int *out) {
+  switch (type) {
+    case kF32: return matvec_occupancy_t<kF32>(mb, smem, out);
+    case kF16: return matvec_occupancy_t<kF16>(mb, smem, out);
+    case kQ4_0: return matvec_occupancy_t<kQ4_0>(mb, smem, out);
+    case kQ5_0: return matvec_occupancy_t<kQ5_0>(mb, smem, out);
+    case kQ8_0: return matvec_occupancy_t<kQ8_0>(mb, smem, out);
+    case kQ4K: return matvec_occupancy_t<kQ4K>(mb, smem, out);
+    case kQ5K: return matvec_occupancy_t<kQ5K>(mb, smem, out);
+    case kQ6K: return matvec_occupancy_t<kQ6K>(mb, smem, out);
+  }
+  return FCU_ERR_ARG;
+}
+
+// Cached per (device, format, vectors, shared memory): the decode step calls
+// the matvec with a handful of shapes, many times.
+int matvec_occupancy(int type, int mb, size_t smem, int *out) {
+  struct Entry {
+    int dev = -1, type = -1, mb = 0;
+    size_t smem = 0;
+    int per_sm = 0;
+  };
+  static thread_local Entry cache[32];
+  static thread_local int next = 0;
+  int dev = 0;
+  FCU_CHECK_CUDA(cudaGetDevice(&dev));
+  for (const Entry &e : cache)
+    if (e.dev == dev && e.type == type && e.mb == mb && e.smem == smem) {
+      *out = e.per_sm;
+      return FCU_OK;
+    }
+  int rc = matvec_occupancy_uncached(type, mb, smem, out);
+  if (rc) return rc;
+  cache[next] = Entry{dev, type, mb, smem, *out};
+  next = (next + 1) % 32;
+  return FCU_OK;
+}
+
+template <int T>
 void launch_dequant_t(cudaStream_t st, int grid, const uint8_t *W, int64_t N, int64_t K, int64_t rb,
                       const int32_t *rows, int64_t nrows, float *out) {
   dequant_rows_kernel<T><<<grid, 256, 0, st>>>(W, N, K, rb, rows, nrows, out);
@@ -557,22 +708,32 @@ int fcu_quant_matvec(fcu_ctx *ctx, int type, const void *W, int64_t N, int64_t K
   const int64_t rb = fcu_ggml_row_bytes(type, K);
   FCU_REQUIRE(rb <= kQmvChunk, "fcu_quant_matvec: a row of %lld bytes exceeds the %d-byte stage",
               (long long)rb, kQmvChunk);
+  // a stage holds 8 rows (one per warp), else 4 (two warps per row), where
+  // that fits in kQmvChunkMax
+  int64_t stage = kQmvChunk;
+  for (int rows = kQmvWarps; rows >= 4; rows /= 2)
+    if (rb * rows <= kQmvChunkMax) {
+      if (rb * rows > stage) stage = (rb * rows + 15) & ~(int64_t)15;
+      break;
+    }
   FCU_REQUIRE(K <= 24576, "fcu_quant_matvec: K=%lld exceeds 24576", (long long)K);
   int *err = nullptr;
   int rc = tc_error_word(ctx, &err);
   if (rc) return rc;
   // vectors per launch: as many as fit beside the stages (<= 8)
-  const int64_t x_budget = 227 * 1024 - kQmvHeader - kQmvStages * kQmvBuf;
+  const int64_t x_budget = 227 * 1024 - qmv_header(8) - kQmvStages * (stage + kQmvPad);
   int MB = 8;
   while (MB > 1 && (int64_t)MB * (K + K / 16) * 4 > x_budget) MB >>= 1;
   // rows per chunk: whole warps' worth (a multiple of 8) where rows are
   // narrow, fewer (each split over several warps) where they are wide or the
   // tensor is small, so that every SM gets chunks
-  const int64_t rows_max = kQmvChunk / rb;
+  const int64_t rows_max = stage / rb;
   int64_t R = (N + 4 * ctx->num_sms - 1) / (4 * ctx->num_sms);
   if (R < 1) R = 1;
   if (R > rows_max) R = rows_max;
-  if (R > kQmvWarps) R -= R % kQmvWarps;
+  if (R >= kQmvWarps) R -= R % kQmvWarps;
+  else if (R > 4) R = 4;          // 1, 2 or 4 rows: whole warps per row
+  else if (R == 3) R = 2;
   QmvArgs a{};
   a.W = (const uint8_t *)W;
   a.N = N;
@@ -582,6 +743,8 @@ int fcu_quant_matvec(fcu_ctx *ctx, int type, const void *W, int64_t N, int64_t K
   a.rows_per_chunk = (int)R;
   a.n_chunks = (N + R - 1) / R;
   a.err = err;
+  a.stage_bytes = (int)stage;
+  a.free_run = (a.total_bytes & 15) == 0;
   for (int64_t m0 = 0; m0 < M; m0 += MB) {
     const int mg = (int)(M - m0 < MB ? M - m0 : MB);
     int mb = 1;
@@ -589,8 +752,12 @@ int fcu_quant_matvec(fcu_ctx *ctx, int type, const void *W, int64_t N, int64_t K
     a.X = X + m0 * K;
     a.Y = Y + m0 * N;
     a.M = mg;
-    const size_t smem = kQmvHeader + kQmvStages * kQmvBuf + (size_t)mb * K * 4 + (size_t)mb * (K / 16) * 4;
-    const int per_sm = smem <= 75 * 1024 ? 3 : smem <= 113 * 1024 ? 2 : 1;
+    const size_t smem = qmv_header(mb) + kQmvStages * (size_t)(stage + kQmvPad) + (size_t)mb * K * 4 +
+                        (size_t)mb * (K / 16) * 4;
+    int per_sm = 0;   // CTAs that are resident together on an SM (the persistent grid)
+    rc = matvec_occupancy(type, mb, smem, &per_sm);
+    if (rc) return rc;
+    if (per_sm < 1) per_sm = 1;
     int64_t grid = a.n_chunks < (int64_t)per_sm * ctx->num_sms ? a.n_chunks : (int64_t)per_sm * ctx->num_sms;
     rc = launch_matvec(ctx, type, a, mb, (int)grid, smem);
     if (rc) return rc;
