@@ -224,6 +224,58 @@ __device__ __forceinline__ void row_dot(const uint8_t *row, const float *xs, int
       scale_min_hdr(2 * j, hd.y, hd.z, hd.w, sc0, mn0);
       scale_min_hdr(2 * j + 1, hd.y, hd.z, hd.w, sc1, mn1);
       const int64_t klo = (int64_t)sb * 256 + j * 64 + 16 * h;
+      if constexpr (MB <= 4) {
+      // packed f32x2 sums: (even, odd) elements of the even / odd float4s,
+      // four short FMA chains per half
+      float2 slo[MB][2], shi[MB][2];
+#pragma unroll
+      for (int m = 0; m < MB; m++)
+        slo[m][0] = slo[m][1] = shi[m][0] = shi[m][1] = make_float2(0.f, 0.f);
+      const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+      const uint32_t hw[4] = {qhv.x, qhv.y, qhv.z, qhv.w};
+      const float2 bias = make_float2(-8388608.0f, -8388608.0f);
+#pragma unroll
+      for (int f = 0; f < 4; f++) {
+        uint32_t lo = qw[f] & 0x0F0F0F0Fu, hi = (qw[f] >> 4) & 0x0F0F0F0Fu;
+        if (T == kQ5K) {   // bit 2j (low) / 2j+1 (high) of each qh byte is the 5th bit
+          lo |= ((hw[f] >> (2 * j)) & 0x01010101u) << 4;
+          hi |= ((hw[f] >> (2 * j + 1)) & 0x01010101u) << 4;
+        }
+        // the bytes as 2^23 + q, the 2^23 removed two at a time
+        float2 ql[2], qh[2];
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          ql[e] = add2(make_float2(__int_as_float((int)__byte_perm(lo, 0x4B000000u, 0x7650u | (2 * e))),
+                                   __int_as_float((int)__byte_perm(lo, 0x4B000000u, 0x7650u | (2 * e + 1)))),
+                       bias);
+          qh[e] = add2(make_float2(__int_as_float((int)__byte_perm(hi, 0x4B000000u, 0x7650u | (2 * e))),
+                                   __int_as_float((int)__byte_perm(hi, 0x4B000000u, 0x7650u | (2 * e + 1)))),
+                       bias);
+        }
+#pragma unroll
+        for (int m = 0; m < MB; m++)
+          if (m < M) {
+            const float4 xl = *reinterpret_cast<const float4 *>(xs + m * K + xs_swz<T>(klo + 4 * f));
+            const float4 xh = *reinterpret_cast<const float4 *>(xs + m * K + xs_swz<T>(klo + 32 + 4 * f));
+            float2 &sl = slo[m][f & 1], &sh = shi[m][f & 1];
+            sl = fma2(ql[0], make_float2(xl.x, xl.y), sl);
+            sl = fma2(ql[1], make_float2(xl.z, xl.w), sl);
+            sh = fma2(qh[0], make_float2(xh.x, xh.y), sh);
+            sh = fma2(qh[1], make_float2(xh.z, xh.w), sh);
+          }
+      }
+      const float d1 = d * sc0, n1 = dmin * mn0, d2 = d * sc1, n2 = dmin * mn1;
+#pragma unroll
+      for (int m = 0; m < MB; m++)
+        if (m < M) {
+          const float xl = xsum[m * (K >> 4) + (klo >> 4)], xh = xsum[m * (K >> 4) + (klo >> 4) + 2];
+          const float2 l2 = add2(slo[m][0], slo[m][1]), h2 = add2(shi[m][0], shi[m][1]);
+          acc[m] = fmaf(d1, l2.x + l2.y, acc[m]);
+          acc[m] = fmaf(-n1, xl, acc[m]);
+          acc[m] = fmaf(d2, h2.x + h2.y, acc[m]);
+          acc[m] = fmaf(-n2, xh, acc[m]);
+        }
+      } else {   // 8 vectors: scalar sums (the packed ones would spill)
       // two partial sums per half (even / odd float4) keep the FMA chains short
       float slo[MB][2], shi[MB][2];
 #pragma unroll
@@ -269,6 +321,7 @@ __device__ __forceinline__ void row_dot(const uint8_t *row, const float *xs, int
           acc[m] = fmaf(d2, shi[m][0] + shi[m][1], acc[m]);
           acc[m] = fmaf(-n2, xh, acc[m]);
         }
+      }
     }
   } else if (T == kQ6K) {
     const int half = lane >> 4, l0 = (lane & 15) * 2, is = l0 >> 4;
@@ -314,6 +367,29 @@ __device__ __forceinline__ void row_dot(const uint8_t *row, const float *xs, int
       if constexpr (T == kQ8_0) {
         // d * sum(q x): int8 q as a float by one byte permute into 2^23's
         // exponent (q + 128 after the sign flip), then the bias removed
+        if constexpr (MB <= 4) {
+        float2 q[4];
+        const float2 bias = make_float2(-8388736.0f, -8388736.0f);
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          const uint32_t v = ld16(b + 2 + o + e);
+          q[e / 2] = add2(make_float2(__int_as_float((int)(__byte_perm(v, 0x4B000000u, 0x7650u) ^ 0x80u)),
+                                      __int_as_float((int)(__byte_perm(v, 0x4B000000u, 0x7651u) ^ 0x80u))),
+                          bias);
+        }
+        const int64_t k = blk * 32 + o;
+#pragma unroll
+        for (int m = 0; m < MB; m++)
+          if (m < M) {
+            const float4 x0 = *reinterpret_cast<const float4 *>(xs + m * K + xs_swz<T>(k));
+            const float4 x1 = *reinterpret_cast<const float4 *>(xs + m * K + xs_swz<T>(k + 4));
+            float2 sa = mul2(q[0], make_float2(x0.x, x0.y)), sb = mul2(q[2], make_float2(x1.x, x1.y));
+            sa = fma2(q[1], make_float2(x0.z, x0.w), sa);
+            sb = fma2(q[3], make_float2(x1.z, x1.w), sb);
+            const float2 t = add2(sa, sb);
+            acc[m] = fmaf(d, t.x + t.y, acc[m]);
+          }
+        } else {
         float q[8];
 #pragma unroll
         for (int e = 0; e < 8; e += 2) {
@@ -336,6 +412,7 @@ __device__ __forceinline__ void row_dot(const uint8_t *row, const float *xs, int
             sb = fmaf(q[7], x1.w, sb);
             acc[m] = fmaf(d, sa + sb, acc[m]);
           }
+        }
       } else {
         // byte 2 + j/2, nibble j&1 (the reference's reading of these blocks)
         float w[8];
