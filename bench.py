@@ -48,13 +48,13 @@ GEMM_DRAM_BY_SHAPE = {
     "gateup_fwd": (110621952, 480962304),
     "down_fwd": (272200192, 161538048),
     "down_dx": (103938560, 214766336),
-    "down_dw": (608569088, 42380800),
+    "down_dw": (400041728, 25601280),
     "gateup_dx": (693938944, 177318400),
-    "gateup_dw": (1263725312, 42735616),
+    "gateup_dw": (721460992, 41953792),
     "wo_dx": (101913600, 59498240),
-    "wo_dw": (335384832, 23501824),
+    "wo_dw": (207480064, 22033920),
     "qkv_dx": (169878528, 154056704),
-    "qkv_dw": (485890560, 22544896),
+    "qkv_dw": (281069312, 22850816),
     "logits_fwd": (418706432, 2039416576),
     "lm_dx": (1302358784, 41938176),
     "lm_dw": (1562301952, 86944768),
@@ -496,24 +496,26 @@ def run_decode(args):
     tr = F.Transformer(cfg).loadWeights(w)
     wbytes = tr.tokEmb.bytesSize() + sum(q.bytesSize() for L in tr.layers for k, q in L.items()
                                          if isinstance(q, I.QuantLinear))
-    for B in (1, 32):
-        cache = F.KVCache(cfg.nLayers, cfg.maxSeq, cfg.kvDim, batch=B)
-        toks = [int(x) for x in F.RNG(5).ints(B, cfg.vocabSize)]
-        state = {"pos": 0}
+    for graph in (False, True):
+        for B in (1, 32):
+            cache = F.KVCache(cfg.nLayers, cfg.maxSeq, cfg.kvDim, batch=B)
+            toks = [int(x) for x in F.RNG(5).ints(B, cfg.vocabSize)]
+            state = {"pos": 0}
 
-        def step():
-            p = state["pos"] % 512 + 256          # positions 256..767: a half-filled cache
-            tr.forwardBatch(toks, [p] * B, cache)
-            state["pos"] += 1
+            def step():
+                p = state["pos"] % 512 + 256          # positions 256..767: a half-filled cache
+                tr.forwardBatch(toks, [p] * B, cache, graph=graph)
+                state["pos"] += 1
 
-        for p in range(256):                      # fill the first 256 positions
-            tr.forwardBatch(toks, [p] * B, cache)
-        ms = _time_ms(step, args.steps, args.warmup)
-        print(json.dumps({"config": "decode", "kernel": "Transformer.forwardBatch (config-5 model, Q4_K)",
-                          "B": B, "metric": "decode tokens/s", "value": B / (ms / 1e3), "unit": "tokens/s",
-                          "ms_per_step": ms, "weight_bytes": wbytes,
-                          "weights_gb_per_s": wbytes / 1e9 / (ms / 1e3),
-                          "note": "eager host loop: 12 layers x 11 launches + embed / head per step"}), flush=True)
+            for p in range(256):                      # fill the first 256 positions
+                tr.forwardBatch(toks, [p] * B, cache, graph=graph)
+            ms = _time_ms(step, args.steps, args.warmup)
+            note = ("CUDA graph replay of the step (tokens and positions copied in first)" if graph else
+                    "eager host loop: 12 layers x 11 launches + embed / head per step")
+            print(json.dumps({"config": "decode", "kernel": "Transformer.forwardBatch (config-5 model, Q4_K)",
+                              "B": B, "graph": graph, "metric": "decode tokens/s", "value": B / (ms / 1e3),
+                              "unit": "tokens/s", "ms_per_step": ms, "weight_bytes": wbytes,
+                              "weights_gb_per_s": wbytes / 1e9 / (ms / 1e3), "note": note}), flush=True)
 
 
 def profile_collectives(F, AD, model, opt, dp, batch):

@@ -258,22 +258,60 @@ class Transformer:
                                      lens=torch.empty(B, dtype=torch.int32, device=dev))
         return b
 
-    def forward(self, token: int, pos: int, cache: KVCache) -> torch.Tensor:
+    def forward(self, token: int, pos: int, cache: KVCache, graph: bool = False) -> torch.Tensor:
         """One token at position pos (transformer.js:134-185): logits [vocab]."""
-        return self.forwardBatch([token], [pos], cache)[0]
+        return self.forwardBatch([token], [pos], cache, graph=graph)[0]
 
-    def forwardBatch(self, tokens, positions, cache: KVCache) -> torch.Tensor:
+    def forwardBatch(self, tokens, positions, cache: KVCache, graph: bool = False) -> torch.Tensor:
+        """Logits [B, vocab] of one decode step.  graph=True replays the step
+        as a CUDA graph: the first call for a (batch size, cache) pair runs
+        op by op and captures the same launches; later calls copy the tokens
+        and positions into the step's device buffers and replay, which removes
+        the ~140 host launches per step.  The returned logits buffer is
+        rewritten by the next step."""
         c = self.cfg
         B = len(tokens)
         if B > cache.batch:
             raise ValueError(f"{B} sequences for a cache of {cache.batch}")
         bf = self._buffers(B)
-        h = ctx().handle
         host = np.array([list(tokens), list(positions), [p + 1 for p in positions]], np.int32)
         dev_host = torch.from_numpy(host)
         bf["ids"].copy_(dev_host[0])
         bf["pos"].copy_(dev_host[1])
         bf["lens"].copy_(dev_host[2])
+        cache.len = max(cache.len, max(positions) + 1)
+        if not graph:
+            return self._step(B, cache)
+        from ._lib import lib
+        import ctypes
+        graphs = self.__dict__.setdefault("_graphs", {})
+        key = (B, id(cache))
+        scr = ctypes.c_size_t(0)
+        lib().fcu_ctx_scratch_bytes(ctx().handle, ctypes.byref(scr))
+        g = graphs.get(key)
+        # a graph holds the context scratch's address: if the scratch has
+        # grown since the capture, capture again
+        if g is not None and g[1] == scr.value and g[2] is cache.k:
+            g[0].replay()
+            return bf["logits"]
+        out = self._step(B, cache)          # this step, op by op (sizes every workspace)
+        lib().fcu_ctx_scratch_bytes(ctx().handle, ctypes.byref(scr))
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        graph_ = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph_, stream=side):
+                self._step(B, cache)
+        torch.cuda.current_stream().wait_stream(side)
+        ctx()                               # the context follows the caller's stream again
+        graphs[key] = (graph_, scr.value, cache.k)
+        return out
+
+    def _step(self, B: int, cache: KVCache) -> torch.Tensor:
+        """The launches of one decode step on the step's device buffers."""
+        c = self.cfg
+        bf = self._bufs[B]
+        h = ctx().handle
         D, dH = c.dim, c.dHead
         x, xb, xb2, inv, q, att = bf["x"], bf["xb"], bf["xb2"], bf["inv"], bf["q"], bf["att"]
         self.tokEmb.rows(bf["ids"], out=x)
@@ -302,5 +340,4 @@ class Transformer:
         call("fcu_rmsnorm_fwd", h, x.data_ptr(), self.lnF.data_ptr(), B, D, float(c.normEps), xb.data_ptr(),
              inv.data_ptr())
         self.wcls.forward(xb, out=bf["logits"])
-        cache.len = max(cache.len, max(positions) + 1)
         return bf["logits"]

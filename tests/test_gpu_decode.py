@@ -286,3 +286,28 @@ def test_transformer_batch_and_paged_cache_match_single_sequences():
             for s in active:
                 assert np.array_equal(logits[s], alone[s][pos[s]]), (type(cache).__name__, s, pos[s])
                 pos[s] += 1
+
+
+def test_transformer_graph_replay_matches_eager():
+    """forwardBatch(graph=True): the first step runs op by op and captures,
+    later steps replay the captured launches with new tokens and positions;
+    every step's logits equal the eager step's bit for bit (one sequence and
+    a paged batch of three)."""
+    import forgellm as F
+    cfg, _, tr = _models(O.Q4_K, O.Q8_0)
+    ids = O.RNG(31).ints(10, cfg.vocabSize)
+    eager, graphed = F.KVCache(cfg.nLayers, cfg.maxSeq, cfg.kvDim), F.KVCache(cfg.nLayers, cfg.maxSeq, cfg.kvDim)
+    for t, tok in enumerate(ids):
+        want = tr.forward(int(tok), t, eager).cpu().numpy().copy()
+        got = tr.forward(int(tok), t, graphed, graph=True).cpu().numpy()
+        assert np.array_equal(want, got), t
+    table = np.random.default_rng(7).permutation(12).astype(np.int32).reshape(3, 4)
+    pe = F.PagedKVCache(cfg.nLayers, cfg.maxSeq, cfg.kvDim, blockSize=8, batch=3, table=table)
+    pg = F.PagedKVCache(cfg.nLayers, cfg.maxSeq, cfg.kvDim, blockSize=8, batch=3, table=table)
+    seqs = [O.RNG(40 + s).ints(6, cfg.vocabSize) for s in range(3)]
+    for p in range(6):
+        toks = [int(seqs[s][p]) for s in range(3)]
+        ps = [p + s for s in range(3)]
+        want = tr.forwardBatch(toks, ps, pe).cpu().numpy().copy()
+        got = tr.forwardBatch(toks, ps, pg, graph=True).cpu().numpy()
+        assert np.array_equal(want, got), p
