@@ -48,12 +48,6 @@ constexpr float kRescaleLog2 = 8.f;
 // one pair in 4; one in 2 is slower.  The forward keeps MUFU only (its
 // softmax slowed from 246 to 260 us with one pair in 4).
 constexpr int kPolyEvery = FCU_POLY_BWD;
-// max(a, b, c) in one instruction (sm_100 three-input max.f32).
-__device__ __forceinline__ float max3f(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
 template <int kEvery>
 __device__ __forceinline__ float2 exp2_pair(float2 x, int pair) {
   if constexpr (kEvery > 0)
@@ -222,16 +216,14 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int c = 0; c < kBN; c++)
           if (c > lim) s[c] = -INFINITY;
       }
-      // Row max over 8 independent chains of three-input maxima (short
-      // dependency chains, half the instructions of pairwise fmaxf).
+      // Row max and sum over 8 independent chains (short dependency chains).
       float mx8[8];
 #pragma unroll
-      for (int u = 0; u < 8; u++) mx8[u] = max3f(s[u], s[u + 8], s[u + 16]);
+      for (int u = 0; u < 8; u++) mx8[u] = s[u];
 #pragma unroll
-      for (int c = 24; c < kBN; c += 16)
-#pragma unroll
-        for (int u = 0; u < 8; u++) mx8[u] = max3f(mx8[u], s[c + u], s[c + 8 + u]);
-      float mx = max3f(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+      for (int c = 8; c < kBN; c++) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
+      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       mx *= p.scale_log2;
       float alpha = 1.f;
       bool rescale_o = false;
@@ -241,16 +233,16 @@ __global__ void __launch_bounds__(kThreads, 2)
         m = mx;
       }
       const float neg_m = -m;
-      float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};   // packed row sums
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t pk[kBN / 2];                     // P as bf16 pairs
 #pragma unroll
       for (int c = 0; c < kBN; c += 2) {
         const float2 e = exp2_pair<0>(fma2(make_float2(s[c], s[c + 1]), make_float2(p.scale_log2, p.scale_log2),
                                         make_float2(neg_m, neg_m)), c / 2);
-        rs2[(c >> 1) & 1] = add2(rs2[(c >> 1) & 1], e);
+        rs4[(c >> 1) & 3] += e.x + e.y;
         pk[c / 2] = pack2_bf16(e.x, e.y);
       }
-      const float rs = (rs2[0].x + rs2[1].x) + (rs2[0].y + rs2[1].y);
+      const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       l = l * alpha + rs;
       // PV_{j-1} must be done with P and O before P is overwritten / O rescaled.
       if (j > 0 && !warp_wait(o_done, (uint32_t)(j - 1) & 1u, abort_flag)) { ok = false; break; }
