@@ -45,9 +45,10 @@ constexpr float kRescaleLog2 = 8.f;
 // In the backward element loops one exponential pair in kPolyEvery is
 // computed on the FMA pipe (exp2_poly2) instead of the MUFU unit (0: MUFU
 // only).  Measured at config 4: dK/dV 461 -> 440 us and dQ 385 -> 377 us with
-// one pair in 4; one in 2 is slower.  The forward keeps MUFU only (its
-// softmax slowed from 246 to 260 us with one pair in 4).
+// one pair in 4; one in 2 is slower.  The forward softmax, whose issue slots
+// are scarcer, takes one pair in 8 (247 -> 236 us; one in 4: 260 us).
 constexpr int kPolyEvery = FCU_POLY_BWD;
+constexpr int kPolyEveryFwd = 8;
 template <int kEvery>
 __device__ __forceinline__ float2 exp2_pair(float2 x, int pair) {
   if constexpr (kEvery > 0)
@@ -237,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       uint32_t pk[kBN / 2];                     // P as bf16 pairs
 #pragma unroll
       for (int c = 0; c < kBN; c += 2) {
-        const float2 e = exp2_pair<0>(fma2(make_float2(s[c], s[c + 1]), make_float2(p.scale_log2, p.scale_log2),
+        const float2 e = exp2_pair<kPolyEveryFwd>(fma2(make_float2(s[c], s[c + 1]), make_float2(p.scale_log2, p.scale_log2),
                                         make_float2(neg_m, neg_m)), c / 2);
         rs4[(c >> 1) & 3] += e.x + e.y;
         pk[c / 2] = pack2_bf16(e.x, e.y);
