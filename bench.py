@@ -242,6 +242,12 @@ def run_reference(args):
                                    "over all 100M params; the reference is JavaScript and this box "
                                    "has no JS runtime, so its C restatement (oracle/) runs"},
         "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "same_config": False,
+        "note": (f"tokens/s of a bounded sample (1 sequence x {toks} tokens, fwd+bwd+Adam over all 100M "
+                 f"parameters, {threads} host threads) standing in for the 64 x 1024-token step, whose "
+                 "CPU run would take hours; at 16 tokens the per-token attention work is far smaller "
+                 "than at 1024, and the reference's own path is single-threaded JavaScript (the GPU "
+                 "arm's cpu_baseline is the 1-thread figure)"),
     }
     print(json.dumps(line), flush=True)
 
