@@ -713,7 +713,7 @@ int fcu_attn_fwd_bf16(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int 
               "fcu_attn_fwd_bf16: qkv row stride %lld", (long long)ld_qkv);
   FCU_REQUIRE(qkv && O && lse && (((uintptr_t)qkv | (uintptr_t)O) & 15) == 0,
               "fcu_attn_fwd_bf16: null or unaligned pointer");
-  if (attn_tmem_supported(dH)) return attn_fwd_tmem(ctx, qkv, ld_qkv, B, T, nH, nKV, O, lse, dH);
+  if (attn_tmem_fwd_supported(dH)) return attn_fwd_tmem(ctx, qkv, ld_qkv, B, T, nH, nKV, O, lse, dH);
   if (attn_tmem_padded(dH)) return attn_fwd_tmem_padded(ctx, qkv, ld_qkv, B, T, nH, nKV, dH, O, lse);
   const int64_t qD = (int64_t)nH * dH, kvD = (int64_t)nKV * dH;
   Args a{};

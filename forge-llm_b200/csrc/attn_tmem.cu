@@ -57,28 +57,45 @@ __device__ __forceinline__ float2 exp2_pair(float2 x, int pair) {
 }
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Shared memory map (byte offsets; tiles 1024-byte aligned for the swizzle).
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTile;           // kFwdStages tiles
-constexpr int kOffV = kOffK + kFwdStages * kTile;
-constexpr int kOffBar = kOffV + kFwdStages * kTile;
-constexpr int kSmemBytes = kOffBar + (6 + 4 * kFwdStages) * 8 + 16;
+// The forward at head dim D (64 or 128).  A [128][D] bf16 tile is D / 64
+// TMA boxes of [128 rows][64 columns] (16 KB, 1024-byte aligned for the
+// swizzle), one after the other.  D = 64: a 3-deep K/V ring and 256 TMEM
+// columns (S [0,128), O [128,192), P [192,256)), two CTAs per SM.  D = 128:
+// a 2-deep ring (the shared memory of three would exceed 227 KB) and 512
+// columns (O [128,256), P [256,320)), one CTA per SM.
+template <int D>
+struct FwdCfg {
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kTileQ = kBM * D * 2;
+  static constexpr int kTileKV = kBN * D * 2;
+  static constexpr int kStages = D == 64 ? kFwdStages : 2;
+  static constexpr uint32_t kCols = D == 64 ? 256u : 512u;
+  static constexpr int kMinBlocks = D == 64 ? 2 : 1;
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kOffQ + kTileQ;             // kStages tiles
+  static constexpr int kOffV = kOffK + kStages * kTileKV;
+  static constexpr int kOffBar = kOffV + kStages * kTileKV;
+  static constexpr int kSmemBytes = kOffBar + (6 + 4 * kStages) * 8 + 16;
+};
 
 struct FwdParams {
   int B, T, nH, nKV, n_qt;
   float scale_log2;          // softmax scale * log2(e)
-  __nv_bfloat16 *O;          // [B*T, nH*64]
+  __nv_bfloat16 *O;          // [B*T, nH*D]
   float *lse;                // [B][nH][T], natural log
   int *err;
 };
 
-__global__ void __launch_bounds__(kThreads, 2)
+template <int D>
+__global__ void __launch_bounds__(kThreads, FwdCfg<D>::kMinBlocks)
     attn_fwd_tmem_kernel(const __grid_constant__ CUtensorMap tm, FwdParams p) {
   fcu::pdl_trigger();
+  using Cfg = FwdCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem[];
-  uint8_t *sQ = smem + kOffQ, *sK = smem + kOffK, *sV = smem + kOffV;
-  uint64_t *bars = (uint64_t *)(smem + kOffBar);
-  constexpr int S = kFwdStages;
+  uint8_t *sQ = smem + Cfg::kOffQ, *sK = smem + Cfg::kOffK, *sV = smem + Cfg::kOffV;
+  uint64_t *bars = (uint64_t *)(smem + Cfg::kOffBar);
+  constexpr int S = Cfg::kStages;
+  constexpr int kBoxBytes = kBM * 64 * 2;        // one [128][64] box: 16 KB
   uint64_t *q_full = bars + 0;
   uint64_t *k_full = bars + 1, *k_empty = bars + 1 + S;         // [S] each
   uint64_t *v_full = bars + 1 + 2 * S, *v_empty = bars + 1 + 3 * S;
@@ -116,12 +133,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (!aligned) atomicExch(p.err, 10);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == 1) tmem_alloc(tmem_slot, Cfg::kCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 128, tP = tmem + 192;
+  const uint32_t tS = tmem, tO = tmem + 128, tP = tmem + 128 + D;
   pdl_wait();   // the previous kernel's outputs are complete from here on
 
   if (!aligned) {
@@ -130,18 +147,25 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---------------- TMA producer
     int nk = 0, nv = 0;
     bool ok = true;
-    mbar_expect_tx(q_full, kTile);
-    tma_load_2d(sQ, &tm, h * kD, row0 + q0, q_full);
+    mbar_expect_tx(q_full, Cfg::kTileQ);
+#pragma unroll
+    for (int a = 0; a < Cfg::kBoxes; a++) tma_load_2d(sQ + a * kBoxBytes, &tm, h * D + 64 * a, row0 + q0, q_full);
     for (int j = 0; j < nkv; j++) {
       const int s = j % S;
       const uint32_t ph = (uint32_t)(j / S) & 1u;
       if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
-      mbar_expect_tx(&k_full[s], kTile);
-      tma_load_2d(sK + s * kTile, &tm, (p.nH + kvh) * kD, row0 + j * kBN, &k_full[s]);
+      mbar_expect_tx(&k_full[s], Cfg::kTileKV);
+#pragma unroll
+      for (int a = 0; a < Cfg::kBoxes; a++)
+        tma_load_2d(sK + s * Cfg::kTileKV + a * kBoxBytes, &tm, (p.nH + kvh) * D + 64 * a, row0 + j * kBN,
+                    &k_full[s]);
       nk++;
       if (!mbar_wait(&v_empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
-      mbar_expect_tx(&v_full[s], kTile);
-      tma_load_2d(sV + s * kTile, &tm, (p.nH + p.nKV + kvh) * kD, row0 + j * kBN, &v_full[s]);
+      mbar_expect_tx(&v_full[s], Cfg::kTileKV);
+#pragma unroll
+      for (int a = 0; a < Cfg::kBoxes; a++)
+        tma_load_2d(sV + s * Cfg::kTileKV + a * kBoxBytes, &tm, (p.nH + p.nKV + kvh) * D + 64 * a,
+                    row0 + j * kBN, &v_full[s]);
       nv++;
     }
     if (!ok) {
@@ -155,11 +179,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else if (warp == 1) {
     // ---------------- MMA issuer (whole warp; elect.sync picks the issuing lane)
     const uint32_t id_s = instr_desc_bf16(0, 0, kBM, kBN);   // Q, K both K-major
-    const uint32_t id_o = instr_desc_bf16(0, 1, kBM, kD);    // P K-major, V MN-major
+    const uint32_t id_o = instr_desc_bf16(0, 1, kBM, D);     // P K-major, V MN-major
     bool ok = warp_wait(q_full, 0, abort_flag);
     const uint64_t dQ = desc_k(smem_u32(sQ));
+    // V's D / 64 boxes are its MN-major atoms, kBN rows (16 KB) apart
     const uint64_t dK0 = desc_k(smem_u32(sK)), dV0 = desc_mn(smem_u32(sV), kBN);
-    constexpr uint64_t kTileStep = kTile >> 4;
+    constexpr uint64_t kTileStep = Cfg::kTileKV >> 4, kBoxStep = kBoxBytes >> 4;
     for (int j = 0; j <= nkv && ok; j++) {
       if (j < nkv) {
         const int s = j % S;
@@ -167,9 +192,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (j > 0 && !warp_wait(s_free, (uint32_t)(j - 1) & 1u, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint64_t dK = dK0 + (uint64_t)s * kTileStep;
+        // K = D: 4 slices of 16 per 64-column box
 #pragma unroll
-        for (int k = 0; k < kD / 16; k++)
-          umma_bf16_w(tS, dQ + k * kDescKStep, dK + k * kDescKStep, id_s, k > 0 ? 1u : 0u);
+        for (int k = 0; k < D / 16; k++)
+          umma_bf16_w(tS, dQ + (k >> 2) * kBoxStep + (k & 3) * kDescKStep,
+                      dK + (k >> 2) * kBoxStep + (k & 3) * kDescKStep, id_s, k > 0 ? 1u : 0u);
         umma_commit_w(s_full);
         umma_commit_w(&k_empty[s]);
       }
@@ -252,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (__any_sync(0xffffffffu, rescale_o)) {   // warp-collective: alpha = 1 on other rows
         tc_fence_after();
 #pragma unroll
-        for (int half = 0; half < 2; half++) {
+        for (int half = 0; half < D / 32; half++) {
           uint32_t o[32];
           tmem_ld32(tO + lane_addr + half * 32, o);
 #pragma unroll
@@ -267,22 +294,25 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     if (ok && warp_wait(o_done, (uint32_t)(nkv - 1) & 1u, abort_flag)) {
       tc_fence_after();
-      float o[kD];
-      tmem_ld64(tO + lane_addr, o);
-      if (q < p.T) {
-        const float inv = 1.f / l;
-        uint4 *dst = reinterpret_cast<uint4 *>(p.O + ((int64_t)(row0 + q) * p.nH + h) * kD);
+      const float inv = 1.f / l;
 #pragma unroll
-        for (int c8 = 0; c8 < kD / 8; c8++) {
-          uint4 v;
-          v.x = pack2_bf16(o[8 * c8 + 0] * inv, o[8 * c8 + 1] * inv);
-          v.y = pack2_bf16(o[8 * c8 + 2] * inv, o[8 * c8 + 3] * inv);
-          v.z = pack2_bf16(o[8 * c8 + 4] * inv, o[8 * c8 + 5] * inv);
-          v.w = pack2_bf16(o[8 * c8 + 6] * inv, o[8 * c8 + 7] * inv);
-          dst[c8] = v;
+      for (int a = 0; a < D / 64; a++) {        // 64 columns of O at a time
+        float o[64];
+        tmem_ld64(tO + lane_addr + (uint32_t)(64 * a), o);
+        if (q < p.T) {
+          uint4 *dst = reinterpret_cast<uint4 *>(p.O + ((int64_t)(row0 + q) * p.nH + h) * D + 64 * a);
+#pragma unroll
+          for (int c8 = 0; c8 < 8; c8++) {
+            uint4 v;
+            v.x = pack2_bf16(o[8 * c8 + 0] * inv, o[8 * c8 + 1] * inv);
+            v.y = pack2_bf16(o[8 * c8 + 2] * inv, o[8 * c8 + 3] * inv);
+            v.z = pack2_bf16(o[8 * c8 + 4] * inv, o[8 * c8 + 5] * inv);
+            v.w = pack2_bf16(o[8 * c8 + 6] * inv, o[8 * c8 + 7] * inv);
+            dst[c8] = v;
+          }
         }
-        p.lse[((int64_t)b * p.nH + h) * p.T + q] = (m + log2f(l)) / kLog2e;
       }
+      if (q < p.T) p.lse[((int64_t)b * p.nH + h) * p.T + q] = (m + log2f(l)) / kLog2e;
     } else {
       ok = false;
     }
@@ -294,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+  if (warp == 1) tmem_dealloc(tmem, Cfg::kCols);
 }
 
 // ------------------------------------------------------------------ backward
@@ -1020,18 +1050,20 @@ __global__ void attn_kv_reduce64_kernel(const float *__restrict__ pk, const floa
 
 bool attn_tmem_supported(int dH) { return dH == kD; }
 
-// O [B*T, nH*64] bf16 and lse [B][nH][T] from the bf16 qkv buffer (row stride
-// ld_qkv elements: q heads, then k heads, then v heads, 64 columns each).
-int attn_fwd_tmem(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, int nH, int nKV,
-                  void *O, float *lse, int dh) {
+// O [B*T, nH*D] bf16 and lse [B][nH][T] from the bf16 qkv buffer (row stride
+// ld_qkv elements: q heads, then k heads, then v heads, D columns each; D =
+// 128 when dh is 128, else 64 with heads of dh < 64 zero-padded).
+template <int D>
+int attn_fwd_tmem_d(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, int nH, int nKV, void *O,
+                    float *lse, int dh) {
+  using Cfg = FwdCfg<D>;
   int rc = tc_get_encode();
   if (rc) return rc;
   int *err = nullptr;
   rc = tc_error_word(ctx, &err);
   if (rc) return rc;
   CUtensorMap map;
-  rc = tc_make_map(&map, qkv, (uint64_t)B * T, (uint64_t)(nH + 2 * nKV) * kD, (uint64_t)ld_qkv, 64,
-                   kBM);
+  rc = tc_make_map(&map, qkv, (uint64_t)B * T, (uint64_t)(nH + 2 * nKV) * D, (uint64_t)ld_qkv, 64, kBM);
   if (rc) return rc;
   FwdParams p{};
   p.B = B;
@@ -1045,16 +1077,22 @@ int attn_fwd_tmem(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, i
   p.err = err;
   static bool attr_set[64] = {false};
   if (!attr_set[ctx->device & 63]) {
-    FCU_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_tmem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        kSmemBytes));
+    FCU_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_tmem_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        Cfg::kSmemBytes));
     attr_set[ctx->device & 63] = true;
   }
   const int64_t grid = (int64_t)p.n_qt * nH * B;
   FCU_REQUIRE(grid <= INT32_MAX, "attention: grid too large");
-  FCU_CHECK_CUDA(launch_pdl(attn_fwd_tmem_kernel, dim3((unsigned)grid), dim3(kThreads), kSmemBytes,
+  FCU_CHECK_CUDA(launch_pdl(attn_fwd_tmem_kernel<D>, dim3((unsigned)grid), dim3(kThreads), Cfg::kSmemBytes,
                             ctx->stream, map, p));
   FCU_CHECK_LAUNCH();
   return FCU_OK;
+}
+
+int attn_fwd_tmem(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, int nH, int nKV,
+                  void *O, float *lse, int dh) {
+  if (dh == 128) return attn_fwd_tmem_d<128>(ctx, qkv, ld_qkv, B, T, nH, nKV, O, lse, dh);
+  return attn_fwd_tmem_d<64>(ctx, qkv, ld_qkv, B, T, nH, nKV, O, lse, dh);
 }
 
 // Backward from the bf16 qkv buffer, dO and O ([B*T, nH*64] bf16) and the
@@ -1164,13 +1202,13 @@ int op_buffer(fcu_ctx *ctx, size_t bytes, void **out) {
 // they produce are zero and dropped, so the padded problem is the original
 // one (the softmax scale stays 1/sqrt(dh)).
 
-// dst[r, col0 + h*64 + c] = bf16(src[r, h*dh + c]) for c < dh, 0 for dh <= c < 64
-__global__ void pack_bf16_kernel(const float *__restrict__ src, int64_t rows, int heads, int dh,
+// dst[r, col0 + h*hw + c] = bf16(src[r, h*dh + c]) for c < dh, 0 for dh <= c < hw
+__global__ void pack_bf16_kernel(const float *__restrict__ src, int64_t rows, int heads, int dh, int hw,
                                  __nv_bfloat16 *dst, int64_t ld, int col0) {
-  const int64_t n = rows * heads * (kD / 4);
+  const int64_t n = rows * heads * (hw / 4);
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t rh = i / (kD / 4);
-    const int c = (int)(i - rh * (kD / 4)) * 4;
+    const int64_t rh = i / (hw / 4);
+    const int c = (int)(i - rh * (hw / 4)) * 4;
     const int64_t r = rh / heads;
     const int h = (int)(rh - r * heads);
     uint2 u = make_uint2(0u, 0u);
@@ -1180,13 +1218,13 @@ __global__ void pack_bf16_kernel(const float *__restrict__ src, int64_t rows, in
       u.x = *reinterpret_cast<uint32_t *>(&a);
       u.y = *reinterpret_cast<uint32_t *>(&b);
     }
-    *reinterpret_cast<uint2 *>(dst + r * ld + col0 + h * kD + c) = u;
+    *reinterpret_cast<uint2 *>(dst + r * ld + col0 + h * hw + c) = u;
   }
 }
 
-// dst[r, h*dh + c] (+)= float(src[r, col0 + h*64 + c]) for c < dh
+// dst[r, h*dh + c] (+)= float(src[r, col0 + h*hw + c]) for c < dh
 __global__ void unpack_bf16_kernel(const __nv_bfloat16 *__restrict__ src, int64_t ld, int col0, int64_t rows,
-                                   int heads, int dh, float *dst, int accumulate) {
+                                   int heads, int dh, int hw, float *dst, int accumulate) {
   const int c4 = dh / 4;
   const int64_t n = rows * heads * c4;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
@@ -1194,7 +1232,7 @@ __global__ void unpack_bf16_kernel(const __nv_bfloat16 *__restrict__ src, int64_
     const int c = (int)(i - rh * c4) * 4;
     const int64_t r = rh / heads;
     const int h = (int)(rh - r * heads);
-    const uint2 u = *reinterpret_cast<const uint2 *>(src + r * ld + col0 + h * kD + c);
+    const uint2 u = *reinterpret_cast<const uint2 *>(src + r * ld + col0 + h * hw + c);
     const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.x));
     const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.y));
     float4 v = make_float4(a.x, a.y, b.x, b.y);
@@ -1236,18 +1274,19 @@ int grid_for(fcu_ctx *ctx, int64_t n) {
   return (int)((n + 255) / 256 < 16 * ctx->num_sms ? (n + 255) / 256 : 16 * ctx->num_sms);
 }
 
+// hw: the head width of the bf16 layout (64, or 128 for heads of 128)
 int pack(fcu_ctx *ctx, const float *src, int64_t rows, int heads, int dh, __nv_bfloat16 *dst, int64_t ld,
-         int col0) {
-  pack_bf16_kernel<<<grid_for(ctx, rows * heads * (kD / 4)), 256, 0, ctx->stream>>>(src, rows, heads, dh, dst,
-                                                                                     ld, col0);
+         int col0, int hw = kD) {
+  pack_bf16_kernel<<<grid_for(ctx, rows * heads * (hw / 4)), 256, 0, ctx->stream>>>(src, rows, heads, dh, hw,
+                                                                                     dst, ld, col0);
   FCU_CHECK_LAUNCH();
   return FCU_OK;
 }
 
 int unpack(fcu_ctx *ctx, const __nv_bfloat16 *src, int64_t ld, int col0, int64_t rows, int heads, int dh,
-           float *dst, int accumulate) {
-  unpack_bf16_kernel<<<grid_for(ctx, rows * heads * (dh / 4)), 256, 0, ctx->stream>>>(src, ld, col0, rows,
-                                                                                       heads, dh, dst, accumulate);
+           float *dst, int accumulate, int hw = kD) {
+  unpack_bf16_kernel<<<grid_for(ctx, rows * heads * (dh / 4)), 256, 0, ctx->stream>>>(
+      src, ld, col0, rows, heads, dh, hw, dst, accumulate);
   FCU_CHECK_LAUNCH();
   return FCU_OK;
 }
@@ -1272,19 +1311,22 @@ bool attn_tmem_op_supported(int dH, const void *a, const void *b, const void *c,
 
 int attn_fwd_op_tmem(fcu_ctx *ctx, const float *Q, const float *K, const float *V, int B, int T, int nH,
                      int nKV, int dH, float *O, float *lse) {
-  const int64_t rows = (int64_t)B * T, W = (int64_t)(nH + 2 * nKV) * kD, qD = (int64_t)nH * kD,
-                kvD = (int64_t)nKV * kD;
+  const int hw = dH == 128 ? 128 : kD;   // head width of the bf16 layout
+  const int64_t rows = (int64_t)B * T, W = (int64_t)(nH + 2 * nKV) * hw, qD = (int64_t)nH * hw,
+                kvD = (int64_t)nKV * hw;
   void *buf = nullptr;
   int rc = op_buffer(ctx, (size_t)rows * (W + qD) * sizeof(__nv_bfloat16), &buf);
   if (rc) return rc;
   __nv_bfloat16 *qkv = (__nv_bfloat16 *)buf, *Ob = qkv + rows * W;
-  if ((rc = pack(ctx, Q, rows, nH, dH, qkv, W, 0)) || (rc = pack(ctx, K, rows, nKV, dH, qkv, W, (int)qD)) ||
-      (rc = pack(ctx, V, rows, nKV, dH, qkv, W, (int)(qD + kvD))))
+  if ((rc = pack(ctx, Q, rows, nH, dH, qkv, W, 0, hw)) || (rc = pack(ctx, K, rows, nKV, dH, qkv, W, (int)qD, hw)) ||
+      (rc = pack(ctx, V, rows, nKV, dH, qkv, W, (int)(qD + kvD), hw)))
     return rc;
   rc = attn_fwd_tmem(ctx, qkv, W, B, T, nH, nKV, Ob, lse, dH);
   if (rc) return rc;
-  return unpack(ctx, Ob, qD, 0, rows, nH, dH, O, 0);
+  return unpack(ctx, Ob, qD, 0, rows, nH, dH, O, 0, hw);
 }
+
+bool attn_tmem_fwd_supported(int dH) { return dH == kD || dH == 128; }
 
 namespace {
 

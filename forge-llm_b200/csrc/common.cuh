@@ -56,10 +56,14 @@ int attn_bwd_op_tmem(fcu_ctx *ctx, const float *dO, const float *Q, const float 
                      const float *O, const float *lse, int B, int T, int nH, int nKV, int dH, float *dQ,
                      float *dK, float *dV, int accumulate);
 
-// tcgen05 attention (attn_tmem.cu) on a bf16 qkv buffer of 64-column heads;
+// tcgen05 attention (attn_tmem.cu) on a bf16 qkv buffer of 64-column heads
+// (128-column heads for the forward at dh = 128);
 // dh is the heads' true width (the softmax scale is 1/sqrt(dh); columns past
 // dh must be zero).
 bool attn_tmem_supported(int dH);
+// The forward kernel also takes heads of 128 columns (the backward kernels
+// only 64: at 128 the mma.sync backward runs).
+bool attn_tmem_fwd_supported(int dH);
 int attn_fwd_tmem(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, int nH, int nKV,
                   void *O, float *lse, int dh);
 int attn_bwd_tmem(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv, const void *O,

@@ -304,7 +304,7 @@ ATTN_BF16_BOUND = 2e-2   # bf16 Q/K/V/P/dS operands, fp32 softmax and accumulati
 
 
 @pytest.mark.parametrize("B,T,nH,nKV,dH", [(1, 64, 4, 4, 16), (2, 130, 4, 1, 64), (3, 100, 6, 2, 32),
-                                          (1, 257, 2, 2, 128), (2, 1024, 12, 4, 64)])
+                                          (1, 257, 2, 2, 128), (2, 1024, 12, 4, 64), (2, 300, 8, 2, 128)])
 def test_tc_attention_bf16_bound(B, T, nH, nKV, dH):
     import forgellm as F
     rng = O.RNG(31 + B * T + dH)
@@ -356,12 +356,15 @@ def _attn_ref64(qkv, B, T, nH, nKV, dH):
 @pytest.mark.parametrize("B,T,nH,nKV,extra,dH", [(1, 64, 2, 2, 0, 64), (2, 130, 4, 1, 0, 64), (3, 300, 6, 2, 64, 64),
                                                  (2, 1024, 12, 4, 0, 64), (1, 2048, 32, 8, 0, 64),
                                                  (1, 64, 4, 4, 0, 16), (2, 130, 4, 1, 8, 16),
-                                                 (3, 300, 6, 2, 64, 32), (2, 1024, 12, 4, 0, 32)])
+                                                 (3, 300, 6, 2, 64, 32), (2, 1024, 12, 4, 0, 32),
+                                                 (2, 130, 4, 1, 0, 128), (3, 300, 6, 2, 128, 128),
+                                                 (1, 2048, 16, 4, 0, 128)])
 def test_attn_fwd_bf16_entry(B, T, nH, nKV, extra, dH):
     """The fused path's attention forward (bf16 qkv in, bf16 O + fp32 lse out)
     against float64 attention of the same bf16 inputs: only P's and O's bf16
     rounding differ (relL2 <= 1e-2), the log-sum-exp to 1e-5.  Head dims 16
-    and 32 run the same tcgen05 kernels on zero-padded 64-column heads."""
+    and 32 run the same tcgen05 kernels on zero-padded 64-column heads, head
+    dim 128 the forward kernel's 128-column instantiation."""
     from forgellm import _lib
     from forgellm.autograd import ctx
     width = (nH + 2 * nKV) * dH
@@ -400,7 +403,8 @@ def _rope_back64(d, B, T, heads, dH, theta):
                                                  (16, 1024, 12, 4, 10000.0, 64), (40, 512, 12, 4, 10000.0, 64),
                                                  (1, 2048, 32, 8, 10000.0, 64),
                                                  (1, 64, 4, 4, 10000.0, 16), (2, 130, 4, 1, 0.0, 16),
-                                                 (3, 300, 6, 2, 10000.0, 32), (16, 256, 12, 4, 10000.0, 32)])
+                                                 (3, 300, 6, 2, 10000.0, 32), (16, 256, 12, 4, 10000.0, 32),
+                                                 (2, 130, 4, 2, 10000.0, 128)])
 def test_attn_bwd_bf16_entry(B, T, nH, nKV, theta, dH):
     """The fused path's attention backward (dq | dk | dv into the bf16 dqkv
     buffer, RoPE rotated back) against float64 autograd of the same bf16
