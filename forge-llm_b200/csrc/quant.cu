@@ -212,17 +212,26 @@ __device__ __forceinline__ void row_dot(const uint8_t *row, const float *xs, int
     const int sbl = lane >> 3, j = (lane >> 1) & 3, h = lane & 1;
     const int nsb = (int)(K >> 8);
     const float *xsum = xs + (int64_t)M * K;     // [M][K / 16]
+    // The loop runs warp-uniformly (the scale shuffles need every lane); a
+    // lane group past the row's last super-block reads super-block 0 and
+    // skips the sums.
 #pragma unroll 1
-    for (int sb = u0 * 4 + sbl; sb < nsb; sb += ustep * 4) {
-      const uint8_t *b = row + (int64_t)sb * fmt_bb(T);
+    for (int base = u0 * 4; base < nsb; base += ustep * 4) {
+      const int sb = base + sbl;
+      const bool act = sb < nsb;
+      const uint8_t *b = row + (int64_t)(act ? sb : 0) * fmt_bb(T);
       const uint4 hd = *reinterpret_cast<const uint4 *>(b);   // d, dmin, scales[12]
       const uint4 qv = *reinterpret_cast<const uint4 *>(b + (T == kQ4K ? 16 : 48) + j * 32 + 16 * h);
       uint4 qhv = make_uint4(0, 0, 0, 0);
       if (T == kQ5K) qhv = *reinterpret_cast<const uint4 *>(b + 16 + 16 * h);
       const float d = h2f(hd.x & 0xFFFFu), dmin = h2f(hd.x >> 16);
-      float sc0, mn0, sc1, mn1;
-      scale_min_hdr(2 * j, hd.y, hd.z, hd.w, sc0, mn0);
-      scale_min_hdr(2 * j + 1, hd.y, hd.z, hd.w, sc1, mn1);
+      // the 8 lanes of a super-block decode one sub-block's scale / min each
+      // (lane (j, h): sub-block 2j + h) and fetch their pair's by shuffle
+      float scm, mnm;
+      scale_min_hdr(2 * j + h, hd.y, hd.z, hd.w, scm, mnm);
+      const float sc0 = __shfl_sync(0xffffffffu, scm, lane & ~1), sc1 = __shfl_sync(0xffffffffu, scm, lane | 1);
+      const float mn0 = __shfl_sync(0xffffffffu, mnm, lane & ~1), mn1 = __shfl_sync(0xffffffffu, mnm, lane | 1);
+      if (!act) continue;
       const int64_t klo = (int64_t)sb * 256 + j * 64 + 16 * h;
       if constexpr (MB <= 4) {
       // packed f32x2 sums: (even, odd) elements of the even / odd float4s,
