@@ -332,7 +332,47 @@ __device__ __forceinline__ void row_dot(const uint8_t *row, const float *xs, int
         }
       }
     }
-  } else if (T == kQ6K) {
+  } else if (T == kQ6K && MB <= 4) {
+    // 16 lanes per super-block (two super-blocks per warp step): lane (sub,
+    // half, l0) takes elements half*128 + qd*32 + l0 .. +3 for qd = 0..3.
+    // The 4 low-nibble bytes and the 4 high-bit bytes of those elements are
+    // combined 4 at a time in 32-bit words, each byte becomes 2^23 + q by one
+    // permute, and the 2^23 + 32 offset goes in one packed add; the 16-element
+    // group's scale multiplies the group's sum.  (Blocks are 210 bytes, so
+    // the words are read as 16-bit halves.)
+    const int sub = lane >> 4, half = (lane >> 3) & 1, l0 = (lane & 7) * 4, is = l0 >> 4;
+    const int nsb = (int)(K >> 8);
+    const float2 bias = make_float2(-8388640.0f, -8388640.0f);   // -(2^23 + 32)
+#pragma unroll 2
+    for (int sb = 2 * u0 + sub; sb < nsb; sb += 2 * ustep) {
+      const uint8_t *b = row + (int64_t)sb * 210;
+      const float d = h2f(ld16(b + 208));
+      const uint8_t *qlp = b + half * 64 + l0, *qhp = b + 128 + half * 32 + l0;
+      const uint32_t qa = ld16(qlp) | (ld16(qlp + 2) << 16);          // qd 0 (low nibbles), 2 (high)
+      const uint32_t qb = ld16(qlp + 32) | (ld16(qlp + 34) << 16);    // qd 1, 3
+      const uint32_t qh = ld16(qhp) | (ld16(qhp + 2) << 16);
+      const int64_t k0 = (int64_t)sb * 256 + half * 128 + l0;
+#pragma unroll
+      for (int qd = 0; qd < 4; qd++) {
+        const uint32_t src = (qd & 1) ? qb : qa;
+        const uint32_t q4 = ((qd < 2 ? src : (src >> 4)) & 0x0F0F0F0Fu) | (((qh >> (2 * qd)) & 0x03030303u) << 4);
+        const float dq = d * (float)(int8_t)b[192 + half * 8 + is + 2 * qd];
+        const float2 w01 = add2(make_float2(__int_as_float((int)__byte_perm(q4, 0x4B000000u, 0x7650u)),
+                                            __int_as_float((int)__byte_perm(q4, 0x4B000000u, 0x7651u))),
+                                bias);
+        const float2 w23 = add2(make_float2(__int_as_float((int)__byte_perm(q4, 0x4B000000u, 0x7652u)),
+                                            __int_as_float((int)__byte_perm(q4, 0x4B000000u, 0x7653u))),
+                                bias);
+#pragma unroll
+        for (int m = 0; m < MB; m++)
+          if (m < M) {
+            const float4 x = *reinterpret_cast<const float4 *>(xs + m * K + k0 + qd * 32);
+            const float2 t = fma2(w23, make_float2(x.z, x.w), mul2(w01, make_float2(x.x, x.y)));
+            acc[m] = fmaf(dq, t.x + t.y, acc[m]);
+          }
+      }
+    }
+  } else if (T == kQ6K) {   // 8 vectors: a lane per 2 elements of 4 groups (fewer live registers)
     const int half = lane >> 4, l0 = (lane & 15) * 2, is = l0 >> 4;
     const int nsb = (int)(K >> 8);
 #pragma unroll 2
