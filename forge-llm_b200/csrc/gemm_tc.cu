@@ -42,15 +42,25 @@ constexpr int GROUP_M = 16;                     // tile raster: GROUP_M m-blocks
 // Output tile width.  128 x 256 is the main tile; 128 x 128 doubles the tile
 // count of narrow products that would otherwise leave SMs idle in the last
 // wave (few tokens per GPU), at the same operand traffic per FLOP on A.
-template <int BN_>
+//
+// PAIR: a cluster of two CTAs on two SMs computes one 256 x 256 tile with
+// tcgen05 .cta_group::2 MMAs (M = 256).  Each CTA stages its own 128 rows of
+// A and half (128 rows) of B, so a k-block costs an SM 32 KB of shared memory
+// instead of 48 KB and the ring is 6 deep instead of 4: twice the B traffic
+// per FLOP is saved and 50% more MMA time is covered by loads in flight.
+// Each CTA's TMEM receives its own 128 rows x 256 columns, which its own
+// epilogue warps write out.
+template <int BN_, bool PAIR = false>
 struct TileCfg {
-  static constexpr int BN = BN_;
-  static constexpr int STAGES = BN_ == 256 ? 4 : 6;
-  static constexpr int B_BYTES = BN_ * BK * 2;            // 32 / 16 KB
+  static constexpr int BN = BN_;                          // output columns per tile
+  static constexpr int BNL = PAIR ? BN_ / 2 : BN_;        // B rows this CTA stages
+  static constexpr int STAGES = (PAIR || BN_ != 256) ? 6 : 4;
+  static constexpr int B_BYTES = BNL * BK * 2;            // 32 / 16 KB
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 48 / 32 KB
   static constexpr uint32_t TMEM_COLS = 2 * BN_;          // 512 / 256
   static constexpr size_t SMEM_BYTES =
       1024 /*align slack*/ + (size_t)STAGES * STAGE_BYTES + EPI_BYTES + 256;
+  static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 };
 
 // Epilogue modes (what the epilogue warps do with one fp32 accumulator row):
@@ -175,19 +185,24 @@ __device__ __forceinline__ void store_chunk(const TcParams &p, int64_t gm, int n
 
 // SW selects the epilogue at compile time: 0 the generic modes, 1
 // kOutSwiGLU, 2 kOutSwiGLUBwd (each instantiation holds one epilogue, so the
-// register allocation of one does not constrain the others).
-template <int BN_, int SW>
+// register allocation of one does not constrain the others).  PAIR: launched
+// in clusters of two, one 256-row tile per cluster (see TileCfg); p.tiles_m
+// then counts 256-row tiles.
+template <int BN_, int SW, bool PAIR = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC,
                         const __grid_constant__ CUtensorMap tmC2, TcParams p) {
   fcu::pdl_trigger();
-  constexpr int BN = TileCfg<BN_>::BN;
-  constexpr int STAGES = TileCfg<BN_>::STAGES;
-  constexpr int B_BYTES = TileCfg<BN_>::B_BYTES;
-  constexpr int STAGE_BYTES = TileCfg<BN_>::STAGE_BYTES;
-  constexpr uint32_t TMEM_COLS = TileCfg<BN_>::TMEM_COLS;
+  using Cfg = TileCfg<BN_, PAIR>;
+  constexpr int BN = Cfg::BN;
+  constexpr int BNL = Cfg::BNL;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int B_BYTES = Cfg::B_BYTES;
+  constexpr int STAGE_BYTES = Cfg::STAGE_BYTES;
+  constexpr uint32_t TMEM_COLS = Cfg::TMEM_COLS;
+  constexpr int TILE_M = PAIR ? 2 * BM : BM;   // output rows per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *sA = smem;
@@ -202,6 +217,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // PAIR: rank 0 of the cluster issues the MMAs; its full barriers count the
+  // bytes both CTAs load and its tempty barriers the epilogue warps of both.
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int unit0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int ustep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
       mbar_init(&full[s], 1);
@@ -209,20 +229,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4);
+      mbar_init(&tempty[i], PAIR ? 8 : 4);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (PAIR) cluster_sync();   // both CTAs' barriers exist before either signals the other's
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
+    if (PAIR) tmem_alloc2(tmem_slot, TMEM_COLS);
+    else tmem_alloc(tmem_slot, TMEM_COLS);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();   // the previous kernel's outputs are complete from here on
+  // The barriers of the MMA-issuing CTA, as shared::cluster addresses.
+  const uint32_t full_cl = PAIR ? mapa_shared(smem_u32(full), 0) : smem_u32(full);
+  const uint32_t tempty_cl = PAIR ? mapa_shared(smem_u32(tempty), 0) : smem_u32(tempty);
 
   // Work units: (output tile, K slice).  With split-K (p.splits > 1) unit u
   // covers k-blocks [kb0, kb1) of slice u / num_tiles of tile u % num_tiles;
@@ -238,13 +263,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ---------------- TMA producer
     int it = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+    // One load into this CTA's stage; PAIR completes it on the MMA CTA's barrier.
+    auto load = [&](void *dst, const CUtensorMap *map, int c0, int c1, int s) {
+      if (PAIR) tma_load_2d_pair(dst, map, c0, c1, full_cl + 8u * (uint32_t)s);
+      else tma_load_2d(dst, map, c0, c1, &full[s]);
+    };
+    for (int u = unit0; u < units && ok; u += ustep) {
       const int sp = u / num_tiles, t = u - sp * num_tiles;
       const int kb0 = (int)((int64_t)nk * sp / p.splits);
       const int kb1 = (int)((int64_t)nk * (sp + 1) / p.splits);
       int tm, tn;
       tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
-      const int m0 = tm * BM, n0 = tn * BN;
+      // this CTA's A rows and B rows (PAIR: rank 1 takes the second half of each)
+      const int m0 = tm * TILE_M + (int)rank * BM, n0 = tn * BN + (int)rank * BNL;
       for (int kb = kb0; kb < kb1; kb++, it++) {
         const int s = it % STAGES;
         const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
@@ -252,25 +283,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ok = false;
           break;
         }
-        mbar_expect_tx(&full[s], STAGE_BYTES);
+        if (rank == 0) mbar_expect_tx(&full[s], PAIR ? 2 * STAGE_BYTES : STAGE_BYTES);
         uint8_t *a = sA + s * A_BYTES;
         uint8_t *b = sB + s * B_BYTES;
         const int k0 = kb * BK;
         if (!p.a_mn) {
-          tma_load_2d(a, &tmA, k0, m0, &full[s]);
+          load(a, &tmA, k0, m0, s);
         } else {
 #pragma unroll
-          for (int j = 0; j < BM / 64; j++) tma_load_2d(a + j * BK * 128, &tmA, m0 + 64 * j, k0, &full[s]);
+          for (int j = 0; j < BM / 64; j++) load(a + j * BK * 128, &tmA, m0 + 64 * j, k0, s);
         }
         if (SW == 1) {
           // gate rows j0.. then up rows H + j0.. of the same 128 hidden units
-          tma_load_2d(b, &tmB, k0, tn * 128, &full[s]);
-          tma_load_2d(b + 128 * 128, &tmB, k0, p.H + tn * 128, &full[s]);
+          // (PAIR: rank 0 stages the gate rows, rank 1 the up rows)
+          if (!PAIR || rank == 0) load(b, &tmB, k0, tn * 128, s);
+          if (!PAIR || rank == 1) load(PAIR ? b : b + 128 * 128, &tmB, k0, p.H + tn * 128, s);
         } else if (!p.b_mn) {
-          tma_load_2d(b, &tmB, k0, n0, &full[s]);
+          load(b, &tmB, k0, n0, s);
         } else {
 #pragma unroll
-          for (int j = 0; j < BN / 64; j++) tma_load_2d(b + j * BK * 128, &tmB, n0 + 64 * j, k0, &full[s]);
+          for (int j = 0; j < BNL / 64; j++) load(b + j * BK * 128, &tmB, n0 + 64 * j, k0, s);
         }
       }
     }
@@ -281,24 +313,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // Drain: every copy this thread issued has landed before the CTA exits.
     // The wait ignores the abort flag (another role may have set it): the
     // copies always complete, and none may still write this CTA's shared
-    // memory once it has exited.
-    for (int i = it - STAGES < 0 ? 0 : it - STAGES; i < it; i++)
-      mbar_wait_drain(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u);
+    // memory once it has exited.  PAIR: the full barriers live in rank 0 and
+    // count both CTAs' copies, so rank 0 drains for both, and the cluster
+    // barrier before exit holds rank 1 until then.
+    if (rank == 0)
+      for (int i = it - STAGES < 0 ? 0 : it - STAGES; i < it; i++)
+        mbar_wait_drain(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u);
+  } else if (warp == 1 && PAIR && rank == 1) {
+    // The peer's MMAs write this CTA's TMEM: wait for their completion
+    // (signalled by rank 0's final commit) before TMEM is freed.
+    mbar_wait_drain(mma_done, 0);
   } else if (warp == 1) {
     // ---------------- MMA issuer (whole warp; elect.sync picks the issuing lane)
-    const uint32_t idesc = instr_desc_bf16(p.a_mn, p.b_mn, BM, BN);
+    const uint32_t idesc = instr_desc_bf16(p.a_mn, p.b_mn, TILE_M, BN);
     const uint64_t dA0 = p.a_mn ? desc_mn(smem_u32(sA), BK) : desc_k(smem_u32(sA));
     const uint64_t dB0 = p.b_mn ? desc_mn(smem_u32(sB), BK) : desc_k(smem_u32(sB));
     const uint64_t kA = p.a_mn ? kDescMNStep : kDescKStep, kB = p.b_mn ? kDescMNStep : kDescKStep;
+    // PAIR: each commit arrives on this CTA's barrier and on the peer's
+    // barrier at the same offset (two commits, no multicast).
+    auto commit = [&](uint64_t *bar) {
+      if (PAIR) {
+        umma2_commit_w(smem_u32(bar));
+        umma2_commit_w(mapa_shared(smem_u32(bar), 1));
+      } else {
+        umma_commit_w(bar);
+      }
+    };
     int it = 0, ti = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ti++) {
+    for (int u = unit0; u < units && ok; u += ustep, ti++) {
       const int sp = u / num_tiles;
       const int kb0 = (int)((int64_t)nk * sp / p.splits);
       const int kb1 = (int)((int64_t)nk * (sp + 1) / p.splits);
       const int acc = ti & 1;
       const uint32_t aph = (uint32_t)(ti >> 1) & 1u;
-      if (!warp_wait(&tempty[acc], aph ^ 1u, abort_flag)) {
+      if (!(PAIR ? warp_wait_cl(&tempty[acc], aph ^ 1u, abort_flag) : warp_wait(&tempty[acc], aph ^ 1u, abort_flag))) {
         ok = false;
         break;
       }
@@ -315,18 +364,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint64_t a = dA0 + (uint64_t)s * (A_BYTES >> 4);
         const uint64_t b = dB0 + (uint64_t)s * (B_BYTES >> 4);
 #pragma unroll
-        for (int k = 0; k < BK / UMMA_K; k++)
-          umma_bf16_w(d_tmem, a + k * kA, b + k * kB, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
-        umma_commit_w(&empty[s]);  // frees the stage once these MMAs have read it
+        for (int k = 0; k < BK / UMMA_K; k++) {
+          if (PAIR) umma2_bf16_w(d_tmem, a + k * kA, b + k * kB, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+          else umma_bf16_w(d_tmem, a + k * kA, b + k * kB, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+        }
+        commit(&empty[s]);  // frees the stage once these MMAs have read it
       }
       if (!ok) break;
-      umma_commit_w(&tfull[acc]);  // accumulator complete
+      commit(&tfull[acc]);  // accumulator complete
     }
     if (!ok) {
       *abort_flag = 1;
       atomicExch(p.err, 2);
     }
-    umma_commit_w(mma_done);
+    commit(mma_done);
     mbar_wait_drain(mma_done, 0);   // every MMA issued has completed before TMEM is freed
   } else if (warp >= 2) {
     // ---------------- epilogue
@@ -342,7 +393,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int cw = bf16_out ? 64 : 32;
     uint8_t *stg = sEpi + q * 2 * EPI_BOX;
     int seq = 0;                        // boxes this warp has stored (staging buffer = seq & 1)
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ti++) {
+    // Frees accumulator `acc` for the MMA issuer (PAIR: on rank 0's barrier).
+    auto release_acc = [&](int acc) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (PAIR && rank == 1) mbar_arrive_remote(tempty_cl + 8u * (uint32_t)acc);
+        else mbar_arrive(&tempty[acc]);
+      }
+    };
+    for (int u = unit0; u < units; u += ustep, ti++) {
       const int sp = u / num_tiles, t = u - sp * num_tiles;
       int tm, tn;
       tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
@@ -353,7 +413,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       tc_fence_after();
-      const int64_t gm = (int64_t)tm * BM + row;
+      const int mrow0 = tm * TILE_M + (int)rank * BM;   // first output row of this CTA's accumulator
+      const int64_t gm = (int64_t)mrow0 + row;
       const int n0 = tn * BN;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       if (SW == 0 && !p.tma_out) {
@@ -364,12 +425,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tmem_ld32(tbase + (uint32_t)(c * 32), r);
           if (gm < p.M) store_chunk(p.splits > 1 ? part : p, gm, n0 + c * 32, r);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[acc]);
+        release_acc(acc);
         continue;
       }
-      const int m_box = tm * BM + q * 32;          // first output row of this warp's boxes
+      const int m_box = mrow0 + q * 32;            // first output row of this warp's boxes
       // One 32-row x 64-column bf16 box of packed words w through the
       // staging buffer to `map` at column x.
       auto emit_bf16 = [&](const uint32_t *w, const CUtensorMap *map, int x) {
@@ -406,11 +465,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint32_t gw[32], uw[32];
           load_bf16x64(c * 64, gw);
           load_bf16x64(128 + c * 64, uw);
-          if (c == 1) {                            // accumulator no longer needed
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[acc]);
-          }
+          if (c == 1) release_acc(acc);            // accumulator no longer needed
           emit_bf16(gw, &tmC, j0 + c * 64);
           emit_bf16(uw, &tmC, p.H + j0 + c * 64);
 #pragma unroll
@@ -463,11 +518,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               *reinterpret_cast<uint4 *>(stg + EPI_BOX + off) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
             }
           }
-          if (c == nb - 1) {                       // accumulator no longer needed
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[acc]);
-          }
+          if (c == nb - 1) release_acc(acc);       // accumulator no longer needed
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0 && m_box < p.M) {
@@ -476,11 +527,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             bulk_commit();
           }
         }
-        if (nb == 0) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[acc]);
-        }
+        if (nb == 0) release_acc(acc);
         continue;
       }
       const int nbox = min(BN, p.N - n0) > 0 ? (min(BN, p.N - n0) + cw - 1) / cw : 0;
@@ -511,11 +558,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           v[i] = __uint_as_float(r0[i]);
           v[32 + i] = bf16_out ? __uint_as_float(r1[i]) : 0.f;
         }
-        if (c == nbox - 1) {                       // accumulator no longer needed
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[acc]);
-        }
+        if (c == nbox - 1) release_acc(acc);       // accumulator no longer needed
         uint8_t *box = stg + (seq & 1) * EPI_BOX;
         if (lane == 0) bulk_wait_read<1>();        // the store that last used this buffer has read it
         __syncwarp();
@@ -549,11 +592,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         seq++;
       }
-      if (nbox == 0) {
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[acc]);
-      }
+      if (nbox == 0) release_acc(acc);
     }
     if (lane == 0) bulk_wait_all();
     if (!ok) {
@@ -562,10 +601,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   }
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  // PAIR: neither CTA exits (or frees TMEM) while the other may still signal
+  // its barriers, read its shared memory or write its TMEM.
+  if (PAIR) cluster_sync();
+  else __syncthreads();
   tc_fence_after();
   if (warp == 1) {
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if (PAIR) tmem_dealloc2(tmem_base, TMEM_COLS);
+    else tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -814,18 +858,61 @@ struct TcOut {
 
 namespace {
 
+// FORGECU_GEMM_PAIR=0 keeps every product on single-CTA tiles; =1 takes the
+// CTA-pair tile wherever the shape allows it; unset, the pair tile runs the
+// products with at least two waves of 256 x 256 tiles and no split-K.
+int pair_setting() {
+  const char *e = getenv("FORGECU_GEMM_PAIR");
+  return (e && (e[0] == '0' || e[0] == '1')) ? e[0] - '0' : -1;
+}
+
 // Launches one instantiation (its shared-memory opt-in set on first use).
-template <int BN_, int SW>
-int launch_tc(fcu_ctx *ctx, int grid, const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
+// PAIR instantiations launch in clusters of two CTAs; `units` caps the grid
+// at one cluster (PAIR) or CTA per work unit.
+template <int BN_, int SW, bool PAIR>
+int launch_tc(fcu_ctx *ctx, int units, const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
               const CUtensorMap &tc2, const TcParams &p) {
+  using Cfg = TileCfg<BN_, PAIR>;
+  auto kern = gemm_bf16_tc_kernel<BN_, SW, PAIR>;
   static bool attr_set = false;
+  static int max_clusters = 0;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = ctx->stream;
+  cfg.attrs = attr;
+  int na = 0;
+  if (PAIR) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 2;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    na++;
+  }
   if (!attr_set) {
-    FCU_CHECK_CUDA(cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN_, SW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)TileCfg<BN_>::SMEM_BYTES));
+    FCU_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM_BYTES));
+    if (PAIR) {
+      cfg.gridDim = dim3(2 * (ctx->num_sms / 2));
+      cfg.numAttrs = na;
+      FCU_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg));
+      if (max_clusters < 1) {
+        set_error("no CTA pair of the tensor-core GEMM fits on this device");
+        return FCU_ERR_UNSUPPORTED;
+      }
+    }
     attr_set = true;
   }
-  FCU_CHECK_CUDA(launch_pdl(gemm_bf16_tc_kernel<BN_, SW>, dim3(grid), dim3(NUM_THREADS), TileCfg<BN_>::SMEM_BYTES,
-                            ctx->stream, ta, tb, tc, tc2, p));
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    na++;
+  }
+  cfg.numAttrs = na;
+  const int cap = PAIR ? max_clusters : ctx->num_sms;
+  const int n = units < cap ? units : cap;
+  cfg.gridDim = dim3(PAIR ? 2 * n : n);
+  FCU_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, tc2, p));
   return FCU_OK;
 }
 
@@ -836,30 +923,40 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
                  int64_t M, int64_t N, int64_t K, const TcOut &o, int *err) {
   int rc = tc_get_encode();
   if (rc) return rc;
+  // Tile: the CTA pair (256 x 256 over two SMs) whenever the product has at
+  // least two waves of pair tiles, or a contraction long enough to split
+  // (below); otherwise single-CTA 128 x 256 tiles, or 128 x 128 where those
+  // would leave SMs idle in the last wave.
   // Split-K when a product has too few output tiles to fill the GPU twice
   // over and a long contraction (the weight gradients, whose contraction runs
   // over every token; the LM-head input gradient): each slice keeps at least
   // 16 k-blocks, so the partial-tile traffic stays small next to the MMAs.
-  // Otherwise a product that would leave SMs idle in its last wave takes the
-  // 128-wide tile (twice the tiles).
   const int nk = (int)((K + BK - 1) / BK);
-  const int64_t tiles256 = ((M + BM - 1) / BM) * ((N + 255) / 256);
   const bool swiglu = o.mode == kOutSwiGLU || o.mode == kOutSwiGLUBwd;
+  const int64_t tiles256 = ((M + BM - 1) / BM) * ((N + 255) / 256);
+  const int64_t tiles_pair = ((M + 255) / 256) * ((N + 255) / 256);
+  const int ps = pair_setting();
+  const bool pair = M > BM && ps != 0 &&
+                    (ps == 1 || tiles_pair >= ctx->num_sms || (!swiglu && nk >= 32));
+  // units that fill every SM (pair: every SM pair) twice
+  const int64_t fill = pair ? ctx->num_sms : 2 * ctx->num_sms;
+  const int64_t tiles = pair ? tiles_pair : tiles256;
   int splits = 1;
-  if (!swiglu && tiles256 < 2 * ctx->num_sms && nk >= 32) {
-    int s = (int)((2 * ctx->num_sms + tiles256 - 1) / tiles256);
+  if (!swiglu && tiles < fill && nk >= 32) {
+    int s = (int)((fill + tiles - 1) / tiles);
     s = s > 16 ? 16 : s;
     s = s > nk / 16 ? nk / 16 : s;
     if (s >= 2) splits = s;
   }
   // (the SwiGLU forward pairs gate and up halves in one 256-wide tile)
-  const int bn = (o.mode != kOutSwiGLU && splits == 1 && tiles256 < 2 * ctx->num_sms && N > 128) ? 128 : 256;
+  const int bn = (!pair && o.mode != kOutSwiGLU && splits == 1 && tiles256 < 2 * ctx->num_sms && N > 128) ? 128 : 256;
+  const uint32_t b_rows = pair ? 128u : (uint32_t)bn;   // B rows one CTA stages
   CUtensorMap ta, tb;
   int a_mn = 0, b_mn = 0;
   switch (op) {
     case GemmOp::kFwd:
       rc = tc_make_map(&ta, A, M, K, K, 64, BM);
-      if (!rc) rc = tc_make_map(&tb, B, N, K, K, 64, o.mode == kOutSwiGLU ? 128u : (uint32_t)bn);
+      if (!rc) rc = tc_make_map(&tb, B, N, K, K, 64, o.mode == kOutSwiGLU ? 128u : b_rows);
       break;
     case GemmOp::kDx:
       b_mn = 1;
@@ -889,14 +986,15 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
   p.head_dim = o.head_dim;
   p.a_mn = a_mn;
   p.b_mn = b_mn;
-  p.tiles_m = (int)((M + BM - 1) / BM);
+  const int tile_m = pair ? 2 * BM : BM;
+  p.tiles_m = (int)((M + tile_m - 1) / tile_m);
   p.tiles_n = o.mode == kOutSwiGLU ? (int)(N / 256) : (int)((N + bn - 1) / bn);
   p.H = o.mode == kOutSwiGLU ? (int)(N / 2) : (int)N;
   p.aux = o.aux;
   p.err = err;
   p.splits = splits;
   p.ws = nullptr;
-  p.ws_rows = (int)(p.tiles_m * BM);
+  p.ws_rows = p.tiles_m * tile_m;
   if (splits > 1) {
     void *w = nullptr;
     rc = partials(ctx, sizeof(float) * (size_t)splits * (size_t)p.ws_rows * (size_t)N, &w);
@@ -936,15 +1034,18 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
     }
   }
   const int units = p.tiles_m * p.tiles_n * p.splits;
-  const int grid = units < ctx->num_sms ? units : ctx->num_sms;
   const int sw = o.mode == kOutSwiGLU ? 1 : o.mode == kOutSwiGLUBwd ? 2 : 0;
-  if (bn == 256) {
-    rc = sw == 1 ? launch_tc<256, 1>(ctx, grid, ta, tb, tc, tc2, p)
-       : sw == 2 ? launch_tc<256, 2>(ctx, grid, ta, tb, tc, tc2, p)
-                 : launch_tc<256, 0>(ctx, grid, ta, tb, tc, tc2, p);
+  if (pair) {
+    rc = sw == 1 ? launch_tc<256, 1, true>(ctx, units, ta, tb, tc, tc2, p)
+       : sw == 2 ? launch_tc<256, 2, true>(ctx, units, ta, tb, tc, tc2, p)
+                 : launch_tc<256, 0, true>(ctx, units, ta, tb, tc, tc2, p);
+  } else if (bn == 256) {
+    rc = sw == 1 ? launch_tc<256, 1, false>(ctx, units, ta, tb, tc, tc2, p)
+       : sw == 2 ? launch_tc<256, 2, false>(ctx, units, ta, tb, tc, tc2, p)
+                 : launch_tc<256, 0, false>(ctx, units, ta, tb, tc, tc2, p);
   } else {
-    rc = sw == 2 ? launch_tc<128, 2>(ctx, grid, ta, tb, tc, tc2, p)
-                 : launch_tc<128, 0>(ctx, grid, ta, tb, tc, tc2, p);
+    rc = sw == 2 ? launch_tc<128, 2, false>(ctx, units, ta, tb, tc, tc2, p)
+                 : launch_tc<128, 0, false>(ctx, units, ta, tb, tc, tc2, p);
   }
   if (rc) return rc;
   FCU_CHECK_LAUNCH();

@@ -199,6 +199,106 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
       : "memory");
 }
 
+// ---- CTA pairs (cluster of 2, tcgen05 .cta_group::2).  Every tcgen05
+// instruction of a pair kernel uses .cta_group::2: the even CTA of the
+// cluster issues the MMAs, which read A rows 0..127 and B rows 0..N/2-1 from
+// its own shared memory and the rest from its peer's at the same offsets, and
+// write each CTA's 128 accumulator rows into that CTA's TMEM.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Every thread of every CTA of the cluster (converged warps).
+__device__ __forceinline__ void cluster_sync() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The shared::cluster address of `addr` (a shared::cta address) in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cl_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
+}
+
+// try_wait with cluster-scope acquire: for a barrier that threads of the
+// peer CTA arrive on.
+__device__ __forceinline__ bool mbar_try_wait_cl(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool warp_wait_cl(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+  bool ok = true;
+  if (!mbar_try_wait_cl(bar, parity)) {
+    const long long t0 = clock64();
+    while (true) {
+      if (mbar_try_wait_cl(bar, parity)) break;
+      if (*abort_flag || clock64() - t0 > kWaitCycles) {
+        ok = false;
+        break;
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
+// 2-D TMA load into this CTA's shared memory that completes on an mbarrier
+// of either CTA of the pair (bar_cl: a shared::cluster address).  No
+// multicast: each CTA loads only its own half of the operands.
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, int c0, int c1,
+                                                 uint32_t bar_cl) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(bar_cl)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma2_bf16_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred e, p;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrives on the mbarrier at shared::cluster address bar_cl (this CTA's or
+// the peer's) once every pair MMA this thread issued has completed.
+__device__ __forceinline__ void umma2_commit_w(uint32_t bar_cl) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(bar_cl)
+      : "memory");
+}
+
+// Pair allocation: one warp of each CTA of the pair executes it.
+__device__ __forceinline__ void tmem_alloc2(uint32_t *slot, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+               "r"(cols));
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+}
+
+__device__ __forceinline__ void tmem_dealloc2(uint32_t base, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols));
+}
+
 __device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t cols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                    smem_u32(slot)),

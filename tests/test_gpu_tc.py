@@ -471,3 +471,91 @@ def test_tc_attention_operator_accumulates_on_tcgen05(dH):
     for one, two in zip(*snaps):
         assert torch.isfinite(one).all()
         assert torch.equal(two, 2 * one)
+
+
+# ------------------------------------------------------------------ CTA-pair (cta_group::2) tiles
+def _gemm_case(op, M, N, K, mode, accumulate, seed):
+    """Operands and a float64 reference for one fcu_gemm_bf16 call."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    na = M * K if op != 2 else K * M
+    nb = N * K if op == 0 else K * N
+    A = torch.randn(na, device="cuda", generator=g).to(torch.bfloat16)
+    B = torch.randn(nb, device="cuda", generator=g).to(torch.bfloat16)
+    R = torch.randn(M * N, device="cuda", generator=g)
+    out0 = torch.randn(M * N, device="cuda", generator=g)
+    Ad, Bd = A.double().cpu(), B.double().cpu()
+    if op == 0:
+        ref = Ad.view(M, K) @ Bd.view(N, K).T
+    elif op == 1:
+        ref = Ad.view(M, K) @ Bd.view(K, N)
+    else:
+        ref = Ad.view(K, M).T @ Bd.view(K, N)
+    if accumulate:
+        ref += out0.double().cpu().view(M, N)
+    if mode == 1:
+        ref += R.double().cpu().view(M, N)
+    return A, B, R, out0, ref
+
+
+@pytest.mark.parametrize("op,M,N,K", [(0, 300, 520, 768),      # ragged rows and columns
+                                      (0, 1000, 1280, 768),
+                                      (1, 513, 768, 1024),     # dX layout: B MN-major
+                                      (2, 768, 512, 1024),     # dW layout: A and B MN-major
+                                      (0, 200, 256, 64)])      # second CTA of the pair past M
+@pytest.mark.parametrize("mode", [0, 1, 2, 3, 4])
+def test_gemm_pair_tile_matches_single_cta(op, M, N, K, mode, monkeypatch):
+    """The 256 x 256 CTA-pair tile (FORGECU_GEMM_PAIR=1) writes the same bits
+    as the single-CTA tiles (=0) in every output mode, and both match float64
+    of the same bf16 operands."""
+    import ctypes
+    from forgellm import _lib
+    from forgellm.autograd import ctx
+    accumulate = 1 if mode == 4 else 0
+    mode = 0 if mode == 4 else mode
+    A, B, R, out0, ref = _gemm_case(op, M, N, K, mode, accumulate, 31 * op + 7 * mode + M)
+    T_rope, hd, rc = 64, 64, 128
+    outs = {}
+    for setting in ("0", "1"):
+        monkeypatch.setenv("FORGECU_GEMM_PAIR", setting)
+        out = out0.clone() if mode < 2 else torch.zeros(M * N, device="cuda", dtype=torch.bfloat16)
+        o = _lib.GemmOut(mode, out.data_ptr(), accumulate, R.data_ptr() if mode == 1 else None,
+                         T_rope if mode == 3 else 0, rc if mode == 3 else 0, hd if mode == 3 else 0,
+                         10000.0 if mode == 3 else 0.0)
+        _lib.call("fcu_gemm_bf16", ctx().handle, op, A.data_ptr(), B.data_ptr(), M, N, K, ctypes.byref(o))
+        torch.cuda.synchronize()
+        device_ok()
+        outs[setting] = out
+    assert torch.equal(outs["0"], outs["1"])
+    if mode < 2:
+        assert relf(ref.numpy(), outs["1"].double().cpu().view(M, N).numpy()) <= EXACT
+
+
+@pytest.mark.parametrize("M,H,K", [(333, 384, 96), (1000, 2048, 768)])
+def test_gemm_pair_tile_swiglu_epilogues(M, H, K, monkeypatch):
+    """Both SwiGLU epilogues on the CTA-pair tile (rank 0 stages the gate
+    rows, rank 1 the up rows) write what the single-CTA tiles write."""
+    import ctypes
+    from forgellm import _lib
+    from forgellm.autograd import ctx
+    h = ctx().handle
+    g = torch.Generator(device="cuda").manual_seed(3 * M + H + K)
+    A = torch.randn(M * K, device="cuda", generator=g).to(torch.bfloat16)
+    B = (0.3 * torch.randn(2 * H * K, device="cuda", generator=g)).to(torch.bfloat16)
+    W = (0.3 * torch.randn(K * H, device="cuda", generator=g)).to(torch.bfloat16)
+    res = {}
+    for setting in ("0", "1"):
+        monkeypatch.setenv("FORGECU_GEMM_PAIR", setting)
+        gu = torch.full((M * 2 * H,), 7.0, device="cuda", dtype=torch.bfloat16)
+        act = torch.full((M * H,), 7.0, device="cuda", dtype=torch.bfloat16)
+        dgu = torch.full((M * 2 * H,), 7.0, device="cuda", dtype=torch.bfloat16)
+        _lib.call("fcu_gemm_bf16", h, 0, A.data_ptr(), B.data_ptr(), M, 2 * H, K,
+                  ctypes.byref(_gemm_out(_lib.OUT_BF16_SWIGLU, gu, out2=act)))
+        _lib.call("fcu_gemm_bf16", h, 1, A.data_ptr(), W.data_ptr(), M, H, K,
+                  ctypes.byref(_gemm_out(_lib.OUT_BF16_SWIGLU_BWD, dgu, aux=gu)))
+        torch.cuda.synchronize()
+        device_ok()
+        res[setting] = (gu, act, dgu)
+    for a, b in zip(res["0"], res["1"]):
+        assert torch.equal(a, b)
+    ref = A.double().view(M, K) @ B.double().view(2 * H, K).T
+    assert relf(ref.cpu().numpy(), res["1"][0].double().cpu().view(M, 2 * H).numpy()) <= 5e-3
