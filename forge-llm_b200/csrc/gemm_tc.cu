@@ -866,6 +866,63 @@ int pair_setting() {
   return (e && (e[0] == '0' || e[0] == '1')) ? e[0] - '0' : -1;
 }
 
+// Clusters of two GEMM CTAs that fit on the device at once (every pair
+// instantiation has the same block and shared-memory size).
+int pair_slots(fcu_ctx *ctx, int *out) {
+  static int slots = 0;
+  if (!slots) {
+    auto kern = gemm_bf16_tc_kernel<256, 0, true>;
+    FCU_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)TileCfg<256, true>::SMEM_BYTES));
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * (ctx->num_sms / 2));
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = TileCfg<256, true>::SMEM_BYTES;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    FCU_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    if (n < 1) {
+      set_error("no CTA pair of the tensor-core GEMM fits on this device");
+      return FCU_ERR_UNSUPPORTED;
+    }
+    slots = n;
+  }
+  *out = slots;
+  return FCU_OK;
+}
+
+// K slices for a product of `tiles` output tiles (of M x N outputs in all)
+// and nk k-blocks on `slots` concurrent units, from a cost model in units of
+// one k-block on every slot: units are dealt round-robin to the persistent
+// CTAs, so a split into sp slices costs ceil(tiles * sp / slots) waves of
+// ceil(nk / sp) k-blocks plus a fixed per-unit overhead (pipeline fill and
+// the partial tile's epilogue, about 4 k-blocks), and each slice adds its
+// partial tile's write and read-back (8 bytes per output at the copy
+// bandwidth, about 0.3 us per k-block wave).  1 = no split; at most 16
+// slices of at least 16 k-blocks each.
+int choose_splits(int64_t tiles, int nk, int64_t slots, int64_t outputs) {
+  constexpr double kUnitOverhead = 4.0;
+  const double reduce_per_slice = (double)outputs * 8.0 / 6.0e12 / 0.3e-6;
+  const int hi = nk / 16 < 16 ? nk / 16 : 16;
+  int best = 1;
+  double best_t = (double)((tiles + slots - 1) / slots) * (nk + kUnitOverhead);
+  for (int sp = 2; sp <= hi; sp++) {
+    const double t = (double)((tiles * sp + slots - 1) / slots) * ((nk + sp - 1) / sp + kUnitOverhead) +
+                     sp * reduce_per_slice;
+    if (t < best_t) {
+      best = sp;
+      best_t = t;
+    }
+  }
+  return best;
+}
+
 // Launches one instantiation (its shared-memory opt-in set on first use).
 // PAIR instantiations launch in clusters of two CTAs; `units` caps the grid
 // at one cluster (PAIR) or CTA per work unit.
@@ -875,7 +932,11 @@ int launch_tc(fcu_ctx *ctx, int units, const CUtensorMap &ta, const CUtensorMap 
   using Cfg = TileCfg<BN_, PAIR>;
   auto kern = gemm_bf16_tc_kernel<BN_, SW, PAIR>;
   static bool attr_set = false;
-  static int max_clusters = 0;
+  int max_clusters = 0;
+  if (PAIR) {
+    const int rc = pair_slots(ctx, &max_clusters);
+    if (rc) return rc;
+  }
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
   cfg.blockDim = dim3(NUM_THREADS);
@@ -892,15 +953,6 @@ int launch_tc(fcu_ctx *ctx, int units, const CUtensorMap &ta, const CUtensorMap 
   }
   if (!attr_set) {
     FCU_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM_BYTES));
-    if (PAIR) {
-      cfg.gridDim = dim3(2 * (ctx->num_sms / 2));
-      cfg.numAttrs = na;
-      FCU_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg));
-      if (max_clusters < 1) {
-        set_error("no CTA pair of the tensor-core GEMM fits on this device");
-        return FCU_ERR_UNSUPPORTED;
-      }
-    }
     attr_set = true;
   }
   if (pdl_enabled()) {
@@ -930,7 +982,8 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
   // Split-K when a product has too few output tiles to fill the GPU twice
   // over and a long contraction (the weight gradients, whose contraction runs
   // over every token; the LM-head input gradient): each slice keeps at least
-  // 16 k-blocks, so the partial-tile traffic stays small next to the MMAs.
+  // 16 k-blocks, so the partial-tile traffic stays small next to the MMAs,
+  // and the slice count is chosen for the fullest last wave.
   const int nk = (int)((K + BK - 1) / BK);
   const bool swiglu = o.mode == kOutSwiGLU || o.mode == kOutSwiGLUBwd;
   const int64_t tiles256 = ((M + BM - 1) / BM) * ((N + 255) / 256);
@@ -938,16 +991,14 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
   const int ps = pair_setting();
   const bool pair = M > BM && ps != 0 &&
                     (ps == 1 || tiles_pair >= ctx->num_sms || (!swiglu && nk >= 32));
-  // units that fill every SM (pair: every SM pair) twice
-  const int64_t fill = pair ? ctx->num_sms : 2 * ctx->num_sms;
+  int slots = ctx->num_sms;   // concurrent work units
+  if (pair) {
+    rc = pair_slots(ctx, &slots);
+    if (rc) return rc;
+  }
   const int64_t tiles = pair ? tiles_pair : tiles256;
   int splits = 1;
-  if (!swiglu && tiles < fill && nk >= 32) {
-    int s = (int)((fill + tiles - 1) / tiles);
-    s = s > 16 ? 16 : s;
-    s = s > nk / 16 ? nk / 16 : s;
-    if (s >= 2) splits = s;
-  }
+  if (!swiglu && tiles < 2 * slots && nk >= 32) splits = choose_splits(tiles, nk, slots, M * N);
   // (the SwiGLU forward pairs gate and up halves in one 256-wide tile)
   const int bn = (!pair && o.mode != kOutSwiGLU && splits == 1 && tiles256 < 2 * ctx->num_sms && N > 128) ? 128 : 256;
   const uint32_t b_rows = pair ? 128u : (uint32_t)bn;   // B rows one CTA stages
