@@ -37,27 +37,27 @@ C5 = dict(vocabSize=32000, dim=768, nLayers=12, nHeads=12, nKvHeads=4, hidden=20
           normEps=1e-5, ropeTheta=10000)
 GLOBAL_BATCH, SEQ, LR, SEED = 64, 1024, 3e-4, 5
 # DRAM bytes (read, written) of one launch of each distinct GEMM of the
-# config-5 step, from single-launch ncu captures (`bench.py --micro gemm` at
-# that shape, dram__bytes_read.sum / dram__bytes_write.sum, one pass; the
-# commands are in profiles/gemm_dram_c5_shapes.md).  The twelve per-layer
-# shapes run 12 times a step at 65,536 tokens; the three LM-head shapes were
-# captured at 16,384 tokens (a 2 GB case instead of 8 GB) and count 4 times.
+# config-5 step (batch 64), from one single-pass ncu capture of the 147 GEMM
+# launches of a step of `bench.py --steps 1 --warmup 1` (dram__bytes_read.sum /
+# dram__bytes_write.sum; the command is in profiles/gemm_dram_c5_shapes.md),
+# each shape the mean over its launches.  The twelve per-layer shapes run 12
+# times a step, the three LM-head shapes once.
 GEMM_DRAM_BY_SHAPE = {
-    "qkv_fwd": (102702336, 119859968),
-    "wo_fwd": (101916672, 143022080),
-    "gateup_fwd": (110621952, 480962304),
-    "down_fwd": (272200192, 161538048),
-    "down_dx": (103938560, 214766336),
-    "down_dw": (400041728, 25601280),
-    "gateup_dx": (693938944, 177318400),
-    "gateup_dw": (721460992, 41953792),
-    "wo_dx": (101913600, 59498240),
-    "wo_dw": (207480064, 22033920),
-    "qkv_dx": (169878528, 154056704),
-    "qkv_dw": (281069312, 22850816),
-    "logits_fwd": (418706432, 2039416576),
-    "lm_dx": (1302358784, 41938176),
-    "lm_dw": (1562301952, 86944768),
+    "qkv_fwd": (102966784, 113806336),
+    "wo_fwd": (101923178, 140066282),
+    "gateup_fwd": (107071125, 475336021),
+    "down_fwd": (271996309, 159808874),
+    "down_dx": (103879466, 208736618),
+    "down_dw": (369171861, 729685),
+    "gateup_dx": (593923242, 174608661),
+    "gateup_dw": (682318506, 19698837),
+    "wo_dx": (101923114, 56008597),
+    "wo_dw": (201403925, 361834),
+    "qkv_dx": (169844970, 149911466),
+    "qkv_dw": (275875925, 19459712),
+    "logits_fwd": (903636736, 8327181312),
+    "lm_dx": (6781332480, 194534400),
+    "lm_dw": (5208344064, 97285632),
 }
 GEMM_LAUNCHES_B64 = 12 * 12 + 3
 
@@ -67,7 +67,7 @@ def gemm_dram_bytes_per_launch_b64() -> float:
     `traffic`), from the per-shape captures above."""
     total = 0
     for k, (r, w) in GEMM_DRAM_BY_SHAPE.items():
-        total += (4 if k in ("logits_fwd", "lm_dx", "lm_dw") else 12) * (r + w)
+        total += (1 if k in ("logits_fwd", "lm_dx", "lm_dw") else 12) * (r + w)
     return total / GEMM_LAUNCHES_B64
 
 
@@ -771,7 +771,7 @@ def main():
                          "frac": achieved / peak if peak else None,
                          "peak_kind": f"bf16 dense sustained ({pk_kind})",
                          "traffic": traffic,
-                         "traffic_unit": "DRAM bytes per GEMM launch (ncu single-launch captures per shape, mean over the step's launches)",
+                         "traffic_unit": "DRAM bytes per GEMM launch (single-pass ncu capture of the step's 147 GEMM launches, mean per launch)",
                          "algorithmic_bytes_per_launch": alg_bytes,
                          "gemm_share_of_step": (gemm_ms / gemm_steps) / (ms / args.steps) if ms else None,
                          "measured": gemm_where,

@@ -86,6 +86,7 @@ struct TcParams {
   int beta;
   int a_mn, b_mn;
   int tiles_m, tiles_n;
+  int row_major;           // tile raster (tile_coords)
   int *err;
   int mode;
   const float *R;          // kOutF32Res (row stride ldc)
@@ -102,7 +103,17 @@ struct TcParams {
 
 using namespace tc;
 
-__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &tm, int &tn) {
+// Tile t of the raster.  row_major: n fastest, so the few column tiles that
+// share one row block of A run side by side in the same wave and A streams
+// from DRAM once (products a few tiles wide: every wave then holds whole
+// rows of tiles, and B, re-read by every row, stays in L2).  Otherwise
+// groups of GROUP_M row blocks swept m fastest, column by column.
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int row_major, int &tm, int &tn) {
+  if (row_major) {
+    tm = t / tiles_n;
+    tn = t - tm * tiles_n;
+    return;
+  }
   const int per_group = GROUP_M * tiles_n;
   const int g = t / per_group;
   const int first = g * GROUP_M;
@@ -273,7 +284,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int kb0 = (int)((int64_t)nk * sp / p.splits);
       const int kb1 = (int)((int64_t)nk * (sp + 1) / p.splits);
       int tm, tn;
-      tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+      tile_coords(t, p.tiles_m, p.tiles_n, p.row_major, tm, tn);
       // this CTA's A rows and B rows (PAIR: rank 1 takes the second half of each)
       const int m0 = tm * TILE_M + (int)rank * BM, n0 = tn * BN + (int)rank * BNL;
       for (int kb = kb0; kb < kb1; kb++, it++) {
@@ -405,7 +416,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int u = unit0; u < units; u += ustep, ti++) {
       const int sp = u / num_tiles, t = u - sp * num_tiles;
       int tm, tn;
-      tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+      tile_coords(t, p.tiles_m, p.tiles_n, p.row_major, tm, tn);
       const int acc = ti & 1;
       const uint32_t aph = (uint32_t)(ti >> 1) & 1u;
       if (!warp_wait(&tfull[acc], aph, abort_flag)) {
@@ -1084,6 +1095,8 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
       p.tma_out = 1;
     }
   }
+  // n-fastest raster when a wave holds at least two whole rows of tiles
+  p.row_major = 2 * p.tiles_n <= slots;
   const int units = p.tiles_m * p.tiles_n * p.splits;
   const int sw = o.mode == kOutSwiGLU ? 1 : o.mode == kOutSwiGLUBwd ? 2 : 0;
   if (pair) {
