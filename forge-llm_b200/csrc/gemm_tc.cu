@@ -542,6 +542,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         continue;
       }
       const int nbox = min(BN, p.N - n0) > 0 ? (min(BN, p.N - n0) + cw - 1) / cw : 0;
+      // The accumulator columns of box c are loaded while box c - 1 is
+      // converted and stored (r0 | r1: the box after the one in v).
+      uint32_t r0[32], r1[32];
+      if (nbox > 0) {
+        tmem_ld32_nw(tbase, r0);
+        if (bf16_out) tmem_ld32_nw(tbase + 32u, r1);
+        tmem_wait_ld_r(r0);
+        if (bf16_out) tmem_wait_ld_r(r1);
+      }
 #pragma unroll 1
       for (int c = 0; c < nbox; c++) {
         const int n = n0 + c * cw;
@@ -560,16 +569,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             cs[2 * i + 1] = make_float2(t.z, t.w);
           }
         }
-        uint32_t r0[32], r1[32];
-        tmem_ld32(tbase + (uint32_t)(c * cw), r0);
-        if (bf16_out) tmem_ld32(tbase + (uint32_t)(c * cw + 32), r1);
         float v[64];
 #pragma unroll
         for (int i = 0; i < 32; i++) {
           v[i] = __uint_as_float(r0[i]);
           v[32 + i] = bf16_out ? __uint_as_float(r1[i]) : 0.f;
         }
-        if (c == nbox - 1) release_acc(acc);       // accumulator no longer needed
+        const bool more = c + 1 < nbox;
+        if (more) {
+          tmem_ld32_nw(tbase + (uint32_t)((c + 1) * cw), r0);
+          if (bf16_out) tmem_ld32_nw(tbase + (uint32_t)((c + 1) * cw + 32), r1);
+        } else {
+          release_acc(acc);                        // every column of the accumulator is loaded
+        }
         uint8_t *box = stg + (seq & 1) * EPI_BOX;
         if (lane == 0) bulk_wait_read<1>();        // the store that last used this buffer has read it
         __syncwarp();
@@ -602,6 +614,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           bulk_commit();
         }
         seq++;
+        if (more) {
+          tmem_wait_ld_r(r0);
+          if (bf16_out) tmem_wait_ld_r(r1);
+        }
       }
       if (nbox == 0) release_acc(acc);
     }

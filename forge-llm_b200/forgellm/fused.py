@@ -27,6 +27,7 @@ copy of them (the GEMMs' weight operand) is kept current by Adam.
 from __future__ import annotations
 
 import ctypes as C
+import os
 
 import torch
 
@@ -97,9 +98,11 @@ class FusedStep:
         # bits as the standalone kernels, but off by default -- on B200 the
         # GEMM epilogue's stores already limit those short-K products, and
         # the extra g/u/act traffic there (measured at the config-5 shapes:
-        # 644 us vs 360 + 150 us forward, 842 us vs 207 + 210 us backward)
-        # costs more than the separate HBM passes it saves.
-        self.fuse_swiglu = False
+        # 644 us vs 360 + 150 us forward, 842 us vs 207 + 210 us backward;
+        # the whole batch-64 step 66.7 ms fused vs 61.9 ms with CTA-pair
+        # tiles) costs more than the separate HBM passes it saves.
+        # FORGECU_FUSE_SWIGLU=1 turns it on.
+        self.fuse_swiglu = os.environ.get("FORGECU_FUSE_SWIGLU") == "1"
         self.can_fuse_swiglu = H % 128 == 0
 
     # ------------------------------------------------------------ helpers
