@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint64_t dB0 = p.b_mn ? desc_mn(smem_u32(sB), BK) : desc_k(smem_u32(sB));
     const uint64_t kA = p.a_mn ? kDescMNStep : kDescKStep, kB = p.b_mn ? kDescMNStep : kDescKStep;
     // PAIR: each commit arrives on this CTA's barrier and on the peer's
-    // barrier at the same offset (two commits, no multicast).
+    // barrier at the same offset (two separate commits, one per CTA).
     auto commit = [&](uint64_t *bar) {
       if (PAIR) {
         umma2_commit_w(smem_u32(bar));

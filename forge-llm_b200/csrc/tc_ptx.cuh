@@ -257,8 +257,8 @@ __device__ __forceinline__ bool warp_wait_cl(uint64_t *bar, uint32_t parity, vol
 }
 
 // 2-D TMA load into this CTA's shared memory that completes on an mbarrier
-// of either CTA of the pair (bar_cl: a shared::cluster address).  No
-// multicast: each CTA loads only its own half of the operands.
+// of either CTA of the pair (bar_cl: a shared::cluster address).  Each CTA
+// loads only its own half of the operands, into its own shared memory.
 __device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, int c0, int c1,
                                                  uint32_t bar_cl) {
   asm volatile(
