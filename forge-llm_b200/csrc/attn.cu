@@ -375,9 +375,7 @@ int fcu_attn_fwd(fcu_ctx *ctx, const float *Q, const float *K, const float *V, i
   if (rc) return rc;
   FCU_REQUIRE(Q && K && V && O && lse, "fcu_attn_fwd: null pointer");
   cudaStream_t st = ctx->stream;
-  if (ctx->precision == FCU_PREC_BF16 &&
-      (fcu::attn_tmem_op_supported(dH, Q, K, V, O) ||
-       (dH == 128 && fcu::attn_tmem_op_supported(64, Q, K, V, O))))   // the forward kernel at 128
+  if (ctx->precision == FCU_PREC_BF16 && fcu::attn_tmem_op_supported(dH, Q, K, V, O))
     return fcu::attn_fwd_op_tmem(ctx, Q, K, V, B, T, nH, nKV, dH, O, lse);
   if (ctx->precision == FCU_PREC_BF16 && fcu::attn_tc_supported(dH, Q, K, V))
     return fcu::attn_fwd_tc(st, Q, K, V, B, T, nH, nKV, dH, O, lse);

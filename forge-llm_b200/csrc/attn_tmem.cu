@@ -427,26 +427,49 @@ __device__ __forceinline__ void dkdv_mask(int lo, int hi, uint32_t (&pp)[32], ui
   }
 }
 
-// dK/dV kernel shared memory: K / V double-buffered per item, a (Q, dO, lse,
-// delta) ring across items
-constexpr int kKStages = 4;
-constexpr int kKV_K = 0;                              // [2]
-constexpr int kKV_V = kKV_K + 2 * kTile;              // [2]
-constexpr int kKV_Q = kKV_V + 2 * kTile;              // kKStages tiles
-constexpr int kKV_G = kKV_Q + kKStages * kTile;       // kKStages tiles (dO)
-constexpr int kKV_L = kKV_G + kKStages * kTile;       // [kKStages][128] f32
-constexpr int kKV_D = kKV_L + kKStages * 128 * 4;     // [kKStages][128] f32
-constexpr int kKV_Bar = kKV_D + kKStages * 128 * 4;
-constexpr int kKVSmem = kKV_Bar + (13 + 2 * kKStages) * 8 + 16;
+// dK/dV kernel shared memory at head dim D: K / V per item (double-buffered
+// at D = 64, single at D = 128), a (Q, dO, lse, delta) ring across items (4
+// deep at D = 64, 2 at D = 128).  The TMEM columns (S^T, dP^T, one 64-column
+// slice of dV and of dK, bf16 P^T and dS^T) are those of D = 64: at D = 128
+// each work item accumulates one 64-column half of dV and dK, its S^T / dP^T
+// contracting over all 128 columns (two 64-column boxes).
+template <int D>
+struct KvCfg {
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kTileT = kBM * D * 2;
+  static constexpr int kKV = D == 64 ? 2 : 1;          // K / V buffers
+  static constexpr int kStages = D == 64 ? 4 : 2;
+  static constexpr int K = 0;                          // [kKV] tiles
+  static constexpr int V = K + kKV * kTileT;           // [kKV] tiles
+  static constexpr int Q = V + kKV * kTileT;           // kStages tiles
+  static constexpr int G = Q + kStages * kTileT;       // kStages tiles (dO)
+  static constexpr int L = G + kStages * kTileT;       // [kStages][128] f32
+  static constexpr int Dl = L + kStages * 128 * 4;     // [kStages][128] f32
+  static constexpr int Bar = Dl + kStages * 128 * 4;
+  static constexpr int Smem = Bar + (13 + 2 * kStages) * 8 + 16;
+  static_assert(Smem <= 232448, "dK/dV shared memory");
+};
 
-// dQ kernel shared memory: Q / dO double-buffered per item, a K/V ring
-constexpr int kQStages = 4;
-constexpr int kQ_Q = 0;                               // [2] Q tiles
-constexpr int kQ_G = kQ_Q + 2 * kTile;                // [2] dO tiles
-constexpr int kQ_K = kQ_G + 2 * kTile;                // kQStages tiles
-constexpr int kQ_V = kQ_K + kQStages * kTile;         // kQStages tiles
-constexpr int kQ_Bar = kQ_V + kQStages * kTile;
-constexpr int kQSmem = kQ_Bar + (13 + 2 * kQStages) * 8 + 16;
+// dQ kernel shared memory at head dim D: Q / dO tiles per item (double-
+// buffered at D = 64, single at D = 128), a K/V ring (4 deep at D = 64, 2 at
+// D = 128: [128][128] tiles are 32 KB), and TMEM S [0,128), dP [128,256),
+// dS [256,320), dQ accumulators from 320 (two of 64 columns at D = 64, one of
+// 128 at D = 128).  A [128][D] tile is D / 64 boxes of [128][64], 16 KB each.
+template <int D>
+struct DqCfg {
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kTileT = kBM * D * 2;
+  static constexpr int kQG = D == 64 ? 2 : 1;          // Q / dO buffers
+  static constexpr int kStages = D == 64 ? 4 : 2;      // K / V ring
+  static constexpr int kNAcc = D == 64 ? 2 : 1;        // dQ accumulators
+  static constexpr int Q = 0;
+  static constexpr int G = Q + kQG * kTileT;
+  static constexpr int K = G + kQG * kTileT;
+  static constexpr int V = K + kStages * kTileT;
+  static constexpr int Bar = V + kStages * kTileT;
+  static constexpr int Smem = Bar + (13 + 2 * kStages) * 8 + 16;
+  static_assert(Smem <= 232448 && 320 + kNAcc * D <= 512, "dQ shared memory / TMEM");
+};
 
 // Rotates interleaved pairs back by R^T: (x, y) -> (x c + y s, -x s + y c).
 __device__ __forceinline__ void rope_back(float &x, float &y, float2 cs) {
@@ -455,14 +478,18 @@ __device__ __forceinline__ void rope_back(float &x, float &y, float2 cs) {
   y = w;
 }
 
+template <int D>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_dkdv_tmem_kernel(const __grid_constant__ CUtensorMap tm_qkv,
                               const __grid_constant__ CUtensorMap tm_do, BwdParams p) {
   fcu::pdl_trigger();
+  using Cfg = KvCfg<D>;
+  constexpr int kKStages = Cfg::kStages, kKV = Cfg::kKV, kTileT = Cfg::kTileT, kHalves = D / 64;
+  constexpr uint64_t kBoxStep = kTile >> 4;            // next 64-column box of a tile
   extern __shared__ __align__(1024) uint8_t smem[];
-  uint8_t *sK = smem + kKV_K, *sV = smem + kKV_V, *sQ = smem + kKV_Q, *sG = smem + kKV_G;
-  float *sL = (float *)(smem + kKV_L), *sDl = (float *)(smem + kKV_D);
-  uint64_t *bars = (uint64_t *)(smem + kKV_Bar);
+  uint8_t *sK = smem + Cfg::K, *sV = smem + Cfg::V, *sQ = smem + Cfg::Q, *sG = smem + Cfg::G;
+  float *sL = (float *)(smem + Cfg::L), *sDl = (float *)(smem + Cfg::Dl);
+  uint64_t *bars = (uint64_t *)(smem + Cfg::Bar);
   uint64_t *kv_full = bars, *kv_empty = bars + 2;                        // [2]
   uint64_t *q_full = bars + 4, *q_empty = bars + 4 + kKStages;           // [kKStages]
   uint64_t *st_full = bars + 4 + 2 * kKStages, *st_free = st_full + 1;
@@ -472,20 +499,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Work items (key tile, head, sequence), early key tiles (most query tiles
-  // after them) first, strided over the persistent grid.
+  // Work items (key tile, head, sequence, 64-column half of dV / dK), early
+  // key tiles (most query tiles after them) first, strided over the
+  // persistent grid.
   const int heads_cta = p.split ? p.nH : p.nKV;
-  const int per = heads_cta * p.B;
+  const int per = heads_cta * p.B * kHalves;
   const int n_items = p.n_t * per;
   const int n_heads = p.split ? 1 : p.group;
   const bool aligned = (smem_u32(smem) & 1023u) == 0;
   struct Item {
-    int kt, kvh, h_begin, b, per_head, n_iter;
+    int kt, kvh, h_begin, b, per_head, n_iter, dh;
   };
   auto item = [&](int idx) {
     Item w;
     w.kt = idx / per;
-    const int rest = idx % per, hx = rest % heads_cta;
+    const int rest0 = idx % per;
+    w.dh = rest0 % kHalves;
+    const int rest = rest0 / kHalves, hx = rest % heads_cta;
     w.b = rest / heads_cta;
     w.kvh = p.split ? hx / p.group : hx;
     w.h_begin = p.split ? hx : w.kvh * p.group;
@@ -495,7 +525,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   };
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < kKV; i++) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
@@ -530,15 +560,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     int u = 0, nk = 0;
     for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
       const Item w = item(idx);
-      const int row0 = w.b * p.T, kb = nk & 1;
-      if (!warp_wait(&kv_empty[kb], ((uint32_t)(nk >> 1) & 1u) ^ 1u, abort_flag)) {
+      const int row0 = w.b * p.T, kb = nk % kKV;
+      if (!warp_wait(&kv_empty[kb], ((uint32_t)(nk / kKV) & 1u) ^ 1u, abort_flag)) {
         ok = false;
         break;
       }
       if (lane == 0) {
-        mbar_expect_tx(&kv_full[kb], 2 * kTile);
-        tma_load_2d(sK + kb * kTile, &tm_qkv, (p.nH + w.kvh) * kD, row0 + w.kt * kBN, &kv_full[kb]);
-        tma_load_2d(sV + kb * kTile, &tm_qkv, (p.nH + p.nKV + w.kvh) * kD, row0 + w.kt * kBN, &kv_full[kb]);
+        mbar_expect_tx(&kv_full[kb], 2 * kTileT);
+#pragma unroll
+        for (int bx = 0; bx < Cfg::kBoxes; bx++) {
+          tma_load_2d(sK + kb * kTileT + bx * kTile, &tm_qkv, (p.nH + w.kvh) * D + bx * 64, row0 + w.kt * kBN,
+                      &kv_full[kb]);
+          tma_load_2d(sV + kb * kTileT + bx * kTile, &tm_qkv, (p.nH + p.nKV + w.kvh) * D + bx * 64,
+                      row0 + w.kt * kBN, &kv_full[kb]);
+        }
       }
       nk++;
       for (int it = 0; it < w.n_iter; it++, u++) {
@@ -550,9 +585,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int h = w.h_begin + it / w.per_head;
         const int q0 = (w.kt + it % w.per_head) * kBM;
         if (lane == 0) {                      // copies first: their latency overlaps the loads below
-          mbar_expect_tx(&q_full[s], 2 * kTile);
-          tma_load_2d(sQ + s * kTile, &tm_qkv, h * kD, row0 + q0, &q_full[s]);
-          tma_load_2d(sG + s * kTile, &tm_do, h * kD, row0 + q0, &q_full[s]);
+          mbar_expect_tx(&q_full[s], 2 * kTileT);
+#pragma unroll
+          for (int bx = 0; bx < Cfg::kBoxes; bx++) {
+            tma_load_2d(sQ + s * kTileT + bx * kTile, &tm_qkv, h * D + bx * 64, row0 + q0, &q_full[s]);
+            tma_load_2d(sG + s * kTileT + bx * kTile, &tm_do, h * D + bx * 64, row0 + q0, &q_full[s]);
+          }
         }
         const int64_t lrow = ((int64_t)w.b * p.nH + h) * p.T;
 #pragma unroll
@@ -570,7 +608,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         *abort_flag = 1;
         atomicExch(p.err, 21);
       }
-      for (int i = nk - 2 < 0 ? 0 : nk - 2; i < nk; i++) mbar_wait_drain(&kv_full[i & 1], (uint32_t)(i >> 1) & 1u);
+      for (int i = nk - kKV < 0 ? 0 : nk - kKV; i < nk; i++)
+        mbar_wait_drain(&kv_full[i % kKV], (uint32_t)(i / kKV) & 1u);
       for (int i = u - kKStages < 0 ? 0 : u - kKStages; i < u; i++)
         mbar_wait_drain(&q_full[i % kKStages], (uint32_t)(i / kKStages) & 1u);
     }
@@ -578,19 +617,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // ---------------- MMA issuer (whole warp; elect.sync picks the issuing lane)
     {
       const uint32_t id_n128 = instr_desc_bf16(0, 0, kBM, kBN);
-      const uint32_t id_n64 = instr_desc_bf16(0, 1, kBM, kD);
-      constexpr uint64_t kTileStep = kTile >> 4;
+      const uint32_t id_n64 = instr_desc_bf16(0, 1, kBM, 64);
+      constexpr uint64_t kTileStep = kTileT >> 4;
       const uint64_t dK0 = desc_k(smem_u32(sK)), dV0 = desc_k(smem_u32(sV));
       const uint64_t dQk0 = desc_k(smem_u32(sQ)), dGk0 = desc_k(smem_u32(sG));
       const uint64_t dQm0 = desc_mn(smem_u32(sQ), kBM), dGm0 = desc_mn(smem_u32(sG), kBM);
       bool ok = true, have_prev = false, prev_first = false, prev_last = false;
-      int u = 0, ii = 0, prev_u = 0, prev_s = 0, prev_kb = 0, prev_ii = 0;
-      // dV += P^T dO, dK += dS^T Q for the previous unit (one unit behind its S / dP MMAs)
+      int u = 0, ii = 0, prev_u = 0, prev_s = 0, prev_kb = 0, prev_ii = 0, prev_dh = 0;
+      // dV += P^T dO, dK += dS^T Q for the previous unit (one unit behind its
+      // S / dP MMAs), over the item's 64-column box of dO and Q
       auto issue_dvdk = [&]() -> bool {
         if (!warp_wait(pds_full, (uint32_t)prev_u & 1u, abort_flag)) return false;
         if (prev_first && !warp_wait(acc_free, ((uint32_t)prev_ii & 1u) ^ 1u, abort_flag)) return false;
         tc_fence_after();
-        const uint64_t bq = dQm0 + (uint64_t)prev_s * kTileStep, bg = dGm0 + (uint64_t)prev_s * kTileStep;
+        const uint64_t bq = dQm0 + (uint64_t)prev_s * kTileStep + (uint64_t)prev_dh * kBoxStep;
+        const uint64_t bg = dGm0 + (uint64_t)prev_s * kTileStep + (uint64_t)prev_dh * kBoxStep;
 #pragma unroll
         for (int k = 0; k < kBM / 16; k++)
           umma_bf16_ts_w(tdV, tPt + (uint32_t)(8 * k), bg + k * kDescMNStep, id_n64, (!prev_first || k > 0) ? 1u : 0u);
@@ -607,8 +648,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       };
       for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x, ii++) {
         const Item w = item(idx);
-        const int kb = ii & 1;
-        if (!warp_wait(&kv_full[kb], (uint32_t)(ii >> 1) & 1u, abort_flag)) {
+        const int kb = ii % kKV;
+        // With one K/V buffer (D = 128) the producer refills it once the
+        // previous item's last dV / dK MMAs have committed: issue them now
+        // rather than after this item's first S^T / dP^T.
+        if (kKV == 1 && have_prev) {
+          if (!issue_dvdk()) {
+            ok = false;
+            break;
+          }
+          have_prev = false;
+        }
+        if (!warp_wait(&kv_full[kb], (uint32_t)(ii / kKV) & 1u, abort_flag)) {
           ok = false;
           break;
         }
@@ -623,11 +674,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           tc_fence_after();
           const uint64_t bq = dQk0 + (uint64_t)s * kTileStep, bg = dGk0 + (uint64_t)s * kTileStep;
 #pragma unroll
-          for (int k = 0; k < kD / 16; k++)
-            umma_bf16_w(tS, ak + k * kDescKStep, bq + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
+          for (int k = 0; k < D / 16; k++)
+            umma_bf16_w(tS, ak + (k >> 2) * kBoxStep + (k & 3) * kDescKStep, bq + (k >> 2) * kBoxStep + (k & 3) * kDescKStep,
+                        id_n128, k > 0 ? 1u : 0u);
 #pragma unroll
-          for (int k = 0; k < kD / 16; k++)
-            umma_bf16_w(tdP, av + k * kDescKStep, bg + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
+          for (int k = 0; k < D / 16; k++)
+            umma_bf16_w(tdP, av + (k >> 2) * kBoxStep + (k & 3) * kDescKStep, bg + (k >> 2) * kBoxStep + (k & 3) * kDescKStep,
+                        id_n128, k > 0 ? 1u : 0u);
           umma_commit_w(st_full);
           if (have_prev && !issue_dvdk()) {
             ok = false;
@@ -638,6 +691,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           prev_s = s;
           prev_kb = kb;
           prev_ii = ii;
+          prev_dh = w.dh;
           prev_first = it == 0;
           prev_last = it == w.n_iter - 1;
         }
@@ -710,7 +764,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (p.split) {
           const int g = w.h_begin - w.kvh * p.group;
           float *dst = (half ? p.pk : p.pv) +
-                       ((int64_t)g * p.B * p.T + row0 + key) * ((int64_t)p.nKV * kD) + w.kvh * kD;
+                       ((int64_t)g * p.B * p.T + row0 + key) * ((int64_t)p.nKV * D) + w.kvh * D + w.dh * 64;
 #pragma unroll
           for (int c4 = 0; c4 < 16; c4++)
             reinterpret_cast<float4 *>(dst)[c4] =
@@ -720,10 +774,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           for (int c = 0; c < 64; c++) v[c] *= mul;
           if (half && p.rope) {
 #pragma unroll
-            for (int i = 0; i < 32; i++) rope_back(v[2 * i], v[2 * i + 1], p.rope[(int64_t)key * 32 + i]);
+            for (int i = 0; i < 32; i++)
+              rope_back(v[2 * i], v[2 * i + 1], p.rope[(int64_t)key * (D / 2) + w.dh * 32 + i]);
           }
           uint4 *dst = reinterpret_cast<uint4 *>(p.dqkv + (int64_t)(row0 + key) * p.ld +
-                                                 (int64_t)(p.nH + (half ? 0 : p.nKV) + w.kvh) * kD);
+                                                 (int64_t)(p.nH + (half ? 0 : p.nKV) + w.kvh) * D + w.dh * 64);
 #pragma unroll
           for (int c8 = 0; c8 < 8; c8++)
             dst[c8] = make_uint4(pack2_bf16(v[8 * c8], v[8 * c8 + 1]), pack2_bf16(v[8 * c8 + 2], v[8 * c8 + 3]),
@@ -749,13 +804,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // two TMEM accumulators (cols [320,384), [384,448)), so one item's epilogue
 // (dQ * scale rotated back by RoPE) overlaps the next item's first MMAs.
 // Q/dO tiles are double-buffered per item; the K/V ring runs across items.
+template <int D>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_dq_tmem_kernel(const __grid_constant__ CUtensorMap tm_qkv,
                             const __grid_constant__ CUtensorMap tm_do, BwdParams p) {
   fcu::pdl_trigger();
+  using Cfg = DqCfg<D>;
+  constexpr int kQStages = Cfg::kStages, kQG = Cfg::kQG, kNAcc = Cfg::kNAcc, kTileT = Cfg::kTileT;
+  constexpr uint64_t kBoxStep = kTile >> 4;            // next 64-column box of a tile
   extern __shared__ __align__(1024) uint8_t smem[];
-  uint8_t *sQ = smem + kQ_Q, *sG = smem + kQ_G, *sK = smem + kQ_K, *sV = smem + kQ_V;
-  uint64_t *bars = (uint64_t *)(smem + kQ_Bar);
+  uint8_t *sQ = smem + Cfg::Q, *sG = smem + Cfg::G, *sK = smem + Cfg::K, *sV = smem + Cfg::V;
+  uint64_t *bars = (uint64_t *)(smem + Cfg::Bar);
   uint64_t *qg_full = bars, *qg_empty = bars + 2;                       // [2]
   uint64_t *kv_full = bars + 4, *kv_empty = bars + 4 + kQStages;        // [kQStages]
   uint64_t *sp_full = bars + 4 + 2 * kQStages, *sp_free = sp_full + 1;
@@ -807,14 +866,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
         const int qt = p.n_t - 1 - idx / per, rest = idx % per;
         const int h = rest % p.nH, b = rest / p.nH, kvh = h / p.group;
-        const int row0 = b * p.T, qb = nq & 1;
-        if (!mbar_wait(&qg_empty[qb], ((uint32_t)(nq >> 1) & 1u) ^ 1u, abort_flag)) {
+        const int row0 = b * p.T, qb = nq % kQG;
+        if (!mbar_wait(&qg_empty[qb], ((uint32_t)(nq / kQG) & 1u) ^ 1u, abort_flag)) {
           ok = false;
           break;
         }
-        mbar_expect_tx(&qg_full[qb], 2 * kTile);
-        tma_load_2d(sQ + qb * kTile, &tm_qkv, h * kD, row0 + qt * kBM, &qg_full[qb]);
-        tma_load_2d(sG + qb * kTile, &tm_do, h * kD, row0 + qt * kBM, &qg_full[qb]);
+        mbar_expect_tx(&qg_full[qb], 2 * kTileT);
+#pragma unroll
+        for (int bx = 0; bx < Cfg::kBoxes; bx++) {
+          tma_load_2d(sQ + qb * kTileT + bx * kTile, &tm_qkv, h * D + bx * 64, row0 + qt * kBM, &qg_full[qb]);
+          tma_load_2d(sG + qb * kTileT + bx * kTile, &tm_do, h * D + bx * 64, row0 + qt * kBM, &qg_full[qb]);
+        }
         nq++;
         for (int j = 0; j <= qt; j++, u++) {
           const int s = u % kQStages;
@@ -822,16 +884,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             ok = false;
             break;
           }
-          mbar_expect_tx(&kv_full[s], 2 * kTile);
-          tma_load_2d(sK + s * kTile, &tm_qkv, (p.nH + kvh) * kD, row0 + j * kBN, &kv_full[s]);
-          tma_load_2d(sV + s * kTile, &tm_qkv, (p.nH + p.nKV + kvh) * kD, row0 + j * kBN, &kv_full[s]);
+          mbar_expect_tx(&kv_full[s], 2 * kTileT);
+#pragma unroll
+          for (int bx = 0; bx < Cfg::kBoxes; bx++) {
+            tma_load_2d(sK + s * kTileT + bx * kTile, &tm_qkv, (p.nH + kvh) * D + bx * 64, row0 + j * kBN, &kv_full[s]);
+            tma_load_2d(sV + s * kTileT + bx * kTile, &tm_qkv, (p.nH + p.nKV + kvh) * D + bx * 64, row0 + j * kBN,
+                        &kv_full[s]);
+          }
         }
       }
       if (!ok) {
         *abort_flag = 1;
         atomicExch(p.err, 31);
       }
-      for (int i = nq - 2 < 0 ? 0 : nq - 2; i < nq; i++) mbar_wait_drain(&qg_full[i & 1], (uint32_t)(i >> 1) & 1u);
+      for (int i = nq - kQG < 0 ? 0 : nq - kQG; i < nq; i++)
+        mbar_wait_drain(&qg_full[i % kQG], (uint32_t)(i / kQG) & 1u);
       for (int i = u - kQStages < 0 ? 0 : u - kQStages; i < u; i++)
         mbar_wait_drain(&kv_full[i % kQStages], (uint32_t)(i / kQStages) & 1u);
     }
@@ -839,32 +906,36 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // ---------------- MMA issuer (whole warp; elect.sync picks the issuing lane)
     {
       const uint32_t id_n128 = instr_desc_bf16(0, 0, kBM, kBN);
-      const uint32_t id_n64 = instr_desc_bf16(0, 1, kBM, kD);
+      const uint32_t id_nD = instr_desc_bf16(0, 1, kBM, D);
       const uint64_t dQ0 = desc_k(smem_u32(sQ)), dG0 = desc_k(smem_u32(sG));
       const uint64_t dKk0 = desc_k(smem_u32(sK)), dVk0 = desc_k(smem_u32(sV));
-      const uint64_t dKm0 = desc_mn(smem_u32(sK), kBN);
-      constexpr uint64_t kTileStep = kTile >> 4;
+      const uint64_t dKm0 = desc_mn(smem_u32(sK), kBN);   // K as B of dS K: D / 64 atoms 16 KB apart
+      constexpr uint64_t kTileStep = kTileT >> 4;
       bool ok = true, have_prev = false, prev_first = false, prev_last = false;
-      int u = 0, ii = 0, prev_u = 0, prev_s = 0, prev_qb = 0;
-      // dQ += dS K for the previous unit (one unit behind its S / dP MMAs)
+      int u = 0, ii = 0, prev_u = 0, prev_s = 0, prev_ab = 0, prev_ii = 0;
+      // dQ += dS K for the previous unit (one unit behind its S / dP MMAs).
+      // An item's first dQ MMA waits for the epilogue that last read its
+      // accumulator; with one accumulator (D = 128) that is the previous
+      // item's, whose own last dQ MMA has been issued by then.
       auto issue_dq = [&]() -> bool {
         if (!warp_wait(ds_full, (uint32_t)prev_u & 1u, abort_flag)) return false;
+        if (prev_first && !warp_wait(&acc_free[prev_ab], ((uint32_t)(prev_ii / kNAcc) & 1u) ^ 1u, abort_flag))
+          return false;
         tc_fence_after();
         const uint64_t bk = dKm0 + (uint64_t)prev_s * kTileStep;
-        const uint32_t acc = tdQ0 + (uint32_t)(prev_qb * kD);
+        const uint32_t acc = tdQ0 + (uint32_t)(prev_ab * D);
 #pragma unroll
         for (int k = 0; k < kBN / 16; k++)
-          umma_bf16_ts_w(acc, tdS + (uint32_t)(8 * k), bk + k * kDescMNStep, id_n64, (!prev_first || k > 0) ? 1u : 0u);
+          umma_bf16_ts_w(acc, tdS + (uint32_t)(8 * k), bk + k * kDescMNStep, id_nD, (!prev_first || k > 0) ? 1u : 0u);
         umma_commit_w(ds_free);
         umma_commit_w(&kv_empty[prev_s]);
-        if (prev_last) umma_commit_w(&acc_full[prev_qb]);
+        if (prev_last) umma_commit_w(&acc_full[prev_ab]);
         return true;
       };
       for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x, ii++) {
         const int qt = p.n_t - 1 - idx / per;
-        const int qb = ii & 1;
-        if (!warp_wait(&qg_full[qb], (uint32_t)(ii >> 1) & 1u, abort_flag) ||
-            !warp_wait(&acc_free[qb], ((uint32_t)(ii >> 1) & 1u) ^ 1u, abort_flag)) {
+        const int qb = ii % kQG, ab = ii % kNAcc;
+        if (!warp_wait(&qg_full[qb], (uint32_t)(ii / kQG) & 1u, abort_flag)) {
           ok = false;
           break;
         }
@@ -879,11 +950,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           tc_fence_after();
           const uint64_t bk = dKk0 + (uint64_t)s * kTileStep, bv = dVk0 + (uint64_t)s * kTileStep;
 #pragma unroll
-          for (int k = 0; k < kD / 16; k++)
-            umma_bf16_w(tS, aq + k * kDescKStep, bk + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
+          for (int k = 0; k < D / 16; k++)
+            umma_bf16_w(tS, aq + (k >> 2) * kBoxStep + (k & 3) * kDescKStep, bk + (k >> 2) * kBoxStep + (k & 3) * kDescKStep,
+                        id_n128, k > 0 ? 1u : 0u);
 #pragma unroll
-          for (int k = 0; k < kD / 16; k++)
-            umma_bf16_w(tdP, ag + k * kDescKStep, bv + k * kDescKStep, id_n128, k > 0 ? 1u : 0u);
+          for (int k = 0; k < D / 16; k++)
+            umma_bf16_w(tdP, ag + (k >> 2) * kBoxStep + (k & 3) * kDescKStep, bv + (k >> 2) * kBoxStep + (k & 3) * kDescKStep,
+                        id_n128, k > 0 ? 1u : 0u);
           umma_commit_w(sp_full);
           if (j == qt) umma_commit_w(&qg_empty[qb]);   // this item's Q / dO are read
           if (have_prev && !issue_dq()) {
@@ -893,7 +966,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           have_prev = true;
           prev_u = u;
           prev_s = s;
-          prev_qb = qb;
+          prev_ab = ab;
+          prev_ii = ii;
           prev_first = j == 0;
           prev_last = j == qt;
         }
@@ -917,7 +991,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x, ii++) {
       const int qt = p.n_t - 1 - idx / per, rest = idx % per;
       const int h = rest % p.nH, b = rest / p.nH;
-      const int q = qt * kBM + r, qb = ii & 1;
+      const int q = qt * kBM + r, ab = ii % kNAcc;
       const int64_t li = ((int64_t)b * p.nH + h) * p.T + q;
       const float L = q < p.T ? p.lse[li] * kLog2e : 0.f;
       const float Dq = q < p.T ? p.delta[li] : 0.f;
@@ -948,27 +1022,37 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(ds_full);
       }
-      if (!ok || !warp_wait(&acc_full[qb], (uint32_t)(ii >> 1) & 1u, abort_flag)) {
+      if (!ok || !warp_wait(&acc_full[ab], (uint32_t)(ii / kNAcc) & 1u, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t uq[32];
-      tmem_ld32(tdQ0 + (uint32_t)(qb * kD) + la + (uint32_t)(half * 32), uq);
+      // this warp's D / 2 columns of dQ
+      constexpr int kHalf = D / 2;
+      float v[kHalf];
+      const uint32_t tq = tdQ0 + (uint32_t)(ab * D) + la + (uint32_t)(half * kHalf);
+      if constexpr (kHalf == 32) {
+        uint32_t uq[32];
+        tmem_ld32(tq, uq);
+#pragma unroll
+        for (int c = 0; c < 32; c++) v[c] = __uint_as_float(uq[c]);
+      } else {
+        tmem_ld64(tq, v);
+      }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_free[qb]);
+      if (lane == 0) mbar_arrive(&acc_free[ab]);
       if (q < p.T) {
-        float v[32];
 #pragma unroll
-        for (int c = 0; c < 32; c++) v[c] = __uint_as_float(uq[c]) * p.scale;
+        for (int c = 0; c < kHalf; c++) v[c] *= p.scale;
         if (p.rope) {
 #pragma unroll
-          for (int i = 0; i < 16; i++) rope_back(v[2 * i], v[2 * i + 1], p.rope[(int64_t)q * 32 + half * 16 + i]);
+          for (int i = 0; i < kHalf / 2; i++)
+            rope_back(v[2 * i], v[2 * i + 1], p.rope[(int64_t)q * (D / 2) + half * (kHalf / 2) + i]);
         }
-        uint4 *dst = reinterpret_cast<uint4 *>(p.dqkv + (int64_t)(b * p.T + q) * p.ld + (int64_t)h * kD + half * 32);
+        uint4 *dst = reinterpret_cast<uint4 *>(p.dqkv + (int64_t)(b * p.T + q) * p.ld + (int64_t)h * D + half * kHalf);
 #pragma unroll
-        for (int c8 = 0; c8 < 4; c8++)
+        for (int c8 = 0; c8 < kHalf / 8; c8++)
           dst[c8] = make_uint4(pack2_bf16(v[8 * c8], v[8 * c8 + 1]), pack2_bf16(v[8 * c8 + 2], v[8 * c8 + 3]),
                                pack2_bf16(v[8 * c8 + 4], v[8 * c8 + 5]), pack2_bf16(v[8 * c8 + 6], v[8 * c8 + 7]));
       }
@@ -984,14 +1068,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, kBwdTmemCols);
 }
 
-// delta[b][h][t] = sum_d dO[bt, h*64 + d] * O[bt, h*64 + d]; 8 threads per
-// (token, head), one 16-byte load of each operand per thread.
-__global__ void attn_delta64_kernel(const __nv_bfloat16 *__restrict__ dO,
-                                    const __nv_bfloat16 *__restrict__ O, int64_t units, int nH, int T,
-                                    float *__restrict__ delta) {
+// delta[b][h][t] = sum_d dO[bt, h*D + d] * O[bt, h*D + d]; D / 8 threads
+// per (token, head), one 16-byte load of each operand per thread.
+template <int D>
+__global__ void attn_delta_kernel(const __nv_bfloat16 *__restrict__ dO,
+                                  const __nv_bfloat16 *__restrict__ O, int64_t units, int nH, int T,
+                                  float *__restrict__ delta) {
   fcu::pdl_trigger();
+  constexpr int kLanes = D / 8;
   const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int64_t unit = t >> 3;                  // token row * nH + head
+  const int64_t unit = t / kLanes;              // token row * nH + head
   float s = 0.f;
   if (unit < units) {
     const uint4 g = reinterpret_cast<const uint4 *>(dO)[t];
@@ -1005,10 +1091,9 @@ __global__ void attn_delta64_kernel(const __nv_bfloat16 *__restrict__ dO,
       s = fmaf(a.y, c.y, s);
     }
   }
-  s += __shfl_xor_sync(0xffffffffu, s, 4);
-  s += __shfl_xor_sync(0xffffffffu, s, 2);
-  s += __shfl_xor_sync(0xffffffffu, s, 1);
-  if (unit < units && (t & 7) == 0) {
+#pragma unroll
+  for (int o = kLanes / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (unit < units && (t % kLanes) == 0) {
     const int64_t row = unit / nH;
     const int h = (int)(unit - row * nH);
     const int64_t b = row / T, tt = row - b * T;
@@ -1018,11 +1103,12 @@ __global__ void attn_delta64_kernel(const __nv_bfloat16 *__restrict__ dO,
 
 // Head-split dK/dV: sums the group's fp32 partials in order, rotates dK back
 // and stores both as bf16 into the dqkv buffer.  One thread per 4 columns.
-__global__ void attn_kv_reduce64_kernel(const float *__restrict__ pk, const float *__restrict__ pv,
-                                        int group, int64_t rows, int nH, int nKV, int T,
-                                        const float2 *__restrict__ rope, __nv_bfloat16 *dqkv, int64_t ld) {
+template <int D>
+__global__ void attn_kv_reduce_kernel(const float *__restrict__ pk, const float *__restrict__ pv,
+                                      int group, int64_t rows, int nH, int nKV, int T,
+                                      const float2 *__restrict__ rope, __nv_bfloat16 *dqkv, int64_t ld) {
   fcu::pdl_trigger();
-  const int64_t kvD = (int64_t)nKV * kD, q4 = kvD / 4, n = rows * q4;
+  const int64_t kvD = (int64_t)nKV * D, q4 = kvD / 4, n = rows * q4;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
     const int64_t row = e / q4;
     const int64_t c = (e - row * q4) * 4;
@@ -1035,11 +1121,11 @@ __global__ void attn_kv_reduce64_kernel(const float *__restrict__ pk, const floa
       v.x += d.x; v.y += d.y; v.z += d.z; v.w += d.w;
     }
     if (rope) {
-      const float2 *cs = rope + (row % T) * 32 + (c % kD) / 2;
+      const float2 *cs = rope + (row % T) * (D / 2) + (c % D) / 2;
       rope_back(k.x, k.y, cs[0]);
       rope_back(k.z, k.w, cs[1]);
     }
-    __nv_bfloat16 *dk = dqkv + row * ld + (int64_t)nH * kD + c;
+    __nv_bfloat16 *dk = dqkv + row * ld + (int64_t)nH * D + c;
     __nv_bfloat16 *dv = dk + kvD;
     *reinterpret_cast<uint2 *>(dk) = make_uint2(pack2_bf16(k.x, k.y), pack2_bf16(k.z, k.w));
     *reinterpret_cast<uint2 *>(dv) = make_uint2(pack2_bf16(v.x, v.y), pack2_bf16(v.z, v.w));
@@ -1048,7 +1134,7 @@ __global__ void attn_kv_reduce64_kernel(const float *__restrict__ pk, const floa
 
 }  // namespace
 
-bool attn_tmem_supported(int dH) { return dH == kD; }
+bool attn_tmem_supported(int dH) { return dH == kD || dH == 128; }
 
 // O [B*T, nH*D] bf16 and lse [B][nH][T] from the bf16 qkv buffer (row stride
 // ld_qkv elements: q heads, then k heads, then v heads, D columns each; D =
@@ -1095,26 +1181,25 @@ int attn_fwd_tmem(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int T, i
   return attn_fwd_tmem_d<64>(ctx, qkv, ld_qkv, B, T, nH, nKV, O, lse, dh);
 }
 
-// Backward from the bf16 qkv buffer, dO and O ([B*T, nH*64] bf16) and the
-// forward's lse: dq | dk | dv (RoPE rotated back when `rope` is given) into
-// the bf16 dqkv buffer (same layout and row stride as qkv).  `delta` is
-// scratch of B*nH*T floats; `pk`, `pv` are the head-split partial buffers
-// (group * B*T * nKV*64 floats each), used when `split` is set.
-int attn_bwd_tmem(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv, const void *O,
-                  const float *lse, float *delta, int B, int T, int nH, int nKV, const float2 *rope,
-                  void *dqkv, int split, float *pk, float *pv, int dh) {
+namespace {
+
+// Backward at head width D (64: heads of dh <= 64, zero-padded below 64; 128).
+template <int D>
+int attn_bwd_tmem_d(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv, const void *O,
+                    const float *lse, float *delta, int B, int T, int nH, int nKV, const float2 *rope,
+                    void *dqkv, int split, float *pk, float *pv, int dh) {
   int rc = tc_get_encode();
   if (rc) return rc;
   int *err = nullptr;
   rc = tc_error_word(ctx, &err);
   if (rc) return rc;
   CUtensorMap map_qkv, map_do;
-  rc = tc_make_map(&map_qkv, qkv, (uint64_t)B * T, (uint64_t)(nH + 2 * nKV) * kD, (uint64_t)ld_qkv, 64,
+  rc = tc_make_map(&map_qkv, qkv, (uint64_t)B * T, (uint64_t)(nH + 2 * nKV) * D, (uint64_t)ld_qkv, 64,
                    kBM);
-  if (!rc) rc = tc_make_map(&map_do, dO, (uint64_t)B * T, (uint64_t)nH * kD, (uint64_t)nH * kD, 64, kBM);
+  if (!rc) rc = tc_make_map(&map_do, dO, (uint64_t)B * T, (uint64_t)nH * D, (uint64_t)nH * D, 64, kBM);
   if (rc) return rc;
   const int64_t units = (int64_t)B * T * nH;
-  attn_delta64_kernel<<<(unsigned)((units * 8 + 255) / 256), 256, 0, ctx->stream>>>(
+  attn_delta_kernel<D><<<(unsigned)((units * (D / 8) + 255) / 256), 256, 0, ctx->stream>>>(
       (const __nv_bfloat16 *)dO, (const __nv_bfloat16 *)O, units, nH, T, delta);
   FCU_CHECK_LAUNCH();
   BwdParams p{};
@@ -1137,32 +1222,47 @@ int attn_bwd_tmem(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv,
   p.err = err;
   static bool attr_set[64] = {false};
   if (!attr_set[ctx->device & 63]) {
-    FCU_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd_dkdv_tmem_kernel,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kKVSmem));
-    FCU_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd_dq_tmem_kernel,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kQSmem));
+    FCU_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd_dkdv_tmem_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        KvCfg<D>::Smem));
+    FCU_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd_dq_tmem_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        DqCfg<D>::Smem));
     attr_set[ctx->device & 63] = true;
   }
-  const int64_t items_kv = (int64_t)p.n_t * (split ? nH : nKV) * B;
+  const int64_t items_kv = (int64_t)p.n_t * (split ? nH : nKV) * B * (D / 64);
   const int64_t grid_kv = items_kv < ctx->num_sms ? items_kv : ctx->num_sms;   // persistent
   const int64_t items_q = (int64_t)p.n_t * nH * B;
   const int64_t grid_q = items_q < ctx->num_sms ? items_q : ctx->num_sms;   // persistent
-  FCU_REQUIRE(items_q <= INT32_MAX, "attention backward: grid too large");
-  FCU_CHECK_CUDA(launch_pdl(attn_bwd_dkdv_tmem_kernel, dim3((unsigned)grid_kv), dim3(kBwdThreads), kKVSmem,
-                            ctx->stream, map_qkv, map_do, p));
+  FCU_REQUIRE(items_q <= INT32_MAX && items_kv <= INT32_MAX, "attention backward: grid too large");
+  FCU_CHECK_CUDA(launch_pdl(attn_bwd_dkdv_tmem_kernel<D>, dim3((unsigned)grid_kv), dim3(kBwdThreads),
+                            KvCfg<D>::Smem, ctx->stream, map_qkv, map_do, p));
   FCU_CHECK_LAUNCH();
   if (split) {
-    const int64_t n = (int64_t)B * T * nKV * kD / 4;
+    const int64_t n = (int64_t)B * T * nKV * D / 4;
     int blocks = (int)((n + 255) / 256);
     if (blocks > 16 * ctx->num_sms) blocks = 16 * ctx->num_sms;
-    attn_kv_reduce64_kernel<<<blocks, 256, 0, ctx->stream>>>(pk, pv, p.group, (int64_t)B * T, nH, nKV, T,
-                                                            rope, (__nv_bfloat16 *)dqkv, ld_qkv);
+    attn_kv_reduce_kernel<D><<<blocks, 256, 0, ctx->stream>>>(pk, pv, p.group, (int64_t)B * T, nH, nKV, T, rope,
+                                                              (__nv_bfloat16 *)dqkv, ld_qkv);
     FCU_CHECK_LAUNCH();
   }
-  FCU_CHECK_CUDA(launch_pdl(attn_bwd_dq_tmem_kernel, dim3((unsigned)grid_q), dim3(kBwdThreads), kQSmem,
+  FCU_CHECK_CUDA(launch_pdl(attn_bwd_dq_tmem_kernel<D>, dim3((unsigned)grid_q), dim3(kBwdThreads), DqCfg<D>::Smem,
                             ctx->stream, map_qkv, map_do, p));
   FCU_CHECK_LAUNCH();
   return FCU_OK;
+}
+
+}  // namespace
+
+// Backward from the bf16 qkv buffer, dO and O ([B*T, nH*W] bf16, W = 128 when
+// dh is 128, else 64) and the forward's lse: dq | dk | dv (RoPE rotated back
+// when `rope` is given) into the bf16 dqkv buffer (same layout and row stride
+// as qkv).  `delta` is scratch of B*nH*T floats; `pk`, `pv` are the head-split
+// partial buffers (group * B*T * nKV*W floats each), used when `split` is set.
+int attn_bwd_tmem(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv, const void *O,
+                  const float *lse, float *delta, int B, int T, int nH, int nKV, const float2 *rope,
+                  void *dqkv, int split, float *pk, float *pv, int dh) {
+  if (dh == 128)
+    return attn_bwd_tmem_d<128>(ctx, dO, qkv, ld_qkv, O, lse, delta, B, T, nH, nKV, rope, dqkv, split, pk, pv, dh);
+  return attn_bwd_tmem_d<64>(ctx, dO, qkv, ld_qkv, O, lse, delta, B, T, nH, nKV, rope, dqkv, split, pk, pv, dh);
 }
 
 // ------------------------------------------------------------------ operator entries
@@ -1306,7 +1406,7 @@ bool op_aligned(const void *p) { return ((uintptr_t)p & 15) == 0; }
 bool attn_tmem_padded(int dH) { return dH > 0 && dH <= kD && dH % 4 == 0; }
 
 bool attn_tmem_op_supported(int dH, const void *a, const void *b, const void *c, const void *d) {
-  return attn_tmem_padded(dH) && op_aligned(a) && op_aligned(b) && op_aligned(c) && op_aligned(d);
+  return (attn_tmem_padded(dH) || dH == 128) && op_aligned(a) && op_aligned(b) && op_aligned(c) && op_aligned(d);
 }
 
 int attn_fwd_op_tmem(fcu_ctx *ctx, const float *Q, const float *K, const float *V, int B, int T, int nH,
@@ -1333,11 +1433,11 @@ namespace {
 // delta, and the head-split dK / dV partials (kv columns padded to 64 per
 // head) on small grids, from the context scratch.
 int bwd_scratch(fcu_ctx *ctx, int B, int T, int nH, int nKV, int *split, float **delta, float **pk,
-                float **pv) {
+                float **pv, int hw = kD) {
   const int64_t ctas = (int64_t)div_up(T, kBM) * nKV * B;
   *split = (nH > nKV && ctas < 4 * (int64_t)ctx->num_sms) ? 1 : 0;
   const size_t delta_bytes = (sizeof(float) * (size_t)B * nH * T + 255) & ~(size_t)255;
-  const size_t part_bytes = *split ? sizeof(float) * (size_t)(nH / nKV) * B * T * nKV * kD : 0;
+  const size_t part_bytes = *split ? sizeof(float) * (size_t)(nH / nKV) * B * T * nKV * hw : 0;
   void *scr = nullptr;
   int rc = ctx_scratch(ctx, delta_bytes + 2 * part_bytes, &scr);
   if (rc) return rc;
@@ -1352,27 +1452,28 @@ int bwd_scratch(fcu_ctx *ctx, int B, int T, int nH, int nKV, int *split, float *
 int attn_bwd_op_tmem(fcu_ctx *ctx, const float *dO, const float *Q, const float *K, const float *V,
                      const float *O, const float *lse, int B, int T, int nH, int nKV, int dH, float *dQ,
                      float *dK, float *dV, int accumulate) {
-  const int64_t rows = (int64_t)B * T, W = (int64_t)(nH + 2 * nKV) * kD, qD = (int64_t)nH * kD,
-                kvD = (int64_t)nKV * kD;
+  const int hw = dH == 128 ? 128 : kD;   // head width of the bf16 layout
+  const int64_t rows = (int64_t)B * T, W = (int64_t)(nH + 2 * nKV) * hw, qD = (int64_t)nH * hw,
+                kvD = (int64_t)nKV * hw;
   void *buf = nullptr;
   // qkv and dqkv [rows, W], dO and O [rows, qD], all bf16
   int rc = op_buffer(ctx, (size_t)rows * (2 * W + 2 * qD) * sizeof(__nv_bfloat16), &buf);
   if (rc) return rc;
   __nv_bfloat16 *qkv = (__nv_bfloat16 *)buf, *dqkv = qkv + rows * W, *dOb = dqkv + rows * W,
                 *Ob = dOb + rows * qD;
-  if ((rc = pack(ctx, Q, rows, nH, dH, qkv, W, 0)) || (rc = pack(ctx, K, rows, nKV, dH, qkv, W, (int)qD)) ||
-      (rc = pack(ctx, V, rows, nKV, dH, qkv, W, (int)(qD + kvD))) ||
-      (rc = pack(ctx, dO, rows, nH, dH, dOb, qD, 0)) || (rc = pack(ctx, O, rows, nH, dH, Ob, qD, 0)))
+  if ((rc = pack(ctx, Q, rows, nH, dH, qkv, W, 0, hw)) || (rc = pack(ctx, K, rows, nKV, dH, qkv, W, (int)qD, hw)) ||
+      (rc = pack(ctx, V, rows, nKV, dH, qkv, W, (int)(qD + kvD), hw)) ||
+      (rc = pack(ctx, dO, rows, nH, dH, dOb, qD, 0, hw)) || (rc = pack(ctx, O, rows, nH, dH, Ob, qD, 0, hw)))
     return rc;
   int split = 0;
   float *delta = nullptr, *pk = nullptr, *pv = nullptr;
-  if ((rc = bwd_scratch(ctx, B, T, nH, nKV, &split, &delta, &pk, &pv))) return rc;
+  if ((rc = bwd_scratch(ctx, B, T, nH, nKV, &split, &delta, &pk, &pv, hw))) return rc;
   rc = attn_bwd_tmem(ctx, dOb, qkv, W, Ob, lse, delta, B, T, nH, nKV, nullptr, dqkv, split, pk, pv, dH);
   if (rc) return rc;
-  if ((rc = unpack(ctx, dqkv, W, 0, rows, nH, dH, dQ, accumulate)) ||
-      (rc = unpack(ctx, dqkv, W, (int)qD, rows, nKV, dH, dK, accumulate)))
+  if ((rc = unpack(ctx, dqkv, W, 0, rows, nH, dH, dQ, accumulate, hw)) ||
+      (rc = unpack(ctx, dqkv, W, (int)qD, rows, nKV, dH, dK, accumulate, hw)))
     return rc;
-  return unpack(ctx, dqkv, W, (int)(qD + kvD), rows, nKV, dH, dV, accumulate);
+  return unpack(ctx, dqkv, W, (int)(qD + kvD), rows, nKV, dH, dV, accumulate, hw);
 }
 
 // The fused path's bf16 entries at head dims below 64: qkv (and dO, O) are

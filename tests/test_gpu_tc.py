@@ -404,12 +404,16 @@ def _rope_back64(d, B, T, heads, dH, theta):
                                                  (1, 2048, 32, 8, 10000.0, 64),
                                                  (1, 64, 4, 4, 10000.0, 16), (2, 130, 4, 1, 0.0, 16),
                                                  (3, 300, 6, 2, 10000.0, 32), (16, 256, 12, 4, 10000.0, 32),
-                                                 (2, 130, 4, 2, 10000.0, 128)])
+                                                 (2, 130, 4, 2, 10000.0, 128), (3, 300, 4, 4, 0.0, 128),
+                                                 (8, 1024, 8, 2, 10000.0, 128), (1, 2048, 16, 4, 10000.0, 128),
+                                                 (64, 512, 8, 4, 10000.0, 128)])
 def test_attn_bwd_bf16_entry(B, T, nH, nKV, theta, dH):
     """The fused path's attention backward (dq | dk | dv into the bf16 dqkv
     buffer, RoPE rotated back) against float64 autograd of the same bf16
     inputs: relL2 <= 2e-2 (P and dS are bf16 operands), every gradient finite.
-    Head dims 16 and 32 run on zero-padded 64-column heads."""
+    Head dims 16 and 32 run on zero-padded 64-column heads; head dim 128 on
+    the 128-wide tcgen05 kernels (dV / dK in two 64-column halves), with one
+    CTA per kv head and, for few sequences, one per q head (head split)."""
     from forgellm import _lib
     from forgellm.autograd import ctx
     width = (nH + 2 * nKV) * dH
@@ -444,7 +448,7 @@ def test_attn_bwd_bf16_entry(B, T, nH, nKV, theta, dH):
         assert err <= 2e-2, (name, err)
 
 
-@pytest.mark.parametrize("dH", [64, 32, 16])
+@pytest.mark.parametrize("dH", [64, 32, 16, 128])
 def test_tc_attention_operator_accumulates_on_tcgen05(dH):
     """causalAttnBatch in bf16 mode runs the tcgen05 kernels on packed bf16
     copies of its fp32 operands (heads below 64 columns zero-padded); its
