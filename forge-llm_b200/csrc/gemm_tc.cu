@@ -931,11 +931,12 @@ int pair_slots(fcu_ctx *ctx, int *out) {
 // ceil(nk / sp) k-blocks plus a fixed per-unit overhead (pipeline fill and
 // the partial tile's epilogue, about 4 k-blocks), and each slice adds its
 // partial tile's write and read-back (8 bytes per output at the copy
-// bandwidth, about 0.3 us per k-block wave).  1 = no split; at most 16
-// slices of at least 16 k-blocks each.
+// bandwidth; a k-block wave takes about 0.45 us, as measured on the batch-8
+// weight gradients).  1 = no split; at most 16 slices of at least 16
+// k-blocks each.
 int choose_splits(int64_t tiles, int nk, int64_t slots, int64_t outputs) {
   constexpr double kUnitOverhead = 4.0;
-  const double reduce_per_slice = (double)outputs * 8.0 / 6.0e12 / 0.3e-6;
+  const double reduce_per_slice = (double)outputs * 8.0 / 6.0e12 / 0.45e-6;
   const int hi = nk / 16 < 16 ? nk / 16 : 16;
   int best = 1;
   double best_t = (double)((tiles + slots - 1) / slots) * (nk + kUnitOverhead);
