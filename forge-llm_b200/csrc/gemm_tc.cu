@@ -551,23 +551,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_wait_ld_r(r0);
         if (bf16_out) tmem_wait_ld_r(r1);
       }
+      // RoPE (cos, sin) of this row's position for a box's 32 column pairs
+      // (a box's 64 columns lie inside one head: head_dim % 64 == 0).  Every
+      // box of the row uses the same 32 pairs when heads are 64 wide, so they
+      // are loaded once per tile and again only when a box's pair offset in
+      // its head differs from the one held.
+      float2 cs[32];
+      int cs_at = -1;
 #pragma unroll 1
       for (int c = 0; c < nbox; c++) {
         const int n = n0 + c * cw;
-        // RoPE (cos, sin) of this row's position for the box's head, loaded
-        // before the TMEM read so the two latencies overlap (the box's 64
-        // columns lie inside one head: head_dim % 64 == 0)
         const bool rope_box = bf16_out && p.mode == kOutBF16Rope && n < p.rope_cols && gm < p.M;
-        float2 cs[32];
-        if (rope_box) {
+        const int cs_off = rope_box ? (n % p.head_dim) / 2 : -1;
+        if (rope_box && cs_off != cs_at) {
           const int half = p.head_dim >> 1;
-          const float4 *cs4 = reinterpret_cast<const float4 *>(p.rope + (gm % p.rope_T) * half + (n % p.head_dim) / 2);
+          const float4 *cs4 = reinterpret_cast<const float4 *>(p.rope + (gm % p.rope_T) * half + cs_off);
 #pragma unroll
           for (int i = 0; i < 16; i++) {
             const float4 t = cs4[i];
             cs[2 * i] = make_float2(t.x, t.y);
             cs[2 * i + 1] = make_float2(t.z, t.w);
           }
+          cs_at = cs_off;
         }
         float v[64];
 #pragma unroll
