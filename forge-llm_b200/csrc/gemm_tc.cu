@@ -487,19 +487,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if (SW == 2) {
         const int nb = (min(BN, p.N - n0) + 63) / 64;   // p.N = H, a multiple of 64
-#pragma unroll 1
-        for (int c = 0; c < nb; c++) {
-          const int j = n0 + c * 64;
-          // dg goes through staging buffer 0 and du through buffer 1, both
-          // written 32 columns at a time
-          if (lane == 0) bulk_wait_read<0>();
-          __syncwarp();
-          // this row's forward g and u for the whole box, loaded before the
-          // TMEM reads so the latencies overlap
-          uint4 g4[8], u4[8];
-          if (gm < p.M) {
-            const uint4 *gp = reinterpret_cast<const uint4 *>(p.aux + gm * 2 * p.H + j);
-            const uint4 *up = reinterpret_cast<const uint4 *>(p.aux + gm * 2 * p.H + p.H + j);
+        // this row's forward g and u for box c (8 x 16 bytes of each), loaded
+        // one box ahead so their latency overlaps the previous box's work
+        auto load_gu = [&](int c, uint4 (&g4)[8], uint4 (&u4)[8]) {
+          if (gm < p.M && c < nb) {
+            const uint4 *gp = reinterpret_cast<const uint4 *>(p.aux + gm * 2 * p.H + n0 + c * 64);
+            const uint4 *up = reinterpret_cast<const uint4 *>(p.aux + gm * 2 * p.H + p.H + n0 + c * 64);
 #pragma unroll
             for (int i = 0; i < 8; i++) {
               g4[i] = __ldg(gp + i);
@@ -509,10 +502,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
             for (int i = 0; i < 8; i++) g4[i] = u4[i] = make_uint4(0u, 0u, 0u, 0u);
           }
+        };
+        uint4 g4[8], u4[8];
+        load_gu(0, g4, u4);
+#pragma unroll 1
+        for (int c = 0; c < nb; c++) {
+          const int j = n0 + c * 64;
+          uint32_t r0[32], r1[32];
+          tmem_ld32_nw(tbase + (uint32_t)(c * 64), r0);
+          tmem_ld32_nw(tbase + (uint32_t)(c * 64 + 32), r1);
+          uint4 gn[8], un[8];
+          load_gu(c + 1, gn, un);
+          tmem_wait_ld_r(r0);
+          tmem_wait_ld_r(r1);
+          if (c == nb - 1) release_acc(acc);       // accumulator no longer needed
+          // dg goes through staging buffer 0 and du through buffer 1, both
+          // written 32 columns at a time
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
 #pragma unroll
           for (int h = 0; h < 2; h++) {
-            uint32_t r[32];
-            tmem_ld32(tbase + (uint32_t)(c * 64 + 32 * h), r);
 #pragma unroll
             for (int i = 0; i < 4; i++) {
               const uint4 ga = g4[4 * h + i], ua = u4[4 * h + i];
@@ -521,6 +530,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               uint32_t og[4], ou[4];
 #pragma unroll
               for (int k = 0; k < 4; k++) {
+                const uint32_t *r = h ? r1 : r0;
                 const uint32_t dw = pack2_bf16(__uint_as_float(r[8 * i + 2 * k]), __uint_as_float(r[8 * i + 2 * k + 1]));
                 swiglu_bwd_pair(dw, gw[k], uw[k], og[k], ou[k]);
               }
@@ -529,13 +539,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               *reinterpret_cast<uint4 *>(stg + EPI_BOX + off) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
             }
           }
-          if (c == nb - 1) release_acc(acc);       // accumulator no longer needed
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0 && m_box < p.M) {
             tma_store_2d(&tmC, stg, j, m_box);
             tma_store_2d(&tmC, stg + EPI_BOX, p.H + j, m_box);
             bulk_commit();
+          }
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            g4[i] = gn[i];
+            u4[i] = un[i];
           }
         }
         if (nb == 0) release_acc(acc);
