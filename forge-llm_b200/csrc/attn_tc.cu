@@ -9,14 +9,15 @@
 // P and dS are re-used from the accumulator registers as the A operand of the
 // next product).
 //
-// Two input flavours share the kernels:
-//   fp32 tensors (the op-level API): rounded to bf16 while staged;
-//   bf16 tensors (the fused model path): q, k, v read straight out of one
-//   [N, (nH+2nKV)*dH] qkv buffer by row stride + column offset, staged with
-//   cp.async into double-buffered tiles so the next tile loads during the
-//   current tile's MMAs.  There O is written in bf16, and dQ/dK/dV are
-//   written in bf16 into one dqkv buffer with the RoPE backward (R^T,
-//   src/L2/tensor.js:150-165) applied to dQ and dK on the way out.
+// These mma.sync kernels serve the op-level API (fp32 tensors, rounded to
+// bf16 while staged) when its operands cannot take the tcgen05 path of
+// attn_tmem.cu (a tensor that is not 16-byte aligned).  The fused model
+// path's bf16 entries at the end of this file validate their operands and
+// always run the tcgen05 kernels.  The templates also take bf16 tensors read
+// straight out of one [N, (nH+2nKV)*dH] qkv buffer by row stride and column
+// offset (O and dQ/dK/dV written in bf16, the RoPE backward R^T,
+// src/L2/tensor.js:150-165, applied to dQ and dK on the way out); no entry
+// instantiates that flavour now.
 //
 // Backward is two deterministic kernels (no atomics):
 //   dK/dV: a CTA owns 64 keys of one kv head and sweeps the group's q heads
@@ -714,19 +715,8 @@ int fcu_attn_fwd_bf16(fcu_ctx *ctx, const void *qkv, int64_t ld_qkv, int B, int 
   FCU_REQUIRE(qkv && O && lse && (((uintptr_t)qkv | (uintptr_t)O) & 15) == 0,
               "fcu_attn_fwd_bf16: null or unaligned pointer");
   if (attn_tmem_fwd_supported(dH)) return attn_fwd_tmem(ctx, qkv, ld_qkv, B, T, nH, nKV, O, lse, dH);
-  if (attn_tmem_padded(dH)) return attn_fwd_tmem_padded(ctx, qkv, ld_qkv, B, T, nH, nKV, dH, O, lse);
-  const int64_t qD = (int64_t)nH * dH, kvD = (int64_t)nKV * dH;
-  Args a{};
-  a.q = {qkv, ld_qkv, 0};
-  a.k = {qkv, ld_qkv, qD};
-  a.v = {qkv, ld_qkv, qD + kvD};
-  a.o = {O, qD, 0};
-  a.lse = lse;
-  a.T = T;
-  a.nH = nH;
-  a.nKV = nKV;
-  a.scale = (float)(1.0 / sqrt((double)dH));
-  return fwd_dispatch<__nv_bfloat16, __nv_bfloat16>(ctx->stream, a, B, dH);
+  // dH is 16 or 32 here: zero-padded to 64-column heads
+  return attn_fwd_tmem_padded(ctx, qkv, ld_qkv, B, T, nH, nKV, dH, O, lse);
 }
 
 int fcu_attn_bwd_bf16(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_qkv, const void *O,
@@ -742,7 +732,7 @@ int fcu_attn_bwd_bf16(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_
   FCU_REQUIRE(dO && qkv && O && lse && dqkv &&
                   (((uintptr_t)dO | (uintptr_t)qkv | (uintptr_t)O | (uintptr_t)dqkv) & 15) == 0,
               "fcu_attn_bwd_bf16: null or unaligned pointer");
-  const int64_t qD = (int64_t)nH * dH, kvD = (int64_t)nKV * dH;
+  const int64_t kvD = (int64_t)nKV * dH;
   if (attn_tmem_supported(dH)) {
     // tcgen05 kernels, one CTA per SM: split dK/dV per q head when one CTA
     // per kv head would leave the GPU with fewer than 4 CTAs per SM.
@@ -763,47 +753,8 @@ int fcu_attn_bwd_bf16(fcu_ctx *ctx, const void *dO, const void *qkv, int64_t ld_
     return attn_bwd_tmem(ctx, dO, qkv, ld_qkv, O, lse, (float *)scr, B, T, nH, nKV, rope, dqkv, split,
                          pk, pv, dH);
   }
-  if (attn_tmem_padded(dH))
-    return attn_bwd_tmem_padded(ctx, dO, qkv, ld_qkv, O, lse, B, T, nH, nKV, dH, rope_theta, dqkv);
-  // Small grids (few sequences per GPU) balance the causal work better with
-  // one dK/dV CTA per q head and a reduction over each GQA group.
-  const int64_t kv_ctas = (int64_t)div_up(T, kTile) * nKV * B;
-  const int split = (nH > nKV && kv_ctas < 8 * (int64_t)ctx->num_sms) ? 1 : 0;
-  const size_t delta_bytes = (sizeof(float) * (size_t)B * nH * T + 255) & ~(size_t)255;
-  const size_t part_bytes = split ? sizeof(float) * (size_t)(nH / nKV) * B * T * kvD : 0;
-  void *scr = nullptr;
-  int rc = ctx_scratch(ctx, delta_bytes + 2 * part_bytes, &scr);
-  if (rc) return rc;
-  Args a{};
-  a.split_heads = split;
-  a.rows = (int64_t)B * T;
-  if (split) {
-    a.pk = (float *)((uint8_t *)scr + delta_bytes);
-    a.pv = (float *)((uint8_t *)scr + delta_bytes + part_bytes);
-  }
-  a.q = {qkv, ld_qkv, 0};
-  a.k = {qkv, ld_qkv, qD};
-  a.v = {qkv, ld_qkv, qD + kvD};
-  a.o_in = {O, qD, 0};
-  a.dO = {dO, qD, 0};
-  a.dq = {dqkv, ld_qkv, 0};
-  a.dk = {dqkv, ld_qkv, qD};
-  a.dv = {dqkv, ld_qkv, qD + kvD};
-  a.lse = const_cast<float *>(lse);
-  a.delta = (const float *)scr;
-  a.T = T;
-  a.nH = nH;
-  a.nKV = nKV;
-  a.scale = (float)(1.0 / sqrt((double)dH));
-  if (rope_theta > 0) {
-    rc = rope_table_f32(ctx, T, dH, rope_theta, &a.rope);
-    if (rc) return rc;
-  }
-  const int64_t rows = (int64_t)B * T * nH;
-  attn_delta_tc_kernel<__nv_bfloat16><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, ctx->stream>>>(
-      a, B, dH);
-  FCU_CHECK_LAUNCH();
-  return bwd_dispatch<__nv_bfloat16, __nv_bfloat16>(ctx->stream, a, B, dH);
+  // dH is 16 or 32 here: zero-padded to 64-column heads
+  return attn_bwd_tmem_padded(ctx, dO, qkv, ld_qkv, O, lse, B, T, nH, nKV, dH, rope_theta, dqkv);
 }
 
 }  // extern "C"
