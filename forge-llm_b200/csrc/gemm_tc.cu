@@ -913,10 +913,10 @@ int pair_setting() {
 }
 
 // Clusters of two GEMM CTAs that fit on the device at once (every pair
-// instantiation has the same block and shared-memory size).
+// instantiation has the same block and shared-memory size); 0 when none fits.
 int pair_slots(fcu_ctx *ctx, int *out) {
-  static int slots = 0;
-  if (!slots) {
+  static int slots = -1;
+  if (slots < 0) {
     auto kern = gemm_bf16_tc_kernel<256, 0, true>;
     FCU_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)TileCfg<256, true>::SMEM_BYTES));
@@ -933,11 +933,7 @@ int pair_slots(fcu_ctx *ctx, int *out) {
     cfg.numAttrs = 1;
     int n = 0;
     FCU_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
-    if (n < 1) {
-      set_error("no CTA pair of the tensor-core GEMM fits on this device");
-      return FCU_ERR_UNSUPPORTED;
-    }
-    slots = n;
+    slots = n > 0 ? n : 0;
   }
   *out = slots;
   return FCU_OK;
@@ -970,6 +966,52 @@ int choose_splits(int64_t tiles, int nk, int64_t slots, int64_t outputs) {
   return best;
 }
 
+}  // namespace
+
+// How one product runs: the tile (CTA pair or single CTA, width bn), the K
+// slices and the raster.  A pure function of the shape, the output mode and
+// the device (num_sms SMs; slots_pair CTA pairs fit at once, 0: none), so
+// the host can state the plan without a GPU (fcu_gemm_plan).  setting is
+// FORGECU_GEMM_PAIR (-1 unset, 0 never, 1 wherever the shape allows).
+//   Tile: the CTA pair (256 x 256 over two SMs) whenever the product has at
+//   least two waves of pair tiles, or a contraction long enough to split;
+//   otherwise single-CTA 128 x 256 tiles, or 128 x 128 where those would
+//   leave SMs idle in the last wave.
+//   Split-K when a product has too few output tiles to fill the GPU twice
+//   over and a long contraction (the weight gradients, whose contraction
+//   runs over every token; the LM-head input gradient): choose_splits.
+//   Raster n-fastest when a wave holds at least two whole rows of tiles.
+struct GemmPlan {
+  bool pair;          // CTA-pair tile (256 x 256 over two SMs)
+  int bn;             // output columns per tile
+  int splits;         // K slices (1: none)
+  bool row_major;     // n-fastest raster
+  int tiles_m, tiles_n;
+};
+
+GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int mode, int num_sms, int slots_pair, int setting) {
+  GemmPlan g;
+  const int nk = (int)((K + BK - 1) / BK);
+  const bool swiglu = mode == kOutSwiGLU || mode == kOutSwiGLUBwd;
+  const int64_t tiles256 = ((M + BM - 1) / BM) * ((N + 255) / 256);
+  const int64_t tiles_pair = ((M + 255) / 256) * ((N + 255) / 256);
+  g.pair = slots_pair > 0 && M > BM && setting != 0 &&
+           (setting == 1 || tiles_pair >= num_sms || (!swiglu && nk >= 32));
+  const int slots = g.pair ? slots_pair : num_sms;   // concurrent work units
+  const int64_t tiles = g.pair ? tiles_pair : tiles256;
+  g.splits = 1;
+  if (!swiglu && tiles < 2 * slots && nk >= 32) g.splits = choose_splits(tiles, nk, slots, M * N);
+  // (the SwiGLU forward pairs gate and up halves in one 256-wide tile)
+  g.bn = (!g.pair && mode != kOutSwiGLU && g.splits == 1 && tiles256 < 2 * num_sms && N > 128) ? 128 : 256;
+  const int tile_m = g.pair ? 2 * BM : BM;
+  g.tiles_m = (int)((M + tile_m - 1) / tile_m);
+  g.tiles_n = mode == kOutSwiGLU ? (int)(N / 256) : (int)((N + g.bn - 1) / g.bn);
+  g.row_major = 2 * g.tiles_n <= slots;
+  return g;
+}
+
+namespace {
+
 // Launches one instantiation (its shared-memory opt-in set on first use).
 // PAIR instantiations launch in clusters of two CTAs; `units` caps the grid
 // at one cluster (PAIR) or CTA per work unit.
@@ -983,6 +1025,10 @@ int launch_tc(fcu_ctx *ctx, int units, const CUtensorMap &ta, const CUtensorMap 
   if (PAIR) {
     const int rc = pair_slots(ctx, &max_clusters);
     if (rc) return rc;
+    if (max_clusters < 1) {
+      set_error("no CTA pair of the tensor-core GEMM fits on this device");
+      return FCU_ERR_UNSUPPORTED;
+    }
   }
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
@@ -1022,32 +1068,12 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
                  int64_t M, int64_t N, int64_t K, const TcOut &o, int *err) {
   int rc = tc_get_encode();
   if (rc) return rc;
-  // Tile: the CTA pair (256 x 256 over two SMs) whenever the product has at
-  // least two waves of pair tiles, or a contraction long enough to split
-  // (below); otherwise single-CTA 128 x 256 tiles, or 128 x 128 where those
-  // would leave SMs idle in the last wave.
-  // Split-K when a product has too few output tiles to fill the GPU twice
-  // over and a long contraction (the weight gradients, whose contraction runs
-  // over every token; the LM-head input gradient): each slice keeps at least
-  // 16 k-blocks, so the partial-tile traffic stays small next to the MMAs,
-  // and the slice count is chosen for the fullest last wave.
-  const int nk = (int)((K + BK - 1) / BK);
+  int slots_pair = 0;
+  if (pair_setting() != 0 && (rc = pair_slots(ctx, &slots_pair))) return rc;
+  const GemmPlan plan = plan_gemm(M, N, K, o.mode, ctx->num_sms, slots_pair, pair_setting());
+  const bool pair = plan.pair;
+  const int splits = plan.splits, bn = plan.bn;
   const bool swiglu = o.mode == kOutSwiGLU || o.mode == kOutSwiGLUBwd;
-  const int64_t tiles256 = ((M + BM - 1) / BM) * ((N + 255) / 256);
-  const int64_t tiles_pair = ((M + 255) / 256) * ((N + 255) / 256);
-  const int ps = pair_setting();
-  const bool pair = M > BM && ps != 0 &&
-                    (ps == 1 || tiles_pair >= ctx->num_sms || (!swiglu && nk >= 32));
-  int slots = ctx->num_sms;   // concurrent work units
-  if (pair) {
-    rc = pair_slots(ctx, &slots);
-    if (rc) return rc;
-  }
-  const int64_t tiles = pair ? tiles_pair : tiles256;
-  int splits = 1;
-  if (!swiglu && tiles < 2 * slots && nk >= 32) splits = choose_splits(tiles, nk, slots, M * N);
-  // (the SwiGLU forward pairs gate and up halves in one 256-wide tile)
-  const int bn = (!pair && o.mode != kOutSwiGLU && splits == 1 && tiles256 < 2 * ctx->num_sms && N > 128) ? 128 : 256;
   const uint32_t b_rows = pair ? 128u : (uint32_t)bn;   // B rows one CTA stages
   CUtensorMap ta, tb;
   int a_mn = 0, b_mn = 0;
@@ -1085,8 +1111,8 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
   p.a_mn = a_mn;
   p.b_mn = b_mn;
   const int tile_m = pair ? 2 * BM : BM;
-  p.tiles_m = (int)((M + tile_m - 1) / tile_m);
-  p.tiles_n = o.mode == kOutSwiGLU ? (int)(N / 256) : (int)((N + bn - 1) / bn);
+  p.tiles_m = plan.tiles_m;
+  p.tiles_n = plan.tiles_n;
   p.H = o.mode == kOutSwiGLU ? (int)(N / 2) : (int)N;
   p.aux = o.aux;
   p.err = err;
@@ -1131,8 +1157,7 @@ int gemm_bf16_tc(fcu_ctx *ctx, GemmOp op, const __nv_bfloat16 *A, const __nv_bfl
       p.tma_out = 1;
     }
   }
-  // n-fastest raster when a wave holds at least two whole rows of tiles
-  p.row_major = 2 * p.tiles_n <= slots;
+  p.row_major = plan.row_major;
   const int units = p.tiles_m * p.tiles_n * p.splits;
   const int sw = o.mode == kOutSwiGLU ? 1 : o.mode == kOutSwiGLUBwd ? 2 : 0;
   if (pair) {
@@ -1420,6 +1445,26 @@ extern "C" int fcu_gemm_bf16(fcu_ctx *ctx, int op, const void *A, const void *B,
   int rc = workspace(ctx, 0, &ws, &err);
   if (rc) return rc;
   return gemm_bf16_tc(ctx, gop, (const __nv_bfloat16 *)A, (const __nv_bfloat16 *)B, M, N, K, o, err);
+}
+
+// The plan fcu_gemm_bf16 follows for a product, from the same function, on
+// the host alone (plan_gemm).
+extern "C" int fcu_gemm_plan(int64_t M, int64_t N, int64_t K, int mode, int num_sms, int pair_slots,
+                             int pair_setting, int *plan) {
+  FCU_REQUIRE(plan != nullptr, "fcu_gemm_plan: null plan");
+  FCU_REQUIRE(M > 0 && N > 0 && K > 0 && M <= INT32_MAX && N <= INT32_MAX && K <= INT32_MAX,
+              "fcu_gemm_plan: shape M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  FCU_REQUIRE(num_sms > 0 && pair_slots >= 0, "fcu_gemm_plan: num_sms %d, pair_slots %d", num_sms, pair_slots);
+  FCU_REQUIRE(mode >= FCU_OUT_F32 && mode <= FCU_OUT_BF16_SWIGLU_BWD, "fcu_gemm_plan: unknown mode %d", mode);
+  const fcu::GemmPlan g =
+      fcu::plan_gemm(M, N, K, mode, num_sms, pair_slots, pair_setting < 0 ? -1 : (pair_setting ? 1 : 0));
+  plan[0] = g.pair ? 1 : 0;
+  plan[1] = g.bn;
+  plan[2] = g.splits;
+  plan[3] = g.row_major ? 1 : 0;
+  plan[4] = g.tiles_m;
+  plan[5] = g.tiles_n;
+  return FCU_OK;
 }
 
 namespace fcu {

@@ -111,6 +111,7 @@ _SIGS = {
     "fcu_sumsq": (_INT, [_P, _P, _I64, _P, _INT]),
     "fcu_scale": (_INT, [_P, _P, _I64, C.c_float]),
     "fcu_gemm_bf16": (_INT, [_P, _INT, _P, _P, _I64, _I64, _I64, _P]),
+    "fcu_gemm_plan": (_INT, [_I64, _I64, _I64, _INT, _INT, _INT, _INT, _P]),
     "fcu_rmsnorm_fwd_bf16": (_INT, [_P, _P, _P, _I64, _I64, _D, _P, _P]),
     "fcu_rmsnorm_fwd_bf16_add": (_INT, [_P, _P, _P, _P, _I64, _I64, _D, _P, _P, _P]),
     "fcu_rmsnorm_bwd_fused": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _P, _INT, _P, _P, _INT]),

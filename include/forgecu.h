@@ -154,6 +154,18 @@ typedef struct {
 int fcu_gemm_bf16(fcu_ctx *ctx, int op, const void *A, const void *B, int64_t M, int64_t N,
                   int64_t K, const fcu_gemm_out *out);
 
+/* The launch plan fcu_gemm_bf16 picks for an M x N x K product in output mode
+ * `mode` (FCU_OUT_*), computed on the host without a device: plan[0] = 1 for
+ * the CTA-pair tile (256 x 256 over two SMs, tcgen05 cta_group::2), plan[1] =
+ * the tile width in columns, plan[2] = the K slices (1: no split-K), plan[3] =
+ * 1 for the n-fastest tile raster, plan[4] / plan[5] = row / column tiles.
+ * num_sms and pair_slots describe the device (148 SMs and 74 concurrent CTA
+ * pairs on a B200; pair_slots 0 rules the pair tile out); pair_setting is the
+ * FORGECU_GEMM_PAIR switch (-1 unset, 0 never, 1 wherever the shape allows).
+ * Not in the reference: an introspection aid for the kernel choices. */
+int fcu_gemm_plan(int64_t M, int64_t N, int64_t K, int mode, int num_sms, int pair_slots, int pair_setting,
+                  int *plan);
+
 /* rmsNorm forward (src/L2/tensor.js:103-113) writing bf16 out[T,D] and fp32
  * inv[T].  D % 4 == 0. */
 int fcu_rmsnorm_fwd_bf16(fcu_ctx *ctx, const float *X, const float *w, int64_t T, int64_t D,
