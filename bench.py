@@ -39,7 +39,7 @@ GLOBAL_BATCH, SEQ, LR, SEED = 64, 1024, 3e-4, 5
 # DRAM bytes (read, written) of one launch of each distinct GEMM of the
 # config-5 step (batch 64), from one single-pass ncu capture of the 147 GEMM
 # launches of a step of `bench.py --steps 1 --warmup 1` (dram__bytes_read.sum /
-# dram__bytes_write.sum; the command is in profiles/gemm_dram_c5_shapes.md),
+# dram__bytes_write.sum, captured with `ncu --metrics ... -k regex:gemm_bf16 -s 147 -c 147`),
 # each shape the mean over its launches.  The twelve per-layer shapes run 12
 # times a step, the three LM-head shapes once.
 GEMM_DRAM_BY_SHAPE = {
